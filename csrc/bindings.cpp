@@ -1,0 +1,32 @@
+// Python bindings for every helexa_b200 CUDA op (one function per kernel family).
+#include <torch/extension.h>
+
+void gemv(torch::Tensor W, torch::Tensor x, torch::Tensor y, int64_t mode, c10::optional<torch::Tensor> resid,
+          c10::optional<torch::Tensor> norm_w, double eps);
+void gemv_experts(torch::Tensor W, torch::Tensor x, torch::Tensor ids, torch::Tensor y, int64_t mode,
+                  int64_t x_row_div, c10::optional<torch::Tensor> norm_w, double eps);
+void moe_topk(torch::Tensor logits, int64_t E, int64_t k, bool has_shared, bool norm_topk, torch::Tensor ids,
+              torch::Tensor wts);
+void moe_down(torch::Tensor Wd, torch::Tensor act, torch::Tensor ids, torch::Tensor wts, torch::Tensor x,
+              c10::optional<torch::Tensor> partial_out);
+void gdn_decode(torch::Tensor proj, torch::Tensor conv_w, torch::Tensor conv_ring, torch::Tensor rec,
+                torch::Tensor A_log, torch::Tensor dt_bias, torch::Tensor norm_w, torch::Tensor slots,
+                torch::Tensor pos, torch::Tensor out, int64_t Hk, int64_t Hv, int64_t Dk, int64_t Dv, double eps);
+void attn_decode(torch::Tensor proj, c10::optional<torch::Tensor> q_norm_w, c10::optional<torch::Tensor> k_norm_w,
+                 torch::Tensor inv_freq, torch::Tensor kc, torch::Tensor vc, torch::Tensor slots, torch::Tensor pos,
+                 torch::Tensor part_o, torch::Tensor part_ml, torch::Tensor counters, torch::Tensor out, int64_t Hq,
+                 int64_t Hkv, int64_t D, int64_t rot, bool gated, double eps);
+void embed(torch::Tensor E, torch::Tensor tok, torch::Tensor x);
+void argmax_step(torch::Tensor logits, torch::Tensor tok, c10::optional<torch::Tensor> slots,
+                 c10::optional<torch::Tensor> pos, c10::optional<torch::Tensor> out, c10::optional<torch::Tensor> step);
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.def("gemv", &gemv);
+  m.def("gemv_experts", &gemv_experts);
+  m.def("moe_topk", &moe_topk);
+  m.def("moe_down", &moe_down);
+  m.def("gdn_decode", &gdn_decode);
+  m.def("attn_decode", &attn_decode);
+  m.def("embed", &embed);
+  m.def("argmax_step", &argmax_step);
+}
