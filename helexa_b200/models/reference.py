@@ -119,9 +119,10 @@ def delta_rule_chunked(q, k, v, g, beta, state, chunk: int = 64):
     gc = g.cumsum(-1)                                             # [H, n, C]
     kb = k * beta[..., None]
     vb = v * beta[..., None]
-    lower = torch.tril(torch.ones(chunk, chunk, dtype=torch.bool), -1)
-    decay = torch.exp((gc[..., :, None] - gc[..., None, :]).masked_fill(~torch.tril(
-        torch.ones(chunk, chunk, dtype=torch.bool)), float("-inf")))
+    dev = q.device
+    lower = torch.tril(torch.ones(chunk, chunk, dtype=torch.bool, device=dev), -1)
+    causal = torch.tril(torch.ones(chunk, chunk, dtype=torch.bool, device=dev))
+    decay = torch.exp((gc[..., :, None] - gc[..., None, :]).masked_fill(~causal, float("-inf")))
     A = -(kb @ k.transpose(-1, -2)) * decay
     A = A.masked_fill(~lower, 0.0)
     # forward substitution: T = (I - A)^-1 applied row by row
@@ -129,12 +130,11 @@ def delta_rule_chunked(q, k, v, g, beta, state, chunk: int = 64):
     for i in range(1, chunk):
         row = Tm[..., i, :i].clone()
         Tm[..., i, :i] = row + (row[..., :, None] * Tm[..., :i, :i]).sum(-2)
-    Tm = Tm + torch.eye(chunk)
+    Tm = Tm + torch.eye(chunk, device=dev)
     u = Tm @ vb                                                   # [H, n, C, Dv]
     w = Tm @ (kb * torch.exp(gc)[..., None])                      # [H, n, C, Dk]
     S = state.clone().float()
-    out = torch.empty(H, n, chunk, Dv)
-    causal = torch.tril(torch.ones(chunk, chunk, dtype=torch.bool))
+    out = torch.empty(H, n, chunk, Dv, device=dev)
     for c in range(n):
         qi, ki = q[:, c], k[:, c]
         attn = (qi @ ki.transpose(-1, -2)) * decay[:, c]
