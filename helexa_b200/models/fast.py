@@ -1,0 +1,412 @@
+"""The CUDA model: fused per-rank weights, slot-pooled sequence state and a
+graph-captured decode step built from the sm_100a kernels in csrc/.
+
+State lives in preallocated pools indexed by a slot id, so batched decode works on
+any subset of live sequences without the reference's assemble/extract copies
+(harness/engine.rs:691-877, arch/qwen3_5/snapshot.rs:200-311):
+
+  pos       int32 [S]                 position of each slot's next token
+  kc, vc    bf16  [S, Hkv, maxlen, D] per full-attention layer (contiguous, never
+                                      re-concatenated -- the ref's ConcatKvCache
+                                      reallocates on every append, full_attn.rs:156)
+  conv      bf16  [S, C, K]           GDN conv inputs, ring indexed by position % K
+  rec       f32   [S, Hv, Dk, Dv]     GDN recurrent state
+
+A decode step (one token for each of B slots) is: embed -> per layer
+{norm-fused GEMV, fused token mixer, residual GEMV, MoE/MLP} -> norm-fused lm_head
+GEMV -> on-device arg-max that advances the slot positions. Every launch reads its
+dynamic inputs (token ids, slots, positions) from device memory, so the whole step
+is captured once per batch size and replayed.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Callable
+
+import torch
+
+from .. import ops
+from ..config import ModelConfig
+from . import layout
+
+
+@dataclass
+class DecodeBuffers:
+    B: int
+    tok: torch.Tensor          # int32 [B] current input token -> next token
+    slots: torch.Tensor        # int32 [B]
+    x: torch.Tensor            # bf16 [B, H] residual stream
+    proj_gdn: torch.Tensor | None
+    gdn_out: torch.Tensor | None
+    proj_attn: torch.Tensor | None
+    attn_out: torch.Tensor | None
+    part_o: torch.Tensor | None
+    part_ml: torch.Tensor | None
+    counters: torch.Tensor | None
+    rlogits: torch.Tensor | None
+    ids: torch.Tensor | None
+    wts: torch.Tensor | None
+    act_moe: torch.Tensor | None   # bf16 [B*J, moe_inter]
+    act_mlp: torch.Tensor | None   # bf16 [B, inter]
+    partial: torch.Tensor      # bf16 [B, H] row-parallel partial sums (TP)
+    logits: torch.Tensor       # f32 [B, V]
+    out_tokens: torch.Tensor   # int32 [B, cap]
+    step: torch.Tensor         # int32 [B]
+    graph: torch.cuda.CUDAGraph | None = None
+    graph_steps: int = 0
+
+
+class FastModel:
+    """CUDA inference model for Qwen3 / Qwen3-MoE / Qwen3-Next on one rank."""
+
+    def __init__(self, cfg: ModelConfig, layers: list[dict[str, torch.Tensor]], embed: torch.Tensor,
+                 lm_head: torch.Tensor, final_norm: torch.Tensor, dims: layout.LocalDims,
+                 device: torch.device, max_slots: int = 4, max_len: int = 16384, comm=None,
+                 attn_splits: int | None = None):
+        if device.type != "cuda":
+            raise ValueError("FastModel runs on CUDA only; use ReferenceModel on the CPU")
+        self.cfg, self.dims, self.device = cfg, dims, device
+        self.layers, self.embed_w, self.lm_head, self.final_norm = layers, embed, lm_head, final_norm
+        self.max_slots, self.max_len = max_slots, max_len
+        self.comm = comm  # parallel.TPComm or None (single rank)
+        self.C = ops.C
+        rd = cfg.rotary_dim
+        inv = 1.0 / (cfg.rope_theta ** (torch.arange(0, rd, 2, dtype=torch.int64).float() / rd))
+        self.inv_freq = inv.to(device)
+        self.has_shared = cfg.shared_expert_intermediate_size > 0
+        sm = torch.cuda.get_device_properties(device).multi_processor_count
+        self.attn_splits = attn_splits or max(1, min(64, sm // max(1, dims.hkv)))
+        # ---- state pools -------------------------------------------------
+        self.pos = torch.zeros(max_slots, dtype=torch.int32, device=device)
+        self.kc: dict[int, torch.Tensor] = {}
+        self.vc: dict[int, torch.Tensor] = {}
+        self.conv: dict[int, torch.Tensor] = {}
+        self.rec: dict[int, torch.Tensor] = {}
+        for i in range(cfg.num_hidden_layers):
+            if cfg.is_linear(i):
+                self.conv[i] = torch.zeros(max_slots, dims.gdn_conv, cfg.linear_conv_kernel_dim,
+                                           dtype=torch.bfloat16, device=device)
+                self.rec[i] = torch.zeros(max_slots, dims.hv, dims.dk, dims.dv, dtype=torch.float32,
+                                          device=device)
+            else:
+                shp = (max_slots, dims.hkv, max_len, dims.D)
+                self.kc[i] = torch.zeros(shp, dtype=torch.bfloat16, device=device)
+                self.vc[i] = torch.zeros(shp, dtype=torch.bfloat16, device=device)
+        self._bufs: dict[int, DecodeBuffers] = {}
+
+    # ------------------------------------------------------------------
+    # construction
+    # ------------------------------------------------------------------
+    @classmethod
+    def from_hf(cls, cfg: ModelConfig, get: Callable[[str], torch.Tensor] | dict, device,
+                rank: int = 0, ws: int = 1, **kw) -> "FastModel":
+        """Load from HF-layout tensors (a dict or a name -> tensor callable)."""
+        if isinstance(get, dict):
+            get = get.__getitem__
+        device = torch.device(device)
+        dims = layout.local_dims(cfg, rank, ws)
+        layers = []
+        for i in range(cfg.num_hidden_layers):
+            fl = layout.fuse_layer(cfg, dims, i, get)
+            layers.append({k: v.to(device) for k, v in fl.items()})
+        embed = get("model.embed_tokens.weight").to(device=device, dtype=torch.bfloat16).contiguous()
+        lm = embed if cfg.tie_word_embeddings else get("lm_head.weight").to(device=device, dtype=torch.bfloat16)
+        fn = layout.norm_f32(cfg, get("model.norm.weight")).to(device)
+        return cls(cfg, layers, embed, lm.contiguous(), fn, dims, device, **kw)
+
+    @classmethod
+    def random(cls, cfg: ModelConfig, device, seed: int = 0, rank: int = 0, ws: int = 1, std: float = 0.02,
+               **kw) -> "FastModel":
+        """Random-init N(0, std) directly in the fused layout on the device (large models)."""
+        device = torch.device(device)
+        dims = layout.local_dims(cfg, rank, ws)
+        g = torch.Generator(device=device).manual_seed(seed + 7919 * rank)
+
+        def mk(shape, dtype):
+            t = torch.empty(shape, dtype=dtype, device=device)
+            return t.normal_(0.0, std, generator=g)
+
+        layers = []
+        for i in range(cfg.num_hidden_layers):
+            lw = {}
+            for name, (shape, dtype) in layout.layer_shapes(cfg, dims, i).items():
+                t = mk(shape, dtype)
+                if name in ("ln1", "ln2", "q_norm", "k_norm"):
+                    t += cfg.norm_offset
+                lw[name] = t
+            layers.append(lw)
+        embed = mk((cfg.vocab_size, cfg.hidden_size), torch.bfloat16)
+        lm = embed if cfg.tie_word_embeddings else mk((cfg.vocab_size, cfg.hidden_size), torch.bfloat16)
+        fn = mk((cfg.hidden_size,), torch.float32) + cfg.norm_offset
+        return cls(cfg, layers, embed, lm, fn, dims, device, **kw)
+
+    def weight_bytes(self) -> int:
+        n = sum(t.numel() * t.element_size() for lw in self.layers for t in lw.values())
+        n += self.embed_w.numel() * 2 + (0 if self.lm_head is self.embed_w else self.lm_head.numel() * 2)
+        return n
+
+    def decode_bytes_per_token(self) -> int:
+        """Weight bytes a bs=1 decode step streams (active experts only)."""
+        cfg, n = self.cfg, 0
+        for i, lw in enumerate(self.layers):
+            for k, t in lw.items():
+                if k in ("w_gu", "w_d") and cfg.layer_uses_moe(i):
+                    per = t[0].numel() * t.element_size()
+                    n += per * (cfg.num_experts_per_tok + (1 if self.has_shared else 0))
+                else:
+                    n += t.numel() * t.element_size()
+        return n + self.lm_head.numel() * 2 + self.cfg.hidden_size * 2
+
+    # ------------------------------------------------------------------
+    # decode
+    # ------------------------------------------------------------------
+    def buffers(self, B: int, out_cap: int = 4096) -> DecodeBuffers:
+        if B in self._bufs:
+            return self._bufs[B]
+        cfg, d, dev = self.cfg, self.dims, self.device
+        bf, f32, i32 = torch.bfloat16, torch.float32, torch.int32
+        z = lambda *s, dt=bf: torch.zeros(*s, dtype=dt, device=dev)  # noqa: E731
+        J = cfg.num_experts_per_tok + (1 if self.has_shared else 0)
+        any_mlp = any(not cfg.layer_uses_moe(i) for i in range(cfg.num_hidden_layers))
+        nb = DecodeBuffers(
+            B=B, tok=z(B, dt=i32), slots=torch.arange(B, dtype=i32, device=dev), x=z(B, d.H),
+            proj_gdn=z(B, d.gdn_in_rows) if cfg.num_linear_layers else None,
+            gdn_out=z(B, d.gdn_vd) if cfg.num_linear_layers else None,
+            proj_attn=z(B, d.qkv_rows) if cfg.num_full_layers else None,
+            attn_out=z(B, d.hq * d.D) if cfg.num_full_layers else None,
+            part_o=z(B, d.hq, self.attn_splits, d.D, dt=f32) if cfg.num_full_layers else None,
+            part_ml=z(B, d.hq, self.attn_splits, 2, dt=f32) if cfg.num_full_layers else None,
+            counters=z(B, max(1, d.hkv), dt=i32) if cfg.num_full_layers else None,
+            rlogits=z(B, cfg.num_experts + (1 if self.has_shared else 0), dt=f32) if cfg.num_experts else None,
+            ids=z(B, J, dt=i32) if cfg.num_experts else None,
+            wts=z(B, J, dt=f32) if cfg.num_experts else None,
+            act_moe=z(B * J, d.moe_inter) if cfg.num_experts else None,
+            act_mlp=z(B, d.inter) if any_mlp else None,
+            partial=z(B, d.H),
+            logits=z(B, cfg.vocab_size, dt=f32), out_tokens=z(B, out_cap, dt=i32), step=z(B, dt=i32))
+        self._bufs[B] = nb
+        return nb
+
+    def _row_parallel(self, W, inp, nb: DecodeBuffers):
+        """x += W . inp, summed across TP ranks when the layer is sharded."""
+        if self.comm is None or self.dims.ws == 1:
+            self.C.gemv(W, inp, nb.x, ops.RESID_ADD, nb.x, None, 0.0)
+        else:
+            self.comm.gemv_allreduce_residual(W, inp, nb.x, nb.partial)
+
+    def _decode_layer(self, i: int, nb: DecodeBuffers):
+        C, cfg, d, lw = self.C, self.cfg, self.dims, self.layers[i]
+        eps = cfg.rms_norm_eps
+        if cfg.is_linear(i):
+            C.gemv(lw["w_in"], nb.x, nb.proj_gdn, ops.STORE_BF16, None, lw["ln1"], eps)
+            C.gdn_decode(nb.proj_gdn, lw["conv_w"], self.conv[i], self.rec[i], lw["A_log"], lw["dt_bias"],
+                         lw["gnorm"], nb.slots, self.pos, nb.gdn_out, d.hk, d.hv, d.dk, d.dv, eps)
+            self._row_parallel(lw["out_w"], nb.gdn_out, nb)
+        else:
+            C.gemv(lw["w_qkv"], nb.x, nb.proj_attn, ops.STORE_BF16, None, lw["ln1"], eps)
+            C.attn_decode(nb.proj_attn, lw.get("q_norm"), lw.get("k_norm"), self.inv_freq, self.kc[i], self.vc[i],
+                          nb.slots, self.pos, nb.part_o, nb.part_ml, nb.counters, nb.attn_out, d.hq, d.hkv, d.D,
+                          cfg.rotary_dim, cfg.attn_output_gate, eps)
+            self._row_parallel(lw["o_w"], nb.attn_out, nb)
+        if cfg.layer_uses_moe(i):
+            E, k = cfg.num_experts, cfg.num_experts_per_tok
+            J = k + (1 if self.has_shared else 0)
+            C.gemv(lw["router"], nb.x, nb.rlogits, ops.STORE_F32, None, lw["ln2"], eps)
+            C.moe_topk(nb.rlogits, E, k, self.has_shared, cfg.norm_topk_prob, nb.ids, nb.wts)
+            C.gemv_experts(lw["w_gu"], nb.x, nb.ids.view(-1), nb.act_moe, ops.SILU_PAIR, J, lw["ln2"], eps)
+            if self.comm is None or d.ws == 1:
+                C.moe_down(lw["w_d"], nb.act_moe, nb.ids, nb.wts, nb.x, None)
+            else:
+                self.comm.moe_down_allreduce_residual(lw["w_d"], nb.act_moe, nb.ids, nb.wts, nb.x, nb.partial)
+        else:
+            C.gemv(lw["w_gu"], nb.x, nb.act_mlp, ops.SILU_PAIR, None, lw["ln2"], eps)
+            self._row_parallel(lw["w_d"], nb.act_mlp, nb)
+
+    def decode_step_launch(self, nb: DecodeBuffers):
+        """Enqueue one decode step for the nb.B slots in nb.slots (graph-capturable)."""
+        C = self.C
+        C.embed(self.embed_w, nb.tok, nb.x)
+        for i in range(self.cfg.num_hidden_layers):
+            self._decode_layer(i, nb)
+        C.gemv(self.lm_head, nb.x, nb.logits, ops.STORE_F32, None, self.final_norm, self.cfg.rms_norm_eps)
+        C.argmax_step(nb.logits, nb.tok, nb.slots, self.pos, nb.out_tokens, nb.step)
+
+    def launches_per_step(self) -> int:
+        cfg = self.cfg
+        n = 3  # embed, lm_head, argmax
+        for i in range(cfg.num_hidden_layers):
+            n += 3 + (4 if cfg.layer_uses_moe(i) else 2)
+            if self.comm is not None and self.dims.ws > 1:
+                n += self.comm.launches_per_reduce * 2
+        return n
+
+    def capture(self, B: int, steps: int = 1) -> DecodeBuffers:
+        """Capture `steps` consecutive decode steps for batch B into one CUDA graph.
+
+        Capture runs one eager warm-up step first; pool state it touches (positions,
+        KV at the current position, GDN state) is saved and restored around it.
+        """
+        nb = self.buffers(B)
+        if nb.graph is not None and nb.graph_steps == steps:
+            return nb
+        saved = self._save_slots(nb.slots.tolist())
+        step_saved, tok_saved = nb.step.clone(), nb.tok.clone()
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            self.decode_step_launch(nb)
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        torch.cuda.synchronize(self.device)
+        self._restore_slots(saved)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            for _ in range(steps):
+                self.decode_step_launch(nb)
+        torch.cuda.synchronize(self.device)
+        nb.step.copy_(step_saved)
+        nb.tok.copy_(tok_saved)
+        nb.graph, nb.graph_steps = g, steps
+        return nb
+
+    def _save_slots(self, slots: list[int]):
+        return {"pos": self.pos.clone(),
+                "conv": {i: t[slots].clone() for i, t in self.conv.items()},
+                "rec": {i: t[slots].clone() for i, t in self.rec.items()}, "slots": slots}
+
+    def _restore_slots(self, saved):
+        sl = saved["slots"]
+        self.pos.copy_(saved["pos"])
+        for i, t in saved["conv"].items():
+            self.conv[i][sl] = t
+        for i, t in saved["rec"].items():
+            self.rec[i][sl] = t
+
+    def replay(self, nb: DecodeBuffers):
+        nb.graph.replay()
+
+    # ------------------------------------------------------------------
+    # prefill
+    # ------------------------------------------------------------------
+    def _rms(self, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        xf = x.float()
+        return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.cfg.rms_norm_eps) * w).to(torch.bfloat16)
+
+    def _reduce(self, t: torch.Tensor) -> torch.Tensor:
+        if self.comm is not None and self.dims.ws > 1:
+            self.comm.all_reduce_(t)
+        return t
+
+    def _gdn_prefill(self, i: int, h: torch.Tensor, slot: int, p0: int) -> torch.Tensor:
+        from .reference import causal_conv1d, delta_rule_chunked, delta_rule_recurrent, gdn_gating, l2norm
+        d, lw, cfg = self.dims, self.layers[i], self.cfg
+        T = h.shape[0]
+        kd, vd, K = d.gdn_kd, d.gdn_vd, cfg.linear_conv_kernel_dim
+        proj = h @ lw["w_in"].t()
+        mixed = proj[:, :2 * kd + vd]
+        z = proj[:, 2 * kd + vd:2 * kd + 2 * vd]
+        bb = proj[:, 2 * kd + 2 * vd:2 * kd + 2 * vd + d.hv]
+        aa = proj[:, 2 * kd + 2 * vd + d.hv:]
+        ring = self.conv[i][slot]                                   # [C, K]
+        prev = [p0 - (K - 1) + j for j in range(K - 1)]
+        state = torch.stack([ring[:, p % K] if p >= 0 else torch.zeros_like(ring[:, 0]) for p in prev], 1)
+        y, _ = causal_conv1d(mixed, lw["conv_w"], state)
+        y = y.to(torch.bfloat16)
+        for p in range(max(p0, p0 + T - K), p0 + T):
+            ring[:, p % K] = mixed[p - p0]
+        r = d.hv // d.hk
+        q = y[:, :kd].float().view(T, d.hk, d.dk).repeat_interleave(r, 1)
+        k = y[:, kd:2 * kd].float().view(T, d.hk, d.dk).repeat_interleave(r, 1)
+        v = y[:, 2 * kd:].float().view(T, d.hv, d.dv)
+        g, beta = gdn_gating(aa, bb, lw["A_log"], lw["dt_bias"])
+        q = l2norm(q) * (d.dk ** -0.5)
+        k = l2norm(k)
+        fn = delta_rule_chunked if T >= 64 else delta_rule_recurrent
+        o, S = fn(q, k, v, g, beta, self.rec[i][slot])
+        self.rec[i][slot] = S
+        o = o.to(torch.bfloat16).float()
+        o = o * torch.rsqrt(o.pow(2).mean(-1, keepdim=True) + cfg.rms_norm_eps)
+        o = o.to(torch.bfloat16).float() * lw["gnorm"]
+        o = (o * torch.nn.functional.silu(z.float().view(T, d.hv, d.dv))).to(torch.bfloat16)
+        return o.reshape(T, vd) @ lw["out_w"].t()
+
+    def _attn_prefill(self, i: int, h: torch.Tensor, slot: int, p0: int) -> torch.Tensor:
+        from .reference import apply_rope, rope_cos_sin
+        d, lw, cfg = self.dims, self.layers[i], self.cfg
+        T, D = h.shape[0], d.D
+        qkv = h @ lw["w_qkv"].t()
+        qp = qkv[:, :d.hq * d.qw].view(T, d.hq, d.qw)
+        q, gate = qp[..., :D], (qp[..., D:] if cfg.attn_output_gate else None)
+        k = qkv[:, d.hq * d.qw:d.hq * d.qw + d.hkv * D].view(T, d.hkv, D)
+        v = qkv[:, d.hq * d.qw + d.hkv * D:].view(T, d.hkv, D)
+        if "q_norm" in lw:
+            q, k = self._rms(q, lw["q_norm"]), self._rms(k, lw["k_norm"])
+        cos, sin = rope_cos_sin(torch.arange(p0, p0 + T, device=h.device), cfg.rotary_dim, cfg.rope_theta)
+        q = apply_rope(q.float(), cos, sin).to(torch.bfloat16)
+        k = apply_rope(k.float(), cos, sin).to(torch.bfloat16)
+        self.kc[i][slot, :, p0:p0 + T] = k.transpose(0, 1)
+        self.vc[i][slot, :, p0:p0 + T] = v.transpose(0, 1)
+        L = p0 + T
+        Kc, Vc = self.kc[i][slot, :, :L], self.vc[i][slot, :, :L]
+        mask = torch.arange(L, device=h.device)[None, :] <= torch.arange(p0, L, device=h.device)[:, None]
+        o = torch.nn.functional.scaled_dot_product_attention(
+            q.transpose(0, 1)[None], Kc[None], Vc[None], attn_mask=mask, enable_gqa=True)[0]
+        o = o.transpose(0, 1).reshape(T, d.hq * D)
+        if gate is not None:
+            o = (o.float() * torch.sigmoid(gate.reshape(T, d.hq * D).float())).to(torch.bfloat16)
+        return o @ lw["o_w"].t()
+
+    def _ffn_prefill(self, i: int, hn: torch.Tensor) -> torch.Tensor:
+        cfg, lw = self.cfg, self.layers[i]
+        silu = torch.nn.functional.silu
+        if not cfg.layer_uses_moe(i):
+            y = hn @ lw["w_gu"].t()
+            act = (silu(y[:, 0::2].float()).to(torch.bfloat16).float() * y[:, 1::2].float()).to(torch.bfloat16)
+            return act @ lw["w_d"].t()
+        E, k = cfg.num_experts, cfg.num_experts_per_tok
+        logits = (hn @ lw["router"].t()).float()
+        probs = torch.softmax(logits[:, :E], -1)
+        topv, topi = torch.topk(probs, k, -1)
+        if cfg.norm_topk_prob:
+            topv = topv / topv.sum(-1, keepdim=True)
+        out = torch.zeros(hn.shape[0], cfg.hidden_size, dtype=torch.float32, device=hn.device)
+        order = torch.argsort(topi.view(-1), stable=True)
+        counts = torch.bincount(topi.view(-1), minlength=E).tolist()
+        tok_of = order // k
+        w_of = topv.view(-1)[order]
+        start = 0
+        for e, c in enumerate(counts):
+            if c == 0:
+                continue
+            rows = tok_of[start:start + c]
+            y = hn[rows] @ lw["w_gu"][e].t()
+            act = (silu(y[:, 0::2].float()).to(torch.bfloat16).float() * y[:, 1::2].float()).to(torch.bfloat16)
+            out.index_add_(0, rows, (act @ lw["w_d"][e].t()).float() * w_of[start:start + c, None])
+            start += c
+        if self.has_shared:
+            y = hn @ lw["w_gu"][E].t()
+            act = (silu(y[:, 0::2].float()).to(torch.bfloat16).float() * y[:, 1::2].float()).to(torch.bfloat16)
+            out += (act @ lw["w_d"][E].t()).float() * torch.sigmoid(logits[:, E:E + 1])
+        return out.to(torch.bfloat16)
+
+    @torch.no_grad()
+    def prefill(self, slot: int, tokens: torch.Tensor, p0: int) -> torch.Tensor:
+        """Run `tokens` (device int tensor [T]) for `slot` starting at position p0.
+
+        Updates the slot's KV / GDN state and position; returns the last token's
+        f32 logits [V].
+        """
+        cfg = self.cfg
+        T = tokens.shape[0]
+        if p0 + T > self.max_len:
+            raise ValueError(f"sequence of {p0 + T} tokens exceeds max_len {self.max_len}")
+        x = self.embed_w[tokens.long()]
+        for i in range(cfg.num_hidden_layers):
+            lw = self.layers[i]
+            h = self._rms(x, lw["ln1"])
+            o = self._gdn_prefill(i, h, slot, p0) if cfg.is_linear(i) else self._attn_prefill(i, h, slot, p0)
+            x = x + self._reduce(o)
+            o = self._ffn_prefill(i, self._rms(x, lw["ln2"]))
+            x = x + self._reduce(o)
+        last = self._rms(x[-1:], self.final_norm)
+        self.pos[slot] = p0 + T
+        return (last @ self.lm_head.t()).float()[0]
