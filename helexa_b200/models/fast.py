@@ -30,6 +30,10 @@ from ..config import ModelConfig
 from . import layout
 
 
+# Tests of the prefill layout logic (pure torch ops) may build the model on the CPU.
+_allow_cpu_prefill = False
+
+
 @dataclass
 class DecodeBuffers:
     B: int
@@ -63,18 +67,18 @@ class FastModel:
                  lm_head: torch.Tensor, final_norm: torch.Tensor, dims: layout.LocalDims,
                  device: torch.device, max_slots: int = 4, max_len: int = 16384, comm=None,
                  attn_splits: int | None = None):
-        if device.type != "cuda":
+        if device.type != "cuda" and not _allow_cpu_prefill:
             raise ValueError("FastModel runs on CUDA only; use ReferenceModel on the CPU")
         self.cfg, self.dims, self.device = cfg, dims, device
         self.layers, self.embed_w, self.lm_head, self.final_norm = layers, embed, lm_head, final_norm
         self.max_slots, self.max_len = max_slots, max_len
         self.comm = comm  # parallel.TPComm or None (single rank)
-        self.C = ops.C
+        self.C = ops.C if device.type == "cuda" else None
         rd = cfg.rotary_dim
         inv = 1.0 / (cfg.rope_theta ** (torch.arange(0, rd, 2, dtype=torch.int64).float() / rd))
         self.inv_freq = inv.to(device)
         self.has_shared = cfg.shared_expert_intermediate_size > 0
-        sm = torch.cuda.get_device_properties(device).multi_processor_count
+        sm = torch.cuda.get_device_properties(device).multi_processor_count if device.type == "cuda" else 1
         self.attn_splits = attn_splits or max(1, min(64, sm // max(1, dims.hkv)))
         # ---- state pools -------------------------------------------------
         self.pos = torch.zeros(max_slots, dtype=torch.int32, device=device)
