@@ -20,6 +20,13 @@ void embed(torch::Tensor E, torch::Tensor tok, torch::Tensor x);
 void argmax_step(torch::Tensor logits, torch::Tensor tok, c10::optional<torch::Tensor> slots,
                  c10::optional<torch::Tensor> pos, c10::optional<torch::Tensor> out, c10::optional<torch::Tensor> step);
 
+std::vector<torch::Tensor> ipc_alloc(int64_t bytes, int64_t device);
+int64_t ipc_open(torch::Tensor handle, int64_t device);
+void ipc_close(int64_t ptr);
+void ar_oneshot(std::vector<int64_t> peer_bases, int64_t rank, torch::Tensor partial, torch::Tensor x,
+                c10::optional<torch::Tensor> out_plain, int64_t data_bytes, torch::Tensor epoch, torch::Tensor err,
+                int64_t ctas, double timeout_s);
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemv", &gemv);
   m.def("gemv_experts", &gemv_experts);
@@ -29,4 +36,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_decode", &attn_decode);
   m.def("embed", &embed);
   m.def("argmax_step", &argmax_step);
+  m.def("ipc_alloc", &ipc_alloc);
+  m.def("ipc_open", &ipc_open);
+  m.def("ipc_close", &ipc_close);
+  m.def("ar_oneshot", &ar_oneshot);
 }

@@ -1,0 +1,116 @@
+"""Tensor-parallel communicator for one process per GPU.
+
+Two reduction backends for the row-parallel layers (attention o_proj, GDN out_proj,
+MLP down_proj, MoE block end -- the reference's two all-reduces per decoder layer,
+tp/tp_linear.rs:285-293, tp/tp_qwen3_5.rs:1268-1271):
+
+  "p2p"   (default) one-shot reduction over CUDA-IPC peer buffers on NVLink, fused
+          with the residual add, bounded waits, CUDA-graph safe (csrc/allreduce.cu)
+  "nccl"  the reference-equivalent baseline: ncclAllReduce (through
+          torch.distributed) of the row-parallel partial, then the residual add
+
+Rendezvous and prefill-size reductions use torch.distributed (NCCL on GPUs, gloo on
+CPU ranks in tests), standing in for the reference's hex-encoded ncclUniqueId sent
+over worker stdin (tp/nccl_state.rs:120-359).
+"""
+from __future__ import annotations
+
+import os
+
+import torch
+import torch.distributed as dist
+
+from .. import ops
+
+_FLAG_BYTES = 4096
+
+
+class TPError(RuntimeError):
+    """A peer failed to arrive within the reduction timeout (see `check`)."""
+
+
+class TPComm:
+    def __init__(self, group=None, device: torch.device | None = None, mode: str | None = None,
+                 max_elems: int = 8 * 16384, timeout_s: float = 5.0):
+        self.group = group or dist.group.WORLD
+        self.ws = dist.get_world_size(self.group)
+        self.rank = dist.get_rank(self.group)
+        self.device = device or torch.device("cpu")
+        self.mode = mode or os.environ.get("HELEXA_TP_MODE", "p2p")
+        if self.device.type != "cuda":
+            self.mode = "host"
+        self.timeout_s = timeout_s
+        self.launches_per_reduce = 1
+        if self.mode == "p2p":
+            self._init_p2p(max_elems)
+
+    # ---- rendezvous of the IPC regions ----------------------------------
+    def _init_p2p(self, max_elems: int):
+        C = ops.C
+        self.data_bytes = ((max_elems * 2 + 255) // 256) * 256
+        region, handle = C.ipc_alloc(_FLAG_BYTES + 2 * self.data_bytes, self.device.index)
+        self._region = region
+        handles: list = [None] * self.ws
+        dist.all_gather_object(handles, bytes(handle.numpy().tobytes()), group=self.group)
+        self.bases: list[int] = []
+        self._opened: list[int] = []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                self.bases.append(region.data_ptr())
+            else:
+                p = C.ipc_open(torch.frombuffer(bytearray(h), dtype=torch.uint8), self.device.index)
+                self.bases.append(p)
+                self._opened.append(p)
+        self.epoch = torch.zeros(2, dtype=torch.int32, device=self.device)
+        self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
+        dist.barrier(group=self.group)
+
+    def close(self):
+        if self.mode == "p2p":
+            torch.cuda.synchronize(self.device)
+            dist.barrier(group=self.group)
+            for p in self._opened:
+                ops.C.ipc_close(p)
+            self._opened = []
+
+    def check(self):
+        """Raise TPError if a device-side wait timed out since the last check."""
+        if self.mode == "p2p":
+            e = int(self.err.item())
+            if e:
+                raise TPError(f"rank {self.rank}: peer {e - 1000} did not arrive within {self.timeout_s}s")
+
+    # ---- reductions -------------------------------------------------------
+    def all_reduce_(self, t: torch.Tensor) -> torch.Tensor:
+        """Sum in place across ranks (prefill-sized tensors)."""
+        if self.mode == "p2p" and t.numel() * 2 <= self.data_bytes and t.dtype == torch.bfloat16:
+            flat = t.view(-1)
+            ops.C.ar_oneshot(self.bases, self.rank, flat, flat, flat, self.data_bytes, self.epoch, self.err,
+                             self._ctas(flat.numel()), self.timeout_s)
+            return t
+        dist.all_reduce(t, group=self.group)
+        return t
+
+    def _ctas(self, n: int) -> int:
+        return max(1, min(64, (n + 2047) // 2048))
+
+    def _reduce_residual(self, partial: torch.Tensor, x: torch.Tensor):
+        if self.mode == "p2p":
+            ops.C.ar_oneshot(self.bases, self.rank, partial.view(-1), x.view(-1), None, self.data_bytes,
+                             self.epoch, self.err, self._ctas(partial.numel()), self.timeout_s)
+        else:
+            dist.all_reduce(partial, group=self.group)
+            x.add_(partial)
+
+    def gemv_allreduce_residual(self, W, inp, x, partial):
+        """x += allreduce(W . inp) for a row-parallel layer at decode."""
+        B = x.shape[0]
+        p = partial[:B]
+        ops.C.gemv(W, inp, p, ops.STORE_BF16, None, None, 0.0)
+        self._reduce_residual(p, x)
+
+    def moe_down_allreduce_residual(self, Wd, act, ids, wts, x, partial):
+        B = x.shape[0]
+        p = partial[:B]
+        ops.C.moe_down(Wd, act, ids, wts, x, p)
+        self._reduce_residual(p, x)

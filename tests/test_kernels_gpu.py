@@ -93,7 +93,7 @@ def test_gdn_decode_matches_recurrent(Dk, Hk, Hv):
     C.gdn_decode(proj, conv_w, ring, rec, A_log, dt_bias, nw, slots, pos, out, Hk, Hv, Dk, Dv, 1e-6)
     r = Hv // Hk
     for b in range(B):
-        s, p = int(slots[b]), int(pos[s])
+        s = int(slots[b]); p = int(pos[s])
         x = proj[b].float()
         mixed = x[:Cc]
         prev = torch.stack([ring0[s][:, (p - 3 + j) % K].float() if p - 3 + j >= 0 else torch.zeros(Cc, device="cuda")
@@ -143,7 +143,7 @@ def test_attn_decode(D, Hq, Hkv, gated, L):
         C.attn_decode(proj, qn, kn, inv, kc, vc, slots, pos, part_o, part_ml, cnt, out, Hq, Hkv, D, rot, gated, 1e-6)
         assert int(cnt.abs().sum()) == 0
         for b in range(B):
-            s, p = int(slots[b]), int(pos[slots[b]])
+            s = int(slots[b]); p = int(pos[s])
             x = proj[b]
             q = x[:Hq * qw].view(Hq, qw)[:, :D]
             gate = x[:Hq * qw].view(Hq, qw)[:, D:] if gated else None
