@@ -27,6 +27,10 @@ void ar_oneshot(std::vector<int64_t> peer_bases, int64_t rank, torch::Tensor par
                 c10::optional<torch::Tensor> out_plain, int64_t data_bytes, torch::Tensor epoch, torch::Tensor err,
                 int64_t ctas, double timeout_s);
 
+void gemm(torch::Tensor A, torch::Tensor B, torch::Tensor C, int64_t epi, torch::Tensor err);
+void gemm_grouped(torch::Tensor A, torch::Tensor B, torch::Tensor C, torch::Tensor tiles, int64_t n, int64_t epi,
+                  torch::Tensor err);
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemv", &gemv);
   m.def("gemv_experts", &gemv_experts);
@@ -40,4 +44,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ipc_open", &ipc_open);
   m.def("ipc_close", &ipc_close);
   m.def("ar_oneshot", &ar_oneshot);
+  m.def("gemm", &gemm);
+  m.def("gemm_grouped", &gemm_grouped);
 }

@@ -1,0 +1,310 @@
+// Persistent warp-specialised bf16 GEMM on the 5th-generation tensor cores.
+//
+//   C[m, n] = sum_k A[m, k] * B[n, k]        (A: [M, K] row-major, B: [N, K] row-major,
+//                                            i.e. y = x W^T for an nn.Linear weight W)
+//
+// Per CTA (one per SM, persistent over tiles): warp 0 issues TMA loads of 128x64 A
+// and BNx64 B tiles into a STAGES-deep shared-memory ring; warp 1 allocates TMEM and
+// issues tcgen05.mma (M=128, N=BN, K=16) from one elected thread, releasing each
+// stage with tcgen05.commit; warps 2-5 drain the f32 accumulator from TMEM with
+// tcgen05.ld and run the epilogue. The accumulator is double-buffered in TMEM so the
+// epilogue of tile i overlaps the mainloop of tile i+1.
+//
+// Grouped mode (MoE experts): a tile table gives each 128-row block its A row
+// offset, its B row offset (the expert's weight slice in a stacked [E*N, K] tensor),
+// its number of valid rows and its output row offset.
+//
+// Epilogues: bf16 store; SwiGLU over interleaved (gate, up) output columns
+// (out[:, j] = silu(c[:, 2j]) * c[:, 2j+1]); f32 store.
+//
+// Every mbarrier wait is bounded; on timeout the CTA records an error code, stops
+// issuing work and frees its TMEM before exiting.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include <mutex>
+#include <unordered_map>
+
+#include "tc_common.cuh"
+
+namespace hx {
+
+constexpr int kBM = 128, kBK = 64;
+enum GemmEpi : int { kEpiBf16 = 0, kEpiSwiGLU = 1, kEpiF32 = 2 };
+
+struct GemmTile {   // grouped mode: one entry per 128-row block
+  int a_row0;       // first row of A for this block
+  int b_row0;       // row offset into stacked B (expert * N)
+  int rows;         // valid rows in this block (<= 128)
+  int out_row0;     // first output row
+};
+
+struct GemmParams {
+  int M, N, K;
+  void* C;
+  int ldc;                 // output row stride (elements)
+  int epi;
+  int num_m_blocks;        // plain mode
+  int num_n_blocks;
+  const GemmTile* tiles;   // grouped mode (nullptr = plain)
+  int num_entries;
+  int* err;
+};
+
+template <int BN, int STAGES>
+struct GemmSmem {
+  alignas(1024) __nv_bfloat16 A[STAGES][kBM * kBK];
+  alignas(1024) __nv_bfloat16 B[STAGES][BN * kBK];
+  uint64_t full[STAGES], empty[STAGES];
+  uint64_t tfull[2], tempty[2];
+  uint32_t tmem_base;
+  int abort;
+};
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(192, 1) gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap mapA,
+                                                              const __grid_constant__ CUtensorMap mapB,
+                                                              GemmParams p) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  // re-align to 1 KB (the 128B-swizzle atoms must start on 1024-byte boundaries)
+  auto* s = reinterpret_cast<GemmSmem<BN, STAGES>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_entries = p.tiles ? p.num_entries : p.num_m_blocks;
+  const int total_tiles = num_entries * p.num_n_blocks;
+  const int kblocks = (p.K + kBK - 1) / kBK;
+  constexpr uint32_t kStageBytes = (kBM + BN) * kBK * 2;
+  constexpr uint32_t kTmemCols = 2 * BN;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < STAGES; ++i) { tc::mbar_init(&s->full[i], 1); tc::mbar_init(&s->empty[i], 1); }
+    for (int i = 0; i < 2; ++i) { tc::mbar_init(&s->tfull[i], 1); tc::mbar_init(&s->tempty[i], 4); }
+    s->abort = 0;
+    tc::fence_barrier_init();
+    tc::prefetch_tmap(&mapA);
+    tc::prefetch_tmap(&mapB);
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(&s->tmem_base, kTmemCols);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = s->tmem_base;
+
+  auto tile_coords = [&](int t, int& a_row, int& b_row, int& rows, int& out_row, int& n_blk) {
+    const int e = t % num_entries;
+    n_blk = t / num_entries;
+    if (p.tiles) {
+      const GemmTile g = p.tiles[e];
+      a_row = g.a_row0; b_row = g.b_row0 + n_blk * BN; rows = g.rows; out_row = g.out_row0;
+    } else {
+      a_row = e * kBM; b_row = n_blk * BN; rows = min(kBM, p.M - e * kBM); out_row = e * kBM;
+    }
+  };
+
+  if (warp == 0) {
+    // ------------------------------ TMA producer ------------------------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int t = blockIdx.x; t < total_tiles && !s->abort; t += gridDim.x) {
+        int a_row, b_row, rows, out_row, n_blk;
+        tile_coords(t, a_row, b_row, rows, out_row, n_blk);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!tc::mbar_wait(&s->empty[stage], phase ^ 1, p.err, 11)) { s->abort = 1; break; }
+          tc::mbar_expect_tx(&s->full[stage], kStageBytes);
+          tc::tma_load_2d(s->A[stage], &mapA, &s->full[stage], kb * kBK, a_row);
+          tc::tma_load_2d(s->B[stage], &mapB, &s->full[stage], kb * kBK, b_row);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------ MMA issuer --------------------------------
+    if (lane == 0) {
+      constexpr uint32_t idesc = tc::idesc_bf16_f32(kBM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      for (int t = blockIdx.x; t < total_tiles && !s->abort; t += gridDim.x, ++it) {
+        const int acc = it & 1;
+        const uint32_t tph = (it >> 1) & 1;
+        if (!tc::mbar_wait(&s->tempty[acc], tph ^ 1, p.err, 12)) { s->abort = 1; break; }
+        tc::tc_fence_after();
+        const uint32_t d = tmem + acc * BN;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!tc::mbar_wait(&s->full[stage], phase, p.err, 13)) { s->abort = 1; break; }
+          tc::tc_fence_after();
+          const uint32_t a0 = tc::smem_u32(s->A[stage]), b0 = tc::smem_u32(s->B[stage]);
+#pragma unroll
+          for (int j = 0; j < kBK / 16; ++j) {
+            tc::umma_bf16(d, tc::sdesc_k128(a0 + j * 32), tc::sdesc_k128(b0 + j * 32), idesc,
+                          (kb > 0 || j > 0) ? 1u : 0u);
+          }
+          tc::umma_commit(&s->empty[stage]);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        tc::umma_commit(&s->tfull[acc]);
+      }
+    }
+  } else {
+    // ------------------------------ epilogue (warps 2-5) ----------------------
+    const int q = warp & 3;              // TMEM lane quarter this warp may access
+    const int row_in_tile = q * 32 + lane;
+    int it = 0;
+    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++it) {
+      const int acc = it & 1;
+      const uint32_t tph = (it >> 1) & 1;
+      if (!tc::mbar_wait(&s->tfull[acc], tph, p.err, 14)) { s->abort = 1; break; }
+      tc::tc_fence_after();
+      int a_row, b_row, rows, out_row, n_blk;
+      tile_coords(t, a_row, b_row, rows, out_row, n_blk);
+      const bool valid = row_in_tile < rows;
+      const long long orow = (long long)(out_row + row_in_tile);
+      const int n0 = n_blk * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        float v[32];
+        tc::tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + acc * BN + c * 32, v);
+        const int col = n0 + c * 32;
+        if (!valid || col >= p.N) continue;
+        if (col + 32 > p.N) {  // ragged right edge: scalar stores of the valid columns
+          for (int i = 0; i < p.N - col; ++i) {
+            if (p.epi == kEpiF32) reinterpret_cast<float*>(p.C)[orow * p.ldc + col + i] = v[i];
+            else reinterpret_cast<__nv_bfloat16*>(p.C)[orow * p.ldc + col + i] = __float2bfloat16(v[i]);
+          }
+          continue;
+        }
+        if (p.epi == kEpiF32) {
+          float* dst = reinterpret_cast<float*>(p.C) + orow * p.ldc + col;
+#pragma unroll
+          for (int i = 0; i < 32; i += 4) *reinterpret_cast<float4*>(dst + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+        } else if (p.epi == kEpiSwiGLU) {
+          float o[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            float g = __bfloat162float(__float2bfloat16(v[2 * i]));
+            float u = __bfloat162float(__float2bfloat16(v[2 * i + 1]));
+            o[i] = silu(g) * u;
+          }
+          __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.C) + orow * p.ldc + col / 2;
+          *reinterpret_cast<bf16x8*>(dst) = pack8(o);
+          *reinterpret_cast<bf16x8*>(dst + 8) = pack8(o + 8);
+        } else {
+          __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.C) + orow * p.ldc + col;
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) *reinterpret_cast<bf16x8*>(dst + i) = pack8(v + i);
+        }
+      }
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&s->tempty[acc]);
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side: tensor maps (cached), launch
+// ---------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* f = nullptr;
+    HX_CUDA_CHECK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q));
+    TORCH_CHECK(q == cudaDriverEntryPointSuccess && f, "cuTensorMapEncodeTiled unavailable");
+    fn = reinterpret_cast<EncodeTiledFn>(f);
+  });
+  return fn;
+}
+
+// 2D bf16 map over a row-major [rows, cols] tensor with leading stride ld (elements),
+// box = box_rows x 64 columns, 128-byte swizzle; out-of-bounds reads fill zeros.
+static CUtensorMap make_map(const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(ptr) % 16 == 0, "TMA base must be 16-byte aligned");
+  TORCH_CHECK((ld * 2) % 16 == 0, "TMA row stride must be a multiple of 16 bytes");
+  CUtensorMap m;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed: ", (int)r);
+  return m;
+}
+
+template <int BN, int STAGES>
+static void launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const GemmParams& p, int total_tiles,
+                        cudaStream_t st) {
+  auto k = gemm_tcgen05_kernel<BN, STAGES>;
+  const size_t smem = sizeof(GemmSmem<BN, STAGES>) + 1024;
+  static bool attr_set = false;
+  if (!attr_set) {
+    HX_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    attr_set = true;
+  }
+  int dev = 0, sms = 0;
+  HX_CUDA_CHECK(cudaGetDevice(&dev));
+  HX_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  const int grid = std::max(1, std::min(total_tiles, sms));
+  k<<<grid, 192, smem, st>>>(ma, mb, p);
+  HX_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace hx
+
+using namespace hx;
+
+static void gemm_common(torch::Tensor A, torch::Tensor B, torch::Tensor C, int64_t epi, const GemmTile* tiles,
+                        int num_entries, int n_per_group, torch::Tensor err) {
+  TORCH_CHECK(A.is_cuda() && A.scalar_type() == at::kBFloat16 && A.dim() == 2 && A.stride(1) == 1, "A [M,K] bf16");
+  TORCH_CHECK(B.scalar_type() == at::kBFloat16 && B.dim() == 2 && B.stride(1) == 1, "B [N,K] bf16");
+  const int M = A.size(0), K = A.size(1);
+  const int N = n_per_group;
+  TORCH_CHECK(B.size(1) == K, "K mismatch");
+  TORCH_CHECK(K % 8 == 0, "K must be a multiple of 8 (TMA 16-byte rows)");
+  constexpr int BN = 256;
+  GemmParams p{};
+  p.M = M; p.N = N; p.K = K; p.C = C.data_ptr(); p.ldc = C.stride(0); p.epi = (int)epi;
+  p.num_m_blocks = (M + kBM - 1) / kBM;
+  p.num_n_blocks = (N + BN - 1) / BN;
+  p.tiles = tiles; p.num_entries = num_entries;
+  p.err = err.data_ptr<int>();
+  if (epi == kEpiSwiGLU) TORCH_CHECK(N % 32 == 0 && C.size(1) * 2 >= N, "SwiGLU output width");
+  TORCH_CHECK(C.scalar_type() == (epi == kEpiF32 ? at::kFloat : at::kBFloat16), "output dtype");
+  TORCH_CHECK((p.ldc * C.element_size()) % 16 == 0, "output row stride must be 16-byte aligned");
+  CUtensorMap ma = make_map(A.data_ptr(), M, K, A.stride(0), kBM);
+  CUtensorMap mb = make_map(B.data_ptr(), B.size(0), K, B.stride(0), BN);
+  const int total = (tiles ? num_entries : p.num_m_blocks) * p.num_n_blocks;
+  if (total == 0) return;
+  launch_gemm<BN, 4>(ma, mb, p, total, at::cuda::getCurrentCUDAStream());
+}
+
+// C = A @ B^T (bf16 in, f32 accumulate); epi: 0 bf16, 1 SwiGLU on interleaved columns, 2 f32.
+void gemm(torch::Tensor A, torch::Tensor B, torch::Tensor C, int64_t epi, torch::Tensor err) {
+  gemm_common(A, B, C, epi, nullptr, 0, B.size(0), err);
+}
+
+// Grouped: tiles int32 [num_entries, 4] = (a_row0, b_row0, rows, out_row0); B is the
+// stacked [G*N, K] weight; n = N per group.
+void gemm_grouped(torch::Tensor A, torch::Tensor B, torch::Tensor C, torch::Tensor tiles, int64_t n, int64_t epi,
+                  torch::Tensor err) {
+  TORCH_CHECK(tiles.scalar_type() == at::kInt && tiles.dim() == 2 && tiles.size(1) == 4 && tiles.is_cuda(),
+              "tiles int32 [T,4] on device");
+  gemm_common(A, B, C, epi, reinterpret_cast<const GemmTile*>(tiles.data_ptr()), tiles.size(0), (int)n, err);
+}
