@@ -51,6 +51,9 @@ __global__ void __launch_bounds__(256) ar_oneshot_kernel(PeerPtrs peers, int ran
                                                          size_t data_bytes, unsigned* epoch, int* err,
                                                          unsigned long long timeout_ns) {
   const int cta = blockIdx.x;
+  // a communicator whose earlier exchange timed out is poisoned: fail fast instead of
+  // waiting again on every later call (the host tears it down after `check`)
+  if (*((volatile int*)err) != 0) return;
   const int per = (n + gridDim.x - 1) / gridDim.x;
   const int i0 = cta * per, i1 = min(n, i0 + per);
   const unsigned e = *epoch + 1;  // this call's epoch (same value read by every CTA)

@@ -295,6 +295,30 @@ class FastModel:
         xf = x.float()
         return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.cfg.rms_norm_eps) * w).to(torch.bfloat16)
 
+    def _linear(self, x: torch.Tensor, W: torch.Tensor, epi: int = 0) -> torch.Tensor:
+        """x [T, K] @ W[N, K]^T on the tcgen05 GEMM (epi 1: SwiGLU on interleaved rows)."""
+        x = x.contiguous()
+        if self.C is None:  # CPU layout tests only
+            y = x @ W.t()
+            if epi == 1:
+                y = (torch.nn.functional.silu(y[:, 0::2].float()).to(torch.bfloat16).float()
+                     * y[:, 1::2].float()).to(torch.bfloat16)
+            return y
+        N = W.shape[0] // 2 if epi == 1 else W.shape[0]
+        out = torch.empty(x.shape[0], N, dtype=torch.float32 if epi == 2 else torch.bfloat16, device=x.device)
+        self.C.gemm(x, W, out, epi, self._gemm_err())
+        return out
+
+    def _gemm_err(self) -> torch.Tensor:
+        if not hasattr(self, "_gerr"):
+            self._gerr = torch.zeros(1, dtype=torch.int32, device=self.device)
+        return self._gerr
+
+    def check_errors(self):
+        """Raise if a device-side bounded wait gave up since the model was built."""
+        if hasattr(self, "_gerr") and int(self._gerr.item()):
+            raise RuntimeError(f"GEMM kernel reported error code {int(self._gerr.item())}")
+
     def _reduce(self, t: torch.Tensor) -> torch.Tensor:
         if self.comm is not None and self.dims.ws > 1:
             self.comm.all_reduce_(t)
@@ -305,7 +329,7 @@ class FastModel:
         d, lw, cfg = self.dims, self.layers[i], self.cfg
         T = h.shape[0]
         kd, vd, K = d.gdn_kd, d.gdn_vd, cfg.linear_conv_kernel_dim
-        proj = h @ lw["w_in"].t()
+        proj = self._linear(h, lw["w_in"])
         mixed = proj[:, :2 * kd + vd]
         z = proj[:, 2 * kd + vd:2 * kd + 2 * vd]
         bb = proj[:, 2 * kd + 2 * vd:2 * kd + 2 * vd + d.hv]
@@ -331,13 +355,13 @@ class FastModel:
         o = o * torch.rsqrt(o.pow(2).mean(-1, keepdim=True) + cfg.rms_norm_eps)
         o = o.to(torch.bfloat16).float() * lw["gnorm"]
         o = (o * torch.nn.functional.silu(z.float().view(T, d.hv, d.dv))).to(torch.bfloat16)
-        return o.reshape(T, vd) @ lw["out_w"].t()
+        return self._linear(o.reshape(T, vd), lw["out_w"])
 
     def _attn_prefill(self, i: int, h: torch.Tensor, slot: int, p0: int) -> torch.Tensor:
         from .reference import apply_rope, rope_cos_sin
         d, lw, cfg = self.dims, self.layers[i], self.cfg
         T, D = h.shape[0], d.D
-        qkv = h @ lw["w_qkv"].t()
+        qkv = self._linear(h, lw["w_qkv"])
         qp = qkv[:, :d.hq * d.qw].view(T, d.hq, d.qw)
         q, gate = qp[..., :D], (qp[..., D:] if cfg.attn_output_gate else None)
         k = qkv[:, d.hq * d.qw:d.hq * d.qw + d.hkv * D].view(T, d.hkv, D)
@@ -357,39 +381,63 @@ class FastModel:
         o = o.transpose(0, 1).reshape(T, d.hq * D)
         if gate is not None:
             o = (o.float() * torch.sigmoid(gate.reshape(T, d.hq * D).float())).to(torch.bfloat16)
-        return o @ lw["o_w"].t()
+        return self._linear(o, lw["o_w"])
 
     def _ffn_prefill(self, i: int, hn: torch.Tensor) -> torch.Tensor:
         cfg, lw = self.cfg, self.layers[i]
-        silu = torch.nn.functional.silu
         if not cfg.layer_uses_moe(i):
-            y = hn @ lw["w_gu"].t()
-            act = (silu(y[:, 0::2].float()).to(torch.bfloat16).float() * y[:, 1::2].float()).to(torch.bfloat16)
-            return act @ lw["w_d"].t()
+            return self._linear(self._linear(hn, lw["w_gu"], 1), lw["w_d"])
         E, k = cfg.num_experts, cfg.num_experts_per_tok
-        logits = (hn @ lw["router"].t()).float()
+        T = hn.shape[0]
+        logits = self._linear(hn, lw["router"], 2)
         probs = torch.softmax(logits[:, :E], -1)
         topv, topi = torch.topk(probs, k, -1)
         if cfg.norm_topk_prob:
             topv = topv / topv.sum(-1, keepdim=True)
-        out = torch.zeros(hn.shape[0], cfg.hidden_size, dtype=torch.float32, device=hn.device)
-        order = torch.argsort(topi.view(-1), stable=True)
-        counts = torch.bincount(topi.view(-1), minlength=E).tolist()
+        # group the T*k (token, expert) routes by expert; the shared expert is one more
+        # group that every token visits with weight sigmoid(shared_expert_gate(x))
+        flat = topi.view(-1)
+        order = torch.argsort(flat, stable=True)
         tok_of = order // k
         w_of = topv.view(-1)[order]
-        start = 0
-        for e, c in enumerate(counts):
-            if c == 0:
-                continue
-            rows = tok_of[start:start + c]
-            y = hn[rows] @ lw["w_gu"][e].t()
-            act = (silu(y[:, 0::2].float()).to(torch.bfloat16).float() * y[:, 1::2].float()).to(torch.bfloat16)
-            out.index_add_(0, rows, (act @ lw["w_d"][e].t()).float() * w_of[start:start + c, None])
-            start += c
+        counts = torch.bincount(flat, minlength=E)
+        groups_tok, groups_w, cnt = [tok_of], [w_of], [counts]
         if self.has_shared:
-            y = hn @ lw["w_gu"][E].t()
-            act = (silu(y[:, 0::2].float()).to(torch.bfloat16).float() * y[:, 1::2].float()).to(torch.bfloat16)
-            out += (act @ lw["w_d"][E].t()).float() * torch.sigmoid(logits[:, E:E + 1])
+            groups_tok.append(torch.arange(T, device=hn.device))
+            groups_w.append(torch.sigmoid(logits[:, E]))
+            cnt.append(torch.tensor([T], device=hn.device))
+        tok_all = torch.cat(groups_tok)
+        w_all = torch.cat(groups_w)
+        counts = torch.cat(cnt).tolist()
+        A = hn[tok_all].contiguous()
+        if self.C is None:
+            y = torch.empty(A.shape[0], cfg.hidden_size, dtype=torch.bfloat16)
+            start = 0
+            for e, c in enumerate(counts):
+                if c:
+                    act = self._linear(A[start:start + c], lw["w_gu"][e], 1)
+                    y[start:start + c] = self._linear(act, lw["w_d"][e])
+                start += c
+        else:
+            tiles, row = [], 0
+            for e, c in enumerate(counts):
+                for m0 in range(0, c, 128):
+                    tiles.append((row + m0, e, min(128, c - m0), row + m0))
+                row += c
+            tt = torch.tensor(tiles, dtype=torch.int32)
+            I2 = lw["w_gu"].shape[1]
+            Hh = lw["w_d"].shape[1]
+            t_gu = tt.clone()
+            t_gu[:, 1] *= I2
+            t_d = tt.clone()
+            t_d[:, 1] *= Hh
+            t_gu, t_d = t_gu.to(hn.device, non_blocking=True), t_d.to(hn.device, non_blocking=True)
+            act = torch.empty(A.shape[0], I2 // 2, dtype=torch.bfloat16, device=hn.device)
+            self.C.gemm_grouped(A, lw["w_gu"].view(-1, lw["w_gu"].shape[-1]), act, t_gu, I2, 1, self._gemm_err())
+            y = torch.empty(A.shape[0], Hh, dtype=torch.bfloat16, device=hn.device)
+            self.C.gemm_grouped(act, lw["w_d"].view(-1, lw["w_d"].shape[-1]), y, t_d, Hh, 0, self._gemm_err())
+        out = torch.zeros(T, cfg.hidden_size, dtype=torch.float32, device=hn.device)
+        out.index_add_(0, tok_all, y.float() * w_all[:, None])
         return out.to(torch.bfloat16)
 
     @torch.no_grad()
@@ -413,4 +461,4 @@ class FastModel:
             x = x + self._reduce(o)
         last = self._rms(x[-1:], self.final_norm)
         self.pos[slot] = p0 + T
-        return (last @ self.lm_head.t()).float()[0]
+        return self._linear(last, self.lm_head, 2)[0]

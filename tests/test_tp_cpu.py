@@ -71,5 +71,7 @@ def test_tp_matches_single_rank(name, ws):
         p.join(60)
         assert p.exitcode == 0
     coss = [torch.nn.functional.cosine_similarity(res[r].float(), want.float(), dim=0).item() for r in range(ws)]
-    assert min(coss) > 0.995, coss
+    # ranks sum bf16 partials, so rounding differs from the single-rank model and can
+    # flip a near-tied expert choice; a sharding error drives the cosine far lower
+    assert min(coss) > 0.985, coss
     assert torch.equal(res[0], res[ws - 1])

@@ -19,7 +19,25 @@ def _free_port():
     return p
 
 
+def _log(rank, msg):
+    d = os.environ.get("HELEXA_TEST_LOG_DIR")
+    if d:
+        with open(os.path.join(d, f"tp_rank{rank}.log"), "a") as f:
+            f.write(msg + "\n")
+
+
 def _run(rank, ws, port, mode, q):
+    import torch.distributed as dist
+    _log(rank, f"start ws={ws} mode={mode}")
+    try:
+        _run_inner(rank, ws, port, mode, q)
+    except BaseException as e:  # surface the failure in the log before dying
+        import traceback
+        _log(rank, "FAILED: " + "".join(traceback.format_exception(e)))
+        raise
+
+
+def _run_inner(rank, ws, port, mode, q):
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
@@ -34,11 +52,18 @@ def _run(rank, ws, port, mode, q):
         cfg = get_preset("tiny-qwen3-next")
         torch.manual_seed(0)
         w = _realistic(cfg, random_weights(cfg, seed=0, std=0.05))
+        _log(rank, "pg up")
         comm = TPComm(device=dev, mode=mode) if ws > 1 else None
+        _log(rank, "comm up")
         fm = FastModel.from_hf(cfg, w, dev, rank=rank, ws=ws, max_slots=1, max_len=256, comm=comm)
         prompt = torch.randint(0, cfg.vocab_size, (60,), generator=torch.Generator().manual_seed(1)).int().to(dev)
         lg = fm.prefill(0, prompt, 0)
+        torch.cuda.synchronize()
+        _log(rank, "prefill done")
+        if comm is not None:
+            comm.check()
         nb = fm.capture(1, steps=8)
+        _log(rank, "captured")
         nb.slots.fill_(0)
         nb.tok.fill_(int(lg.argmax()))
         fm.replay(nb)
@@ -60,7 +85,19 @@ def _launch(ws, mode):
     ps = [ctx.Process(target=_run, args=(r, ws, port, mode, q)) for r in range(ws)]
     for p in ps:
         p.start()
-    res = dict((r, (a, b)) for r, a, b in (q.get(timeout=600) for _ in range(ws)))
+    import queue
+    import time
+    res, t0 = {}, time.time()
+    while len(res) < ws:
+        try:
+            r, a, b = q.get(timeout=5)
+            res[r] = (a, b)
+        except queue.Empty:
+            dead = [p.exitcode for p in ps if p.exitcode not in (None, 0)]
+            if dead or time.time() - t0 > 240:
+                for p in ps:
+                    p.kill()
+                pytest.fail(f"TP ranks failed (exit codes {[p.exitcode for p in ps]}) or timed out")
     for p in ps:
         p.join(120)
         assert p.exitcode == 0
