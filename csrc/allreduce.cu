@@ -51,6 +51,8 @@ __global__ void __launch_bounds__(256) ar_oneshot_kernel(PeerPtrs peers, int ran
                                                          size_t data_bytes, unsigned* epoch, int* err,
                                                          unsigned long long timeout_ns) {
   const int cta = blockIdx.x;
+  pdl_launch_dependents();
+  pdl_wait_prior();
   // a communicator whose earlier exchange timed out is poisoned: fail fast instead of
   // waiting again on every later call (the host tears it down after `check`)
   if (*((volatile int*)err) != 0) return;
@@ -154,11 +156,11 @@ void ar_oneshot(std::vector<int64_t> peer_bases, int64_t rank, torch::Tensor par
   TORCH_CHECK(epoch.scalar_type() == at::kInt && epoch.numel() >= 2, "epoch int32[2]");
   PeerPtrs pp{};
   for (int r = 0; r < ws; ++r) pp.base[r] = reinterpret_cast<char*>(peer_bases[r]);
-  ar_oneshot_kernel<<<ctas, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-      pp, rank, ws, reinterpret_cast<const __nv_bfloat16*>(partial.data_ptr()),
-      reinterpret_cast<__nv_bfloat16*>(x.data_ptr()),
-      out_plain ? reinterpret_cast<__nv_bfloat16*>(out_plain->data_ptr()) : nullptr, n, (size_t)data_bytes,
-      reinterpret_cast<unsigned*>(epoch.data_ptr()), err.data_ptr<int>(),
-      (unsigned long long)(timeout_s * 1e9));
+  HX_CUDA_CHECK(hx_launch_pdl(ar_oneshot_kernel, dim3(ctas), dim3(256), 0, at::cuda::getCurrentCUDAStream(), pp,
+                              (int)rank, ws, reinterpret_cast<const __nv_bfloat16*>(partial.data_ptr()),
+                              reinterpret_cast<__nv_bfloat16*>(x.data_ptr()),
+                              out_plain ? reinterpret_cast<__nv_bfloat16*>(out_plain->data_ptr()) : nullptr, n,
+                              (size_t)data_bytes, reinterpret_cast<unsigned*>(epoch.data_ptr()), err.data_ptr<int>(),
+                              (unsigned long long)(timeout_s * 1e9)));
   HX_CUDA_CHECK(cudaGetLastError());
 }

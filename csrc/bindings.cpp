@@ -31,6 +31,19 @@ void gemm(torch::Tensor A, torch::Tensor B, torch::Tensor C, int64_t epi, torch:
 void gemm_grouped(torch::Tensor A, torch::Tensor B, torch::Tensor C, torch::Tensor tiles, int64_t n, int64_t epi,
                   torch::Tensor err);
 
+void sgemv(int64_t mode, torch::Tensor W, torch::Tensor x, c10::optional<torch::Tensor> y,
+           c10::optional<torch::Tensor> resid, c10::optional<torch::Tensor> norm_w, double eps,
+           c10::optional<torch::Tensor> ids, c10::optional<torch::Tensor> wts, int64_t J,
+           c10::optional<torch::Tensor> scratch, c10::optional<torch::Tensor> counter,
+           c10::optional<torch::Tensor> out_ids, c10::optional<torch::Tensor> out_wts, int64_t E, int64_t topk,
+           bool has_shared, bool norm_topk, c10::optional<torch::Tensor> tok, c10::optional<torch::Tensor> slots,
+           c10::optional<torch::Tensor> pos, c10::optional<torch::Tensor> out_tokens,
+           c10::optional<torch::Tensor> step, torch::Tensor err, bool pdl);
+
+void gdn_prefill(torch::Tensor proj, torch::Tensor conv_w, torch::Tensor ring, torch::Tensor A_log,
+                 torch::Tensor dt_bias, torch::Tensor norm_w, torch::Tensor state, torch::Tensor out, int64_t Hk,
+                 int64_t Hv, int64_t D, int64_t p0, double eps);
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemv", &gemv);
   m.def("gemv_experts", &gemv_experts);
@@ -45,5 +58,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ipc_close", &ipc_close);
   m.def("ar_oneshot", &ar_oneshot);
   m.def("gemm", &gemm);
+  m.def("gdn_prefill", &gdn_prefill);
+  m.def("sgemv", &sgemv);
   m.def("gemm_grouped", &gemm_grouped);
 }

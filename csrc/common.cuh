@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #define HX_DEVICE __device__ __forceinline__
 
 #define HX_CUDA_CHECK(expr)                                                            \
@@ -75,6 +77,11 @@ HX_DEVICE bf16x8 ld_stream(const bf16x8* p) {
 
 HX_DEVICE float silu(float x) { return x / (1.f + __expf(-x)); }
 
+// Programmatic dependent launch: let the next kernel start launching / wait until
+// the previous kernel's memory is visible. Both are no-ops without the launch attribute.
+HX_DEVICE void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+HX_DEVICE void pdl_wait_prior() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 HX_DEVICE uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
@@ -82,3 +89,21 @@ HX_DEVICE uint64_t globaltimer_ns() {
 }
 
 }  // namespace hx
+
+// Launch with programmatic stream serialization (kernel may start before its
+// predecessor finishes; it must call pdl_wait_prior() before reading its outputs).
+template <typename... KArgs, typename... Args>
+static inline cudaError_t hx_launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                        cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}

@@ -47,8 +47,17 @@ __global__ void __launch_bounds__(512) gdn_decode_kernel(GdnDecodeArgs a) {
   __shared__ float wred[16];
 
   const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
+  pdl_launch_dependents();
+  // slots/pos and the recurrent state were written by earlier decode steps, which are
+  // complete; only the in-projection comes from the immediately preceding kernel.
   const int slot = a.slots[b];
   const int p = a.pos[slot];
+  const int v_ = tid % DV, kg_ = tid / DV;
+  float* S = a.rec + (((long long)slot * a.Hv + h) * DK) * DV;
+  float s[RK];
+#pragma unroll
+  for (int i = 0; i < RK; ++i) s[i] = S[(kg_ * RK + i) * DV + v_];
+  pdl_wait_prior();
   const int r = a.Hv / a.Hk, kh = h / r;
   const int kd = a.Hk * DK;
   const int C = 2 * kd + a.Hv * DV;
@@ -98,14 +107,12 @@ __global__ void __launch_bounds__(512) gdn_decode_kernel(GdnDecodeArgs a) {
   const float beta = scal[0], decay = scal[1], qscale = scal[2], kscale = scal[3];
 
   // ---- delta rule on the state tile -------------------------------------
-  const int v = tid % DV, kg = tid / DV;
-  float* S = a.rec + (((long long)slot * a.Hv + h) * DK) * DV;
-  float s[RK];
+  const int v = v_, kg = kg_;
   float kv = 0.f;
 #pragma unroll
   for (int i = 0; i < RK; ++i) {
     int k = kg * RK + i;
-    s[i] = S[k * DV + v] * decay;
+    s[i] *= decay;
     kv += s[i] * ks[k] * kscale;
   }
   red[kg][v] = kv;
@@ -172,9 +179,8 @@ void gdn_decode(torch::Tensor proj, torch::Tensor conv_w, torch::Tensor conv_rin
   TORCH_CHECK(conv_ring.size(2) == a.KC, "ring slots must equal conv kernel size");
   dim3 grid(Hv, B);
   auto s = at::cuda::getCurrentCUDAStream();
-  if (Dk == 128 && Dv == 128) gdn_decode_kernel<128, 128><<<grid, 512, 0, s>>>(a);
-  else if (Dk == 64 && Dv == 64) gdn_decode_kernel<64, 64><<<grid, 512, 0, s>>>(a);
-  else if (Dk == 32 && Dv == 32) gdn_decode_kernel<32, 32><<<grid, 512, 0, s>>>(a);
+  if (Dk == 128 && Dv == 128) HX_CUDA_CHECK(hx_launch_pdl(gdn_decode_kernel<128, 128>, grid, dim3(512), 0, s, a));
+  else if (Dk == 64 && Dv == 64) HX_CUDA_CHECK(hx_launch_pdl(gdn_decode_kernel<64, 64>, grid, dim3(512), 0, s, a));
+  else if (Dk == 32 && Dv == 32) HX_CUDA_CHECK(hx_launch_pdl(gdn_decode_kernel<32, 32>, grid, dim3(512), 0, s, a));
   else TORCH_CHECK(false, "unsupported GDN head dims");
-  HX_CUDA_CHECK(cudaGetLastError());
 }

@@ -17,6 +17,8 @@ namespace hx {
 __global__ void embed_kernel(const __nv_bfloat16* __restrict__ E, const int* __restrict__ tok,
                              __nv_bfloat16* __restrict__ x, int H, int V) {
   const int b = blockIdx.x;
+  pdl_launch_dependents();
+  pdl_wait_prior();
   int t = tok[b];
   t = t < 0 ? 0 : (t >= V ? V - 1 : t);
   const bf16x8* src = reinterpret_cast<const bf16x8*>(E + (long long)t * H);
@@ -74,9 +76,9 @@ void embed(torch::Tensor E, torch::Tensor tok, torch::Tensor x) {
   TORCH_CHECK(E.scalar_type() == at::kBFloat16 && x.scalar_type() == at::kBFloat16, "bf16");
   const int H = E.size(1);
   TORCH_CHECK(H % 8 == 0, "hidden must be a multiple of 8");
-  embed_kernel<<<tok.numel(), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-      reinterpret_cast<const __nv_bfloat16*>(E.data_ptr()), tok.data_ptr<int>(),
-      reinterpret_cast<__nv_bfloat16*>(x.data_ptr()), H, E.size(0));
+  HX_CUDA_CHECK(hx_launch_pdl(embed_kernel, dim3(tok.numel()), dim3(256), 0, at::cuda::getCurrentCUDAStream(),
+                              reinterpret_cast<const __nv_bfloat16*>(E.data_ptr()), (const int*)tok.data_ptr<int>(),
+                              reinterpret_cast<__nv_bfloat16*>(x.data_ptr()), H, (int)E.size(0)));
   HX_CUDA_CHECK(cudaGetLastError());
 }
 

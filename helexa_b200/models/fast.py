@@ -56,6 +56,9 @@ class DecodeBuffers:
     logits: torch.Tensor       # f32 [B, V]
     out_tokens: torch.Tensor   # int32 [B, cap]
     step: torch.Tensor         # int32 [B]
+    amax: torch.Tensor         # f32 [SMs * B * 2] per-CTA arg-max partials
+    counter: torch.Tensor      # int32 [1] last-CTA election (self-resetting)
+    err: torch.Tensor          # int32 [1] bounded-wait error code
     graph: torch.cuda.CUDAGraph | None = None
     graph_steps: int = 0
 
@@ -79,6 +82,7 @@ class FastModel:
         self.inv_freq = inv.to(device)
         self.has_shared = cfg.shared_expert_intermediate_size > 0
         sm = torch.cuda.get_device_properties(device).multi_processor_count if device.type == "cuda" else 1
+        self.sms = sm
         self.attn_splits = attn_splits or max(1, min(64, sm // max(1, dims.hkv)))
         # ---- state pools -------------------------------------------------
         self.pos = torch.zeros(max_slots, dtype=torch.int32, device=device)
@@ -187,27 +191,38 @@ class FastModel:
             act_moe=z(B * J, d.moe_inter) if cfg.num_experts else None,
             act_mlp=z(B, d.inter) if any_mlp else None,
             partial=z(B, d.H),
-            logits=z(B, cfg.vocab_size, dt=f32), out_tokens=z(B, out_cap, dt=i32), step=z(B, dt=i32))
+            logits=z(B, cfg.vocab_size, dt=f32), out_tokens=z(B, out_cap, dt=i32), step=z(B, dt=i32),
+            amax=z(max(1, self.sms) * B * 2, dt=f32), counter=z(1, dt=i32), err=z(1, dt=i32))
         self._bufs[B] = nb
         return nb
+
+    _SG_TO_GEMV = {0: 0, 1: 1, 2: 2, 3: 3}
+
+    def _dense(self, mode, W, inp, y, nb: DecodeBuffers, resid=None, norm=None):
+        """Streaming GEMV when its shared-memory ring fits, else the register GEMV."""
+        if ops.sgemv_fits(mode, W.shape[-1], inp.shape[0]):
+            ops.sgemv(mode, W, inp, y, resid=resid, norm=norm, eps=self.cfg.rms_norm_eps, err=nb.err)
+        else:
+            self.C.gemv(W, inp, y, self._SG_TO_GEMV[mode], resid, norm, self.cfg.rms_norm_eps)
 
     def _row_parallel(self, W, inp, nb: DecodeBuffers):
         """x += W . inp, summed across TP ranks when the layer is sharded."""
         if self.comm is None or self.dims.ws == 1:
-            self.C.gemv(W, inp, nb.x, ops.RESID_ADD, nb.x, None, 0.0)
+            self._dense(ops.SG_RESID, W, inp, nb.x, nb, resid=nb.x)
         else:
-            self.comm.gemv_allreduce_residual(W, inp, nb.x, nb.partial)
+            self._dense(ops.SG_STORE, W, inp, nb.partial, nb)
+            self.comm.reduce_residual(nb.partial, nb.x)
 
     def _decode_layer(self, i: int, nb: DecodeBuffers):
         C, cfg, d, lw = self.C, self.cfg, self.dims, self.layers[i]
         eps = cfg.rms_norm_eps
         if cfg.is_linear(i):
-            C.gemv(lw["w_in"], nb.x, nb.proj_gdn, ops.STORE_BF16, None, lw["ln1"], eps)
+            self._dense(ops.SG_STORE, lw["w_in"], nb.x, nb.proj_gdn, nb, norm=lw["ln1"])
             C.gdn_decode(nb.proj_gdn, lw["conv_w"], self.conv[i], self.rec[i], lw["A_log"], lw["dt_bias"],
                          lw["gnorm"], nb.slots, self.pos, nb.gdn_out, d.hk, d.hv, d.dk, d.dv, eps)
             self._row_parallel(lw["out_w"], nb.gdn_out, nb)
         else:
-            C.gemv(lw["w_qkv"], nb.x, nb.proj_attn, ops.STORE_BF16, None, lw["ln1"], eps)
+            self._dense(ops.SG_STORE, lw["w_qkv"], nb.x, nb.proj_attn, nb, norm=lw["ln1"])
             C.attn_decode(nb.proj_attn, lw.get("q_norm"), lw.get("k_norm"), self.inv_freq, self.kc[i], self.vc[i],
                           nb.slots, self.pos, nb.part_o, nb.part_ml, nb.counters, nb.attn_out, d.hq, d.hkv, d.D,
                           cfg.rotary_dim, cfg.attn_output_gate, eps)
@@ -215,31 +230,36 @@ class FastModel:
         if cfg.layer_uses_moe(i):
             E, k = cfg.num_experts, cfg.num_experts_per_tok
             J = k + (1 if self.has_shared else 0)
-            C.gemv(lw["router"], nb.x, nb.rlogits, ops.STORE_F32, None, lw["ln2"], eps)
-            C.moe_topk(nb.rlogits, E, k, self.has_shared, cfg.norm_topk_prob, nb.ids, nb.wts)
-            C.gemv_experts(lw["w_gu"], nb.x, nb.ids.view(-1), nb.act_moe, ops.SILU_PAIR, J, lw["ln2"], eps)
+            ops.sgemv(ops.SG_ROUTER, lw["router"], nb.x, norm=lw["ln2"], eps=eps, scratch=nb.rlogits,
+                      counter=nb.counter, out_ids=nb.ids, out_wts=nb.wts, E=E, topk=k, shared=self.has_shared,
+                      norm_topk=cfg.norm_topk_prob, err=nb.err)
+            ops.sgemv(ops.SG_EXPERT, lw["w_gu"], nb.x, nb.act_moe, norm=lw["ln2"], eps=eps, ids=nb.ids.view(-1),
+                      J=J, err=nb.err)
             if self.comm is None or d.ws == 1:
-                C.moe_down(lw["w_d"], nb.act_moe, nb.ids, nb.wts, nb.x, None)
+                ops.sgemv(ops.SG_MOEDOWN, lw["w_d"], nb.act_moe, nb.x, resid=nb.x, ids=nb.ids, wts=nb.wts, J=J,
+                          err=nb.err)
             else:
-                self.comm.moe_down_allreduce_residual(lw["w_d"], nb.act_moe, nb.ids, nb.wts, nb.x, nb.partial)
+                ops.sgemv(ops.SG_MOEDOWN, lw["w_d"], nb.act_moe, nb.partial, ids=nb.ids, wts=nb.wts, J=J,
+                          err=nb.err)
+                self.comm.reduce_residual(nb.partial, nb.x)
         else:
-            C.gemv(lw["w_gu"], nb.x, nb.act_mlp, ops.SILU_PAIR, None, lw["ln2"], eps)
+            self._dense(ops.SG_SILU, lw["w_gu"], nb.x, nb.act_mlp, nb, norm=lw["ln2"])
             self._row_parallel(lw["w_d"], nb.act_mlp, nb)
 
     def decode_step_launch(self, nb: DecodeBuffers):
         """Enqueue one decode step for the nb.B slots in nb.slots (graph-capturable)."""
-        C = self.C
-        C.embed(self.embed_w, nb.tok, nb.x)
+        self.C.embed(self.embed_w, nb.tok, nb.x)
         for i in range(self.cfg.num_hidden_layers):
             self._decode_layer(i, nb)
-        C.gemv(self.lm_head, nb.x, nb.logits, ops.STORE_F32, None, self.final_norm, self.cfg.rms_norm_eps)
-        C.argmax_step(nb.logits, nb.tok, nb.slots, self.pos, nb.out_tokens, nb.step)
+        ops.sgemv(ops.SG_ARGMAX, self.lm_head, nb.x, nb.logits, norm=self.final_norm, eps=self.cfg.rms_norm_eps,
+                  scratch=nb.amax, counter=nb.counter, tok=nb.tok, slots=nb.slots, pos=self.pos,
+                  out_tokens=nb.out_tokens, step=nb.step, err=nb.err)
 
     def launches_per_step(self) -> int:
         cfg = self.cfg
-        n = 3  # embed, lm_head, argmax
+        n = 2  # embed, lm_head(+arg-max)
         for i in range(cfg.num_hidden_layers):
-            n += 3 + (4 if cfg.layer_uses_moe(i) else 2)
+            n += 3 + (3 if cfg.layer_uses_moe(i) else 2)
             if self.comm is not None and self.dims.ws > 1:
                 n += self.comm.launches_per_reduce * 2
         return n
@@ -305,9 +325,10 @@ class FastModel:
                      * y[:, 1::2].float()).to(torch.bfloat16)
             return y
         N = W.shape[0] // 2 if epi == 1 else W.shape[0]
-        out = torch.empty(x.shape[0], N, dtype=torch.float32 if epi == 2 else torch.bfloat16, device=x.device)
+        Np = (N + 7) // 8 * 8  # keep output rows 16-byte aligned for the vector epilogue
+        out = torch.empty(x.shape[0], Np, dtype=torch.float32 if epi == 2 else torch.bfloat16, device=x.device)
         self.C.gemm(x, W, out, epi, self._gemm_err())
-        return out
+        return out if Np == N else out[:, :N]
 
     def _gemm_err(self) -> torch.Tensor:
         if not hasattr(self, "_gerr"):
@@ -330,6 +351,16 @@ class FastModel:
         T = h.shape[0]
         kd, vd, K = d.gdn_kd, d.gdn_vd, cfg.linear_conv_kernel_dim
         proj = self._linear(h, lw["w_in"])
+        if self.C is not None:
+            ring = self.conv[i][slot]
+            o = torch.empty(T, vd, dtype=torch.bfloat16, device=h.device)
+            self.C.gdn_prefill(proj, lw["conv_w"], ring, lw["A_log"], lw["dt_bias"], lw["gnorm"], self.rec[i][slot],
+                               o, d.hk, d.hv, d.dk, p0, cfg.rms_norm_eps)
+            # advance the conv ring to the last K inputs (slot = position % K)
+            lo = max(p0, p0 + T - K)
+            idx = torch.arange(lo, p0 + T, device=h.device)
+            ring[:, idx % K] = proj[idx - p0, :2 * kd + vd].t()
+            return self._linear(o, lw["out_w"])
         mixed = proj[:, :2 * kd + vd]
         z = proj[:, 2 * kd + vd:2 * kd + 2 * vd]
         bb = proj[:, 2 * kd + 2 * vd:2 * kd + 2 * vd + d.hv]

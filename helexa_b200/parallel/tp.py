@@ -94,23 +94,11 @@ class TPComm:
     def _ctas(self, n: int) -> int:
         return max(1, min(64, (n + 2047) // 2048))
 
-    def _reduce_residual(self, partial: torch.Tensor, x: torch.Tensor):
+    def reduce_residual(self, partial: torch.Tensor, x: torch.Tensor):
+        """x += sum over ranks of `partial` (decode-size [B, hidden] bf16)."""
         if self.mode == "p2p":
             ops.C.ar_oneshot(self.bases, self.rank, partial.view(-1), x.view(-1), None, self.data_bytes,
                              self.epoch, self.err, self._ctas(partial.numel()), self.timeout_s)
         else:
             dist.all_reduce(partial, group=self.group)
             x.add_(partial)
-
-    def gemv_allreduce_residual(self, W, inp, x, partial):
-        """x += allreduce(W . inp) for a row-parallel layer at decode."""
-        B = x.shape[0]
-        p = partial[:B]
-        ops.C.gemv(W, inp, p, ops.STORE_BF16, None, None, 0.0)
-        self._reduce_residual(p, x)
-
-    def moe_down_allreduce_residual(self, Wd, act, ids, wts, x, partial):
-        B = x.shape[0]
-        p = partial[:B]
-        ops.C.moe_down(Wd, act, ids, wts, x, p)
-        self._reduce_residual(p, x)

@@ -186,3 +186,39 @@ def test_embed_and_argmax():
     assert int(tok[1]) == 7
     assert pos.tolist() == [0, 1, 1, 1] and step.tolist() == [1, 1, 1]
     assert torch.equal(out[:, 0], tok)
+
+
+@pytest.mark.parametrize("T,p0,D", [(200, 0, 128), (70, 5, 128), (33, 0, 32), (130, 64, 32)])
+def test_gdn_prefill_matches_reference(T, p0, D):
+    C = _C()
+    torch.manual_seed(7)
+    Hk, Hv, K = 2, 4, 4
+    kd, vd = Hk * D, Hv * D
+    Cc = 2 * kd + vd
+    proj = torch.randn(T, 2 * kd + 2 * vd + 2 * Hv, device="cuda").bfloat16()
+    conv_w = torch.randn(Cc, K, device="cuda") * 0.3
+    ring = torch.randn(Cc, K, device="cuda").bfloat16()
+    A_log = torch.randn(Hv, device="cuda") * 0.5
+    dt_bias = torch.randn(Hv, device="cuda") * 0.5
+    nw = torch.rand(D, device="cuda") + 0.5
+    S0 = torch.randn(Hv, D, D, device="cuda") * 0.05
+    S = S0.clone()
+    out = torch.empty(T, vd, device="cuda", dtype=torch.bfloat16)
+    C.gdn_prefill(proj, conv_w, ring, A_log, dt_bias, nw, S, out, Hk, Hv, D, p0, 1e-6)
+    # reference
+    prev = torch.stack([ring[:, (p0 - 3 + j) % K].float() if p0 - 3 + j >= 0 else torch.zeros(Cc, device="cuda")
+                        for j in range(3)], 1)
+    y, _ = R.causal_conv1d(proj[:, :Cc].float(), conv_w, prev)
+    y = y.bfloat16().float()
+    r = Hv // Hk
+    q = R.l2norm(y[:, :kd].view(T, Hk, D).repeat_interleave(r, 1)) * D ** -0.5
+    k = R.l2norm(y[:, kd:2 * kd].view(T, Hk, D).repeat_interleave(r, 1))
+    v = y[:, 2 * kd:].view(T, Hv, D)
+    z = proj[:, Cc:Cc + vd].float().view(T, Hv, D)
+    bb = proj[:, Cc + vd:Cc + vd + Hv].float()
+    aa = proj[:, Cc + vd + Hv:].float()
+    g, beta = R.gdn_gating(aa, bb, A_log, dt_bias)
+    o, S1 = R.delta_rule_recurrent(q, k, v, g, beta, S0)
+    want = R.gated_rms_norm(o, z, nw, 1e-6).reshape(T, vd)
+    _close(S, S1, 2e-2)
+    _close(out, want, 3e-2)
