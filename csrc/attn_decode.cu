@@ -89,6 +89,21 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(AttnDecodeArgs a) {
   const int qw = a.gated ? 2 * D : D;
   const __nv_bfloat16* pr = a.proj + (long long)b * a.ldp;
   const long long cache_base = ((long long)slot * a.Hkv + kvh) * a.maxlen * D;
+  pdl_launch_dependents();
+  {
+    // KV rows < p were written by earlier (complete) steps: pull this CTA's range into
+    // L2 while the preceding projection kernel drains.
+    const int ch = (L + a.nsplit - 1) / a.nsplit;
+    const int t0 = split * ch, t1 = min(p, t0 + ch);
+    const int lines = (t1 > t0 ? (t1 - t0) : 0) * D * 2 / 128;
+    const char* kb = reinterpret_cast<const char*>(a.kc + cache_base + (long long)t0 * D);
+    const char* vb = reinterpret_cast<const char*>(a.vc + cache_base + (long long)t0 * D);
+    for (int i = threadIdx.x; i < lines; i += blockDim.x) {
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(kb + (long long)i * 128));
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(vb + (long long)i * 128));
+    }
+  }
+  pdl_wait_prior();
 
   // ---- q heads: norm + rope, pre-scaled ----------------------------------
   for (int g = warp; g < G; g += NW) {
@@ -215,7 +230,7 @@ static void launch_dg(const AttnDecodeArgs& a, dim3 grid, cudaStream_t s) {
   if (smem > 48 * 1024) {
     HX_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   }
-  k<<<grid, 256, smem, s>>>(a);
+  HX_CUDA_CHECK(hx_launch_pdl(k, grid, dim3(256), smem, s, a));
 }
 
 template <int D>
