@@ -283,3 +283,136 @@ void attn_decode(torch::Tensor proj, c10::optional<torch::Tensor> q_norm_w, c10:
   else TORCH_CHECK(false, "unsupported head dim");
   HX_CUDA_CHECK(cudaGetLastError());
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free entry point (declared in hx_noalloc.h).
+//
+// Same kernel as `attn_decode`, but the split-K scratch (per-split partial outputs,
+// their max/sum pairs and the election counters) lives in the file-scope device
+// arrays below instead of caller-provided buffers, so the call performs no device
+// allocation of any kind: no cudaMalloc/cudaFree and no allocator of a framework.
+//
+// Set-up: host code cannot use the arrays' names as device addresses (in host code
+// they are only stand-ins), so the first call on each device, with that device
+// current, resolves their addresses with cudaGetSymbolAddress and caches them.
+// Make that first call on each device before any stream capture.
+//
+// Sharing: every call on a device uses the same scratch, which keeps what the last
+// call left there. The election counters must start at zero, so each call clears the
+// part it uses on `stream` before the launch. Calls whose execution overlaps on the
+// GPU (different streams without ordering between them) race on the scratch and give
+// wrong results; order them on one stream or with events.
+// ---------------------------------------------------------------------------
+#include <mutex>
+
+#include "hx_noalloc.h"
+
+namespace {
+
+static __device__ __align__(256) float g_na_part_o[HX_NOALLOC_MAX_PART_O];
+static __device__ __align__(256) float g_na_part_ml[HX_NOALLOC_MAX_ROWS * 2];
+static __device__ __align__(256) int g_na_counters[HX_NOALLOC_MAX_COUNTERS];
+
+struct NoAllocScratch {
+  float* part_o = nullptr;
+  float* part_ml = nullptr;
+  int* counters = nullptr;
+  bool ready = false;
+};
+
+constexpr int kMaxDevices = 64;
+NoAllocScratch g_na_dev[kMaxDevices];
+std::mutex g_na_mu;
+thread_local char g_na_err[256] = "";
+
+int na_fail(int code, const char* msg) {
+  snprintf(g_na_err, sizeof(g_na_err), "%s", msg);
+  return code;
+}
+
+int na_setup(int dev, NoAllocScratch** out) {
+  std::lock_guard<std::mutex> lk(g_na_mu);
+  NoAllocScratch& s = g_na_dev[dev];
+  if (!s.ready) {
+    cudaError_t e = cudaGetSymbolAddress((void**)&s.part_o, g_na_part_o);
+    if (e == cudaSuccess) e = cudaGetSymbolAddress((void**)&s.part_ml, g_na_part_ml);
+    if (e == cudaSuccess) e = cudaGetSymbolAddress((void**)&s.counters, g_na_counters);
+    if (e != cudaSuccess) {
+      snprintf(g_na_err, sizeof(g_na_err), "cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+      return (int)e;
+    }
+    s.ready = true;
+  }
+  *out = &s;
+  return 0;
+}
+
+template <int D>
+int na_launch(const hx::AttnDecodeArgs& a, int G, dim3 grid, cudaStream_t st) {
+  try {  // no C++ exception may cross the C boundary
+    switch (G) {
+      case 1: hx::launch_dg<D, 1>(a, grid, st); break;
+      case 2: hx::launch_dg<D, 2>(a, grid, st); break;
+      case 4: hx::launch_dg<D, 4>(a, grid, st); break;
+      case 8: hx::launch_dg<D, 8>(a, grid, st); break;
+      default: return na_fail(2, "unsupported GQA group size (Hq / Hkv must be 1, 2, 4 or 8)");
+    }
+  } catch (const std::exception& ex) {
+    return na_fail(7, ex.what());
+  }
+  return 0;
+}
+
+}  // namespace
+
+extern "C" const char* hx_noalloc_error(void) { return g_na_err; }
+
+extern "C" int hx_attn_decode_noalloc(const void* proj, int ldp, const float* q_norm_w, const float* k_norm_w,
+                                      const float* inv_freq, void* kc, void* vc, int maxlen, const int* slots,
+                                      const int* pos, void* out, int B, int Hq, int Hkv, int D, int rot, int gated,
+                                      float eps, int nsplit, cudaStream_t stream) {
+  g_na_err[0] = 0;
+  if (B < 1 || Hq < 1 || Hkv < 1 || nsplit < 1 || Hq % Hkv) return na_fail(3, "invalid B / Hq / Hkv / nsplit");
+  if ((long long)B * Hq * nsplit * D > HX_NOALLOC_MAX_PART_O || (long long)B * Hq * nsplit > HX_NOALLOC_MAX_ROWS ||
+      (long long)B * Hkv > HX_NOALLOC_MAX_COUNTERS) {
+    snprintf(g_na_err, sizeof(g_na_err),
+             "scratch too small: needs B*Hq*nsplit*D=%lld (max %d), B*Hq*nsplit=%lld (max %d), B*Hkv=%lld (max %d)",
+             (long long)B * Hq * nsplit * D, HX_NOALLOC_MAX_PART_O, (long long)B * Hq * nsplit, HX_NOALLOC_MAX_ROWS,
+             (long long)B * Hkv, HX_NOALLOC_MAX_COUNTERS);
+    return 4;
+  }
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices) return na_fail(5, "cudaGetDevice failed");
+  NoAllocScratch* s = nullptr;
+  int rc = na_setup(dev, &s);
+  if (rc) return rc;
+  e = cudaMemsetAsync(s->counters, 0, sizeof(int) * B * Hkv, stream);
+  if (e != cudaSuccess) return na_fail((int)e, cudaGetErrorString(e));
+  hx::AttnDecodeArgs a{};
+  a.proj = reinterpret_cast<const __nv_bfloat16*>(proj);
+  a.ldp = ldp;
+  a.q_norm_w = q_norm_w;
+  a.k_norm_w = k_norm_w;
+  a.inv_freq = inv_freq;
+  a.kc = reinterpret_cast<__nv_bfloat16*>(kc);
+  a.vc = reinterpret_cast<__nv_bfloat16*>(vc);
+  a.slots = slots;
+  a.pos = pos;
+  a.part_o = s->part_o;
+  a.part_ml = s->part_ml;
+  a.counters = s->counters;
+  a.out = reinterpret_cast<__nv_bfloat16*>(out);
+  a.Hq = Hq; a.Hkv = Hkv; a.maxlen = maxlen; a.rot = rot; a.gated = gated; a.nsplit = nsplit;
+  a.eps = eps; a.scale = 1.f / sqrtf((float)D);
+  dim3 grid(nsplit, Hkv, B);
+  const int G = Hq / Hkv;
+  if (D == 256) rc = na_launch<256>(a, G, grid, stream);
+  else if (D == 128) rc = na_launch<128>(a, G, grid, stream);
+  else if (D == 64) rc = na_launch<64>(a, G, grid, stream);
+  else return na_fail(6, "unsupported head dim (64, 128 or 256)");
+  if (rc) return rc;
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return na_fail((int)e, cudaGetErrorString(e));
+  return 0;
+}
