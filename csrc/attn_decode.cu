@@ -84,8 +84,7 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(AttnDecodeArgs a) {
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int slot = a.slots[b];
-  const int p = a.pos[slot];
-  const int L = p + 1;
+  const int p_hint = a.pos[slot];  // may be one step stale before the wait (prefetch only)
   const int qw = a.gated ? 2 * D : D;
   const __nv_bfloat16* pr = a.proj + (long long)b * a.ldp;
   const long long cache_base = ((long long)slot * a.Hkv + kvh) * a.maxlen * D;
@@ -93,8 +92,8 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(AttnDecodeArgs a) {
   {
     // KV rows < p were written by earlier (complete) steps: pull this CTA's range into
     // L2 while the preceding projection kernel drains.
-    const int ch = (L + a.nsplit - 1) / a.nsplit;
-    const int t0 = split * ch, t1 = min(p, t0 + ch);
+    const int ch = (p_hint + 1 + a.nsplit - 1) / a.nsplit;
+    const int t0 = split * ch, t1 = min(p_hint, t0 + ch);
     const int lines = (t1 > t0 ? (t1 - t0) : 0) * D * 2 / 128;
     const char* kb = reinterpret_cast<const char*>(a.kc + cache_base + (long long)t0 * D);
     const char* vb = reinterpret_cast<const char*>(a.vc + cache_base + (long long)t0 * D);
@@ -104,6 +103,8 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(AttnDecodeArgs a) {
     }
   }
   pdl_wait_prior();
+  const int p = a.pos[slot];
+  const int L = p + 1;
 
   // ---- q heads: norm + rope, pre-scaled ----------------------------------
   for (int g = warp; g < G; g += NW) {

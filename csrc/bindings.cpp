@@ -44,7 +44,10 @@ void gdn_prefill(torch::Tensor proj, torch::Tensor conv_w, torch::Tensor ring, t
                  torch::Tensor dt_bias, torch::Tensor norm_w, torch::Tensor state, torch::Tensor out, int64_t Hk,
                  int64_t Hv, int64_t D, int64_t p0, double eps);
 
+#include "hx_runtime.h"
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.def("set_pdl", [](bool on) { hx_pdl_enabled() = on; });
   m.def("gemv", &gemv);
   m.def("gemv_experts", &gemv_experts);
   m.def("moe_topk", &moe_topk);

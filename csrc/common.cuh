@@ -7,6 +7,8 @@
 
 #include <utility>
 
+#include "hx_runtime.h"
+
 #define HX_DEVICE __device__ __forceinline__
 
 #define HX_CUDA_CHECK(expr)                                                            \
@@ -102,7 +104,7 @@ static inline cudaError_t hx_launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[0].val.programmaticStreamSerializationAllowed = hx_pdl_enabled() ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);

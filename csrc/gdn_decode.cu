@@ -48,16 +48,18 @@ __global__ void __launch_bounds__(512) gdn_decode_kernel(GdnDecodeArgs a) {
 
   const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
   pdl_launch_dependents();
-  // slots/pos and the recurrent state were written by earlier decode steps, which are
-  // complete; only the in-projection comes from the immediately preceding kernel.
+  // slots (host-written before launch) and the recurrent state (last written by this
+  // layer's kernel in an earlier step) may be read before the dependency wait; the
+  // position may not: with programmatic launch this kernel can start while the
+  // previous step's arg-max, which advances it, is still running.
   const int slot = a.slots[b];
-  const int p = a.pos[slot];
   const int v_ = tid % DV, kg_ = tid / DV;
   float* S = a.rec + (((long long)slot * a.Hv + h) * DK) * DV;
   float s[RK];
 #pragma unroll
   for (int i = 0; i < RK; ++i) s[i] = S[(kg_ * RK + i) * DV + v_];
   pdl_wait_prior();
+  const int p = a.pos[slot];
   const int r = a.Hv / a.Hk, kh = h / r;
   const int kd = a.Hk * DK;
   const int C = 2 * kd + a.Hv * DV;

@@ -493,7 +493,7 @@ static void sg_launch(SgArgs a, cudaStream_t st, bool pdl) {
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  attr[0].val.programmaticStreamSerializationAllowed = (pdl && hx_pdl_enabled()) ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   HX_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k, a, nstages, (int)(stage_bytes / 2)));

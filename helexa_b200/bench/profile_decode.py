@@ -29,7 +29,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--eager", action="store_true")
+    ap.add_argument("--no-pdl", action="store_true", help="launch without programmatic dependent launch")
     args = ap.parse_args()
+    if args.no_pdl:
+        from .. import ops
+        ops.C.set_pdl(False)
     cfg = get_preset(args.model)
     if args.layers:
         cfg = dataclasses.replace(cfg, num_hidden_layers=args.layers, layer_types=cfg.layer_types[:args.layers])
@@ -61,7 +65,7 @@ def main():
     ms = e0.elapsed_time(e1) / args.steps
     gb = fm.decode_bytes_per_token() / 1e9
     print(json.dumps({"model": cfg.name, "layers": cfg.num_hidden_layers, "context": args.context, "batch": B,
-                      "graph": not args.eager, "ms_per_step": round(ms, 4),
+                      "graph": not args.eager, "pdl": not args.no_pdl, "ms_per_step": round(ms, 4),
                       "weight_gb_per_step": round(gb, 3), "achieved_gbs": round(gb / (ms / 1e3), 1),
                       "launches_per_step": fm.launches_per_step()}))
 
