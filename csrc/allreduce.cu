@@ -51,8 +51,8 @@ __global__ void __launch_bounds__(256) ar_oneshot_kernel(PeerPtrs peers, int ran
                                                          size_t data_bytes, unsigned* epoch, int* err,
                                                          unsigned long long timeout_ns) {
   const int cta = blockIdx.x;
-  pdl_launch_dependents();
   pdl_wait_prior();
+  pdl_launch_dependents();
   // a communicator whose earlier exchange timed out is poisoned: fail fast instead of
   // waiting again on every later call (the host tears it down after `check`)
   if (*((volatile int*)err) != 0) return;

@@ -71,29 +71,31 @@ HX_DEVICE void norm_rope_head(float* xv, const float* w, const float* inv_freq, 
 }
 
 template <int D, int G>
-__global__ void __launch_bounds__(256) attn_decode_kernel(AttnDecodeArgs a) {
-  constexpr int PER = D / 32;
-  constexpr int NW = 8;
+__global__ void __launch_bounds__(128) attn_decode_kernel(AttnDecodeArgs a) {
+  constexpr int PER = D / 32;   // head dims per lane in the PV phase
+  constexpr int NW = 4;         // warps per CTA
+  constexpr int TILE = 32;      // keys per warp tile (one key per lane in the QK phase)
   extern __shared__ __align__(16) float dsm[];
-  float (*qsm)[D] = reinterpret_cast<float (*)[D]>(dsm);                      // [G][D]
-  float (*tmp)[D] = reinterpret_cast<float (*)[D]>(dsm + G * D);              // [NW][D]
-  float (*wo)[G][D] = reinterpret_cast<float (*)[G][D]>(dsm + (G + NW) * D);  // [NW][G][D]
+  float (*qsm)[D] = reinterpret_cast<float (*)[D]>(dsm);                      // [G][D] normed, roped, scaled
+  float (*tmp)[D] = reinterpret_cast<float (*)[D]>(dsm + G * D);              // [NW][D] rope scratch
+  float (*psm)[G][TILE] = reinterpret_cast<float (*)[G][TILE]>(dsm + (G + NW) * D);  // [NW][G][TILE]
+  float (*wo)[G][D] = reinterpret_cast<float (*)[G][D]>(dsm + (G + NW) * D + NW * G * TILE);  // [NW][G][D]
   __shared__ float wm[NW][G], wl[NW][G];
   __shared__ int is_last;
 
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int slot = a.slots[b];
-  const int p_hint = a.pos[slot];  // may be one step stale before the wait (prefetch only)
   const int qw = a.gated ? 2 * D : D;
   const __nv_bfloat16* pr = a.proj + (long long)b * a.ldp;
   const long long cache_base = ((long long)slot * a.Hkv + kvh) * a.maxlen * D;
-  pdl_launch_dependents();
   {
-    // KV rows < p were written by earlier (complete) steps: pull this CTA's range into
-    // L2 while the preceding projection kernel drains.
-    const int ch = (p_hint + 1 + a.nsplit - 1) / a.nsplit;
-    const int t0 = split * ch, t1 = min(p_hint, t0 + ch);
+    // KV rows before the current position come from earlier, complete steps: start
+    // pulling this CTA's range into L2 while the projection kernel drains. The
+    // position read here may be one step stale; it only steers the prefetch.
+    const int ph = a.pos[slot];
+    const int ch = (ph + 1 + a.nsplit - 1) / a.nsplit;
+    const int t0 = split * ch, t1 = min(ph, t0 + ch);
     const int lines = (t1 > t0 ? (t1 - t0) : 0) * D * 2 / 128;
     const char* kb = reinterpret_cast<const char*>(a.kc + cache_base + (long long)t0 * D);
     const char* vb = reinterpret_cast<const char*>(a.vc + cache_base + (long long)t0 * D);
@@ -103,12 +105,13 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(AttnDecodeArgs a) {
     }
   }
   pdl_wait_prior();
+  pdl_launch_dependents();
   const int p = a.pos[slot];
   const int L = p + 1;
 
   // ---- q heads: norm + rope, pre-scaled ----------------------------------
   for (int g = warp; g < G; g += NW) {
-    int hq = kvh * G + g;
+    const int hq = kvh * G + g;
     float xv[PER];
 #pragma unroll
     for (int i = 0; i < PER; ++i) xv[i] = __bfloat162float(pr[hq * qw + lane * PER + i]);
@@ -116,16 +119,15 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(AttnDecodeArgs a) {
 #pragma unroll
     for (int i = 0; i < PER; ++i) qsm[g][lane * PER + i] = xv[i] * a.scale;
   }
-  // ---- key range ----------------------------------------------------------
   const int chunk = (L + a.nsplit - 1) / a.nsplit;
   const int k0 = split * chunk, k1 = min(L, k0 + chunk);
-  // the split that covers the new token appends K/V[p] (then reads it back itself)
-  if (k0 <= p && p < k1 && warp == 0) {
+  // the split that covers the new token appends K/V[p] before anyone reads it
+  if (k0 <= p && p < k1 && warp == NW - 1) {
     const int qtot = a.Hq * qw;
     float xv[PER];
 #pragma unroll
     for (int i = 0; i < PER; ++i) xv[i] = __bfloat162float(pr[qtot + kvh * D + lane * PER + i]);
-    norm_rope_head<D>(xv, a.k_norm_w, a.inv_freq, a.rot, p, a.eps, tmp[0]);
+    norm_rope_head<D>(xv, a.k_norm_w, a.inv_freq, a.rot, p, a.eps, tmp[NW - 1]);
 #pragma unroll
     for (int i = 0; i < PER; ++i) {
       a.kc[cache_base + (long long)p * D + lane * PER + i] = __float2bfloat16(xv[i]);
@@ -134,35 +136,70 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(AttnDecodeArgs a) {
   }
   __syncthreads();
 
-  // ---- online softmax over this warp's keys -------------------------------
-  float m[G], l[G], acc[G][PER], q[G][PER];
+  float m[G], l[G], acc[G][PER];
 #pragma unroll
   for (int g = 0; g < G; ++g) {
     m[g] = -INFINITY;
     l[g] = 0.f;
 #pragma unroll
-    for (int i = 0; i < PER; ++i) { acc[g][i] = 0.f; q[g][i] = qsm[g][lane * PER + i]; }
+    for (int i = 0; i < PER; ++i) acc[g][i] = 0.f;
   }
-  for (int t = k0 + warp; t < k1; t += NW) {
-    const __nv_bfloat16* kr = a.kc + cache_base + (long long)t * D + lane * PER;
-    const __nv_bfloat16* vr = a.vc + cache_base + (long long)t * D + lane * PER;
-    float kf[PER], vf[PER];
+  for (int tb = k0 + warp * TILE; tb < k1; tb += NW * TILE) {
+    // ---- QK: lane j scores key tb + j against every q head --------------------
+    const int t = tb + lane;
+    const bool valid = t < k1;
+    float sc[G];
 #pragma unroll
-    for (int i = 0; i < PER; ++i) { kf[i] = __bfloat162float(kr[i]); vf[i] = __bfloat162float(vr[i]); }
+    for (int g = 0; g < G; ++g) sc[g] = 0.f;
+    if (valid) {
+      const bf16x8* kr = reinterpret_cast<const bf16x8*>(a.kc + cache_base + (long long)t * D);
+#pragma unroll 4
+      for (int v = 0; v < D / 8; ++v) {
+        float kf[8];
+        unpack8(kr[v], kf);
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          const float4 q0 = *reinterpret_cast<const float4*>(&qsm[g][v * 8]);
+          const float4 q1 = *reinterpret_cast<const float4*>(&qsm[g][v * 8 + 4]);
+          sc[g] += q0.x * kf[0] + q0.y * kf[1] + q0.z * kf[2] + q0.w * kf[3] + q1.x * kf[4] + q1.y * kf[5] +
+                   q1.z * kf[6] + q1.w * kf[7];
+        }
+      }
+    }
+    // ---- online softmax over the tile -----------------------------------------
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-      float sdot = 0.f;
-#pragma unroll
-      for (int i = 0; i < PER; ++i) sdot += q[g][i] * kf[i];
-      sdot = warp_sum(sdot);
-      float mn = fmaxf(m[g], sdot);
-      float corr = __expf(m[g] - mn);
-      float pe = __expf(sdot - mn);
-      l[g] = l[g] * corr + pe;
-#pragma unroll
-      for (int i = 0; i < PER; ++i) acc[g][i] = acc[g][i] * corr + pe * vf[i];
+      const float s = valid ? sc[g] : -INFINITY;
+      const float mt = warp_max(s);
+      const float mn = fmaxf(m[g], mt);
+      const float pe = valid ? __expf(s - mn) : 0.f;
+      const float corr = __expf(m[g] - mn);
+      l[g] = l[g] * corr + warp_sum(pe);
       m[g] = mn;
+#pragma unroll
+      for (int i = 0; i < PER; ++i) acc[g][i] *= corr;
+      psm[warp][g][lane] = pe;
     }
+    __syncwarp();
+    // ---- PV: lanes over head dims ----------------------------------------------
+    const int nk = min(TILE, k1 - tb);
+    for (int j = 0; j < nk; ++j) {
+      const __nv_bfloat16* vr = a.vc + cache_base + (long long)(tb + j) * D + lane * PER;
+      float vf[PER];
+      if (PER == 8) {
+        unpack8(*reinterpret_cast<const bf16x8*>(vr), vf);
+      } else {
+#pragma unroll
+        for (int i = 0; i < PER; ++i) vf[i] = __bfloat162float(vr[i]);
+      }
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float pj = psm[warp][g][j];
+#pragma unroll
+        for (int i = 0; i < PER; ++i) acc[g][i] = fmaf(pj, vf[i], acc[g][i]);
+      }
+    }
+    __syncwarp();
   }
   // ---- combine warps inside the CTA -------------------------------------
 #pragma unroll
@@ -225,13 +262,13 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(AttnDecodeArgs a) {
 
 template <int D, int G>
 static void launch_dg(const AttnDecodeArgs& a, dim3 grid, cudaStream_t s) {
-  constexpr int NW = 8;
-  const size_t smem = (size_t)(G * D + NW * D + NW * G * D) * sizeof(float);
+  constexpr int NW = 4, TILE = 32;
+  const size_t smem = (size_t)(G * D + NW * D + NW * G * TILE + NW * G * D) * sizeof(float);
   auto k = attn_decode_kernel<D, G>;
   if (smem > 48 * 1024) {
     HX_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   }
-  HX_CUDA_CHECK(hx_launch_pdl(k, grid, dim3(256), smem, s, a));
+  HX_CUDA_CHECK(hx_launch_pdl(k, grid, dim3(NW * 32), smem, s, a));
 }
 
 template <int D>

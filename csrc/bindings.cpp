@@ -31,14 +31,13 @@ void gemm(torch::Tensor A, torch::Tensor B, torch::Tensor C, int64_t epi, torch:
 void gemm_grouped(torch::Tensor A, torch::Tensor B, torch::Tensor C, torch::Tensor tiles, int64_t n, int64_t epi,
                   torch::Tensor err);
 
-void sgemv(int64_t mode, torch::Tensor W, torch::Tensor x, c10::optional<torch::Tensor> y,
-           c10::optional<torch::Tensor> resid, c10::optional<torch::Tensor> norm_w, double eps,
-           c10::optional<torch::Tensor> ids, c10::optional<torch::Tensor> wts, int64_t J,
-           c10::optional<torch::Tensor> scratch, c10::optional<torch::Tensor> counter,
-           c10::optional<torch::Tensor> out_ids, c10::optional<torch::Tensor> out_wts, int64_t E, int64_t topk,
-           bool has_shared, bool norm_topk, c10::optional<torch::Tensor> tok, c10::optional<torch::Tensor> slots,
-           c10::optional<torch::Tensor> pos, c10::optional<torch::Tensor> out_tokens,
-           c10::optional<torch::Tensor> step, torch::Tensor err, bool pdl);
+void gemv_router(torch::Tensor W, torch::Tensor x, torch::Tensor logits, torch::Tensor norm_w, double eps,
+                 int64_t E, int64_t topk, bool has_shared, bool norm_topk, torch::Tensor ids, torch::Tensor wts,
+                 torch::Tensor counter);
+void gemv_argmax(torch::Tensor W, torch::Tensor x, c10::optional<torch::Tensor> logits, torch::Tensor norm_w,
+                 double eps, torch::Tensor best, torch::Tensor counter, torch::Tensor tok,
+                 c10::optional<torch::Tensor> slots, c10::optional<torch::Tensor> pos,
+                 c10::optional<torch::Tensor> out_tokens, c10::optional<torch::Tensor> step);
 
 void gdn_prefill(torch::Tensor proj, torch::Tensor conv_w, torch::Tensor ring, torch::Tensor A_log,
                  torch::Tensor dt_bias, torch::Tensor norm_w, torch::Tensor state, torch::Tensor out, int64_t Hk,
@@ -62,6 +61,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ar_oneshot", &ar_oneshot);
   m.def("gemm", &gemm);
   m.def("gdn_prefill", &gdn_prefill);
-  m.def("sgemv", &sgemv);
+  m.def("gemv_router", &gemv_router);
+  m.def("gemv_argmax", &gemv_argmax);
   m.def("gemm_grouped", &gemm_grouped);
 }

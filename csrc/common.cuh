@@ -79,8 +79,12 @@ HX_DEVICE bf16x8 ld_stream(const bf16x8* p) {
 
 HX_DEVICE float silu(float x) { return x / (1.f + __expf(-x)); }
 
-// Programmatic dependent launch: let the next kernel start launching / wait until
-// the previous kernel's memory is visible. Both are no-ops without the launch attribute.
+// Programmatic dependent launch: wait until the previous kernel's memory is visible /
+// let the next kernel start launching. Both are no-ops without the launch attribute.
+// Every kernel here triggers its dependents only AFTER its own wait: a kernel that
+// triggered before waiting would let the whole chain of later kernels start early,
+// and their pre-wait reads could then see data that a still-running older kernel
+// has yet to write.
 HX_DEVICE void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 HX_DEVICE void pdl_wait_prior() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 

@@ -47,7 +47,6 @@ __global__ void __launch_bounds__(512) gdn_decode_kernel(GdnDecodeArgs a) {
   __shared__ float wred[16];
 
   const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
-  pdl_launch_dependents();
   // slots (host-written before launch) and the recurrent state (last written by this
   // layer's kernel in an earlier step) may be read before the dependency wait; the
   // position may not: with programmatic launch this kernel can start while the
@@ -59,6 +58,7 @@ __global__ void __launch_bounds__(512) gdn_decode_kernel(GdnDecodeArgs a) {
 #pragma unroll
   for (int i = 0; i < RK; ++i) s[i] = S[(kg_ * RK + i) * DV + v_];
   pdl_wait_prior();
+  pdl_launch_dependents();
   const int p = a.pos[slot];
   const int r = a.Hv / a.Hk, kh = h / r;
   const int kd = a.Hk * DK;

@@ -1,17 +1,23 @@
 // Decode-time bf16 GEMV (M = batch <= 8) with fused prologues/epilogues.
 //
-// Decode at batch 1 reads every weight once per token, so these kernels are
-// HBM-bound: each warp owns RPW output rows and keeps RPW*UNROLL 16-byte
-// streaming loads in flight per lane; the activation row(s) sit in shared memory.
+// Decode at batch 1 reads every active weight once per token, so these kernels are
+// HBM-bound. Each warp owns RPW output rows; every lane keeps RPW x U 16-byte
+// streaming loads in flight and issues the next batch before consuming the current
+// one (register double buffering). Launched with programmatic dependent launch: the
+// first weight batch is requested before griddepcontrol.wait, so it overlaps the tail
+// of the previous kernel; activations are read after the wait.
 //
-// Fusions (each removes a kernel the reference launches separately):
-//   * RMSNorm prologue: y = W . rmsnorm(x) * w_norm, recomputed per CTA from the
-//     raw residual stream (the norm is over <= 8K values, cheaper than a launch).
-//     Replaces the standalone input/post-attention norms (arch/qwen3_5/decoder.rs:115-133).
-//   * residual epilogue: y = resid + W.x (in place), replacing the add after
-//     o_proj/out_proj/down_proj.
-//   * SwiGLU epilogue over row-interleaved [gate_n, up_n] weights.
-//   * MoE expert indirection: row block j of grid.y reads expert ids[j]'s weights.
+// Fusions (each removes a kernel or a host round trip of the reference):
+//   * RMSNorm prologue on the raw residual stream (arch/qwen3_5/decoder.rs:115-133);
+//   * residual epilogue (in place) after o_proj / out_proj / down_proj;
+//   * SwiGLU epilogue over row-interleaved [gate_n, up_n] weights;
+//   * MoE expert indirection (row block j of grid.y reads expert ids[j]);
+//   * router tail: the last CTA runs softmax / top-k / renorm and appends the shared
+//     expert with weight sigmoid(shared_expert_gate) (arch/qwen3_5/moe.rs:124-199);
+//   * lm_head tail: a packed (value, index) atomicMax per batch row and, in the last
+//     CTA, the decode-step bookkeeping (next token, output ring, position) -- the
+//     reference copies full f32 logits to the host every step instead
+//     (harness/device_worker/dispatch.rs:1306-1312).
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 
@@ -19,12 +25,12 @@
 
 namespace hx {
 
-enum GemvMode : int { kStoreBf16 = 0, kResidAdd = 1, kSiluPair = 2, kStoreF32 = 3 };
+enum GemvMode : int { kStoreBf16 = 0, kResidAdd = 1, kSiluPair = 2, kStoreF32 = 3, kRouter = 4, kArgmax = 5 };
 
 struct GemvArgs {
   const __nv_bfloat16* W;     // [N, K] (or [E, N, K] when ids != nullptr)
-  const __nv_bfloat16* x;     // [B, K] activations (or one row per job with x_row_div)
-  void* y;                    // output
+  const __nv_bfloat16* x;     // [B, K] activations (one row per job in expert mode)
+  void* y;                    // output (f32 logits for router / argmax, optional for argmax)
   const __nv_bfloat16* resid; // residual for kResidAdd (may alias y)
   const float* norm_w;        // RMSNorm weight (offset folded in) or nullptr
   const int* ids;             // expert ids per job (grid.y) or nullptr
@@ -33,22 +39,73 @@ struct GemvArgs {
   long long w_expert_stride;  // elements between experts
   int x_row_div;              // job j reads x row j / x_row_div (expert mode)
   float eps;
+  // tails
+  int* counter;               // last-CTA election (self-resetting)
+  unsigned long long* best;   // [B] packed arg-max words (self-resetting)
+  int E, topk, has_shared, norm_topk;
+  int* out_ids;
+  float* out_wts;
+  int* tok;
+  const int* slots;
+  int* pos;
+  int* out_tokens;
+  int out_cap;
+  int* step;
 };
 
-// One CTA: 8 warps x RPW rows. Batch mode: B rows of x, outputs [B, N].
-// Expert mode (ids): grid.y = job, one x row per job (B must be 1).
+// Order-preserving key of a float (larger float -> larger key), index tiebreak to the
+// smallest index (torch.argmax semantics).
+HX_DEVICE unsigned long long argmax_key(float v, int idx) {
+  unsigned u = __float_as_uint(v);
+  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return ((unsigned long long)u << 32) | (unsigned)(0x7fffffff - idx);
+}
+
 template <int B, int RPW, int MODE>
 __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem_raw);  // [B][K]
   __shared__ float red[8];
-  const int K = a.K;
+  __shared__ int is_last;
+  constexpr int U = 4;
+  const int K = a.K, nvec = K / 8;
   const int job = blockIdx.y;
-  const __nv_bfloat16* W = a.W;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row0 = (blockIdx.x * 8 + warp) * RPW;
+  const bool active = row0 < a.N;
+
+  const bf16x8* wrow[RPW];
+  bf16x8 cur[RPW][U];
+  auto set_rows = [&](const __nv_bfloat16* W) {
+#pragma unroll
+    for (int r = 0; r < RPW; ++r) {
+      int row = min(row0 + r, a.N - 1);
+      wrow[r] = reinterpret_cast<const bf16x8*>(W + (long long)row * K);
+    }
+  };
+  auto load_batch = [&](bf16x8 (&dst)[RPW][U], int v0) {
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+#pragma unroll
+      for (int r = 0; r < RPW; ++r) {
+        int v = v0 + 32 * u;
+        dst[r][u] = ld_stream(wrow[r] + (v < nvec ? v : 0));
+      }
+  };
+  const bool static_w = (a.ids == nullptr);
+  if (static_w && active) {
+    set_rows(a.W);
+    load_batch(cur, lane);  // weights never depend on the previous kernel
+  }
+  pdl_wait_prior();
+  pdl_launch_dependents();
   const __nv_bfloat16* xsrc = a.x;
-  if (a.ids) {
-    W += (long long)a.ids[job] * a.w_expert_stride;
+  if (!static_w) {
     xsrc += (long long)(job / a.x_row_div) * K;
+    if (active) {
+      set_rows(a.W + (long long)a.ids[job] * a.w_expert_stride);
+      load_batch(cur, lane);
+    }
   }
   // ---- stage x (optionally RMS-normalised) into shared memory as bf16 ----
   for (int b = 0; b < B; ++b) {
@@ -79,57 +136,39 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
   }
   __syncthreads();
 
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row0 = (blockIdx.x * 8 + warp) * RPW;
-  if (row0 >= a.N) return;
   float acc[RPW][B];
 #pragma unroll
   for (int r = 0; r < RPW; ++r)
 #pragma unroll
     for (int b = 0; b < B; ++b) acc[r][b] = 0.f;
-
-  const bf16x8* wrow[RPW];
+  if (active) {
+    for (int v0 = lane; v0 < nvec; v0 += 32 * U) {
+      bf16x8 nxt[RPW][U];
+      const bool more = v0 + 32 * U < nvec;
+      if (more) load_batch(nxt, v0 + 32 * U);
 #pragma unroll
-  for (int r = 0; r < RPW; ++r) {
-    int row = min(row0 + r, a.N - 1);
-    wrow[r] = reinterpret_cast<const bf16x8*>(W + (long long)row * K);
-  }
-  constexpr int U = 4;
-  const int nvec = K / 8;
-  int v = lane;
-  for (; v + 32 * (U - 1) < nvec; v += 32 * U) {
-    bf16x8 wv[RPW][U];
+      for (int u = 0; u < U; ++u) {
+        const int v = v0 + 32 * u;
+        if (v < nvec) {
 #pragma unroll
-    for (int u = 0; u < U; ++u)
+          for (int b = 0; b < B; ++b) {
+            float xf[8];
+            unpack8(*reinterpret_cast<const bf16x8*>(xs + b * K + v * 8), xf);
 #pragma unroll
-      for (int r = 0; r < RPW; ++r) wv[r][u] = ld_stream(wrow[r] + v + 32 * u);
+            for (int r = 0; r < RPW; ++r) {
+              float wf[8];
+              unpack8(cur[r][u], wf);
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-#pragma unroll
-      for (int b = 0; b < B; ++b) {
-        float xf[8];
-        unpack8(*reinterpret_cast<const bf16x8*>(xs + b * K + (v + 32 * u) * 8), xf);
-#pragma unroll
-        for (int r = 0; r < RPW; ++r) {
-          float wf[8];
-          unpack8(wv[r][u], wf);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) acc[r][b] = fmaf(wf[i], xf[i], acc[r][b]);
+              for (int i = 0; i < 8; ++i) acc[r][b] = fmaf(wf[i], xf[i], acc[r][b]);
+            }
+          }
         }
       }
-    }
-  }
-  for (; v < nvec; v += 32) {
+      if (more) {
 #pragma unroll
-    for (int r = 0; r < RPW; ++r) {
-      float wf[8];
-      unpack8(ld_stream(wrow[r] + v), wf);
+        for (int r = 0; r < RPW; ++r)
 #pragma unroll
-      for (int b = 0; b < B; ++b) {
-        float xf[8];
-        unpack8(*reinterpret_cast<const bf16x8*>(xs + b * K + v * 8), xf);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) acc[r][b] = fmaf(wf[i], xf[i], acc[r][b]);
+          for (int u = 0; u < U; ++u) cur[r][u] = nxt[r][u];
       }
     }
   }
@@ -137,40 +176,139 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
   for (int r = 0; r < RPW; ++r)
 #pragma unroll
     for (int b = 0; b < B; ++b) acc[r][b] = warp_sum(acc[r][b]);
-  if (lane != 0) return;
-  const int yrow = a.ids ? job : 0;
+
+  if (active && lane == 0) {
+    const int yrow = a.ids ? job : 0;
 #pragma unroll
-  for (int b = 0; b < B; ++b) {
-    const long long ob = (long long)(yrow + b) * a.ldy;
-    if (MODE == kSiluPair) {
+    for (int b = 0; b < B; ++b) {
+      const long long ob = (long long)(yrow + b) * a.ldy;
+      if (MODE == kSiluPair) {
 #pragma unroll
-      for (int r = 0; r + 1 < RPW; r += 2) {
-        int n = (row0 + r) / 2;
-        if (row0 + r + 1 < a.N) {
-          // round like a bf16 model: act(gate) and up are bf16 before the product
-          float g = __bfloat162float(__float2bfloat16(acc[r][b]));
-          float u = __bfloat162float(__float2bfloat16(acc[r + 1][b]));
-          reinterpret_cast<__nv_bfloat16*>(a.y)[ob + n] = __float2bfloat16(silu(g) * u);
+        for (int r = 0; r + 1 < RPW; r += 2) {
+          int n = (row0 + r) / 2;
+          if (row0 + r + 1 < a.N) {
+            // round like a bf16 model: gate and up are bf16 before the product
+            float g = __bfloat162float(__float2bfloat16(acc[r][b]));
+            float u = __bfloat162float(__float2bfloat16(acc[r + 1][b]));
+            reinterpret_cast<__nv_bfloat16*>(a.y)[ob + n] = __float2bfloat16(silu(g) * u);
+          }
         }
-      }
-    } else {
+      } else {
 #pragma unroll
-      for (int r = 0; r < RPW; ++r) {
-        int n = row0 + r;
-        if (n >= a.N) break;
-        if (MODE == kStoreF32) {
-          reinterpret_cast<float*>(a.y)[ob + n] = acc[r][b];
-        } else if (MODE == kResidAdd) {
-          // round the branch output to bf16 first (matches a bf16 model's `x + f(x)`)
-          float br = __bfloat162float(__float2bfloat16(acc[r][b]));
-          float rv = __bfloat162float(a.resid[ob + n]);
-          reinterpret_cast<__nv_bfloat16*>(a.y)[ob + n] = __float2bfloat16(rv + br);
-        } else {
-          reinterpret_cast<__nv_bfloat16*>(a.y)[ob + n] = __float2bfloat16(acc[r][b]);
+        for (int r = 0; r < RPW; ++r) {
+          int n = row0 + r;
+          if (n >= a.N) break;
+          if (MODE == kStoreF32 || MODE == kRouter) {
+            reinterpret_cast<float*>(a.y)[ob + n] = acc[r][b];
+          } else if (MODE == kArgmax) {
+            if (a.y) reinterpret_cast<float*>(a.y)[ob + n] = acc[r][b];
+          } else if (MODE == kResidAdd) {
+            // round the branch output to bf16 first (matches a bf16 model's `x + f(x)`)
+            float br = __bfloat162float(__float2bfloat16(acc[r][b]));
+            float rv = __bfloat162float(a.resid[ob + n]);
+            reinterpret_cast<__nv_bfloat16*>(a.y)[ob + n] = __float2bfloat16(rv + br);
+          } else {
+            reinterpret_cast<__nv_bfloat16*>(a.y)[ob + n] = __float2bfloat16(acc[r][b]);
+          }
         }
       }
     }
   }
+  if (MODE != kRouter && MODE != kArgmax) return;
+
+  // ---- grid tails ------------------------------------------------------------
+  if (MODE == kArgmax) {
+    // block arg-max per batch row, then one packed atomicMax per CTA and row
+    __shared__ unsigned long long wbest[8][B];
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+      unsigned long long k = 0;
+      if (active && lane == 0) {
+#pragma unroll
+        for (int r = 0; r < RPW; ++r)
+          if (row0 + r < a.N) k = max(k, argmax_key(acc[r][b], row0 + r));
+      }
+      if (lane == 0) wbest[warp][b] = k;
+    }
+    __syncthreads();
+    if (threadIdx.x < B) {
+      unsigned long long k = 0;
+      for (int w = 0; w < 8; ++w) k = max(k, wbest[w][threadIdx.x]);
+      atomicMax(&a.best[threadIdx.x], k);
+    }
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) is_last = (atomicAdd(a.counter, 1) == (int)(gridDim.x * gridDim.y) - 1);
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  if (MODE == kArgmax) {
+    if (threadIdx.x < B) {
+      const int b = threadIdx.x;
+      const unsigned long long k = atomicExch(&a.best[b], 0ull);
+      int t = 0x7fffffff - (int)(k & 0xffffffffu);
+      if (k == 0) t = 0;
+      a.tok[b] = t;
+      if (a.out_tokens) {
+        const int s = a.step[b];
+        a.out_tokens[(long long)b * a.out_cap + (s % a.out_cap)] = t;
+        a.step[b] = s + 1;
+      }
+      if (a.pos) a.pos[a.slots[b]] += 1;
+    }
+  } else if (warp < B) {
+    // router: softmax over E, top-k (lowest index on ties), optional renorm, shared expert
+    const int b = warp;
+    const float* lg = reinterpret_cast<const float*>(a.y) + (long long)b * a.ldy;
+    constexpr int PER = 32;  // E <= 1024
+    float v[PER];
+    float m = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      int e = lane + 32 * i;
+      v[i] = e < a.E ? __ldcg(&lg[e]) : -INFINITY;
+      m = fmaxf(m, v[i]);
+    }
+    m = warp_max(m);
+    float den = 0.f;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) den += (lane + 32 * i) < a.E ? expf(v[i] - m) : 0.f;
+    den = warp_sum(den);
+    float sel = 0.f, my_p = 0.f;
+    int my_id = -1;
+    for (int j = 0; j < a.topk; ++j) {
+      float bv = -INFINITY;
+      int bi = 0x7fffffff;
+#pragma unroll
+      for (int i = 0; i < PER; ++i) {
+        int e = lane + 32 * i;
+        if (e < a.E && (v[i] > bv || (v[i] == bv && e < bi))) { bv = v[i]; bi = e; }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+      }
+      float pj = expf(bv - m) / den;
+      sel += pj;
+      if (lane == j) { my_id = bi; my_p = pj; }
+#pragma unroll
+      for (int i = 0; i < PER; ++i)
+        if (lane + 32 * i == bi) v[i] = -INFINITY;
+    }
+    const int ldo = a.topk + (a.has_shared ? 1 : 0);
+    if (lane < a.topk) {
+      a.out_ids[b * ldo + lane] = my_id;
+      a.out_wts[b * ldo + lane] = a.norm_topk ? my_p / sel : my_p;
+    }
+    if (a.has_shared && lane == 0) {
+      a.out_ids[b * ldo + a.topk] = a.E;
+      a.out_wts[b * ldo + a.topk] = 1.f / (1.f + expf(-__ldcg(&lg[a.E])));
+    }
+  }
+  if (threadIdx.x == 0) *a.counter = 0;
 }
 
 template <int B, int MODE>
@@ -182,8 +320,7 @@ static void launch_b(const GemvArgs& a, int jobs, cudaStream_t s) {
   if (smem > 48 * 1024) {
     HX_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   }
-  k<<<grid, 256, smem, s>>>(a);
-  HX_CUDA_CHECK(cudaGetLastError());
+  HX_CUDA_CHECK(hx_launch_pdl(k, grid, dim3(256), smem, s, a));
 }
 
 template <int MODE>
@@ -195,7 +332,7 @@ static void launch_mode(const GemvArgs& a, int B, cudaStream_t s) {
     case 4: launch_b<4, MODE>(a, 1, s); break;
     case 8: launch_b<8, MODE>(a, 1, s); break;
     default: {
-      // split any other batch into pieces of at most 4 rows
+      TORCH_CHECK(MODE != kRouter && MODE != kArgmax, "router / argmax batch must be 1, 2, 3, 4 or 8");
       int done = 0;
       while (done < B) {
         int take = (B - done) >= 4 ? 4 : (B - done);
@@ -214,6 +351,78 @@ static void launch_mode(const GemvArgs& a, int B, cudaStream_t s) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// MoE down projection + routing-weighted combine + residual, one warp per output row
+// ---------------------------------------------------------------------------
+// x[b, h] += sum_j wts[b, j] * (Wd[ids[b, j]][h, :] . act[b*J + j, :])
+// (or partial[b, h] = the sum, for tensor-parallel partial sums).
+// grid (ceil(H / 8), B), 256 threads; VPL = ceil(I / 256) 16-byte vectors per lane and
+// expert row; J <= 16.
+template <int VPL>
+__global__ void __launch_bounds__(256) moe_down_kernel(const __nv_bfloat16* __restrict__ Wd,
+                                                       const __nv_bfloat16* __restrict__ act,
+                                                       const int* __restrict__ ids, const float* __restrict__ wts,
+                                                       __nv_bfloat16* x, __nv_bfloat16* partial_out, int H, int I,
+                                                       int J) {
+  extern __shared__ __align__(16) __nv_bfloat16 acts[];  // [J][I] routing-weight scaled
+  pdl_wait_prior();
+  pdl_launch_dependents();
+  const int b = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h = blockIdx.x * 8 + warp;
+  // issue every expert row's loads for this warp first (J * VPL vectors per lane)
+  bf16x8 w[16][VPL];
+  if (h < H) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      if (j < J) {
+        const long long e = ids[b * J + j];
+        const bf16x8* row = reinterpret_cast<const bf16x8*>(Wd + (e * H + h) * (long long)I);
+#pragma unroll
+        for (int q = 0; q < VPL; ++q) {
+          const int v = lane + 32 * q;
+          w[j][q] = ld_stream(row + (v < I / 8 ? v : 0));
+        }
+      }
+    }
+  }
+  for (int t = threadIdx.x; t < J * I / 8; t += blockDim.x) {
+    const int j = (t * 8) / I;
+    float f[8];
+    unpack8(reinterpret_cast<const bf16x8*>(act + (long long)b * J * I)[t], f);
+    const float s = wts[b * J + j];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) f[i] *= s;
+    reinterpret_cast<bf16x8*>(acts)[t] = pack8(f);
+  }
+  __syncthreads();
+  if (h >= H) return;
+  float acc = 0.f;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    if (j < J) {
+#pragma unroll
+      for (int q = 0; q < VPL; ++q) {
+        if (lane + 32 * q >= I / 8) break;
+        float wf[8], af[8];
+        unpack8(w[j][q], wf);
+        unpack8(reinterpret_cast<const bf16x8*>(acts + (long long)j * I)[lane + 32 * q], af);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc = fmaf(wf[i], af[i], acc);
+      }
+    }
+  }
+  acc = warp_sum(acc);
+  if (lane == 0) {
+    if (partial_out) {
+      partial_out[(long long)b * H + h] = __float2bfloat16(acc);
+    } else {
+      float br = __bfloat162float(__float2bfloat16(acc));
+      x[(long long)b * H + h] = __float2bfloat16(__bfloat162float(x[(long long)b * H + h]) + br);
+    }
+  }
+}
+
 }  // namespace hx
 
 using namespace hx;
@@ -223,7 +432,7 @@ static void check_w(const torch::Tensor& W) {
               "W must be contiguous bf16 CUDA");
 }
 
-// y[B, N] (or resid-added in place / SwiGLU [B, N/2]) = W[N, K] . (rmsnorm?)(x[B, K])
+// y[B, N] (or resid-added in place / SwiGLU [B, N/2] / f32) = W[N, K] . (rmsnorm?)(x[B, K])
 void gemv(torch::Tensor W, torch::Tensor x, torch::Tensor y, int64_t mode, c10::optional<torch::Tensor> resid,
           c10::optional<torch::Tensor> norm_w, double eps) {
   check_w(W);
@@ -232,6 +441,7 @@ void gemv(torch::Tensor W, torch::Tensor x, torch::Tensor y, int64_t mode, c10::
   TORCH_CHECK(x.size(1) == K && K % 8 == 0, "K mismatch or not a multiple of 8");
   TORCH_CHECK(B >= 1 && B <= 64, "batch must be in [1, 64]");
   TORCH_CHECK(y.is_contiguous() && y.size(0) == B, "y: [B, *] contiguous");
+  TORCH_CHECK(mode <= kStoreF32, "use gemv_router / gemv_argmax for the fused tails");
   GemvArgs a{};
   a.W = reinterpret_cast<const __nv_bfloat16*>(W.data_ptr());
   a.x = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
@@ -247,11 +457,7 @@ void gemv(torch::Tensor W, torch::Tensor x, torch::Tensor y, int64_t mode, c10::
   } else {
     TORCH_CHECK(y.size(-1) == N, "output width mismatch");
   }
-  if (mode == kStoreF32) {
-    TORCH_CHECK(y.scalar_type() == at::kFloat, "f32 output expected");
-  } else {
-    TORCH_CHECK(y.scalar_type() == at::kBFloat16, "bf16 output expected");
-  }
+  TORCH_CHECK(y.scalar_type() == (mode == kStoreF32 ? at::kFloat : at::kBFloat16), "output dtype");
   if (mode == kResidAdd) TORCH_CHECK(resid.has_value(), "residual required");
   auto s = at::cuda::getCurrentCUDAStream();
   switch (mode) {
@@ -261,6 +467,52 @@ void gemv(torch::Tensor W, torch::Tensor x, torch::Tensor y, int64_t mode, c10::
     case kStoreF32: launch_mode<kStoreF32>(a, B, s); break;
     default: TORCH_CHECK(false, "bad gemv mode");
   }
+}
+
+// Router GEMV [E(+1), K] -> f32 logits [B, E(+1)] -> (last CTA) ids/wts [B, k(+1)].
+void gemv_router(torch::Tensor W, torch::Tensor x, torch::Tensor logits, torch::Tensor norm_w, double eps,
+                 int64_t E, int64_t topk, bool has_shared, bool norm_topk, torch::Tensor ids, torch::Tensor wts,
+                 torch::Tensor counter) {
+  check_w(W);
+  const int B = x.size(0);
+  TORCH_CHECK(E <= 1024 && topk <= 32 && B <= 8, "router limits: E <= 1024, top-k <= 32, batch <= 8");
+  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.size(1) == W.size(0) && logits.is_contiguous(), "logits");
+  GemvArgs a{};
+  a.W = reinterpret_cast<const __nv_bfloat16*>(W.data_ptr());
+  a.x = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
+  a.y = logits.data_ptr();
+  a.N = W.size(0); a.K = W.size(1); a.ldy = logits.size(1); a.eps = (float)eps; a.x_row_div = 1;
+  a.norm_w = norm_w.data_ptr<float>();
+  a.counter = counter.data_ptr<int>();
+  a.E = E; a.topk = topk; a.has_shared = has_shared; a.norm_topk = norm_topk;
+  a.out_ids = ids.data_ptr<int>(); a.out_wts = wts.data_ptr<float>();
+  launch_mode<kRouter>(a, B, at::cuda::getCurrentCUDAStream());
+}
+
+// lm_head GEMV with fused arg-max and decode-step bookkeeping.
+void gemv_argmax(torch::Tensor W, torch::Tensor x, c10::optional<torch::Tensor> logits, torch::Tensor norm_w,
+                 double eps, torch::Tensor best, torch::Tensor counter, torch::Tensor tok,
+                 c10::optional<torch::Tensor> slots, c10::optional<torch::Tensor> pos,
+                 c10::optional<torch::Tensor> out_tokens, c10::optional<torch::Tensor> step) {
+  check_w(W);
+  const int B = x.size(0);
+  TORCH_CHECK(best.scalar_type() == at::kLong && best.numel() >= B, "best: int64 [B] zero-initialised");
+  GemvArgs a{};
+  a.W = reinterpret_cast<const __nv_bfloat16*>(W.data_ptr());
+  a.x = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
+  a.y = logits ? logits->data_ptr() : nullptr;
+  a.N = W.size(0); a.K = W.size(1); a.ldy = logits ? logits->size(1) : 0; a.eps = (float)eps; a.x_row_div = 1;
+  a.norm_w = norm_w.data_ptr<float>();
+  a.counter = counter.data_ptr<int>();
+  a.best = reinterpret_cast<unsigned long long*>(best.data_ptr());
+  a.tok = tok.data_ptr<int>();
+  a.slots = slots ? slots->data_ptr<int>() : nullptr;
+  a.pos = pos ? pos->data_ptr<int>() : nullptr;
+  if (out_tokens) { a.out_tokens = out_tokens->data_ptr<int>(); a.out_cap = out_tokens->size(1); }
+  a.step = step ? step->data_ptr<int>() : nullptr;
+  TORCH_CHECK(!a.pos || a.slots, "pos needs slots");
+  TORCH_CHECK(!a.out_tokens || a.step, "out_tokens needs step");
+  launch_mode<kArgmax>(a, B, at::cuda::getCurrentCUDAStream());
 }
 
 // MoE expert GEMV: job j = (x row j / x_row_div, expert ids[j]); y[j, :] from W[ids[j]].
@@ -284,4 +536,39 @@ void gemv_experts(torch::Tensor W, torch::Tensor x, torch::Tensor ids, torch::Te
   else if (mode == kStoreBf16) launch_b<1, kStoreBf16>(a, jobs, s);
   else if (mode == kStoreF32) launch_b<1, kStoreF32>(a, jobs, s);
   else TORCH_CHECK(false, "unsupported expert gemv mode");
+}
+
+void moe_down(torch::Tensor Wd, torch::Tensor act, torch::Tensor ids, torch::Tensor wts, torch::Tensor x,
+              c10::optional<torch::Tensor> partial_out) {
+  TORCH_CHECK(Wd.dim() == 3 && Wd.scalar_type() == at::kBFloat16 && Wd.is_contiguous(), "Wd [E,H,I] bf16");
+  const int H = Wd.size(1), I = Wd.size(2);
+  const int B = x.size(0), J = ids.size(1);
+  TORCH_CHECK(J <= 16, "at most 16 experts per token");
+  TORCH_CHECK(act.size(-1) == I && act.is_contiguous(), "act [B*J, I] contiguous");
+  TORCH_CHECK(x.size(1) == H && x.scalar_type() == at::kBFloat16, "x [B,H] bf16");
+  const size_t smem = (size_t)J * I * sizeof(__nv_bfloat16);
+  dim3 grid((H + 7) / 8, B);
+  auto st = at::cuda::getCurrentCUDAStream();
+  auto xp = reinterpret_cast<__nv_bfloat16*>(x.data_ptr());
+  auto pp = partial_out ? reinterpret_cast<__nv_bfloat16*>(partial_out->data_ptr()) : nullptr;
+  auto wp = reinterpret_cast<const __nv_bfloat16*>(Wd.data_ptr());
+  auto ap = reinterpret_cast<const __nv_bfloat16*>(act.data_ptr());
+#define HX_MOE_DOWN(V)                                                                                          \
+  {                                                                                                             \
+    auto k = moe_down_kernel<V>;                                                                                \
+    if (smem > 48 * 1024) {                                                                                     \
+      HX_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));           \
+    }                                                                                                           \
+    HX_CUDA_CHECK(hx_launch_pdl(k, grid, dim3(256), smem, st, wp, ap, (const int*)ids.data_ptr<int>(),          \
+                                (const float*)wts.data_ptr<float>(), xp, pp, H, I, J));                          \
+  }
+  TORCH_CHECK(I % 8 == 0, "moe_down: expert intermediate size must be a multiple of 8");
+  const int vpl = (I / 8 + 31) / 32;
+  if (vpl == 1) HX_MOE_DOWN(1)
+  else if (vpl == 2) HX_MOE_DOWN(2)
+  else if (vpl == 3) HX_MOE_DOWN(3)
+  else if (vpl == 4) HX_MOE_DOWN(4)
+  else if (vpl <= 6) HX_MOE_DOWN(6)
+  else TORCH_CHECK(false, "moe_down: expert intermediate size per rank must be <= 1536");
+#undef HX_MOE_DOWN
 }

@@ -17,8 +17,8 @@ namespace hx {
 __global__ void embed_kernel(const __nv_bfloat16* __restrict__ E, const int* __restrict__ tok,
                              __nv_bfloat16* __restrict__ x, int H, int V) {
   const int b = blockIdx.x;
-  pdl_launch_dependents();
   pdl_wait_prior();
+  pdl_launch_dependents();
   int t = tok[b];
   t = t < 0 ? 0 : (t >= V ? V - 1 : t);
   const bf16x8* src = reinterpret_cast<const bf16x8*>(E + (long long)t * H);

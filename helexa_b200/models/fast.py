@@ -56,7 +56,7 @@ class DecodeBuffers:
     logits: torch.Tensor       # f32 [B, V]
     out_tokens: torch.Tensor   # int32 [B, cap]
     step: torch.Tensor         # int32 [B]
-    amax: torch.Tensor         # f32 [SMs * B * 2] per-CTA arg-max partials
+    best: torch.Tensor         # int64 [B] packed arg-max words (self-resetting)
     counter: torch.Tensor      # int32 [1] last-CTA election (self-resetting)
     err: torch.Tensor          # int32 [1] bounded-wait error code
     graph: torch.cuda.CUDAGraph | None = None
@@ -192,37 +192,28 @@ class FastModel:
             act_mlp=z(B, d.inter) if any_mlp else None,
             partial=z(B, d.H),
             logits=z(B, cfg.vocab_size, dt=f32), out_tokens=z(B, out_cap, dt=i32), step=z(B, dt=i32),
-            amax=z(max(1, self.sms) * B * 2, dt=f32), counter=z(1, dt=i32), err=z(1, dt=i32))
+            best=z(B, dt=torch.int64), counter=z(1, dt=i32), err=z(1, dt=i32))
         self._bufs[B] = nb
         return nb
-
-    _SG_TO_GEMV = {0: 0, 1: 1, 2: 2, 3: 3}
-
-    def _dense(self, mode, W, inp, y, nb: DecodeBuffers, resid=None, norm=None):
-        """Streaming GEMV when its shared-memory ring fits, else the register GEMV."""
-        if ops.sgemv_fits(mode, W.shape[-1], inp.shape[0]):
-            ops.sgemv(mode, W, inp, y, resid=resid, norm=norm, eps=self.cfg.rms_norm_eps, err=nb.err)
-        else:
-            self.C.gemv(W, inp, y, self._SG_TO_GEMV[mode], resid, norm, self.cfg.rms_norm_eps)
 
     def _row_parallel(self, W, inp, nb: DecodeBuffers):
         """x += W . inp, summed across TP ranks when the layer is sharded."""
         if self.comm is None or self.dims.ws == 1:
-            self._dense(ops.SG_RESID, W, inp, nb.x, nb, resid=nb.x)
+            self.C.gemv(W, inp, nb.x, ops.RESID_ADD, nb.x, None, 0.0)
         else:
-            self._dense(ops.SG_STORE, W, inp, nb.partial, nb)
+            self.C.gemv(W, inp, nb.partial, ops.STORE_BF16, None, None, 0.0)
             self.comm.reduce_residual(nb.partial, nb.x)
 
     def _decode_layer(self, i: int, nb: DecodeBuffers):
         C, cfg, d, lw = self.C, self.cfg, self.dims, self.layers[i]
         eps = cfg.rms_norm_eps
         if cfg.is_linear(i):
-            self._dense(ops.SG_STORE, lw["w_in"], nb.x, nb.proj_gdn, nb, norm=lw["ln1"])
+            C.gemv(lw["w_in"], nb.x, nb.proj_gdn, ops.STORE_BF16, None, lw["ln1"], eps)
             C.gdn_decode(nb.proj_gdn, lw["conv_w"], self.conv[i], self.rec[i], lw["A_log"], lw["dt_bias"],
                          lw["gnorm"], nb.slots, self.pos, nb.gdn_out, d.hk, d.hv, d.dk, d.dv, eps)
             self._row_parallel(lw["out_w"], nb.gdn_out, nb)
         else:
-            self._dense(ops.SG_STORE, lw["w_qkv"], nb.x, nb.proj_attn, nb, norm=lw["ln1"])
+            C.gemv(lw["w_qkv"], nb.x, nb.proj_attn, ops.STORE_BF16, None, lw["ln1"], eps)
             C.attn_decode(nb.proj_attn, lw.get("q_norm"), lw.get("k_norm"), self.inv_freq, self.kc[i], self.vc[i],
                           nb.slots, self.pos, nb.part_o, nb.part_ml, nb.counters, nb.attn_out, d.hq, d.hkv, d.D,
                           cfg.rotary_dim, cfg.attn_output_gate, eps)
@@ -230,20 +221,16 @@ class FastModel:
         if cfg.layer_uses_moe(i):
             E, k = cfg.num_experts, cfg.num_experts_per_tok
             J = k + (1 if self.has_shared else 0)
-            ops.sgemv(ops.SG_ROUTER, lw["router"], nb.x, norm=lw["ln2"], eps=eps, scratch=nb.rlogits,
-                      counter=nb.counter, out_ids=nb.ids, out_wts=nb.wts, E=E, topk=k, shared=self.has_shared,
-                      norm_topk=cfg.norm_topk_prob, err=nb.err)
-            ops.sgemv(ops.SG_EXPERT, lw["w_gu"], nb.x, nb.act_moe, norm=lw["ln2"], eps=eps, ids=nb.ids.view(-1),
-                      J=J, err=nb.err)
+            C.gemv_router(lw["router"], nb.x, nb.rlogits, lw["ln2"], eps, E, k, self.has_shared,
+                          cfg.norm_topk_prob, nb.ids, nb.wts, nb.counter)
+            C.gemv_experts(lw["w_gu"], nb.x, nb.ids.view(-1), nb.act_moe, ops.SILU_PAIR, J, lw["ln2"], eps)
             if self.comm is None or d.ws == 1:
-                ops.sgemv(ops.SG_MOEDOWN, lw["w_d"], nb.act_moe, nb.x, resid=nb.x, ids=nb.ids, wts=nb.wts, J=J,
-                          err=nb.err)
+                C.moe_down(lw["w_d"], nb.act_moe, nb.ids, nb.wts, nb.x, None)
             else:
-                ops.sgemv(ops.SG_MOEDOWN, lw["w_d"], nb.act_moe, nb.partial, ids=nb.ids, wts=nb.wts, J=J,
-                          err=nb.err)
+                C.moe_down(lw["w_d"], nb.act_moe, nb.ids, nb.wts, nb.x, nb.partial)
                 self.comm.reduce_residual(nb.partial, nb.x)
         else:
-            self._dense(ops.SG_SILU, lw["w_gu"], nb.x, nb.act_mlp, nb, norm=lw["ln2"])
+            C.gemv(lw["w_gu"], nb.x, nb.act_mlp, ops.SILU_PAIR, None, lw["ln2"], eps)
             self._row_parallel(lw["w_d"], nb.act_mlp, nb)
 
     def decode_step_launch(self, nb: DecodeBuffers):
@@ -251,9 +238,8 @@ class FastModel:
         self.C.embed(self.embed_w, nb.tok, nb.x)
         for i in range(self.cfg.num_hidden_layers):
             self._decode_layer(i, nb)
-        ops.sgemv(ops.SG_ARGMAX, self.lm_head, nb.x, nb.logits, norm=self.final_norm, eps=self.cfg.rms_norm_eps,
-                  scratch=nb.amax, counter=nb.counter, tok=nb.tok, slots=nb.slots, pos=self.pos,
-                  out_tokens=nb.out_tokens, step=nb.step, err=nb.err)
+        self.C.gemv_argmax(self.lm_head, nb.x, nb.logits, self.final_norm, self.cfg.rms_norm_eps, nb.best,
+                           nb.counter, nb.tok, nb.slots, self.pos, nb.out_tokens, nb.step)
 
     def launches_per_step(self) -> int:
         cfg = self.cfg
