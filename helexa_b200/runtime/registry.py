@@ -1,0 +1,205 @@
+"""Model registry: load / unload / list, single-flight loads, poison recovery.
+
+Mirrors the reference's CandleHarness registry (harness/candle.rs:45-885, load 3818,
+unload 4147, recovery 3675-3741): a `ModelSpec` names the source and placement; loads
+of the same id are single-flight; unload refuses while requests are in flight unless
+forced; a poisoned model is unloaded and reloaded from its retained spec while it
+advertises `recovering`. `HELEXA_DEBUG_POISON=<model_id>` forces one recovery (the
+reference's NEURON_DEBUG_POISON test hook).
+"""
+from __future__ import annotations
+
+import asyncio
+import os
+import threading
+from dataclasses import asdict, dataclass, field
+
+import torch
+
+from ..weights.loader import resolve_source
+from .admission import AdmissionConfig, AdmissionController
+from .engine import Engine
+from .prefix_cache import PrefixCache
+from .runner import FastRunner, RefRunner
+from .sampling import GenerationDefaults
+from .serving import ServedModel
+from .tokenizer import load_tokenizer
+
+
+@dataclass
+class ModelSpec:
+    model_id: str
+    source: str
+    harness: str = "helexa"
+    quant: str | None = None
+    tensor_parallel: int = 1
+    devices: list[int] | None = None
+    max_len: int = 16384
+    max_batch: int = 4
+    prefix_cache_mb: int = 1024
+    prefix_cache_entries: int = 8
+    max_in_flight: int | None = None
+    max_queue_depth: int = 16
+    max_wait_s: float = 60.0
+    max_per_principal: int = 0
+    device: str | None = None       # "cuda" / "cpu" (default: cuda when available)
+
+    @classmethod
+    def from_dict(cls, d: dict) -> "ModelSpec":
+        known = {k: v for k, v in d.items() if k in cls.__dataclass_fields__}
+        if "model_id" not in known:
+            raise ValueError("model_id is required")
+        known.setdefault("source", d.get("model") or known["model_id"])
+        return cls(**known)
+
+
+class LoadError(RuntimeError):
+    pass
+
+
+def build_served_model(spec: ModelSpec) -> ServedModel:
+    src = resolve_source(spec.source)
+    cfg = src.config
+    use_cuda = (spec.device or ("cuda" if torch.cuda.is_available() else "cpu")) == "cuda"
+    if spec.tensor_parallel > 1:
+        raise LoadError("tensor_parallel > 1 is served by the rank worker pool (helexa_b200.runtime.worker)")
+    tok = load_tokenizer(src.path, cfg.vocab_size)
+    max_len = min(spec.max_len, cfg.max_position_embeddings)
+    if use_cuda:
+        from ..models.fast import FastModel
+        dev = torch.device("cuda", (spec.devices or [0])[0])
+        kw = dict(max_slots=spec.max_batch + 1, max_len=max_len)
+        if src.kind == "preset":
+            model = FastModel.random(cfg, dev, **kw)
+        elif src.kind == "gguf":
+            from ..weights.gguf import GGUFFile
+            g = GGUFFile(src.path)
+            model = FastModel.from_hf(cfg, g.hf_get, dev, **kw)
+        else:
+            from ..weights.loader import SafetensorsDir
+            st = SafetensorsDir(src.path)
+            model = FastModel.from_hf(cfg, st.get, dev, **kw)
+        runner = FastRunner(model)
+        kv_bpt = cfg.kv_bytes_per_token()
+    else:
+        from ..models.reference import ReferenceModel
+        if src.kind == "preset":
+            from ..weights.random_init import random_weights
+            w = random_weights(cfg, seed=0)
+        elif src.kind == "gguf":
+            from ..weights.gguf import GGUFFile
+            g = GGUFFile(src.path)
+            w = {n: g.tensor(t) for t, n in ((t, _hf(t)) for t in g.tensors) if n}
+        else:
+            from ..weights.loader import SafetensorsDir
+            st = SafetensorsDir(src.path)
+            w = {k: st.get(k) for k in st.keys()}
+        model = ReferenceModel(cfg, w)
+        runner = RefRunner(model, num_slots=spec.max_batch, max_len=max_len)
+        kv_bpt = 0
+    pc = PrefixCache(spec.prefix_cache_mb << 20, spec.prefix_cache_entries) if spec.prefix_cache_mb else None
+    im_start = tok.token_id("<|im_start|>")
+    engine = Engine(runner, prefix_cache=pc, im_start_id=im_start, max_batch=spec.max_batch)
+    adm = AdmissionController(AdmissionConfig(max_in_flight=spec.max_in_flight or spec.max_batch,
+                                              max_queue_depth=spec.max_queue_depth, max_wait_s=spec.max_wait_s,
+                                              max_per_principal=spec.max_per_principal))
+    defaults = GenerationDefaults.from_dir(src.path) if src.path and os.path.isdir(src.path) else \
+        GenerationDefaults()
+    sm = ServedModel(model_id=spec.model_id, engine=engine, tokenizer=tok, config=cfg, admission=adm,
+                     defaults=defaults, devices=spec.devices or ([0] if use_cuda else []),
+                     tensor_parallel=spec.tensor_parallel, spec=asdict(spec), kv_bytes_per_token=kv_bpt)
+    if use_cuda:
+        free, _ = torch.cuda.mem_get_info(sm.devices[0])
+        adm.set_kv_budget_mb(max(0, free - (1500 << 20)) >> 20)
+    return sm
+
+
+def _hf(gname: str):
+    from ..weights.gguf import _hf_name
+    return _hf_name(gname)
+
+
+class ModelRegistry:
+    def __init__(self):
+        self.models: dict[str, ServedModel] = {}
+        self.specs: dict[str, ModelSpec] = {}
+        self.loading: dict[str, asyncio.Future] = {}
+        self.recovering: set[str] = set()
+        self._lock = threading.Lock()
+        self._debug_poison = os.environ.get("HELEXA_DEBUG_POISON")
+
+    def get(self, model_id: str) -> ServedModel | None:
+        m = self.models.get(model_id)
+        if m is not None and self._debug_poison == model_id:
+            self._debug_poison = None
+            m.status = "poisoned"
+        return m
+
+    def list(self) -> list[dict]:
+        out = []
+        for mid, m in self.models.items():
+            lim = m.limits
+            out.append({"id": mid, "status": "recovering" if mid in self.recovering else m.status,
+                        "devices": m.devices, "tensor_parallel": m.tensor_parallel,
+                        "capabilities": m.capabilities,
+                        "limit": {"context": lim.context, "input": lim.input, "output": lim.output},
+                        "tool_call": True, "reasoning": True, "servable": m.status == "loaded"})
+        for mid in self.loading:
+            if mid not in self.models:
+                out.append({"id": mid, "status": "loading"})
+        return out
+
+    async def load(self, spec: ModelSpec) -> ServedModel:
+        if spec.model_id in self.models:
+            return self.models[spec.model_id]
+        fut = self.loading.get(spec.model_id)
+        if fut is not None:
+            return await asyncio.shield(fut)
+        loop = asyncio.get_running_loop()
+        fut = loop.create_future()
+        self.loading[spec.model_id] = fut
+        try:
+            sm = await asyncio.to_thread(build_served_model, spec)
+            self.models[spec.model_id] = sm
+            self.specs[spec.model_id] = spec
+            fut.set_result(sm)
+            return sm
+        except Exception as e:
+            fut.set_exception(LoadError(str(e)))
+            fut.exception()  # mark retrieved
+            raise LoadError(str(e)) from e
+        finally:
+            self.loading.pop(spec.model_id, None)
+
+    async def unload(self, model_id: str, force: bool = False) -> bool:
+        m = self.models.get(model_id)
+        if m is None:
+            return False
+        if not force and (m.engine.in_flight or m.engine.queue_depth):
+            raise LoadError(f"{model_id} has requests in flight")
+        m.admission.close()
+        m.status = "unloading"
+        await asyncio.to_thread(m.engine.shutdown)
+        self.models.pop(model_id, None)
+        del m
+        if torch.cuda.is_available():
+            torch.cuda.empty_cache()
+        return True
+
+    async def recover(self, model_id: str) -> ServedModel:
+        """Single-flight unload + reload of a poisoned model from its retained spec."""
+        if model_id in self.recovering:
+            raise LoadError(f"{model_id} is recovering")
+        spec = self.specs.get(model_id)
+        if spec is None:
+            raise LoadError(f"no retained spec for {model_id}")
+        self.recovering.add(model_id)
+        try:
+            await self.unload(model_id, force=True)
+            return await self.load(spec)
+        finally:
+            self.recovering.discard(model_id)
+
+    async def unload_all(self):
+        for mid in list(self.models):
+            await self.unload(mid, force=True)

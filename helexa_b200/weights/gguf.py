@@ -1,0 +1,252 @@
+"""GGUF container reader/writer (format v3) for Qwen3-family checkpoints.
+
+The container layout and the k-quant block formats are the published GGUF / ggml
+formats (so files interoperate with other runtimes); the code is written from the
+format description:
+
+  header: "GGUF", u32 version, u64 n_tensors, u64 n_kv; key/value metadata;
+  tensor infos (name, n_dims, dims (innermost first), ggml type, data offset);
+  data section aligned to `general.alignment` (default 32).
+
+Block types supported here (bytes per block / values per block):
+  F32, F16, BF16, Q8_0 (34 / 32), Q4_K (144 / 256), Q6_K (210 / 256).
+Quantize / dequantize on the host run in C++ (csrc/gguf_host.cpp); the decode GEMV
+and the prefill path dequantize on the GPU (csrc/gguf.cu).
+
+Qwen3 GGUF tensor names map onto HF names (`blk.{i}.attn_q.weight` ->
+`model.layers.{i}.self_attn.q_proj.weight`, ...); the reference loads GGUF only on
+a single GPU (harness/candle.rs:887-895) while here GGUF tensors are sliced per rank
+on superblock boundaries.
+"""
+from __future__ import annotations
+
+import mmap
+import struct
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from ..config import ModelConfig
+
+GGUF_MAGIC = b"GGUF"
+F32, F16, Q8_0, Q4_K, Q6_K, BF16 = 0, 1, 8, 12, 14, 30
+BLOCK = {F32: (4, 1), F16: (2, 1), BF16: (2, 1), Q8_0: (34, 32), Q4_K: (144, 256), Q6_K: (210, 256)}
+TYPE_NAMES = {F32: "F32", F16: "F16", BF16: "BF16", Q8_0: "Q8_0", Q4_K: "Q4_K", Q6_K: "Q6_K"}
+
+# value types
+_VT = {0: "B", 1: "b", 2: "H", 3: "h", 4: "I", 5: "i", 6: "f", 7: "?", 10: "Q", 11: "q", 12: "d"}
+
+
+def _hf_name(gname: str) -> str | None:
+    if gname == "token_embd.weight":
+        return "model.embed_tokens.weight"
+    if gname == "output_norm.weight":
+        return "model.norm.weight"
+    if gname == "output.weight":
+        return "lm_head.weight"
+    if not gname.startswith("blk."):
+        return None
+    _, i, rest = gname.split(".", 2)
+    m = {
+        "attn_norm.weight": "input_layernorm.weight", "ffn_norm.weight": "post_attention_layernorm.weight",
+        "attn_q.weight": "self_attn.q_proj.weight", "attn_k.weight": "self_attn.k_proj.weight",
+        "attn_v.weight": "self_attn.v_proj.weight", "attn_output.weight": "self_attn.o_proj.weight",
+        "attn_q_norm.weight": "self_attn.q_norm.weight", "attn_k_norm.weight": "self_attn.k_norm.weight",
+        "ffn_gate.weight": "mlp.gate_proj.weight", "ffn_up.weight": "mlp.up_proj.weight",
+        "ffn_down.weight": "mlp.down_proj.weight", "ffn_gate_inp.weight": "mlp.gate.weight",
+    }.get(rest)
+    return None if m is None else f"model.layers.{i}.{m}"
+
+
+def hf_to_gguf_name(hf: str) -> str:
+    rev = {
+        "input_layernorm.weight": "attn_norm.weight", "post_attention_layernorm.weight": "ffn_norm.weight",
+        "self_attn.q_proj.weight": "attn_q.weight", "self_attn.k_proj.weight": "attn_k.weight",
+        "self_attn.v_proj.weight": "attn_v.weight", "self_attn.o_proj.weight": "attn_output.weight",
+        "self_attn.q_norm.weight": "attn_q_norm.weight", "self_attn.k_norm.weight": "attn_k_norm.weight",
+        "mlp.gate_proj.weight": "ffn_gate.weight", "mlp.up_proj.weight": "ffn_up.weight",
+        "mlp.down_proj.weight": "ffn_down.weight", "mlp.gate.weight": "ffn_gate_inp.weight",
+    }
+    if hf == "model.embed_tokens.weight":
+        return "token_embd.weight"
+    if hf == "model.norm.weight":
+        return "output_norm.weight"
+    if hf == "lm_head.weight":
+        return "output.weight"
+    _, _, i, rest = hf.split(".", 3)
+    return f"blk.{i}.{rev[rest]}"
+
+
+@dataclass
+class GGUFTensor:
+    name: str
+    shape: tuple[int, ...]     # torch order (outermost first)
+    gtype: int
+    offset: int
+    nbytes: int
+
+
+class GGUFFile:
+    def __init__(self, path: str):
+        self.path = path
+        self._f = open(path, "rb")
+        self._mm = mmap.mmap(self._f.fileno(), 0, access=mmap.ACCESS_READ)
+        self._pos = 0
+        if self._read(4) != GGUF_MAGIC:
+            raise ValueError(f"{path} is not a GGUF file")
+        self.version = self._u32()
+        n_t, n_kv = self._u64(), self._u64()
+        self.meta: dict = {}
+        for _ in range(n_kv):
+            k = self._str()
+            self.meta[k] = self._value(self._u32())
+        infos = []
+        for _ in range(n_t):
+            name = self._str()
+            nd = self._u32()
+            dims = [self._u64() for _ in range(nd)]
+            gt = self._u32()
+            off = self._u64()
+            infos.append((name, tuple(reversed(dims)), gt, off))
+        align = int(self.meta.get("general.alignment", 32))
+        base = (self._pos + align - 1) // align * align
+        self.tensors: dict[str, GGUFTensor] = {}
+        for name, shape, gt, off in infos:
+            bb, bv = BLOCK[gt]
+            n = int(np.prod(shape))
+            self.tensors[name] = GGUFTensor(name, shape, gt, base + off, n // bv * bb)
+
+    # ---- primitive reads ---------------------------------------------------
+    def _read(self, n):
+        b = self._mm[self._pos:self._pos + n]
+        self._pos += n
+        return b
+
+    def _u32(self):
+        return struct.unpack("<I", self._read(4))[0]
+
+    def _u64(self):
+        return struct.unpack("<Q", self._read(8))[0]
+
+    def _str(self):
+        return self._read(self._u64()).decode("utf-8")
+
+    def _value(self, vt):
+        if vt == 8:
+            return self._str()
+        if vt == 9:
+            et, n = self._u32(), self._u64()
+            return [self._value(et) for _ in range(n)]
+        fmt = _VT[vt]
+        return struct.unpack("<" + fmt, self._read(struct.calcsize(fmt)))[0]
+
+    # ---- access --------------------------------------------------------------
+    def raw(self, name: str) -> torch.Tensor:
+        """Undecoded block bytes as a uint8 tensor (shares the mmap)."""
+        t = self.tensors[name]
+        return torch.frombuffer(self._mm, dtype=torch.uint8, count=t.nbytes, offset=t.offset)
+
+    def tensor(self, name: str) -> torch.Tensor:
+        """Decoded tensor (f32 for quantized types)."""
+        from .. import ops
+        t = self.tensors[name]
+        raw = self.raw(name)
+        if t.gtype == F32:
+            return raw.view(torch.float32).reshape(t.shape).clone()
+        if t.gtype == F16:
+            return raw.view(torch.float16).reshape(t.shape).float()
+        if t.gtype == BF16:
+            return raw.view(torch.bfloat16).reshape(t.shape).float()
+        return ops.C.gguf_dequant_host(raw.clone(), t.gtype, int(np.prod(t.shape))).reshape(t.shape)
+
+    def hf_get(self, hf_name: str) -> torch.Tensor:
+        return self.tensor(hf_to_gguf_name(hf_name))
+
+    def model_config(self) -> ModelConfig:
+        m = self.meta
+        arch = m.get("general.architecture", "qwen3")
+        g = lambda k, d=None: m.get(f"{arch}.{k}", d)  # noqa: E731
+        heads = int(g("attention.head_count"))
+        hidden = int(g("embedding_length"))
+        vocab = len(m.get("tokenizer.ggml.tokens", [])) or int(g("vocab_size", 151936))
+        family = "qwen3_moe" if arch == "qwen3moe" else "qwen3"
+        return ModelConfig(
+            family=family, name=m.get("general.name", "gguf-model"), vocab_size=vocab, hidden_size=hidden,
+            num_hidden_layers=int(g("block_count")), num_attention_heads=heads,
+            num_key_value_heads=int(g("attention.head_count_kv", heads)),
+            head_dim=int(g("attention.key_length", hidden // heads)),
+            intermediate_size=int(g("feed_forward_length", 0)),
+            rms_norm_eps=float(g("attention.layer_norm_rms_epsilon", 1e-6)),
+            rope_theta=float(g("rope.freq_base", 1e6)),
+            max_position_embeddings=int(g("context_length", 40960)),
+            num_experts=int(g("expert_count", 0) or 0), num_experts_per_tok=int(g("expert_used_count", 0) or 0),
+            moe_intermediate_size=int(g("expert_feed_forward_length", 0) or 0),
+            tie_word_embeddings="output.weight" not in self.tensors)
+
+    def close(self):
+        self._mm.close()
+        self._f.close()
+
+
+# ---------------------------------------------------------------------------
+# writer
+# ---------------------------------------------------------------------------
+def _w_str(s: str) -> bytes:
+    b = s.encode("utf-8")
+    return struct.pack("<Q", len(b)) + b
+
+
+def _w_value(v) -> bytes:
+    if isinstance(v, bool):
+        return struct.pack("<I?", 7, v)
+    if isinstance(v, int):
+        return struct.pack("<Iq", 11, v) if v < 0 else struct.pack("<IQ", 10, v) if v >= 2 ** 32 else \
+            struct.pack("<II", 4, v)
+    if isinstance(v, float):
+        return struct.pack("<If", 6, v)
+    if isinstance(v, str):
+        return struct.pack("<I", 8) + _w_str(v)
+    if isinstance(v, list):
+        if all(isinstance(x, str) for x in v):
+            return struct.pack("<IIQ", 9, 8, len(v)) + b"".join(_w_str(x) for x in v)
+        if all(isinstance(x, int) for x in v):
+            return struct.pack("<IIQ", 9, 5, len(v)) + b"".join(struct.pack("<i", x) for x in v)
+        return struct.pack("<IIQ", 9, 6, len(v)) + b"".join(struct.pack("<f", float(x)) for x in v)
+    raise TypeError(type(v))
+
+
+def write_gguf(path: str, meta: dict, tensors: list[tuple[str, torch.Tensor, int]], align: int = 32):
+    """tensors: (gguf name, f32/bf16 tensor, target ggml type); quantizes on the host."""
+    from .. import ops
+    blobs = []
+    for name, t, gt in tensors:
+        t = t.detach().float().contiguous().cpu()
+        if gt == F32:
+            data = t.numpy().tobytes()
+        elif gt == F16:
+            data = t.half().numpy().tobytes()
+        elif gt == BF16:
+            data = t.bfloat16().view(torch.int16).numpy().tobytes()
+        else:
+            data = ops.C.gguf_quant_host(t.view(-1), gt).numpy().tobytes()
+        blobs.append((name, tuple(t.shape), gt, data))
+    head = GGUF_MAGIC + struct.pack("<IQQ", 3, len(blobs), len(meta) + 1)
+    kv = _w_str("general.alignment") + _w_value(align)
+    for k, v in meta.items():
+        kv += _w_str(k) + _w_value(v)
+    infos, off = b"", 0
+    offsets = []
+    for name, shape, gt, data in blobs:
+        offsets.append(off)
+        infos += _w_str(name) + struct.pack("<I", len(shape)) + b"".join(struct.pack("<Q", d) for d in
+                                                                         reversed(shape))
+        infos += struct.pack("<IQ", gt, off)
+        off += (len(data) + align - 1) // align * align
+    with open(path, "wb") as f:
+        hdr = head + kv + infos
+        f.write(hdr)
+        f.write(b"\0" * ((align - len(hdr) % align) % align))
+        for (_, _, _, data) in blobs:
+            f.write(data)
+            f.write(b"\0" * ((align - len(data) % align) % align))
