@@ -265,7 +265,7 @@ static void launch_dg(const AttnDecodeArgs& a, dim3 grid, cudaStream_t s) {
   constexpr int NW = 4, TILE = 32;
   const size_t smem = (size_t)(G * D + NW * D + NW * G * TILE + NW * G * D) * sizeof(float);
   auto k = attn_decode_kernel<D, G>;
-  if (smem > 48 * 1024) {
+  if (smem + 4096 > 48 * 1024) {
     HX_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   }
   HX_CUDA_CHECK(hx_launch_pdl(k, grid, dim3(NW * 32), smem, s, a));

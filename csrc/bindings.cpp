@@ -45,6 +45,12 @@ void gdn_prefill(torch::Tensor proj, torch::Tensor conv_w, torch::Tensor ring, t
 
 #include "hx_runtime.h"
 
+torch::Tensor gguf_dequant_host(torch::Tensor raw, int64_t type, int64_t n);
+torch::Tensor gguf_quant_host(torch::Tensor x, int64_t type);
+void gguf_gemv(torch::Tensor W, int64_t type, int64_t K, torch::Tensor x, torch::Tensor y, int64_t mode,
+               c10::optional<torch::Tensor> resid, c10::optional<torch::Tensor> norm_w, double eps);
+void gguf_dequant(torch::Tensor W, int64_t type, int64_t K, torch::Tensor out);
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("set_pdl", [](bool on) { hx_pdl_enabled() = on; });
   m.def("gemv", &gemv);
@@ -60,6 +66,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ipc_close", &ipc_close);
   m.def("ar_oneshot", &ar_oneshot);
   m.def("gemm", &gemm);
+  m.def("gguf_dequant_host", &gguf_dequant_host);
+  m.def("gguf_quant_host", &gguf_quant_host);
+  m.def("gguf_gemv", &gguf_gemv);
+  m.def("gguf_dequant", &gguf_dequant);
   m.def("gdn_prefill", &gdn_prefill);
   m.def("gemv_router", &gemv_router);
   m.def("gemv_argmax", &gemv_argmax);

@@ -317,7 +317,7 @@ static void launch_b(const GemvArgs& a, int jobs, cudaStream_t s) {
   dim3 grid((a.N + 8 * RPW - 1) / (8 * RPW), jobs);
   size_t smem = (size_t)B * a.K * sizeof(__nv_bfloat16);
   auto k = gemv_kernel<B, RPW, MODE>;
-  if (smem > 48 * 1024) {
+  if (smem + 4096 > 48 * 1024) {
     HX_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   }
   HX_CUDA_CHECK(hx_launch_pdl(k, grid, dim3(256), smem, s, a));
@@ -556,7 +556,7 @@ void moe_down(torch::Tensor Wd, torch::Tensor act, torch::Tensor ids, torch::Ten
 #define HX_MOE_DOWN(V)                                                                                          \
   {                                                                                                             \
     auto k = moe_down_kernel<V>;                                                                                \
-    if (smem > 48 * 1024) {                                                                                     \
+    if (smem + 4096 > 48 * 1024) {                                                                                     \
       HX_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));           \
     }                                                                                                           \
     HX_CUDA_CHECK(hx_launch_pdl(k, grid, dim3(256), smem, st, wp, ap, (const int*)ids.data_ptr<int>(),          \

@@ -1,0 +1,256 @@
+// GGUF k-quant weights on the GPU: Q8_0, Q4_K and Q6_K (block layouts in
+// gguf_host.cpp).
+//
+//   gguf_gemv     decode GEMV with the dequantization fused into the weight stream:
+//                 every lane decodes 8 consecutive values of a row straight from the
+//                 block bytes (no bf16 copy of the weights is ever written); the
+//                 usual epilogues (bf16 store, residual add, SwiGLU pairs, f32) follow.
+//   gguf_dequant  rows -> bf16, for the prefill GEMM.
+//
+// Replaces candle's QMatMul GEMV / dequant-then-cuBLAS switch (tp/tp_linear.rs:76-139).
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+
+#include "common.cuh"
+
+namespace hx {
+
+enum GgufType : int { kQ8_0 = 8, kQ4_K = 12, kQ6_K = 14 };
+
+template <int T>
+struct GgufBlock;
+template <>
+struct GgufBlock<kQ8_0> { static constexpr int bytes = 34, vals = 32; };
+template <>
+struct GgufBlock<kQ4_K> { static constexpr int bytes = 144, vals = 256; };
+template <>
+struct GgufBlock<kQ6_K> { static constexpr int bytes = 210, vals = 256; };
+
+HX_DEVICE float half_at(const uint8_t* p) {
+  unsigned short h = (unsigned short)p[0] | ((unsigned short)p[1] << 8);
+  return __half2float(__ushort_as_half(h));
+}
+
+// Values 8v .. 8v+7 of a row whose blocks start at `row`.
+template <int T>
+HX_DEVICE void dequant8(const uint8_t* __restrict__ row, int v, float* out) {
+  if (T == kQ8_0) {
+    const uint8_t* b = row + (v >> 2) * 34;
+    const float d = half_at(b);
+    const int8_t* q = reinterpret_cast<const int8_t*>(b + 2 + (v & 3) * 8);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) out[i] = d * q[i];
+  } else if (T == kQ4_K) {
+    const uint8_t* b = row + (v >> 5) * 144;
+    const int idx = (v & 31) * 8;           // position in the superblock
+    const int j = idx >> 5, p = idx & 31;   // sub-block, position in it
+    const float d = half_at(b), dmin = half_at(b + 2);
+    const uint8_t* sc = b + 4;
+    int s, m;
+    if (j < 4) {
+      s = sc[j] & 63;
+      m = sc[j + 4] & 63;
+    } else {
+      s = (sc[j + 4] & 0xF) | ((sc[j - 4] >> 6) << 4);
+      m = (sc[j + 4] >> 4) | ((sc[j] >> 6) << 4);
+    }
+    const uint2 raw = *reinterpret_cast<const uint2*>(b + 16 + (j >> 1) * 32 + p);  // 8-byte aligned
+    const uint8_t* qb = reinterpret_cast<const uint8_t*>(&raw);
+    const float ds = d * s, dm = dmin * m;
+    const int shift = (j & 1) * 4;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) out[i] = ds * ((qb[i] >> shift) & 0xF) - dm;
+  } else {
+    const uint8_t* b = row + (v >> 5) * 210;
+    const int idx = (v & 31) * 8;
+    const int h = idx >> 7, k = (idx & 127) >> 5, l0 = idx & 31;
+    const float d = half_at(b + 208);
+    const int8_t sc = reinterpret_cast<const int8_t*>(b + 192)[8 * h + (l0 >> 4) + 2 * k];
+    const uint8_t* ql = b + 64 * h + l0 + 32 * (k & 1);
+    const uint8_t* qh = b + 128 + 32 * h + l0;
+    const int lsh = (k >> 1) * 4, hsh = 2 * k;
+    const float ds = d * sc;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int q = (int)(((ql[i] >> lsh) & 0xF) | (((qh[i] >> hsh) & 3) << 4)) - 32;
+      out[i] = ds * q;
+    }
+  }
+}
+
+// y = W x with W quantized [N rows of row_bytes]; x [B, K] bf16; modes as gemv.cu.
+template <int T, int B, int MODE>
+__global__ void __launch_bounds__(256) gguf_gemv_kernel(const uint8_t* __restrict__ W, long long row_bytes,
+                                                        const __nv_bfloat16* __restrict__ x, void* y, int ldy,
+                                                        const __nv_bfloat16* resid, const float* norm_w, float eps,
+                                                        int N, int K) {
+  extern __shared__ __align__(16) float xs[];  // [B][K] f32
+  __shared__ float red[8];
+  pdl_wait_prior();
+  pdl_launch_dependents();
+  for (int b = 0; b < B; ++b) {
+    const __nv_bfloat16* xr = x + (long long)b * K;
+    float inv = 1.f;
+    if (norm_w) {
+      float ss = 0.f;
+      for (int k = threadIdx.x; k < K; k += 256) {
+        float f = __bfloat162float(xr[k]);
+        ss += f * f;
+      }
+      ss = block_sum(ss, red);
+      inv = rsqrtf(ss / K + eps);
+    }
+    for (int k = threadIdx.x; k < K; k += 256) {
+      float f = __bfloat162float(xr[k]);
+      xs[b * K + k] = norm_w ? __bfloat162float(__float2bfloat16(f * inv * norm_w[k])) : f;
+    }
+  }
+  __syncthreads();
+  constexpr int RPW = 2;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row0 = (blockIdx.x * 8 + warp) * RPW;
+  if (row0 >= N) return;
+  float acc[RPW][B];
+#pragma unroll
+  for (int r = 0; r < RPW; ++r)
+#pragma unroll
+    for (int b = 0; b < B; ++b) acc[r][b] = 0.f;
+  const int nvec = K / 8;
+  for (int v = lane; v < nvec; v += 32) {
+#pragma unroll
+    for (int r = 0; r < RPW; ++r) {
+      const int row = min(row0 + r, N - 1);
+      float wf[8];
+      dequant8<T>(W + (long long)row * row_bytes, v, wf);
+#pragma unroll
+      for (int b = 0; b < B; ++b) {
+        const float* xv = xs + b * K + v * 8;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[r][b] = fmaf(wf[i], xv[i], acc[r][b]);
+      }
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < RPW; ++r)
+#pragma unroll
+    for (int b = 0; b < B; ++b) acc[r][b] = warp_sum(acc[r][b]);
+  if (lane) return;
+#pragma unroll
+  for (int b = 0; b < B; ++b) {
+    const long long ob = (long long)b * ldy;
+    if (MODE == 2) {  // SwiGLU pairs (rows 2j, 2j+1)
+      if (row0 + 1 < N) {
+        const float g = __bfloat162float(__float2bfloat16(acc[0][b]));
+        const float u = __bfloat162float(__float2bfloat16(acc[1][b]));
+        reinterpret_cast<__nv_bfloat16*>(y)[ob + row0 / 2] = __float2bfloat16(silu(g) * u);
+      }
+    } else {
+#pragma unroll
+      for (int r = 0; r < RPW; ++r) {
+        const int n = row0 + r;
+        if (n >= N) break;
+        if (MODE == 3) {
+          reinterpret_cast<float*>(y)[ob + n] = acc[r][b];
+        } else if (MODE == 1) {
+          const float br = __bfloat162float(__float2bfloat16(acc[r][b]));
+          reinterpret_cast<__nv_bfloat16*>(y)[ob + n] = __float2bfloat16(__bfloat162float(resid[ob + n]) + br);
+        } else {
+          reinterpret_cast<__nv_bfloat16*>(y)[ob + n] = __float2bfloat16(acc[r][b]);
+        }
+      }
+    }
+  }
+}
+
+template <int T>
+__global__ void gguf_dequant_kernel(const uint8_t* __restrict__ W, long long row_bytes, __nv_bfloat16* __restrict__ out,
+                                    int N, int K) {
+  const long long nv = (long long)N * (K / 8);
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < nv; i += (long long)gridDim.x * blockDim.x) {
+    const int n = (int)(i / (K / 8)), v = (int)(i % (K / 8));
+    float f[8];
+    dequant8<T>(W + (long long)n * row_bytes, v, f);
+    reinterpret_cast<bf16x8*>(out + (long long)n * K)[v] = pack8(f);
+  }
+}
+
+template <int T, int MODE>
+static void gg_launch(const uint8_t* W, long long rb, const torch::Tensor& x, void* y, int ldy, const __nv_bfloat16* resid,
+                      const float* nw, float eps, int N, int K, int B, cudaStream_t st) {
+  const size_t smem = (size_t)B * K * sizeof(float);
+  dim3 grid((N + 15) / 16);
+  auto xp = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
+#define HX_GG_B(BB)                                                                                                 \
+  {                                                                                                                 \
+    auto k = gguf_gemv_kernel<T, BB, MODE>;                                                                         \
+    if (smem + 4096 > 48 * 1024) HX_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)); \
+    HX_CUDA_CHECK(hx_launch_pdl(k, grid, dim3(256), smem, st, W, rb, xp, y, ldy, resid, nw, eps, N, K));            \
+  }
+  switch (B) {
+    case 1: HX_GG_B(1) break;
+    case 2: HX_GG_B(2) break;
+    case 4: HX_GG_B(4) break;
+    case 8: HX_GG_B(8) break;
+    default: TORCH_CHECK(false, "gguf_gemv batch must be 1, 2, 4 or 8");
+  }
+#undef HX_GG_B
+}
+
+template <int T>
+static void gg_mode(int mode, const uint8_t* W, long long rb, const torch::Tensor& x, void* y, int ldy,
+                    const __nv_bfloat16* resid, const float* nw, float eps, int N, int K, int B, cudaStream_t st) {
+  switch (mode) {
+    case 0: gg_launch<T, 0>(W, rb, x, y, ldy, resid, nw, eps, N, K, B, st); break;
+    case 1: gg_launch<T, 1>(W, rb, x, y, ldy, resid, nw, eps, N, K, B, st); break;
+    case 2: gg_launch<T, 2>(W, rb, x, y, ldy, resid, nw, eps, N, K, B, st); break;
+    case 3: gg_launch<T, 3>(W, rb, x, y, ldy, resid, nw, eps, N, K, B, st); break;
+    default: TORCH_CHECK(false, "bad mode");
+  }
+}
+
+static void block_of(int t, int& bb, int& bv) {
+  if (t == kQ8_0) { bb = 34; bv = 32; }
+  else if (t == kQ4_K) { bb = 144; bv = 256; }
+  else if (t == kQ6_K) { bb = 210; bv = 256; }
+  else TORCH_CHECK(false, "unsupported GGUF type ", t);
+}
+
+}  // namespace hx
+
+using namespace hx;
+
+// W: uint8 [N, row_bytes] block rows; x: [B, K] bf16; mode 0 bf16 / 1 resid / 2 SwiGLU / 3 f32.
+void gguf_gemv(torch::Tensor W, int64_t type, int64_t K, torch::Tensor x, torch::Tensor y, int64_t mode,
+               c10::optional<torch::Tensor> resid, c10::optional<torch::Tensor> norm_w, double eps) {
+  int bb, bv;
+  block_of((int)type, bb, bv);
+  TORCH_CHECK(W.scalar_type() == at::kByte && W.dim() == 2 && W.is_contiguous() && W.is_cuda(), "W uint8 [N, bytes]");
+  TORCH_CHECK(K % bv == 0 && W.size(1) == K / bv * bb, "row bytes do not match K");
+  TORCH_CHECK(x.size(1) == K && x.scalar_type() == at::kBFloat16, "x [B, K] bf16");
+  const int N = W.size(0), B = x.size(0);
+  if (type == kQ4_K) TORCH_CHECK(reinterpret_cast<uintptr_t>(W.data_ptr()) % 16 == 0, "Q4_K rows need 16-byte alignment");
+  auto st = at::cuda::getCurrentCUDAStream();
+  auto wp = W.data_ptr<uint8_t>();
+  auto rp = resid ? reinterpret_cast<const __nv_bfloat16*>(resid->data_ptr()) : nullptr;
+  auto np = norm_w ? norm_w->data_ptr<float>() : nullptr;
+  const long long rb = W.size(1);
+  if (type == kQ8_0) gg_mode<kQ8_0>((int)mode, wp, rb, x, y.data_ptr(), y.size(1), rp, np, (float)eps, N, (int)K, B, st);
+  else if (type == kQ4_K) gg_mode<kQ4_K>((int)mode, wp, rb, x, y.data_ptr(), y.size(1), rp, np, (float)eps, N, (int)K, B, st);
+  else gg_mode<kQ6_K>((int)mode, wp, rb, x, y.data_ptr(), y.size(1), rp, np, (float)eps, N, (int)K, B, st);
+}
+
+void gguf_dequant(torch::Tensor W, int64_t type, int64_t K, torch::Tensor out) {
+  int bb, bv;
+  block_of((int)type, bb, bv);
+  TORCH_CHECK(W.scalar_type() == at::kByte && W.dim() == 2 && W.size(1) == K / bv * bb, "W uint8 [N, bytes]");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.size(0) == W.size(0) && out.size(1) == K, "out [N, K] bf16");
+  const int N = W.size(0);
+  auto st = at::cuda::getCurrentCUDAStream();
+  const long long nv = (long long)N * (K / 8);
+  const int grid = (int)std::min<long long>((nv + 255) / 256, 148 * 16);
+  auto op = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  if (type == kQ8_0) gguf_dequant_kernel<kQ8_0><<<grid, 256, 0, st>>>(W.data_ptr<uint8_t>(), W.size(1), op, N, (int)K);
+  else if (type == kQ4_K) gguf_dequant_kernel<kQ4_K><<<grid, 256, 0, st>>>(W.data_ptr<uint8_t>(), W.size(1), op, N, (int)K);
+  else gguf_dequant_kernel<kQ6_K><<<grid, 256, 0, st>>>(W.data_ptr<uint8_t>(), W.size(1), op, N, (int)K);
+  HX_CUDA_CHECK(cudaGetLastError());
+}

@@ -1,0 +1,99 @@
+"""GGUF: host k-quant codecs (C++), container write/read, GPU fused-dequant GEMV."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from helexa_b200.weights import gguf as G
+
+
+def _C():
+    from helexa_b200 import ops
+    return ops.C
+
+
+@pytest.mark.parametrize("gt,tol", [(G.Q8_0, 0.01), (G.Q4_K, 0.12), (G.Q6_K, 0.03)])
+def test_host_quant_roundtrip(gt, tol):
+    torch.manual_seed(0)
+    x = torch.randn(4 * 256 * 8) * 0.02
+    raw = _C().gguf_quant_host(x, gt)
+    bb, bv = G.BLOCK[gt]
+    assert raw.numel() == x.numel() // bv * bb
+    y = _C().gguf_dequant_host(raw, gt, x.numel())
+    rel = ((y - x).norm() / x.norm()).item()
+    assert rel < tol, rel
+    # quantizing the decoded values again is (almost) a fixed point
+    y2 = _C().gguf_dequant_host(_C().gguf_quant_host(y, gt), gt, x.numel())
+    assert ((y2 - y).norm() / y.norm()).item() < tol
+
+
+def test_q6k_block_layout_by_hand():
+    """Decode one hand-built Q6_K block: every value must land in its documented slot."""
+    b = np.zeros(210, dtype=np.uint8)
+    q = (np.arange(256) % 64).astype(np.int64)       # unsigned 6-bit codes
+    sc = np.arange(1, 17, dtype=np.int8)
+    for half in range(2):
+        qq = q[128 * half:128 * half + 128]
+        for l in range(32):
+            q1, q2, q3, q4 = qq[l], qq[l + 32], qq[l + 64], qq[l + 96]
+            b[64 * half + l] = (q1 & 15) | ((q3 & 15) << 4)
+            b[64 * half + l + 32] = (q2 & 15) | ((q4 & 15) << 4)
+            b[128 + 32 * half + l] = (q1 >> 4) | ((q2 >> 4) << 2) | ((q3 >> 4) << 4) | ((q4 >> 4) << 6)
+    b[192:208] = sc.view(np.uint8)
+    b[208:210] = np.frombuffer(np.float16(0.5).tobytes(), dtype=np.uint8)
+    y = _C().gguf_dequant_host(torch.from_numpy(b.copy()), G.Q6_K, 256).numpy()
+    want = np.array([0.5 * sc[j // 16] * (q[j] - 32) for j in range(256)], dtype=np.float32)
+    np.testing.assert_allclose(y, want)
+
+
+def test_gguf_file_roundtrip(tmp_path):
+    torch.manual_seed(1)
+    w = torch.randn(64, 512) * 0.02
+    n = torch.randn(512) * 0.02 + 1
+    path = os.path.join(tmp_path, "m.gguf")
+    meta = {"general.architecture": "qwen3", "general.name": "tiny", "qwen3.block_count": 1,
+            "qwen3.embedding_length": 512, "qwen3.attention.head_count": 4, "qwen3.attention.head_count_kv": 2,
+            "qwen3.feed_forward_length": 1024, "qwen3.context_length": 4096}
+    G.write_gguf(path, meta, [("blk.0.attn_q.weight", w, G.Q4_K), ("blk.0.attn_norm.weight", n, G.F32),
+                              ("blk.0.attn_k.weight", w, G.Q6_K), ("blk.0.attn_v.weight", w, G.Q8_0)])
+    g = G.GGUFFile(path)
+    assert g.meta["general.name"] == "tiny" and g.tensors["blk.0.attn_q.weight"].shape == (64, 512)
+    assert torch.equal(g.tensor("blk.0.attn_norm.weight"), n)
+    for name, tol in (("blk.0.attn_q.weight", 0.12), ("blk.0.attn_k.weight", 0.03), ("blk.0.attn_v.weight", 0.01)):
+        assert ((g.tensor(name) - w).norm() / w.norm()).item() < tol
+    cfg = g.model_config()
+    assert cfg.hidden_size == 512 and cfg.num_key_value_heads == 2 and cfg.head_dim == 128
+    assert G.hf_to_gguf_name("model.layers.3.mlp.down_proj.weight") == "blk.3.ffn_down.weight"
+    assert g.hf_get("model.layers.0.self_attn.q_proj.weight").shape == (64, 512)
+    g.close()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("gt", [G.Q8_0, G.Q4_K, G.Q6_K])
+@pytest.mark.parametrize("B,mode", [(1, 0), (2, 1), (1, 2), (4, 3)])
+def test_gguf_gemv_and_dequant(gt, B, mode):
+    C = _C()
+    torch.manual_seed(2)
+    N, K = 384, 2048
+    w = torch.randn(N, K) * 0.02
+    raw = C.gguf_quant_host(w.view(-1), gt).view(N, -1).cuda()
+    wd = C.gguf_dequant_host(raw.cpu().view(-1), gt, N * K).view(N, K).cuda()
+    out = torch.empty(N, K, dtype=torch.bfloat16, device="cuda")
+    C.gguf_dequant(raw, gt, K, out)
+    torch.testing.assert_close(out.float(), wd, atol=1e-3, rtol=1e-2)
+    x = torch.randn(B, K, device="cuda").bfloat16()
+    ref = x.float() @ wd.t()
+    if mode == 2:
+        y = torch.empty(B, N // 2, device="cuda", dtype=torch.bfloat16)
+        want = torch.nn.functional.silu(ref[:, 0::2]) * ref[:, 1::2]
+    elif mode == 3:
+        y = torch.empty(B, N, device="cuda")
+        want = ref
+    else:
+        y = torch.zeros(B, N, device="cuda", dtype=torch.bfloat16)
+        want = ref
+    C.gguf_gemv(raw, gt, K, x, y, mode, y if mode == 1 else None, None, 0.0)
+    torch.cuda.synchronize()
+    err = (y.float() - want).abs().max().item()
+    assert err <= 2e-2 * want.abs().max().item() + 1e-3, err
