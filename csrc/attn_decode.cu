@@ -73,14 +73,16 @@ HX_DEVICE void norm_rope_head(float* xv, const float* w, const float* inv_freq, 
 template <int D, int G>
 __global__ void __launch_bounds__(128) attn_decode_kernel(AttnDecodeArgs a) {
   constexpr int PER = D / 32;   // head dims per lane in the PV phase
-  constexpr int NW = 4;         // warps per CTA
+  constexpr int NW = 8;         // warps per CTA
   constexpr int TILE = 32;      // keys per warp tile (one key per lane in the QK phase)
+  constexpr int MAXS = 64;      // largest split count the merge supports
   extern __shared__ __align__(16) float dsm[];
   float (*qsm)[D] = reinterpret_cast<float (*)[D]>(dsm);                      // [G][D] normed, roped, scaled
   float (*tmp)[D] = reinterpret_cast<float (*)[D]>(dsm + G * D);              // [NW][D] rope scratch
   float (*psm)[G][TILE] = reinterpret_cast<float (*)[G][TILE]>(dsm + (G + NW) * D);  // [NW][G][TILE]
   float (*wo)[G][D] = reinterpret_cast<float (*)[G][D]>(dsm + (G + NW) * D + NW * G * TILE);  // [NW][G][D]
   __shared__ float wm[NW][G], wl[NW][G];
+  __shared__ float cw[G][MAXS];  // merge weights exp(m_s - M) / L per split
   __shared__ int is_last;
 
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
@@ -236,21 +238,37 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(AttnDecodeArgs a) {
   __syncthreads();
   if (!is_last) return;
   __threadfence();
-  for (int t = threadIdx.x; t < G * D; t += blockDim.x) {
-    int g = t / D, d = t - g * D;
-    int hq = kvh * G + g;
-    long long base = ((long long)b * a.Hq + hq) * a.nsplit;
-    float M = -INFINITY;
-    for (int s2 = 0; s2 < a.nsplit; ++s2) M = fmaxf(M, __ldcg(&a.part_ml[(base + s2) * 2]));
-    float Ls = 0.f, O = 0.f;
-    for (int s2 = 0; s2 < a.nsplit; ++s2) {
-      float ms = __ldcg(&a.part_ml[(base + s2) * 2]);
-      if (ms == -INFINITY) continue;
-      float c = __expf(ms - M);
-      Ls += __ldcg(&a.part_ml[(base + s2) * 2 + 1]) * c;
-      O += __ldcg(&a.part_o[(base + s2) * D + d]) * c;
+  // per head: one warp reads the split (max, sum) pairs and turns them into weights
+  for (int g = warp; g < G; g += NW) {
+    const long long base = ((long long)b * a.Hq + kvh * G + g) * a.nsplit;
+    float ms[2], ls[2];
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const int s2 = lane + 32 * q;
+      ms[q] = s2 < a.nsplit ? __ldcg(&a.part_ml[(base + s2) * 2]) : -INFINITY;
+      ls[q] = s2 < a.nsplit ? __ldcg(&a.part_ml[(base + s2) * 2 + 1]) : 0.f;
     }
-    float o = __bfloat162float(__float2bfloat16(O / Ls));
+    const float M = warp_max(fmaxf(ms[0], ms[1]));
+    float c[2], lsum = 0.f;
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      c[q] = ms[q] == -INFINITY ? 0.f : __expf(ms[q] - M);
+      lsum += ls[q] * c[q];
+    }
+    lsum = warp_sum(lsum);
+#pragma unroll
+    for (int q = 0; q < 2; ++q)
+      if (lane + 32 * q < MAXS) cw[g][lane + 32 * q] = c[q] / lsum;
+  }
+  __syncthreads();
+  for (int t = threadIdx.x; t < G * D; t += blockDim.x) {
+    const int g = t / D, d = t - g * D;
+    const int hq = kvh * G + g;
+    const long long base = ((long long)b * a.Hq + hq) * a.nsplit;
+    float O = 0.f;
+#pragma unroll 8
+    for (int s2 = 0; s2 < a.nsplit; ++s2) O += cw[g][s2] * __ldcg(&a.part_o[(base + s2) * D + d]);
+    float o = __bfloat162float(__float2bfloat16(O));
     if (a.gated) {
       float gt = __bfloat162float(pr[hq * qw + D + d]);
       o = o * (1.f / (1.f + __expf(-gt)));
@@ -262,7 +280,8 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(AttnDecodeArgs a) {
 
 template <int D, int G>
 static void launch_dg(const AttnDecodeArgs& a, dim3 grid, cudaStream_t s) {
-  constexpr int NW = 4, TILE = 32;
+  constexpr int NW = 8, TILE = 32;
+  TORCH_CHECK(a.nsplit >= 1 && a.nsplit <= 64, "attention decode supports 1..64 splits");
   const size_t smem = (size_t)(G * D + NW * D + NW * G * TILE + NW * G * D) * sizeof(float);
   auto k = attn_decode_kernel<D, G>;
   if (smem + 4096 > 48 * 1024) {

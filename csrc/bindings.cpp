@@ -16,6 +16,7 @@ void attn_decode(torch::Tensor proj, c10::optional<torch::Tensor> q_norm_w, c10:
                  torch::Tensor inv_freq, torch::Tensor kc, torch::Tensor vc, torch::Tensor slots, torch::Tensor pos,
                  torch::Tensor part_o, torch::Tensor part_ml, torch::Tensor counters, torch::Tensor out, int64_t Hq,
                  int64_t Hkv, int64_t D, int64_t rot, bool gated, double eps);
+void moe_combine(torch::Tensor y, torch::Tensor rows, torch::Tensor wts, torch::Tensor x);
 void embed(torch::Tensor E, torch::Tensor tok, torch::Tensor x);
 void argmax_step(torch::Tensor logits, torch::Tensor tok, c10::optional<torch::Tensor> slots,
                  c10::optional<torch::Tensor> pos, c10::optional<torch::Tensor> out, c10::optional<torch::Tensor> step);
@@ -57,6 +58,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemv_experts", &gemv_experts);
   m.def("moe_topk", &moe_topk);
   m.def("moe_down", &moe_down);
+  m.def("moe_combine", &moe_combine);
   m.def("gdn_decode", &gdn_decode);
   m.def("attn_decode", &attn_decode);
   m.def("embed", &embed);

@@ -69,9 +69,47 @@ __global__ void moe_topk_kernel(const float* __restrict__ logits, int ld, int E,
   }
 }
 
+// Prefill MoE combine: x[t, :] += sum_j wts[t, j] * y[rows[t, j], :] (the expert outputs
+// of token t live at rows[t, :] of the grouped-GEMM output). Replaces a scatter-add of
+// f32 copies; one CTA per token, 8 values per thread.
+__global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ y, const int* __restrict__ rows,
+                                   const float* __restrict__ wts, __nv_bfloat16* __restrict__ x, int H, int J) {
+  const int t = blockIdx.x;
+  for (int v = threadIdx.x; v < H / 8; v += blockDim.x) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int j = 0; j < J; ++j) {
+      const float w = wts[(long long)t * J + j];
+      float f[8];
+      unpack8(reinterpret_cast<const bf16x8*>(y + (long long)rows[(long long)t * J + j] * H)[v], f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = fmaf(w, f[i], acc[i]);
+    }
+    float xv[8];
+    bf16x8* xp = reinterpret_cast<bf16x8*>(x + (long long)t * H) + v;
+    unpack8(*xp, xv);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) xv[i] += __bfloat162float(__float2bfloat16(acc[i]));
+    *xp = pack8(xv);
+  }
+}
+
 }  // namespace hx
 
 using namespace hx;
+
+void moe_combine(torch::Tensor y, torch::Tensor rows, torch::Tensor wts, torch::Tensor x) {
+  TORCH_CHECK(y.scalar_type() == at::kBFloat16 && x.scalar_type() == at::kBFloat16 && y.is_contiguous() &&
+                  x.is_contiguous(), "bf16 contiguous y / x");
+  TORCH_CHECK(rows.scalar_type() == at::kInt && wts.scalar_type() == at::kFloat && rows.sizes() == wts.sizes(),
+              "rows int32 / wts f32 [T, J]");
+  const int T = x.size(0), H = x.size(1);
+  TORCH_CHECK(H % 8 == 0 && y.size(1) == H && rows.size(0) == T, "shape mismatch");
+  if (T == 0) return;
+  moe_combine_kernel<<<T, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(y.data_ptr()), rows.data_ptr<int>(), wts.data_ptr<float>(),
+      reinterpret_cast<__nv_bfloat16*>(x.data_ptr()), H, rows.size(1));
+  HX_CUDA_CHECK(cudaGetLastError());
+}
 
 void moe_topk(torch::Tensor logits, int64_t E, int64_t k, bool has_shared, bool norm_topk, torch::Tensor ids,
               torch::Tensor wts) {

@@ -34,6 +34,27 @@ from . import layout
 _allow_cpu_prefill = False
 
 
+class PhaseTimer:
+    """Accumulates device time per named phase from CUDA events (mark() starts a phase)."""
+
+    def __init__(self):
+        self.events: list[tuple[str, torch.cuda.Event]] = []
+
+    def mark(self, name: str):
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        self.events.append((name, e))
+
+    def totals(self) -> dict[str, float]:
+        self.mark("_end")
+        self.events[-1][1].synchronize()
+        out: dict[str, float] = {}
+        for (n, a), (_, b) in zip(self.events, self.events[1:]):
+            out[n] = out.get(n, 0.0) + a.elapsed_time(b)
+        self.events = []
+        return {k: round(v, 3) for k, v in out.items()}
+
+
 @dataclass
 class DecodeBuffers:
     B: int
@@ -83,7 +104,9 @@ class FastModel:
         self.has_shared = cfg.shared_expert_intermediate_size > 0
         sm = torch.cuda.get_device_properties(device).multi_processor_count if device.type == "cuda" else 1
         self.sms = sm
-        self.attn_splits = attn_splits or max(1, min(64, sm // max(1, dims.hkv)))
+        # split-K width of decode attention: about 64 CTAs per sequence in total, so the
+        # per-head merge of the partials stays cheap
+        self.attn_splits = attn_splits or max(4, min(64, 64 // max(1, dims.hkv)))
         # ---- state pools -------------------------------------------------
         self.pos = torch.zeros(max_slots, dtype=torch.int32, device=device)
         self.kc: dict[int, torch.Tensor] = {}
@@ -101,6 +124,7 @@ class FastModel:
                 self.kc[i] = torch.zeros(shp, dtype=torch.bfloat16, device=device)
                 self.vc[i] = torch.zeros(shp, dtype=torch.bfloat16, device=device)
         self._bufs: dict[int, DecodeBuffers] = {}
+        self.prefill_timer = None  # optional PhaseTimer (CUDA events per prefill phase)
 
     # ------------------------------------------------------------------
     # construction
@@ -453,6 +477,19 @@ class FastModel:
             self.C.gemm_grouped(A, lw["w_gu"].view(-1, lw["w_gu"].shape[-1]), act, t_gu, I2, 1, self._gemm_err())
             y = torch.empty(A.shape[0], Hh, dtype=torch.bfloat16, device=hn.device)
             self.C.gemm_grouped(act, lw["w_d"].view(-1, lw["w_d"].shape[-1]), y, t_d, Hh, 0, self._gemm_err())
+        J = k + (1 if self.has_shared else 0)
+        if self.C is not None:
+            # rows[t, j]: where token t's j-th expert output sits in y (inverse of the sort)
+            pos = torch.empty_like(order)
+            pos[order] = torch.arange(order.numel(), device=hn.device)
+            rows = pos.view(T, k)
+            wts = topv
+            if self.has_shared:
+                rows = torch.cat([rows, (T * k + torch.arange(T, device=hn.device))[:, None]], 1)
+                wts = torch.cat([wts, torch.sigmoid(logits[:, E:E + 1])], 1)
+            out = torch.zeros(T, cfg.hidden_size, dtype=torch.bfloat16, device=hn.device)
+            self.C.moe_combine(y, rows.to(torch.int32).contiguous(), wts.float().contiguous(), out)
+            return out
         out = torch.zeros(T, cfg.hidden_size, dtype=torch.float32, device=hn.device)
         out.index_add_(0, tok_all, y.float() * w_all[:, None])
         return out.to(torch.bfloat16)
@@ -469,13 +506,21 @@ class FastModel:
         if p0 + T > self.max_len:
             raise ValueError(f"sequence of {p0 + T} tokens exceeds max_len {self.max_len}")
         x = self.embed_w[tokens.long()]
+        tm = self.prefill_timer
         for i in range(cfg.num_hidden_layers):
             lw = self.layers[i]
+            kind = "gdn" if cfg.is_linear(i) else "attn"
+            if tm is not None:
+                tm.mark(kind)
             h = self._rms(x, lw["ln1"])
             o = self._gdn_prefill(i, h, slot, p0) if cfg.is_linear(i) else self._attn_prefill(i, h, slot, p0)
             x = x + self._reduce(o)
+            if tm is not None:
+                tm.mark("moe" if cfg.layer_uses_moe(i) else "mlp")
             o = self._ffn_prefill(i, self._rms(x, lw["ln2"]))
             x = x + self._reduce(o)
+        if tm is not None:
+            tm.mark("head")
         last = self._rms(x[-1:], self.final_norm)
         self.pos[slot] = p0 + T
         return self._linear(last, self.lm_head, 2)[0]
