@@ -1,0 +1,115 @@
+"""Gateway routing, eviction, auth stamping, streaming relay and metrics against mock
+nodes (the reference's cortex-gateway tests use in-process mock neurons the same way)."""
+import json
+
+import httpx
+import pytest
+from fastapi.testclient import TestClient
+
+from helexa_b200.gateway.app import create_gateway
+from helexa_b200.gateway.core import Catalogue, CatalogueEntry, NodeState, NoRoute, Router
+
+
+class MockFleet:
+    def __init__(self):
+        self.nodes = {
+            "a": {"models": {"m1": "loaded"}, "busy": {"m1": 3}, "free": 1000},
+            "b": {"models": {"m1": "loaded", "m2": "loaded"}, "busy": {"m1": 1}, "free": 500},
+        }
+        self.calls = []
+
+    def handler(self, req: httpx.Request) -> httpx.Response:
+        node = req.url.host.split(".")[0]
+        st = self.nodes[node]
+        path = req.url.path
+        self.calls.append((node, req.method, path, dict(req.headers), req.content))
+        if path == "/models":
+            return httpx.Response(200, json={"models": [{"id": k, "status": v} for k, v in st["models"].items()]})
+        if path == "/health":
+            return httpx.Response(200, json={"models": {k: {"in_flight": v, "queue_depth": 0}
+                                                        for k, v in st["busy"].items()}})
+        if path == "/discovery":
+            return httpx.Response(200, json={"devices": [{"memory_free_mb": st["free"]}]})
+        if path == "/models/load":
+            body = json.loads(req.content)
+            st["models"][body["model_id"]] = "loaded"
+            return httpx.Response(200, json={"status": "loaded"})
+        if path == "/models/unload":
+            st["models"].pop(json.loads(req.content)["model_id"], None)
+            return httpx.Response(200, json={"status": "unloaded"})
+        body = json.loads(req.content)
+        if body.get("stream"):
+            return httpx.Response(200, content=b'data: {"content":"x"}\n\ndata: [DONE]\n\n',
+                                  headers={"content-type": "text/event-stream"})
+        return httpx.Response(200, json={"model": body["model"], "served_by": node,
+                                         "usage": {"completion_tokens": 2}})
+
+
+def _cat():
+    return Catalogue([
+        CatalogueEntry("m1", "preset:x", aliases=["fast"], memory_mb=100),
+        CatalogueEntry("m2", "preset:y", memory_mb=100, residency_priority=100),
+        CatalogueEntry("m3", "preset:z", memory_mb=100),
+    ])
+
+
+def _app(fleet, **kw):
+    nodes = [NodeState("a", "http://a.node"), NodeState("b", "http://b.node")]
+    return create_gateway(_cat(), nodes, transport=httpx.MockTransport(fleet.handler), poll_interval_s=3600, **kw)
+
+
+def test_routes_least_busy_and_rewrites_alias():
+    fleet = MockFleet()
+    with TestClient(_app(fleet)) as c:
+        r = c.post("/v1/chat/completions", json={"model": "fast", "messages": []})
+        assert r.json()["served_by"] == "b" and r.json()["model"] == "fast"
+        fleet.nodes["b"]["busy"]["m1"] = 9
+        c.app.state.router.observe("b", [{"id": "m1", "status": "loaded"}, {"id": "m2", "status": "loaded"}],
+                                   {"models": {"m1": {"in_flight": 9}}}, 500)
+        assert c.post("/v1/chat/completions", json={"model": "m1", "messages": []}).json()["served_by"] == "a"
+        m = c.get("/metrics").text
+        assert "cortex_requests_total" in m
+
+
+def test_cold_load_evicts_lru_but_never_pinned():
+    fleet = MockFleet()
+    fleet.nodes["a"]["free"] = 0
+    fleet.nodes["b"]["free"] = 0
+    fleet.nodes["a"]["busy"]["m1"] = 0      # idle, displaceable; m2 on b is pinned
+    with TestClient(_app(fleet)) as c:
+        r = c.post("/v1/chat/completions", json={"model": "m3", "messages": []})
+        assert r.status_code == 200
+        unloads = [x for x in fleet.calls if x[2] == "/models/unload"]
+        assert unloads and all(json.loads(x[4])["model_id"] != "m2" for x in unloads)
+        assert any(x[2] == "/models/load" for x in fleet.calls)
+
+
+def test_auth_stamps_and_strips_headers():
+    fleet = MockFleet()
+    with TestClient(_app(fleet, api_keys={"k1": "acct-1"}, require_auth=True)) as c:
+        assert c.post("/v1/chat/completions", json={"model": "m1"}).status_code == 401
+        c.post("/v1/chat/completions", json={"model": "m1"},
+               headers={"authorization": "Bearer k1", "x-helexa-account": "spoofed"})
+        hdr = [x for x in fleet.calls if x[2] == "/v1/chat/completions"][-1][3]
+        assert hdr["x-helexa-account"] == "acct-1"
+
+
+def test_streaming_relay_and_unknown_model():
+    fleet = MockFleet()
+    with TestClient(_app(fleet)) as c:
+        r = c.post("/v1/chat/completions", json={"model": "m1", "stream": True})
+        assert r.text.endswith("data: [DONE]\n\n")
+        r = c.post("/v1/chat/completions", json={"model": "nope"})
+        assert r.status_code == 404 and r.json()["error"]["code"] == "model_not_found"
+        assert {d["id"] for d in c.get("/v1/models").json()["data"]} == {"m1", "m2", "m3"}
+
+
+def test_recovering_hold_and_debounced_unhealthy():
+    r = Router(_cat(), [NodeState("a", "u")])
+    r.observe("a", [{"id": "m1", "status": "recovering"}], {}, 0)
+    with pytest.raises(NoRoute) as e:
+        r.route("m1")
+    assert e.value.status == 503 and e.value.retry_after > 0
+    for _ in range(3):
+        r.observe("a", None, None)
+    assert not r.nodes["a"].healthy
