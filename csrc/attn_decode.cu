@@ -71,7 +71,7 @@ HX_DEVICE void norm_rope_head(float* xv, const float* w, const float* inv_freq, 
 }
 
 template <int D, int G>
-__global__ void __launch_bounds__(128) attn_decode_kernel(AttnDecodeArgs a) {
+__global__ void __launch_bounds__(256) attn_decode_kernel(AttnDecodeArgs a) {
   constexpr int PER = D / 32;   // head dims per lane in the PV phase
   constexpr int NW = 8;         // warps per CTA
   constexpr int TILE = 32;      // keys per warp tile (one key per lane in the QK phase)

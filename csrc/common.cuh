@@ -101,6 +101,13 @@ HX_DEVICE uint64_t globaltimer_ns() {
 template <typename... KArgs, typename... Args>
 static inline cudaError_t hx_launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
                                         cudaStream_t st, Args&&... args) {
+  // refuse configurations the kernel was not built for instead of launching them
+  cudaFuncAttributes fa;
+  cudaError_t e = cudaFuncGetAttributes(&fa, reinterpret_cast<const void*>(kernel));
+  if (e != cudaSuccess) return e;
+  if ((int)(block.x * block.y * block.z) > fa.maxThreadsPerBlock ||
+      (long long)smem > (long long)fa.maxDynamicSharedSizeBytes)
+    return cudaErrorInvalidConfiguration;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;

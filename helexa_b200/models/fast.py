@@ -416,9 +416,13 @@ class FastModel:
         self.vc[i][slot, :, p0:p0 + T] = v.transpose(0, 1)
         L = p0 + T
         Kc, Vc = self.kc[i][slot, :, :L], self.vc[i][slot, :, :L]
-        mask = torch.arange(L, device=h.device)[None, :] <= torch.arange(p0, L, device=h.device)[:, None]
-        o = torch.nn.functional.scaled_dot_product_attention(
-            q.transpose(0, 1)[None], Kc[None], Vc[None], attn_mask=mask, enable_gqa=True)[0]
+        if p0 == 0:
+            o = torch.nn.functional.scaled_dot_product_attention(
+                q.transpose(0, 1)[None], Kc[None], Vc[None], is_causal=True, enable_gqa=True)[0]
+        else:
+            mask = torch.arange(L, device=h.device)[None, :] <= torch.arange(p0, L, device=h.device)[:, None]
+            o = torch.nn.functional.scaled_dot_product_attention(
+                q.transpose(0, 1)[None], Kc[None], Vc[None], attn_mask=mask, enable_gqa=True)[0]
         o = o.transpose(0, 1).reshape(T, d.hq * D)
         if gate is not None:
             o = (o.float() * torch.sigmoid(gate.reshape(T, d.hq * D).float())).to(torch.bfloat16)
