@@ -1,0 +1,55 @@
+"""Speculative acceptance, context-limit derivation, preflight checks, settings."""
+import pytest
+
+from helexa_b200.config import get_preset
+from helexa_b200.config.settings import load_settings
+from helexa_b200.runtime.context_limit import ContextProfile, derive_limit, kv_reservation_mb
+from helexa_b200.runtime.preflight import PreflightError, preflight
+from helexa_b200.runtime.speculative import greedy_accept
+
+
+def test_greedy_accept():
+    a = greedy_accept([1, 2, 3, 4], [1, 2, 9, 4, 5])
+    assert (a.accepted, a.bonus) == (2, 9) and a.committed([1, 2, 3, 4]) == [1, 2, 9]
+    a = greedy_accept([1, 2], [1, 2, 7])
+    assert a.committed([1, 2]) == [1, 2, 7]
+    with pytest.raises(ValueError):
+        greedy_accept([1], [1])
+
+
+def test_context_limit():
+    cfg = get_preset("qwen3-next-80b-a3b")
+    p = ContextProfile.from_config(cfg)
+    assert p.kv_bytes_per_token == 2 * 12 * 2 * 256 * 2   # only full-attention layers hold KV
+    lim = derive_limit(p, free_bytes_tightest=20 << 30, prefill_tok_s=10000, max_prefill_s=1.0)
+    assert lim.input == 10000 and lim.context <= cfg.max_position_embeddings and lim.kv_budget_mb > 0
+    p8 = ContextProfile.from_config(cfg, tp=8)
+    assert p8.kv_bytes_per_token == p.kv_bytes_per_token // 2   # 2 KV heads -> 1 per rank (replicated)
+    assert kv_reservation_mb(p, 8192, 512) >= (8704 * p.kv_bytes_per_token) >> 20
+
+
+def test_preflight():
+    nxt = get_preset("qwen3-next-80b-a3b")
+    preflight("dense", nxt, tp=8)                       # KV heads replicate at TP8
+    with pytest.raises(PreflightError) as e:
+        preflight("dense", nxt, tp=3)
+    assert e.value.code == "bad_tensor_parallel"
+    with pytest.raises(PreflightError) as e:
+        preflight("diffusers", None)
+    assert e.value.code == "wrong_modality"
+    q32 = get_preset("qwen3-32b")
+    preflight("gguf", q32, tp=4, quant="Q4_K")
+    with pytest.raises(PreflightError) as e:
+        preflight("gguf", q32, tp=8, quant="Q4_K")
+    assert e.value.code == "quant_shard_misaligned"
+    with pytest.raises(PreflightError) as e:
+        preflight("dense", nxt, tp=1, free_bytes_per_device=[80 << 30])
+    assert e.value.code == "insufficient_memory" and "error" in e.value.to_json()
+
+
+def test_settings_env_override(tmp_path):
+    f = tmp_path / "c.json"
+    f.write_text('{"port": 1, "admission": {"max_in_flight": 2}}')
+    s = load_settings(str(f), env={"HELEXA_PORT": "8080", "HELEXA_ADMISSION__MAX_QUEUE_DEPTH": "9",
+                                   "OTHER": "x"})
+    assert s == {"port": 8080, "admission": {"max_in_flight": 2, "max_queue_depth": 9}}
