@@ -28,7 +28,7 @@ LINEAR = "linear_attention"
 
 @dataclass
 class ModelConfig:
-    family: str                     # "qwen3" | "qwen3_moe" | "qwen3_next"
+    family: str                     # "qwen3" | "qwen3_moe" | "qwen3_next" | "llama"
     vocab_size: int
     hidden_size: int
     num_hidden_layers: int
@@ -60,6 +60,7 @@ class ModelConfig:
     linear_key_head_dim: int = 0
     linear_value_head_dim: int = 0
     linear_conv_kernel_dim: int = 4
+    rope_scaling: dict | None = None  # e.g. {"rope_type": "llama3", "factor": 8, ...}
     # bookkeeping
     name: str = ""
     eos_token_ids: list[int] = field(default_factory=list)
@@ -142,6 +143,27 @@ class ModelConfig:
                 n += 3 * h * self.intermediate_size
         return n
 
+    def rope_inv_freq(self):
+        """Inverse RoPE frequencies [rotary_dim/2] (f32), with llama3-style scaling when configured."""
+        import math
+
+        import torch
+        rd = self.rotary_dim
+        inv = 1.0 / (self.rope_theta ** (torch.arange(0, rd, 2, dtype=torch.int64).float() / rd))
+        rs = self.rope_scaling or {}
+        if rs.get("rope_type", rs.get("type")) == "llama3":
+            factor = float(rs.get("factor", 8.0))
+            lo, hi = float(rs.get("low_freq_factor", 1.0)), float(rs.get("high_freq_factor", 4.0))
+            old = float(rs.get("original_max_position_embeddings", 8192))
+            lo_wl, hi_wl = old / lo, old / hi
+            wl = 2 * math.pi / inv
+            smooth = (old / wl - lo) / (hi - lo)
+            scaled = torch.where(wl > lo_wl, inv / factor, inv)
+            mid = (wl <= lo_wl) & (wl >= hi_wl)
+            scaled = torch.where(mid, (1 - smooth) * inv / factor + smooth * inv, scaled)
+            inv = scaled
+        return inv
+
     def to_dict(self) -> dict[str, Any]:
         return dataclasses.asdict(self)
 
@@ -149,7 +171,7 @@ class ModelConfig:
     def to_hf_config(self) -> dict[str, Any]:
         """Emit an HF-style config.json dict that `from_hf_config` (and transformers) parse."""
         arch = {"qwen3": "Qwen3ForCausalLM", "qwen3_moe": "Qwen3MoeForCausalLM",
-                "qwen3_next": "Qwen3NextForCausalLM"}[self.family]
+                "qwen3_next": "Qwen3NextForCausalLM", "llama": "LlamaForCausalLM"}[self.family]
         d: dict[str, Any] = {
             "architectures": [arch], "model_type": self.family,
             "vocab_size": self.vocab_size, "hidden_size": self.hidden_size,
@@ -160,8 +182,8 @@ class ModelConfig:
             "rope_theta": self.rope_theta, "max_position_embeddings": self.max_position_embeddings,
             "tie_word_embeddings": self.tie_word_embeddings, "hidden_act": "silu",
             "attention_bias": False, "torch_dtype": "bfloat16",
-            "rope_parameters": {"rope_type": "default", "rope_theta": self.rope_theta,
-                                "partial_rotary_factor": self.partial_rotary_factor},
+            "rope_parameters": dict(self.rope_scaling or {"rope_type": "default"}, rope_theta=self.rope_theta,
+                                    partial_rotary_factor=self.partial_rotary_factor),
         }
         if self.eos_token_ids:
             d["eos_token_id"] = self.eos_token_ids if len(self.eos_token_ids) > 1 else self.eos_token_ids[0]
@@ -197,6 +219,8 @@ class ModelConfig:
             family = "qwen3_moe"
         elif mt == "qwen3":
             family = "qwen3"
+        elif mt == "llama" or any("Llama" in a for a in archs):
+            family = "llama"
         else:
             raise ValueError(f"unsupported model_type {mt!r} (architectures {archs})")
         rope = raw.get("rope_parameters") or raw.get("rope_scaling") or {}
@@ -222,7 +246,9 @@ class ModelConfig:
             partial_rotary_factor=prf,
             max_position_embeddings=int(raw.get("max_position_embeddings", 32768)),
             tie_word_embeddings=bool(raw.get("tie_word_embeddings", False)),
-            attn_output_gate=(family == "qwen3_next"),
+            attn_output_gate=(family == "qwen3_next"), qk_norm=(family != "llama"),
+            rope_scaling=(rope if rope.get("rope_type", rope.get("type", "default")) not in (None, "default")
+                          else None),
             norm_offset=1.0 if family == "qwen3_next" else 0.0,
             num_experts=int(raw.get("num_experts", 0) or 0),
             num_experts_per_tok=int(raw.get("num_experts_per_tok", 0) or 0),

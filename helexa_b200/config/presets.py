@@ -84,7 +84,28 @@ def tiny_qwen3_moe() -> ModelConfig:
     )
 
 
+def tiny_llama() -> ModelConfig:
+    return ModelConfig(
+        family="llama", name="tiny-llama", vocab_size=1024, hidden_size=256, num_hidden_layers=2,
+        num_attention_heads=4, num_key_value_heads=2, head_dim=64, intermediate_size=512, rope_theta=5e5,
+        qk_norm=False, rope_scaling={"rope_type": "llama3", "factor": 8.0, "low_freq_factor": 1.0,
+                                     "high_freq_factor": 4.0, "original_max_position_embeddings": 64},
+    )
+
+
+def llama3_8b() -> ModelConfig:
+    return ModelConfig(
+        family="llama", name="Llama-3.1-8B", vocab_size=128256, hidden_size=4096, num_hidden_layers=32,
+        num_attention_heads=32, num_key_value_heads=8, head_dim=128, intermediate_size=14336, rope_theta=5e5,
+        rms_norm_eps=1e-5, qk_norm=False, max_position_embeddings=131072,
+        rope_scaling={"rope_type": "llama3", "factor": 8.0, "low_freq_factor": 1.0, "high_freq_factor": 4.0,
+                      "original_max_position_embeddings": 8192}, eos_token_ids=[128001, 128008, 128009],
+    )
+
+
 PRESETS = {
+    "tiny-llama": tiny_llama,
+    "llama-3.1-8b": llama3_8b,
     "tiny-qwen3-next": tiny_qwen3_next,
     "tiny-qwen3": tiny_qwen3,
     "tiny-qwen3-moe": tiny_qwen3_moe,

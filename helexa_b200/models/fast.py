@@ -98,9 +98,7 @@ class FastModel:
         self.max_slots, self.max_len = max_slots, max_len
         self.comm = comm  # parallel.TPComm or None (single rank)
         self.C = ops.C if device.type == "cuda" else None
-        rd = cfg.rotary_dim
-        inv = 1.0 / (cfg.rope_theta ** (torch.arange(0, rd, 2, dtype=torch.int64).float() / rd))
-        self.inv_freq = inv.to(device)
+        self.inv_freq = cfg.rope_inv_freq().to(device)
         self.has_shared = cfg.shared_expert_intermediate_size > 0
         sm = torch.cuda.get_device_properties(device).multi_processor_count if device.type == "cuda" else 1
         self.sms = sm
@@ -409,7 +407,8 @@ class FastModel:
         v = qkv[:, d.hq * d.qw + d.hkv * D:].view(T, d.hkv, D)
         if "q_norm" in lw:
             q, k = self._rms(q, lw["q_norm"]), self._rms(k, lw["k_norm"])
-        cos, sin = rope_cos_sin(torch.arange(p0, p0 + T, device=h.device), cfg.rotary_dim, cfg.rope_theta)
+        cos, sin = rope_cos_sin(torch.arange(p0, p0 + T, device=h.device), cfg.rotary_dim, cfg.rope_theta,
+                                self.inv_freq)
         q = apply_rope(q.float(), cos, sin).to(torch.bfloat16)
         k = apply_rope(k.float(), cos, sin).to(torch.bfloat16)
         self.kc[i][slot, :, p0:p0 + T] = k.transpose(0, 1)

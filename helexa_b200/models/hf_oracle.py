@@ -20,6 +20,10 @@ def build_hf_model(cfg: ModelConfig, weights: dict[str, torch.Tensor], dtype=tor
         hc = transformers.Qwen3NextConfig(**{k: v for k, v in hf_cfg_dict.items()
                                              if k not in ("architectures", "model_type", "torch_dtype")})
         model = transformers.Qwen3NextForCausalLM(hc)
+    elif cfg.family == "llama":
+        hc = transformers.LlamaConfig(**{k: v for k, v in hf_cfg_dict.items()
+                                         if k not in ("architectures", "model_type", "torch_dtype")})
+        model = transformers.LlamaForCausalLM(hc)
     elif cfg.family == "qwen3_moe":
         hc = transformers.Qwen3MoeConfig(**{k: v for k, v in hf_cfg_dict.items()
                                             if k not in ("architectures", "model_type", "torch_dtype")})

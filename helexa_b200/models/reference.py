@@ -48,8 +48,9 @@ def l2norm(x: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
     return x * torch.rsqrt((x * x).sum(-1, keepdim=True) + eps)
 
 
-def rope_cos_sin(positions: torch.Tensor, rotary_dim: int, theta: float):
-    inv = 1.0 / (theta ** (torch.arange(0, rotary_dim, 2, dtype=torch.int64).float() / rotary_dim))
+def rope_cos_sin(positions: torch.Tensor, rotary_dim: int, theta: float, inv: torch.Tensor | None = None):
+    if inv is None:
+        inv = 1.0 / (theta ** (torch.arange(0, rotary_dim, 2, dtype=torch.int64).float() / rotary_dim))
     freqs = positions.float()[:, None] * inv[None, :].to(positions.device)
     emb = torch.cat([freqs, freqs], -1)
     return emb.cos(), emb.sin()
@@ -213,7 +214,7 @@ class ReferenceModel:
             q = rms_norm(q, self.w[p + "q_norm.weight"], c.rms_norm_eps, c.norm_offset).to(x.dtype)
             k = rms_norm(k, self.w[p + "k_norm.weight"], c.rms_norm_eps, c.norm_offset).to(x.dtype)
         pos = torch.arange(pos0, pos0 + T, device=x.device)
-        cos, sin = rope_cos_sin(pos, c.rotary_dim, c.rope_theta)
+        cos, sin = rope_cos_sin(pos, c.rotary_dim, c.rope_theta, c.rope_inv_freq())
         q = apply_rope(q.float(), cos, sin).to(x.dtype)
         k = apply_rope(k.float(), cos, sin).to(x.dtype)
         if i in st.k:

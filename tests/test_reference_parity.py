@@ -24,7 +24,7 @@ def _greedy(model, prompt, n):
     return out
 
 
-@pytest.mark.parametrize("name", ["tiny-qwen3-next", "tiny-qwen3", "tiny-qwen3-moe"])
+@pytest.mark.parametrize("name", ["tiny-qwen3-next", "tiny-qwen3", "tiny-qwen3-moe", "tiny-llama"])
 def test_greedy_matches_hf(name):
     cfg = get_preset(name)
     w = random_weights(cfg, seed=0)
