@@ -155,21 +155,27 @@ __global__ void __launch_bounds__(256) gdn_chunk_kernel(const __nv_bfloat16* __r
     __syncthreads();
   }
   // u = (I + T) (beta v), w = (I + T) (beta k exp(gc)) -- T holds the strictly lower part
+  // fold beta (and exp(gc) for w) into the substitution rows once: tb[i][m] = T[i][m] beta_m
+  if (tid < kGC) rowA[tid] = __expf(gcs[tid]);
+  __syncthreads();
   for (int e = tid; e < kGC * D; e += 256) {
     int i = e / D, d = e - i * D;
     float su = bs[i] * vs[i * (D + 1) + d];
-    float sw = bs[i] * ks[i * (D + 1) + d] * __expf(gcs[i]);
+    float sw = bs[i] * ks[i * (D + 1) + d] * rowA[i];
     for (int m = 0; m < i; ++m) {
       const float tm = Am[i * (kGC + 1) + m] * bs[m];
       su += tm * vs[m * (D + 1) + d];
-      sw += tm * ks[m * (D + 1) + d] * __expf(gcs[m]);
+      sw += tm * ks[m * (D + 1) + d] * rowA[m];
     }
     U[(hc * kGC + i) * D + d] = su;
     Wm[(hc * kGC + i) * D + d] = sw;
   }
 }
 
-// grid (D / 32, Hv), block 256. Walks the chunks in order with the state tile in smem.
+// grid (D / 32, Hv), block 256. Walks the chunks in order with the f32 state tile
+// S [D, 32] in shared memory. Every product uses register micro-tiles (4x2 or 8x2
+// outputs per thread with 4-wide vector loads along the reduction), so each
+// shared-memory load feeds several FMAs.
 template <int D>
 __global__ void __launch_bounds__(256) gdn_scan_kernel(const __nv_bfloat16* __restrict__ qn,
                                                        const __nv_bfloat16* __restrict__ kn,
@@ -179,17 +185,20 @@ __global__ void __launch_bounds__(256) gdn_scan_kernel(const __nv_bfloat16* __re
                                                        int Hv, int Tp, int T, int nchunks,
                                                        __nv_bfloat16* __restrict__ o /* [T, Hv, D] */) {
   constexpr int BV = 32;
+  constexpr int LD = D + 4;        // row stride of the [C][D] tiles (16-byte aligned rows)
+  constexpr int LK = kGC + 4;      // row stride of the [D][C] / [C][C] tiles
   extern __shared__ __align__(16) float sm[];
   float* S = sm;                     // [D][BV]
-  float* Ws = S + D * BV;            // [C][D+1]
-  float* Qs = Ws + kGC * (D + 1);    // [C][D+1]  q * exp(gc)
-  float* Ks = Qs + kGC * (D + 1);    // [C][D+1]  k * exp(glast - gc)
-  float* Ps = Ks + kGC * (D + 1);    // [C][C+1]
-  float* Vn = Ps + kGC * (kGC + 1);  // [C][BV]
+  float* Ws = S + D * BV;            // [C][LD]   w rows
+  float* Qs = Ws + kGC * LD;         // [C][LD]   q * exp(gc)
+  float* KdT = Qs + kGC * LD;        // [D][LK]   (k * exp(glast - gc))^T
+  float* Ps = KdT + D * LK;          // [C][LK]
+  float* Vn = Ps + kGC * LK;         // [C][BV]
   float* gcs = Vn + kGC * BV;        // [C]
   const int vt = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
   const int kh = h / (Hv / Hk);
-  const int v = tid % BV, grp = tid / BV;  // 8 groups
+  const int rg = tid >> 4, cp = tid & 15;   // row group (16) x column pair (16)
+  const int c0 = cp * 2;
   float* Sg = state + (long long)h * D * D;
   for (int i = tid; i < D * BV; i += 256) {
     int k = i / BV, vv = i - k * BV;
@@ -202,44 +211,105 @@ __global__ void __launch_bounds__(256) gdn_scan_kernel(const __nv_bfloat16* __re
     if (tid < kGC) gcs[tid] = GC[hc * kGC + tid];
     __syncthreads();
     const float glast = gcs[kGC - 1];
-    for (int i = tid; i < kGC * D; i += 256) {
-      int r = i / D, d = i - r * D;
-      Ws[r * (D + 1) + d] = Wm[(hc * kGC + r) * D + d];
-      Qs[r * (D + 1) + d] = __bfloat162float(qn[((long long)kh * Tp + t0 + r) * D + d]) * __expf(gcs[r]);
-      Ks[r * (D + 1) + d] = __bfloat162float(kn[((long long)kh * Tp + t0 + r) * D + d]) * __expf(glast - gcs[r]);
-    }
-    for (int i = tid; i < kGC * kGC; i += 256) {
-      int r = i / kGC, cc = i - r * kGC;
-      Ps[r * (kGC + 1) + cc] = P[hc * kGC * kGC + i];
-    }
-    __syncthreads();
-    // vnew = u - w S      (rows grp*8 .. +8, column v)
+    for (int i = tid; i < kGC * D / 4; i += 256) {
+      const int r = (i * 4) / D, d = (i * 4) - r * D;
+      *reinterpret_cast<float4*>(&Ws[r * LD + d]) =
+          *reinterpret_cast<const float4*>(&Wm[(hc * kGC + r) * D + d]);
+      const float eq = __expf(gcs[r]), ek = __expf(glast - gcs[r]);
+      const __nv_bfloat16* qr = qn + ((long long)kh * Tp + t0 + r) * D + d;
+      const __nv_bfloat16* kr = kn + ((long long)kh * Tp + t0 + r) * D + d;
 #pragma unroll
-    for (int rr = 0; rr < 8; ++rr) {
-      const int r = grp * 8 + rr;
-      float s = U[(hc * kGC + r) * D + vt * BV + v];
-      for (int k = 0; k < D; ++k) s -= Ws[r * (D + 1) + k] * S[k * BV + v];
-      Vn[r * BV + v] = s;
+      for (int j = 0; j < 4; ++j) {
+        Qs[r * LD + d + j] = __bfloat162float(qr[j]) * eq;
+        KdT[(d + j) * LK + r] = __bfloat162float(kr[j]) * ek;
+      }
+    }
+    for (int i = tid; i < kGC * kGC / 4; i += 256) {
+      const int r = (i * 4) / kGC, cc = (i * 4) - r * kGC;
+      *reinterpret_cast<float4*>(&Ps[r * LK + cc]) = *reinterpret_cast<const float4*>(&P[hc * kGC * kGC + r * kGC + cc]);
     }
     __syncthreads();
-    // o = (q exp(gc)) S + P vnew
+    // ---- vnew = u - w S : rows rg*4 .. +3, columns c0, c0+1 ------------------------
+    float acc[4][2];
 #pragma unroll
-    for (int rr = 0; rr < 8; ++rr) {
-      const int r = grp * 8 + rr;
-      float s = 0.f;
-      for (int k = 0; k < D; ++k) s += Qs[r * (D + 1) + k] * S[k * BV + v];
-      for (int m = 0; m <= r; ++m) s += Ps[r * (kGC + 1) + m] * Vn[m * BV + v];
-      const long long t = t0 + r;
-      if (t < T) o[(t * Hv + h) * D + vt * BV + v] = __float2bfloat16(s);
+    for (int i = 0; i < 4; ++i) {
+      const int r = rg * 4 + i;
+      const float2 u2 = *reinterpret_cast<const float2*>(&U[(hc * kGC + r) * D + vt * BV + c0]);
+      acc[i][0] = u2.x;
+      acc[i][1] = u2.y;
     }
+    for (int k = 0; k < D; k += 4) {
+      float2 s2[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) s2[j] = *reinterpret_cast<const float2*>(&S[(k + j) * BV + c0]);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float4 w4 = *reinterpret_cast<const float4*>(&Ws[(rg * 4 + i) * LD + k]);
+        acc[i][0] -= w4.x * s2[0].x + w4.y * s2[1].x + w4.z * s2[2].x + w4.w * s2[3].x;
+        acc[i][1] -= w4.x * s2[0].y + w4.y * s2[1].y + w4.z * s2[2].y + w4.w * s2[3].y;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) *reinterpret_cast<float2*>(&Vn[(rg * 4 + i) * BV + c0]) = make_float2(acc[i][0], acc[i][1]);
     __syncthreads();
-    // S = exp(glast) S + (k exp(glast - gc))^T vnew     (state rows grp*16 .. +16)
-    const float dec = __expf(glast);
-    for (int kk = 0; kk < D / 8; ++kk) {
-      const int k = grp * (D / 8) + kk;
-      float s = S[k * BV + v] * dec;
-      for (int m = 0; m < kGC; ++m) s += Ks[m * (D + 1) + k] * Vn[m * BV + v];
-      S[k * BV + v] = s;
+    // ---- o = (q exp(gc)) S + P vnew ---------------------------------------------
+#pragma unroll
+    for (int i = 0; i < 4; ++i) { acc[i][0] = 0.f; acc[i][1] = 0.f; }
+    for (int k = 0; k < D; k += 4) {
+      float2 s2[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) s2[j] = *reinterpret_cast<const float2*>(&S[(k + j) * BV + c0]);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float4 q4 = *reinterpret_cast<const float4*>(&Qs[(rg * 4 + i) * LD + k]);
+        acc[i][0] += q4.x * s2[0].x + q4.y * s2[1].x + q4.z * s2[2].x + q4.w * s2[3].x;
+        acc[i][1] += q4.x * s2[0].y + q4.y * s2[1].y + q4.z * s2[2].y + q4.w * s2[3].y;
+      }
+    }
+    for (int m = 0; m < kGC; m += 4) {  // P is causal (zero above the diagonal)
+      float2 v2[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) v2[j] = *reinterpret_cast<const float2*>(&Vn[(m + j) * BV + c0]);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float4 p4 = *reinterpret_cast<const float4*>(&Ps[(rg * 4 + i) * LK + m]);
+        acc[i][0] += p4.x * v2[0].x + p4.y * v2[1].x + p4.z * v2[2].x + p4.w * v2[3].x;
+        acc[i][1] += p4.x * v2[0].y + p4.y * v2[1].y + p4.z * v2[2].y + p4.w * v2[3].y;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const long long t = t0 + rg * 4 + i;
+      if (t < T) {
+        __nv_bfloat162 ov = __floats2bfloat162_rn(acc[i][0], acc[i][1]);
+        *reinterpret_cast<__nv_bfloat162*>(&o[(t * Hv + h) * D + vt * BV + c0]) = ov;
+      }
+    }
+    // ---- S = exp(glast) S + KdT vnew : state rows rg*(D/16) .. , columns c0, c0+1 ----
+    {
+      constexpr int RS = D / 16;
+      const float dec = __expf(glast);
+      float sa[RS][2];
+#pragma unroll
+      for (int i = 0; i < RS; ++i) {
+        const float2 s2 = *reinterpret_cast<const float2*>(&S[(rg * RS + i) * BV + c0]);
+        sa[i][0] = s2.x * dec;
+        sa[i][1] = s2.y * dec;
+      }
+      for (int m = 0; m < kGC; m += 4) {
+        float2 v2[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v2[j] = *reinterpret_cast<const float2*>(&Vn[(m + j) * BV + c0]);
+#pragma unroll
+        for (int i = 0; i < RS; ++i) {
+          const float4 k4 = *reinterpret_cast<const float4*>(&KdT[(rg * RS + i) * LK + m]);
+          sa[i][0] += k4.x * v2[0].x + k4.y * v2[1].x + k4.z * v2[2].x + k4.w * v2[3].x;
+          sa[i][1] += k4.x * v2[0].y + k4.y * v2[1].y + k4.z * v2[2].y + k4.w * v2[3].y;
+        }
+      }
+      __syncthreads();  // all reads of S for this chunk are done
+#pragma unroll
+      for (int i = 0; i < RS; ++i) *reinterpret_cast<float2*>(&S[(rg * RS + i) * BV + c0]) = make_float2(sa[i][0], sa[i][1]);
     }
   }
   __syncthreads();
@@ -304,7 +374,7 @@ void gdn_prefill(torch::Tensor proj, torch::Tensor conv_w, torch::Tensor ring, t
                                                           beta.data_ptr<float>(), Hk, Hv, Tp, U.data_ptr<float>(), \
                                                           Wm.data_ptr<float>(), P.data_ptr<float>(),               \
                                                           GC.data_ptr<float>());                                    \
-    const size_t sm2 = (DD * 32 + 3 * kGC * (DD + 1) + kGC * (kGC + 1) + kGC * 32 + kGC) * 4;                       \
+    const size_t sm2 = (DD * 32 + 2 * kGC * (DD + 4) + DD * (kGC + 4) + kGC * (kGC + 4) + kGC * 32 + kGC) * 4;                       \
     HX_CUDA_CHECK(cudaFuncSetAttribute(gdn_scan_kernel<DD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm2)); \
     gdn_scan_kernel<DD><<<dim3(DD / 32, Hv), 256, sm2, st>>>(bp(qn), bp(kn), U.data_ptr<float>(),                 \
                                                              Wm.data_ptr<float>(), P.data_ptr<float>(),            \

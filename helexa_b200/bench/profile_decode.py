@@ -30,6 +30,7 @@ def main():
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--eager", action="store_true")
     ap.add_argument("--no-pdl", action="store_true", help="launch without programmatic dependent launch")
+    ap.add_argument("--skip", default="", help="profiling only: comma list of gdn,attn,gdn_core,attn_core,ffn,experts")
     args = ap.parse_args()
     if args.no_pdl:
         from .. import ops
@@ -40,6 +41,7 @@ def main():
     dev = torch.device("cuda", 0)
     fm = FastModel.random(cfg, dev, max_slots=args.batch, max_len=args.context + args.steps * 4 + 64)
     B = args.batch
+    fm.profile_skip = set(x for x in args.skip.split(",") if x)
     if args.eager:
         nb = fm.buffers(B)
     else:
@@ -65,7 +67,7 @@ def main():
     ms = e0.elapsed_time(e1) / args.steps
     gb = fm.decode_bytes_per_token() / 1e9
     print(json.dumps({"model": cfg.name, "layers": cfg.num_hidden_layers, "context": args.context, "batch": B,
-                      "graph": not args.eager, "pdl": not args.no_pdl, "ms_per_step": round(ms, 4),
+                      "graph": not args.eager, "pdl": not args.no_pdl, "skip": args.skip, "ms_per_step": round(ms, 4),
                       "weight_gb_per_step": round(gb, 3), "achieved_gbs": round(gb / (ms / 1e3), 1),
                       "launches_per_step": fm.launches_per_step()}))
 
