@@ -17,6 +17,12 @@ void attn_decode(torch::Tensor proj, c10::optional<torch::Tensor> q_norm_w, c10:
                  torch::Tensor part_o, torch::Tensor part_ml, torch::Tensor counters, torch::Tensor out, int64_t Hq,
                  int64_t Hkv, int64_t D, int64_t rot, bool gated, double eps);
 void moe_combine(torch::Tensor y, torch::Tensor rows, torch::Tensor wts, torch::Tensor x);
+void moe_route_prefill(torch::Tensor logits, int64_t E, int64_t k, bool has_shared, bool norm_topk, torch::Tensor hn,
+                       torch::Tensor ids, torch::Tensor wts, torch::Tensor rows, torch::Tensor counts,
+                       torch::Tensor offsets, torch::Tensor cursor, torch::Tensor tiles, torch::Tensor ntiles,
+                       torch::Tensor A);
+void gemm_grouped_dev(torch::Tensor A, torch::Tensor B, torch::Tensor C, torch::Tensor tiles, torch::Tensor ntiles,
+                      int64_t n, int64_t epi, torch::Tensor err);
 void embed(torch::Tensor E, torch::Tensor tok, torch::Tensor x);
 void argmax_step(torch::Tensor logits, torch::Tensor tok, c10::optional<torch::Tensor> slots,
                  c10::optional<torch::Tensor> pos, c10::optional<torch::Tensor> out, c10::optional<torch::Tensor> step);
@@ -59,6 +65,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_topk", &moe_topk);
   m.def("moe_down", &moe_down);
   m.def("moe_combine", &moe_combine);
+  m.def("moe_route_prefill", &moe_route_prefill);
+  m.def("gemm_grouped_dev", &gemm_grouped_dev);
   m.def("gdn_decode", &gdn_decode);
   m.def("attn_decode", &attn_decode);
   m.def("embed", &embed);

@@ -49,6 +49,8 @@ struct GemmParams {
   int num_n_blocks;
   const GemmTile* tiles;   // grouped mode (nullptr = plain)
   int num_entries;
+  const int* num_entries_dev;  // grouped mode: device-side entry count (overrides num_entries)
+  int b_rows_per_group;    // grouped mode: tile b_row0 holds a group index scaled by this
   int* err;
 };
 
@@ -70,7 +72,8 @@ __global__ void __launch_bounds__(192, 1) gemm_tcgen05_kernel(const __grid_const
   // re-align to 1 KB (the 128B-swizzle atoms must start on 1024-byte boundaries)
   auto* s = reinterpret_cast<GemmSmem<BN, STAGES>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int num_entries = p.tiles ? p.num_entries : p.num_m_blocks;
+  const int num_entries = p.tiles ? (p.num_entries_dev ? min(*p.num_entries_dev, p.num_entries) : p.num_entries)
+                                  : p.num_m_blocks;
   const int total_tiles = num_entries * p.num_n_blocks;
   const int kblocks = (p.K + kBK - 1) / kBK;
   constexpr uint32_t kStageBytes = (kBM + BN) * kBK * 2;
@@ -98,7 +101,7 @@ __global__ void __launch_bounds__(192, 1) gemm_tcgen05_kernel(const __grid_const
     n_blk = t / num_entries;
     if (p.tiles) {
       const GemmTile g = p.tiles[e];
-      a_row = g.a_row0; b_row = g.b_row0 + n_blk * BN; rows = g.rows; out_row = g.out_row0;
+      a_row = g.a_row0; b_row = g.b_row0 * p.b_rows_per_group + n_blk * BN; rows = g.rows; out_row = g.out_row0;
     } else {
       a_row = e * kBM; b_row = n_blk * BN; rows = min(kBM, p.M - e * kBM); out_row = e * kBM;
     }
@@ -271,7 +274,8 @@ static void launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const Gemm
 using namespace hx;
 
 static void gemm_common(torch::Tensor A, torch::Tensor B, torch::Tensor C, int64_t epi, const GemmTile* tiles,
-                        int num_entries, int n_per_group, torch::Tensor err) {
+                        int num_entries, int n_per_group, torch::Tensor err, const int* num_dev = nullptr,
+                        int b_scale = 1) {
   TORCH_CHECK(A.is_cuda() && A.scalar_type() == at::kBFloat16 && A.dim() == 2 && A.stride(1) == 1, "A [M,K] bf16");
   TORCH_CHECK(B.scalar_type() == at::kBFloat16 && B.dim() == 2 && B.stride(1) == 1, "B [N,K] bf16");
   const int M = A.size(0), K = A.size(1);
@@ -283,7 +287,7 @@ static void gemm_common(torch::Tensor A, torch::Tensor B, torch::Tensor C, int64
   p.M = M; p.N = N; p.K = K; p.C = C.data_ptr(); p.ldc = C.stride(0); p.epi = (int)epi;
   p.num_m_blocks = (M + kBM - 1) / kBM;
   p.num_n_blocks = (N + BN - 1) / BN;
-  p.tiles = tiles; p.num_entries = num_entries;
+  p.tiles = tiles; p.num_entries = num_entries; p.num_entries_dev = num_dev; p.b_rows_per_group = b_scale;
   p.err = err.data_ptr<int>();
   if (epi == kEpiSwiGLU) TORCH_CHECK(N % 32 == 0 && C.size(1) * 2 >= N, "SwiGLU output width");
   TORCH_CHECK(C.scalar_type() == (epi == kEpiF32 ? at::kFloat : at::kBFloat16), "output dtype");
@@ -307,4 +311,13 @@ void gemm_grouped(torch::Tensor A, torch::Tensor B, torch::Tensor C, torch::Tens
   TORCH_CHECK(tiles.scalar_type() == at::kInt && tiles.dim() == 2 && tiles.size(1) == 4 && tiles.is_cuda(),
               "tiles int32 [T,4] on device");
   gemm_common(A, B, C, epi, reinterpret_cast<const GemmTile*>(tiles.data_ptr()), tiles.size(0), (int)n, err);
+}
+
+// Grouped with a device-side tile count and tiles naming the group (b_row0 = group index;
+// the kernel scales it by n): the tile table written by moe_route_prefill, no host sync.
+void gemm_grouped_dev(torch::Tensor A, torch::Tensor B, torch::Tensor C, torch::Tensor tiles, torch::Tensor ntiles,
+                      int64_t n, int64_t epi, torch::Tensor err) {
+  TORCH_CHECK(tiles.scalar_type() == at::kInt && tiles.dim() == 2 && tiles.size(1) == 4 && tiles.is_cuda(), "tiles");
+  gemm_common(A, B, C, epi, reinterpret_cast<const GemmTile*>(tiles.data_ptr()), tiles.size(0), (int)n, err,
+              ntiles.data_ptr<int>(), (int)n);
 }

@@ -93,6 +93,104 @@ __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ y, const in
   }
 }
 
+// ---- prefill routing on the device -------------------------------------------------
+// Step 1 (one warp per token): top-k of softmax(logits[t, :E]) -> ids/wts [T, J] (+ shared
+// expert E with sigmoid(logits[t, E]) when has_shared), and per-expert counts.
+__global__ void moe_route_topk_kernel(const float* __restrict__ logits, int ld, int T, int E, int k, int has_shared,
+                                      int norm_topk, int* __restrict__ ids, float* __restrict__ wts,
+                                      int* __restrict__ counts) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= T) return;
+  const int J = k + (has_shared ? 1 : 0);
+  const float* lg = logits + (long long)warp * ld;
+  constexpr int PER = 32;
+  float v[PER];
+  float m = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    int e = lane + 32 * i;
+    v[i] = e < E ? lg[e] : -INFINITY;
+    m = fmaxf(m, v[i]);
+  }
+  m = warp_max(m);
+  float den = 0.f;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) den += (lane + 32 * i) < E ? expf(v[i] - m) : 0.f;
+  den = warp_sum(den);
+  float sel = 0.f, my_p = 0.f;
+  int my_id = -1;
+  for (int j = 0; j < k; ++j) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      int e = lane + 32 * i;
+      if (e < E && (v[i] > bv || (v[i] == bv && e < bi))) { bv = v[i]; bi = e; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    float p = expf(bv - m) / den;
+    sel += p;
+    if (lane == j) { my_id = bi; my_p = p; }
+#pragma unroll
+    for (int i = 0; i < PER; ++i)
+      if (lane + 32 * i == bi) v[i] = -INFINITY;
+  }
+  if (lane < k) {
+    ids[(long long)warp * J + lane] = my_id;
+    wts[(long long)warp * J + lane] = norm_topk ? my_p / sel : my_p;
+    atomicAdd(&counts[my_id], 1);
+  }
+  if (has_shared && lane == 0) {
+    ids[(long long)warp * J + k] = E;
+    wts[(long long)warp * J + k] = 1.f / (1.f + expf(-lg[E]));
+    atomicAdd(&counts[E], 1);
+  }
+}
+
+// Step 2 (one CTA): exclusive scan of counts -> offsets; grouped-GEMM tile table of
+// 128-row blocks (a_row0, group, rows, out_row0); cursor copy for step 3.
+__global__ void moe_route_plan_kernel(const int* __restrict__ counts, int G, int* __restrict__ offsets,
+                                      int* __restrict__ cursor, int* __restrict__ tiles, int* __restrict__ ntiles,
+                                      int max_tiles) {
+  if (threadIdx.x != 0) return;
+  int off = 0, nt = 0;
+  for (int g = 0; g < G; ++g) {
+    const int c = counts[g];
+    offsets[g] = off;
+    cursor[g] = off;
+    for (int m0 = 0; m0 < c && nt < max_tiles; m0 += 128, ++nt) {
+      tiles[nt * 4 + 0] = off + m0;
+      tiles[nt * 4 + 1] = g;
+      tiles[nt * 4 + 2] = min(128, c - m0);
+      tiles[nt * 4 + 3] = off + m0;
+    }
+    off += c;
+  }
+  *ntiles = nt;
+}
+
+// Step 3 (one thread per route): claim a row in its expert's segment, record it, and
+// gather the token's hidden row there (A of the grouped GEMM).
+__global__ void moe_route_place_kernel(const int* __restrict__ ids, int T, int J, int* __restrict__ cursor,
+                                       int* __restrict__ rows, const __nv_bfloat16* __restrict__ hn,
+                                       __nv_bfloat16* __restrict__ A, int H) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= T * J) return;
+  int r = 0;
+  if (lane == 0) r = atomicAdd(&cursor[ids[warp]], 1);
+  r = __shfl_sync(0xffffffffu, r, 0);
+  if (lane == 0) rows[warp] = r;
+  const int t = warp / J;
+  const bf16x8* src = reinterpret_cast<const bf16x8*>(hn + (long long)t * H);
+  bf16x8* dst = reinterpret_cast<bf16x8*>(A + (long long)r * H);
+  for (int v = lane; v < H / 8; v += 32) dst[v] = src[v];
+}
+
 }  // namespace hx
 
 using namespace hx;
@@ -120,5 +218,30 @@ void moe_topk(torch::Tensor logits, int64_t E, int64_t k, bool has_shared, bool 
   moe_topk_kernel<<<B, 32, 0, at::cuda::getCurrentCUDAStream()>>>(
       logits.data_ptr<float>(), logits.size(1), E, k, has_shared, norm_topk, ids.data_ptr<int>(),
       wts.data_ptr<float>(), ids.size(1));
+  HX_CUDA_CHECK(cudaGetLastError());
+}
+
+// Device-side MoE prefill routing. logits [T, ld] f32 -> ids/wts/rows [T, J], tiles
+// [max_tiles, 4] int32 + ntiles [1], A [T*J, H] gathered rows. counts/offsets/cursor are
+// int32 scratch of >= G = E (+1) entries; counts must be zero on entry.
+void moe_route_prefill(torch::Tensor logits, int64_t E, int64_t k, bool has_shared, bool norm_topk, torch::Tensor hn,
+                       torch::Tensor ids, torch::Tensor wts, torch::Tensor rows, torch::Tensor counts,
+                       torch::Tensor offsets, torch::Tensor cursor, torch::Tensor tiles, torch::Tensor ntiles,
+                       torch::Tensor A) {
+  const int T = logits.size(0), H = hn.size(1);
+  const int J = k + (has_shared ? 1 : 0), G = E + (has_shared ? 1 : 0);
+  TORCH_CHECK(E <= 1024 && k <= 32 && H % 8 == 0, "routing limits");
+  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.stride(1) == 1 && hn.is_contiguous(), "logits f32 rows");
+  TORCH_CHECK(ids.size(0) == T && ids.size(1) == J && rows.sizes() == ids.sizes() && A.size(0) >= (long long)T * J,
+              "routing buffer shapes");
+  auto st = at::cuda::getCurrentCUDAStream();
+  moe_route_topk_kernel<<<(T * 32 + 255) / 256, 256, 0, st>>>(logits.data_ptr<float>(), logits.stride(0), T, E, k,
+                                                              has_shared, norm_topk, ids.data_ptr<int>(),
+                                                              wts.data_ptr<float>(), counts.data_ptr<int>());
+  moe_route_plan_kernel<<<1, 32, 0, st>>>(counts.data_ptr<int>(), G, offsets.data_ptr<int>(), cursor.data_ptr<int>(),
+                                          tiles.data_ptr<int>(), ntiles.data_ptr<int>(), tiles.size(0));
+  moe_route_place_kernel<<<((long long)T * J * 32 + 255) / 256, 256, 0, st>>>(
+      ids.data_ptr<int>(), T, J, cursor.data_ptr<int>(), rows.data_ptr<int>(),
+      reinterpret_cast<const __nv_bfloat16*>(hn.data_ptr()), reinterpret_cast<__nv_bfloat16*>(A.data_ptr()), H);
   HX_CUDA_CHECK(cudaGetLastError());
 }

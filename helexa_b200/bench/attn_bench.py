@@ -1,0 +1,62 @@
+"""Standalone decode-attention timing (CUDA events) on one sequence of a given context
+length, small enough for an ncu capture (a few tens of MB on the device).
+
+  python -m helexa_b200.bench.attn_bench --context 8192 --hq 16 --hkv 2 --dim 256 --splits 32
+"""
+from __future__ import annotations
+
+import argparse
+import json
+
+import torch
+
+
+def main():
+    from .. import ops
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--context", type=int, default=8192)
+    ap.add_argument("--hq", type=int, default=16)
+    ap.add_argument("--hkv", type=int, default=2)
+    ap.add_argument("--dim", type=int, default=256)
+    ap.add_argument("--splits", type=int, default=32)
+    ap.add_argument("--iters", type=int, default=50)
+    args = ap.parse_args()
+    C = ops.C
+    D, Hq, Hkv = args.dim, args.hq, args.hkv
+    gated = True
+    qw = 2 * D
+    L = args.context + 16
+    kc = torch.randn(1, Hkv, L, D, device="cuda").bfloat16()
+    vc = torch.randn(1, Hkv, L, D, device="cuda").bfloat16()
+    proj = torch.randn(1, Hq * qw + 2 * Hkv * D, device="cuda").bfloat16()
+    qn = torch.ones(D, device="cuda")
+    inv = (1.0 / (1e7 ** (torch.arange(0, D // 4, 2).float() / (D // 4)))).cuda()
+    part_o = torch.empty(1, Hq, args.splits, D, device="cuda")
+    part_ml = torch.empty(1, Hq, args.splits, 2, device="cuda")
+    cnt = torch.zeros(1, Hkv, dtype=torch.int32, device="cuda")
+    out = torch.empty(1, Hq * D, device="cuda", dtype=torch.bfloat16)
+    slots = torch.zeros(1, dtype=torch.int32, device="cuda")
+    pos = torch.full((1,), args.context, dtype=torch.int32, device="cuda")
+
+    def run():
+        C.attn_decode(proj, qn, qn, inv, kc, vc, slots, pos, part_o, part_ml, cnt, out, Hq, Hkv, D, D // 4, gated,
+                      1e-6)
+
+    for _ in range(5):
+        run()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.iters):
+        run()
+    e1.record()
+    e1.synchronize()
+    us = e0.elapsed_time(e1) / args.iters * 1e3
+    kv_bytes = 2 * Hkv * (args.context + 1) * D * 2
+    print(json.dumps({"context": args.context, "hq": Hq, "hkv": Hkv, "dim": D, "splits": args.splits,
+                      "us": round(us, 2), "kv_MB": round(kv_bytes / 1e6, 2),
+                      "GBps": round(kv_bytes / us / 1e3, 1)}))
+
+
+if __name__ == "__main__":
+    main()

@@ -462,68 +462,57 @@ class FastModel:
         E, k = cfg.num_experts, cfg.num_experts_per_tok
         T = hn.shape[0]
         logits = self._linear(hn, lw["router"], 2)
-        probs = torch.softmax(logits[:, :E], -1)
+        if self.C is not None:
+            return self._moe_prefill_device(lw, hn, logits, E, k)
+        # CPU path (tests without the extension): per-expert loops over sorted routes
+        probs = torch.softmax(logits[:, :E].float(), -1)
         topv, topi = torch.topk(probs, k, -1)
         if cfg.norm_topk_prob:
             topv = topv / topv.sum(-1, keepdim=True)
-        # group the T*k (token, expert) routes by expert; the shared expert is one more
-        # group that every token visits with weight sigmoid(shared_expert_gate(x))
+        out = torch.zeros(T, cfg.hidden_size, dtype=torch.float32, device=hn.device)
         flat = topi.view(-1)
         order = torch.argsort(flat, stable=True)
-        tok_of = order // k
-        w_of = topv.view(-1)[order]
-        counts = torch.bincount(flat, minlength=E)
-        groups_tok, groups_w, cnt = [tok_of], [w_of], [counts]
+        tok_of, w_of = order // k, topv.view(-1)[order]
+        counts = torch.bincount(flat, minlength=E).tolist()
+        start = 0
+        for e, c in enumerate(counts):
+            if c:
+                t = tok_of[start:start + c]
+                y = self._linear(self._linear(hn[t], lw["w_gu"][e], 1), lw["w_d"][e])
+                out.index_add_(0, t, y.float() * w_of[start:start + c, None])
+            start += c
         if self.has_shared:
-            groups_tok.append(torch.arange(T, device=hn.device))
-            groups_w.append(torch.sigmoid(logits[:, E]))
-            cnt.append(torch.tensor([T], device=hn.device))
-        tok_all = torch.cat(groups_tok)
-        w_all = torch.cat(groups_w)
-        counts = torch.cat(cnt).tolist()
-        A = hn[tok_all].contiguous()
-        if self.C is None:
-            y = torch.empty(A.shape[0], cfg.hidden_size, dtype=torch.bfloat16)
-            start = 0
-            for e, c in enumerate(counts):
-                if c:
-                    act = self._linear(A[start:start + c], lw["w_gu"][e], 1)
-                    y[start:start + c] = self._linear(act, lw["w_d"][e])
-                start += c
-        else:
-            tiles, row = [], 0
-            for e, c in enumerate(counts):
-                for m0 in range(0, c, 128):
-                    tiles.append((row + m0, e, min(128, c - m0), row + m0))
-                row += c
-            tt = torch.tensor(tiles, dtype=torch.int32)
-            I2 = lw["w_gu"].shape[1]
-            Hh = lw["w_d"].shape[1]
-            t_gu = tt.clone()
-            t_gu[:, 1] *= I2
-            t_d = tt.clone()
-            t_d[:, 1] *= Hh
-            t_gu, t_d = t_gu.to(hn.device, non_blocking=True), t_d.to(hn.device, non_blocking=True)
-            act = torch.empty(A.shape[0], I2 // 2, dtype=torch.bfloat16, device=hn.device)
-            self.C.gemm_grouped(A, lw["w_gu"].view(-1, lw["w_gu"].shape[-1]), act, t_gu, I2, 1, self._gemm_err())
-            y = torch.empty(A.shape[0], Hh, dtype=torch.bfloat16, device=hn.device)
-            self.C.gemm_grouped(act, lw["w_d"].view(-1, lw["w_d"].shape[-1]), y, t_d, Hh, 0, self._gemm_err())
-        J = k + (1 if self.has_shared else 0)
-        if self.C is not None:
-            # rows[t, j]: where token t's j-th expert output sits in y (inverse of the sort)
-            pos = torch.empty_like(order)
-            pos[order] = torch.arange(order.numel(), device=hn.device)
-            rows = pos.view(T, k)
-            wts = topv
-            if self.has_shared:
-                rows = torch.cat([rows, (T * k + torch.arange(T, device=hn.device))[:, None]], 1)
-                wts = torch.cat([wts, torch.sigmoid(logits[:, E:E + 1])], 1)
-            out = torch.zeros(T, cfg.hidden_size, dtype=torch.bfloat16, device=hn.device)
-            self.C.moe_combine(y, rows.to(torch.int32).contiguous(), wts.float().contiguous(), out)
-            return out
-        out = torch.zeros(T, cfg.hidden_size, dtype=torch.float32, device=hn.device)
-        out.index_add_(0, tok_all, y.float() * w_all[:, None])
+            y = self._linear(self._linear(hn, lw["w_gu"][E], 1), lw["w_d"][E])
+            out += y.float() * torch.sigmoid(logits[:, E:E + 1].float())
         return out.to(torch.bfloat16)
+
+    def _moe_prefill_device(self, lw, hn, logits, E: int, k: int) -> torch.Tensor:
+        """Routing, grouped expert GEMMs and combine with no host synchronisation."""
+        cfg, dev = self.cfg, hn.device
+        T, H = hn.shape
+        shared = self.has_shared
+        J, G = k + int(shared), E + int(shared)
+        i32 = torch.int32
+        ids = torch.empty(T, J, dtype=i32, device=dev)
+        wts = torch.empty(T, J, dtype=torch.float32, device=dev)
+        rows = torch.empty(T, J, dtype=i32, device=dev)
+        counts = torch.zeros(G, dtype=i32, device=dev)
+        offsets = torch.empty(G, dtype=i32, device=dev)
+        cursor = torch.empty(G, dtype=i32, device=dev)
+        tiles = torch.empty((T * J + 127) // 128 + G, 4, dtype=i32, device=dev)
+        ntiles = torch.empty(1, dtype=i32, device=dev)
+        A = torch.empty(T * J, H, dtype=torch.bfloat16, device=dev)
+        self.C.moe_route_prefill(logits, E, k, shared, cfg.norm_topk_prob, hn.contiguous(), ids, wts, rows, counts,
+                                 offsets, cursor, tiles, ntiles, A)
+        I2 = lw["w_gu"].shape[1]
+        act = torch.empty(T * J, I2 // 2, dtype=torch.bfloat16, device=dev)
+        self.C.gemm_grouped_dev(A, lw["w_gu"].view(-1, H), act, tiles, ntiles, I2, 1, self._gemm_err())
+        y = torch.empty(T * J, H, dtype=torch.bfloat16, device=dev)
+        self.C.gemm_grouped_dev(act, lw["w_d"].view(-1, lw["w_d"].shape[-1]), y, tiles, ntiles, H, 0,
+                                self._gemm_err())
+        out = torch.zeros(T, H, dtype=torch.bfloat16, device=dev)
+        self.C.moe_combine(y, rows, wts, out)
+        return out
 
     @torch.no_grad()
     def prefill(self, slot: int, tokens: torch.Tensor, p0: int) -> torch.Tensor:

@@ -72,3 +72,50 @@ def test_gemm_grouped():
         if c:
             _check(C[row:row + c], A[row:row + c].float() @ B[g * N:(g + 1) * N].float().t())
         row += c
+
+
+@pytest.mark.parametrize("shared", [True, False])
+def test_moe_route_prefill_and_grouped_dev(shared):
+    """Device routing (top-k, plan, gather) + grouped GEMMs with a device tile count
+    against a per-token fp32 loop over the selected experts."""
+    torch.manual_seed(3)
+    T, H, E, k, I = 300, 256, 16, 4, 128
+    G, J = E + int(shared), k + int(shared)
+    C = _C()
+    hn = torch.randn(T, H, device="cuda").bfloat16()
+    logits = torch.randn(T, E + 8, device="cuda") * 3
+    w_gu = (torch.randn(G, 2 * I, H, device="cuda") * 0.05).bfloat16()
+    w_d = (torch.randn(G, H, I, device="cuda") * 0.05).bfloat16()
+    i32 = dict(dtype=torch.int32, device="cuda")
+    ids, rows = torch.empty(T, J, **i32), torch.empty(T, J, **i32)
+    wts = torch.empty(T, J, device="cuda")
+    counts, offsets, cursor = torch.zeros(G, **i32), torch.empty(G, **i32), torch.empty(G, **i32)
+    tiles, ntiles = torch.empty((T * J + 127) // 128 + G, 4, **i32), torch.empty(1, **i32)
+    A = torch.empty(T * J, H, device="cuda", dtype=torch.bfloat16)
+    C.moe_route_prefill(logits, E, k, shared, True, hn, ids, wts, rows, counts, offsets, cursor, tiles, ntiles, A)
+    act = torch.empty(T * J, I, device="cuda", dtype=torch.bfloat16)
+    e = _err()
+    C.gemm_grouped_dev(A, w_gu.view(-1, H), act, tiles, ntiles, 2 * I, 1, e)
+    y = torch.empty(T * J, H, device="cuda", dtype=torch.bfloat16)
+    C.gemm_grouped_dev(act, w_d.view(-1, I), y, tiles, ntiles, H, 0, e)
+    out = torch.zeros(T, H, device="cuda", dtype=torch.bfloat16)
+    C.moe_combine(y, rows, wts, out)
+    torch.cuda.synchronize()
+    assert int(e) == 0
+    probs = torch.softmax(logits[:, :E], -1)
+    tv, ti = torch.topk(probs, k, -1)
+    tv = tv / tv.sum(-1, keepdim=True)
+    assert torch.equal(ids[:, :k].long(), ti)
+    assert torch.allclose(wts[:, :k], tv, atol=1e-5)
+    assert sorted(rows.flatten().tolist()) == list(range(T * J))
+    assert torch.equal(A[rows.long()].view(T, J, H), hn[:, None].expand(T, J, H))
+    ref = torch.zeros(T, H, device="cuda")
+    for t in range(T):
+        sel = [(int(ti[t, j]), float(tv[t, j])) for j in range(k)]
+        if shared:
+            sel.append((E, float(torch.sigmoid(logits[t, E]))))
+        for g, w in sel:
+            hgu = hn[t].float() @ w_gu[g].float().t()
+            a = torch.nn.functional.silu(hgu[0::2]) * hgu[1::2]
+            ref[t] += w * (a.bfloat16().float() @ w_d[g].float().t())
+    _check(out, ref, 3e-2)
