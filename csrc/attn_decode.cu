@@ -13,7 +13,11 @@
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 
+#include <cooperative_groups.h>
+
 #include "common.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace hx {
 
@@ -70,31 +74,85 @@ HX_DEVICE void norm_rope_head(float* xv, const float* w, const float* inv_freq, 
   __syncwarp();
 }
 
+// bf16 m16n8k16 tensor-core MMA (f32 accumulate) used for the score tile.
+HX_DEVICE void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                         uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+HX_DEVICE uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// Per-lane slice of one V row in the PV phase (lanes over head dims).
+template <int PER> struct VSlice;
+template <> struct VSlice<8> { using T = uint4; };
+template <> struct VSlice<4> { using T = uint2; };
+template <> struct VSlice<2> { using T = uint32_t; };
+
+template <int PER>
+HX_DEVICE void unpack_slice(const typename VSlice<PER>::T& v, float* f) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+  for (int i = 0; i < PER / 2; ++i) {
+    float2 t = __bfloat1622float2(h[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+
+// Scores on tensor cores: a warp tile of 16 keys against up to 8 query heads is one
+// m16n8k16 chain, S^T[key, head] = K[key, :] . Q[head, :], with K as the A operand
+// loaded straight from the cache. The MMA's k index is a permutation of the head
+// dims (any one works for a dot product, as long as Q uses the same): lane
+// (r = lane/4, c = lane%4) loads the 16-byte chunk at dims 32u + 8c of keys r and
+// r + 8, which supplies its A fragments for k-steps 2u and 2u + 1.
+// The probabilities go through shared memory to the PV phase, where lanes own
+// contiguous head dims and stream V rows with coalesced 16-byte loads.
+// Reduction across splits: the CTAs of one cluster merge their partials through
+// distributed shared memory; one partial per cluster goes to global memory, and the
+// last CTA of the (sequence, kv head) to finish merges those.
 template <int D, int G>
-__global__ void __launch_bounds__(256) attn_decode_kernel(AttnDecodeArgs a) {
-  constexpr int PER = D / 32;   // head dims per lane in the PV phase
-  constexpr int NW = 8;         // warps per CTA
-  constexpr int TILE = 32;      // keys per warp tile (one key per lane in the QK phase)
-  constexpr int MAXS = 64;      // largest split count the merge supports
+__global__ void __launch_bounds__(128, 2) attn_decode_kernel(AttnDecodeArgs a) {
+  constexpr int NW = 4;            // warps per CTA
+  constexpr int TK = 16;           // keys per warp tile
+  constexpr int PER = D / 32;      // head dims per lane in the PV phase
+  constexpr int U = D / 32;        // 16-byte K chunks per key per lane
+  constexpr int S = D / 16;        // MMA k-steps per tile
+  constexpr int NT = (G + 7) / 8;  // MMA n-tiles of 8 heads
+  constexpr int MAXC = 64;         // most cluster partials the final merge supports
+  constexpr int MAXCL = 8;         // largest cluster
+  using VT = typename VSlice<PER>::T;
   extern __shared__ __align__(16) float dsm[];
-  float (*qsm)[D] = reinterpret_cast<float (*)[D]>(dsm);                      // [G][D] normed, roped, scaled
-  float (*tmp)[D] = reinterpret_cast<float (*)[D]>(dsm + G * D);              // [NW][D] rope scratch
-  float (*psm)[G][TILE] = reinterpret_cast<float (*)[G][TILE]>(dsm + (G + NW) * D);  // [NW][G][TILE]
-  float (*wo)[G][D] = reinterpret_cast<float (*)[G][D]>(dsm + (G + NW) * D + NW * G * TILE);  // [NW][G][D]
+  float (*qsm)[D] = reinterpret_cast<float (*)[D]>(dsm);                                  // [G][D]
+  float (*tmp)[D] = reinterpret_cast<float (*)[D]>(dsm + G * D);                          // [NW][D]
+  float (*psm)[TK][G] = reinterpret_cast<float (*)[TK][G]>(dsm + (G + NW) * D);           // [NW][TK][G]
+  float (*wo)[G][D] = reinterpret_cast<float (*)[G][D]>(dsm + (G + NW) * D + NW * TK * G);  // [NW][G][D]
   __shared__ float wm[NW][G], wl[NW][G];
-  __shared__ float cw[G][MAXS];  // merge weights exp(m_s - M) / L per split
+  __shared__ float cm[G], cl[G];                  // this CTA's (max, sum) per head
+  __shared__ float pm[G][MAXCL], pw[G][MAXCL];    // cluster peers' max and merge weights
+  __shared__ float km[G], kl[G];                  // the cluster's (max, sum) per head
+  __shared__ float cw[G][MAXC];
   __shared__ int is_last;
 
+  cg::cluster_group cluster = cg::this_cluster();
+  const int CL = (int)cluster.num_blocks(), crank = (int)cluster.block_rank();
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = lane >> 2, c = lane & 3;
   const int slot = a.slots[b];
   const int qw = a.gated ? 2 * D : D;
   const __nv_bfloat16* pr = a.proj + (long long)b * a.ldp;
   const long long cache_base = ((long long)slot * a.Hkv + kvh) * a.maxlen * D;
   {
-    // KV rows before the current position come from earlier, complete steps: start
-    // pulling this CTA's range into L2 while the projection kernel drains. The
-    // position read here may be one step stale; it only steers the prefetch.
+    // KV rows before the current position come from earlier, complete steps: pull
+    // this CTA's range into L2 while the projection kernel drains. The position read
+    // here may be one step stale; it only steers the prefetch.
     const int ph = a.pos[slot];
     const int ch = (ph + 1 + a.nsplit - 1) / a.nsplit;
     const int t0 = split * ch, t1 = min(ph, t0 + ch);
@@ -111,7 +169,7 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(AttnDecodeArgs a) {
   const int p = a.pos[slot];
   const int L = p + 1;
 
-  // ---- q heads: norm + rope, pre-scaled ----------------------------------
+  // ---- q heads: norm + rope (bf16-exact values; the softmax scale is applied to scores)
   for (int g = warp; g < G; g += NW) {
     const int hq = kvh * G + g;
     float xv[PER];
@@ -119,7 +177,7 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(AttnDecodeArgs a) {
     for (int i = 0; i < PER; ++i) xv[i] = __bfloat162float(pr[hq * qw + lane * PER + i]);
     norm_rope_head<D>(xv, a.q_norm_w, a.inv_freq, a.rot, p, a.eps, tmp[warp]);
 #pragma unroll
-    for (int i = 0; i < PER; ++i) qsm[g][lane * PER + i] = xv[i] * a.scale;
+    for (int i = 0; i < PER; ++i) qsm[g][lane * PER + i] = xv[i];
   }
   const int chunk = (L + a.nsplit - 1) / a.nsplit;
   const int k0 = split * chunk, k1 = min(L, k0 + chunk);
@@ -138,156 +196,273 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(AttnDecodeArgs a) {
   }
   __syncthreads();
 
-  float m[G], l[G], acc[G][PER];
+  // Q as the B operand: head r of n-tile nt, dims permuted as the K loads are
+  uint32_t qb[NT][S][2];
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
-    m[g] = -INFINITY;
-    l[g] = 0.f;
+  for (int nt = 0; nt < NT; ++nt) {
+    const int g = nt * 8 + r;
+#pragma unroll
+    for (int s = 0; s < S; ++s) {
+      const int d0 = 32 * (s >> 1) + 8 * c + 4 * (s & 1);
+      qb[nt][s][0] = g < G ? pack_bf16x2(qsm[g][d0], qsm[g][d0 + 1]) : 0u;
+      qb[nt][s][1] = g < G ? pack_bf16x2(qsm[g][d0 + 2], qsm[g][d0 + 3]) : 0u;
+    }
+  }
+  float m_[NT][2], l_[NT][2], acc[G][PER];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    m_[nt][0] = m_[nt][1] = -INFINITY;
+    l_[nt][0] = l_[nt][1] = 0.f;
+  }
+#pragma unroll
+  for (int g = 0; g < G; ++g)
 #pragma unroll
     for (int i = 0; i < PER; ++i) acc[g][i] = 0.f;
-  }
-  for (int tb = k0 + warp * TILE; tb < k1; tb += NW * TILE) {
-    // ---- QK: lane j scores key tb + j against every q head --------------------
-    const int t = tb + lane;
-    const bool valid = t < k1;
-    float sc[G];
+
+  const __nv_bfloat16* kcb = a.kc + cache_base;
+  const __nv_bfloat16* vcb = a.vc + cache_base;
+  for (int tb = k0 + warp * TK; tb < k1; tb += NW * TK) {
+    const int nk = min(TK, k1 - tb);
+    // rows past the range are clamped to a valid one (finite values, masked below)
+    const uint4* ka = reinterpret_cast<const uint4*>(kcb + (long long)(tb + min(r, nk - 1)) * D);
+    const uint4* kb = reinterpret_cast<const uint4*>(kcb + (long long)(tb + min(r + 8, nk - 1)) * D);
+    uint4 KA[U], KB[U];
 #pragma unroll
-    for (int g = 0; g < G; ++g) sc[g] = 0.f;
-    if (valid) {
-      const bf16x8* kr = reinterpret_cast<const bf16x8*>(a.kc + cache_base + (long long)t * D);
-#pragma unroll 4
-      for (int v = 0; v < D / 8; ++v) {
-        float kf[8];
-        unpack8(kr[v], kf);
+    for (int u = 0; u < U; ++u) {
+      KA[u] = __ldcg(ka + 4 * u + c);
+      KB[u] = __ldcg(kb + 4 * u + c);
+    }
+    // V rows for the PV phase, in flight with the K rows
+    VT VR[TK];
 #pragma unroll
-        for (int g = 0; g < G; ++g) {
-          const float4 q0 = *reinterpret_cast<const float4*>(&qsm[g][v * 8]);
-          const float4 q1 = *reinterpret_cast<const float4*>(&qsm[g][v * 8 + 4]);
-          sc[g] += q0.x * kf[0] + q0.y * kf[1] + q0.z * kf[2] + q0.w * kf[3] + q1.x * kf[4] + q1.y * kf[5] +
-                   q1.z * kf[6] + q1.w * kf[7];
+    for (int j = 0; j < TK; ++j)
+      VR[j] = __ldcg(reinterpret_cast<const VT*>(vcb + (long long)(tb + min(j, nk - 1)) * D) + lane);
+    float sc[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+#pragma unroll
+      for (int s = 0; s < S; ++s) {
+        const uint4& x = KA[s >> 1];
+        const uint4& y = KB[s >> 1];
+        if (s & 1) mma_16816(sc[nt], x.z, y.z, x.w, y.w, qb[nt][s][0], qb[nt][s][1]);
+        else mma_16816(sc[nt], x.x, y.x, x.y, y.y, qb[nt][s][0], qb[nt][s][1]);
+      }
+    }
+    // ---- online softmax: lane holds keys r, r+8 of heads nt*8 + 2c + e ------------
+    float corr[NT][2];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const float s0 = r < nk ? sc[nt][e] * a.scale : -INFINITY;
+        const float s1 = r + 8 < nk ? sc[nt][2 + e] * a.scale : -INFINITY;
+        float mt = fmaxf(s0, s1);
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, o));
+        const float mn = fmaxf(m_[nt][e], mt);
+        const float p0 = __expf(s0 - mn), p1 = __expf(s1 - mn);
+        float ps = p0 + p1;
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+        corr[nt][e] = __expf(m_[nt][e] - mn);
+        l_[nt][e] = l_[nt][e] * corr[nt][e] + ps;
+        m_[nt][e] = mn;
+        const int g = nt * 8 + 2 * c + e;
+        if (g < G) {
+          psm[warp][r][g] = p0;
+          psm[warp][r + 8][g] = p1;
         }
       }
     }
-    // ---- online softmax over the tile -----------------------------------------
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-      const float s = valid ? sc[g] : -INFINITY;
-      const float mt = warp_max(s);
-      const float mn = fmaxf(m[g], mt);
-      const float pe = valid ? __expf(s - mn) : 0.f;
-      const float corr = __expf(m[g] - mn);
-      l[g] = l[g] * corr + warp_sum(pe);
-      m[g] = mn;
+      const float cg_ = __shfl_sync(0xffffffffu, corr[g / 8][g & 1], (g % 8) >> 1);
 #pragma unroll
-      for (int i = 0; i < PER; ++i) acc[g][i] *= corr;
-      psm[warp][g][lane] = pe;
+      for (int i = 0; i < PER; ++i) acc[g][i] *= cg_;
     }
     __syncwarp();
-    // ---- PV: lanes over head dims ----------------------------------------------
-    const int nk = min(TILE, k1 - tb);
-    for (int j = 0; j < nk; ++j) {
-      const __nv_bfloat16* vr = a.vc + cache_base + (long long)(tb + j) * D + lane * PER;
-      float vf[PER];
-      if (PER == 8) {
-        unpack8(*reinterpret_cast<const bf16x8*>(vr), vf);
-      } else {
+    // ---- PV ------------------------------------------------------------------------
 #pragma unroll
-        for (int i = 0; i < PER; ++i) vf[i] = __bfloat162float(vr[i]);
-      }
+    for (int j = 0; j < TK; ++j) {
+      if (j < nk) {
+        float vf[PER];
+        unpack_slice<PER>(VR[j], vf);
 #pragma unroll
-      for (int g = 0; g < G; ++g) {
-        const float pj = psm[warp][g][j];
+        for (int g = 0; g < G; ++g) {
+          const float pj = psm[warp][j][g];
 #pragma unroll
-        for (int i = 0; i < PER; ++i) acc[g][i] = fmaf(pj, vf[i], acc[g][i]);
+          for (int i = 0; i < PER; ++i) acc[g][i] = fmaf(pj, vf[i], acc[g][i]);
+        }
       }
     }
     __syncwarp();
   }
-  // ---- combine warps inside the CTA -------------------------------------
+  // ---- combine the warps of this CTA -------------------------------------------
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
-    if (lane == 0) { wm[warp][g] = m[g]; wl[warp][g] = l[g]; }
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int g = nt * 8 + 2 * c + e;
+      if (r == 0 && g < G) { wm[warp][g] = m_[nt][e]; wl[warp][g] = l_[nt][e]; }
+    }
+#pragma unroll
+  for (int g = 0; g < G; ++g)
 #pragma unroll
     for (int i = 0; i < PER; ++i) wo[warp][g][lane * PER + i] = acc[g][i];
-  }
   __syncthreads();
   for (int t = threadIdx.x; t < G * D; t += blockDim.x) {
-    int g = t / D, d = t - g * D;
+    const int g = t / D, d = t - g * D;
     float M = -INFINITY;
+#pragma unroll
     for (int w = 0; w < NW; ++w) M = fmaxf(M, wm[w][g]);
     float Ls = 0.f, O = 0.f;
     if (M != -INFINITY) {
+#pragma unroll
       for (int w = 0; w < NW; ++w) {
-        float c = __expf(wm[w][g] - M);
-        Ls += wl[w][g] * c;
-        O += wo[w][g][d] * c;
+        const float f = __expf(wm[w][g] - M);
+        Ls += wl[w][g] * f;
+        O += wo[w][g][d] * f;
       }
     }
-    int hq = kvh * G + g;
-    long long pi = (((long long)b * a.Hq + hq) * a.nsplit + split);
-    a.part_o[pi * D + d] = O;
-    if (d == 0) { a.part_ml[pi * 2] = M; a.part_ml[pi * 2 + 1] = Ls; }
+    wo[0][g][d] = O;  // this thread alone reads and writes element (g, d)
+    if (d == 0) { cm[g] = M; cl[g] = Ls; }
   }
-  // ---- last CTA of this (b, kvh) merges the splits -----------------------
+  // ---- merge the cluster's CTAs through distributed shared memory ---------------
+  cluster.sync();
+  for (int t = threadIdx.x; t < G * CL; t += blockDim.x) {
+    const int g = t / CL, q = t - g * CL;
+    pm[g][q] = *cluster.map_shared_rank(&cm[g], q);
+    pw[g][q] = *cluster.map_shared_rank(&cl[g], q);
+  }
+  __syncthreads();
+  if (threadIdx.x < G) {
+    const int g = threadIdx.x;
+    float M = -INFINITY;
+    for (int q = 0; q < CL; ++q) M = fmaxf(M, pm[g][q]);
+    float Ls = 0.f;
+    for (int q = 0; q < CL; ++q) {
+      const float f = M == -INFINITY ? 0.f : __expf(pm[g][q] - M);
+      Ls += pw[g][q] * f;
+      pw[g][q] = f;  // now the peer's weight
+    }
+    km[g] = M;
+    kl[g] = Ls;
+  }
+  __syncthreads();
+  {
+    const int cid = split / CL;
+    const int per = G * D / CL;
+    for (int t = crank * per + threadIdx.x; t < (crank + 1) * per; t += blockDim.x) {
+      const int g = t / D, d = t - g * D;
+      float O = 0.f;
+      for (int q = 0; q < CL; ++q) O += pw[g][q] * cluster.map_shared_rank(&wo[0][g][0], q)[d];
+      const long long pi = ((long long)b * a.Hq + kvh * G + g) * a.nsplit + cid;
+      a.part_o[pi * D + d] = O;
+      if (d == 0) { a.part_ml[pi * 2] = km[g]; a.part_ml[pi * 2 + 1] = kl[g]; }
+    }
+  }
+  cluster.sync();  // peers' shared memory stays alive until every read of it is done
+  // ---- last CTA of this (b, kvh) merges the cluster partials --------------------
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
-    int prev = atomicAdd(&a.counters[b * a.Hkv + kvh], 1);
+    const int prev = atomicAdd(&a.counters[b * a.Hkv + kvh], 1);
     is_last = (prev == a.nsplit - 1);
   }
   __syncthreads();
   if (!is_last) return;
   __threadfence();
-  // per head: one warp reads the split (max, sum) pairs and turns them into weights
+  const int nc = a.nsplit / CL;
   for (int g = warp; g < G; g += NW) {
     const long long base = ((long long)b * a.Hq + kvh * G + g) * a.nsplit;
     float ms[2], ls[2];
 #pragma unroll
     for (int q = 0; q < 2; ++q) {
       const int s2 = lane + 32 * q;
-      ms[q] = s2 < a.nsplit ? __ldcg(&a.part_ml[(base + s2) * 2]) : -INFINITY;
-      ls[q] = s2 < a.nsplit ? __ldcg(&a.part_ml[(base + s2) * 2 + 1]) : 0.f;
+      ms[q] = s2 < nc ? __ldcg(&a.part_ml[(base + s2) * 2]) : -INFINITY;
+      ls[q] = s2 < nc ? __ldcg(&a.part_ml[(base + s2) * 2 + 1]) : 0.f;
     }
     const float M = warp_max(fmaxf(ms[0], ms[1]));
-    float c[2], lsum = 0.f;
+    float f[2], lsum = 0.f;
 #pragma unroll
     for (int q = 0; q < 2; ++q) {
-      c[q] = ms[q] == -INFINITY ? 0.f : __expf(ms[q] - M);
-      lsum += ls[q] * c[q];
+      f[q] = ms[q] == -INFINITY ? 0.f : __expf(ms[q] - M);
+      lsum += ls[q] * f[q];
     }
     lsum = warp_sum(lsum);
 #pragma unroll
     for (int q = 0; q < 2; ++q)
-      if (lane + 32 * q < MAXS) cw[g][lane + 32 * q] = c[q] / lsum;
+      if (lane + 32 * q < MAXC) cw[g][lane + 32 * q] = f[q] / lsum;
   }
   __syncthreads();
-  for (int t = threadIdx.x; t < G * D; t += blockDim.x) {
-    const int g = t / D, d = t - g * D;
-    const int hq = kvh * G + g;
-    const long long base = ((long long)b * a.Hq + hq) * a.nsplit;
-    float O = 0.f;
-#pragma unroll 8
-    for (int s2 = 0; s2 < a.nsplit; ++s2) O += cw[g][s2] * __ldcg(&a.part_o[(base + s2) * D + d]);
-    float o = __bfloat162float(__float2bfloat16(O));
-    if (a.gated) {
-      float gt = __bfloat162float(pr[hq * qw + D + d]);
-      o = o * (1.f / (1.f + __expf(-gt)));
+  // float4 columns; each thread keeps all its columns' loads of 8 partials in flight
+  constexpr int V4 = G * D / 4;
+  constexpr int PT = (V4 + NW * 32 - 1) / (NW * 32);
+  float4 O[PT];
+#pragma unroll
+  for (int j = 0; j < PT; ++j) O[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+  const float4* po = reinterpret_cast<const float4*>(a.part_o) + ((long long)b * a.Hq + kvh * G) * a.nsplit * (D / 4);
+  for (int s0 = 0; s0 < nc; s0 += 8) {
+    float4 v[PT][8];
+#pragma unroll
+    for (int j = 0; j < PT; ++j) {
+      const int t4 = threadIdx.x + j * NW * 32;
+      const int g = t4 / (D / 4), d4 = t4 - g * (D / 4);
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        v[j][u] = (t4 < V4 && s0 + u < nc) ? __ldcg(po + ((long long)g * a.nsplit + s0 + u) * (D / 4) + d4)
+                                           : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    a.out[(long long)b * a.Hq * D + hq * D + d] = __float2bfloat16(o);
+#pragma unroll
+    for (int j = 0; j < PT; ++j) {
+      const int t4 = threadIdx.x + j * NW * 32;
+      const int g = min(t4 / (D / 4), G - 1);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const float w = s0 + u < nc ? cw[g][s0 + u] : 0.f;
+        O[j].x += w * v[j][u].x; O[j].y += w * v[j][u].y; O[j].z += w * v[j][u].z; O[j].w += w * v[j][u].w;
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < PT; ++j) {
+    const int t4 = threadIdx.x + j * NW * 32;
+    if (t4 >= V4) continue;
+    const int g = t4 / (D / 4), d = (t4 - g * (D / 4)) * 4;
+    const int hq = kvh * G + g;
+    const float ov[4] = {O[j].x, O[j].y, O[j].z, O[j].w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float o = __bfloat162float(__float2bfloat16(ov[e]));
+      if (a.gated) {
+        const float gt = __bfloat162float(pr[hq * qw + D + d + e]);
+        o = o * (1.f / (1.f + __expf(-gt)));
+      }
+      a.out[(long long)b * a.Hq * D + hq * D + d + e] = __float2bfloat16(o);
+    }
   }
   if (threadIdx.x == 0) a.counters[b * a.Hkv + kvh] = 0;
 }
 
+// Cluster size for a split count: the largest of 8, 4, 2, 1 that divides it.
+static inline int attn_cluster(int nsplit) {
+  for (int c = 8; c > 1; c >>= 1)
+    if (nsplit % c == 0) return c;
+  return 1;
+}
+
 template <int D, int G>
 static void launch_dg(const AttnDecodeArgs& a, dim3 grid, cudaStream_t s) {
-  constexpr int NW = 8, TILE = 32;
-  TORCH_CHECK(a.nsplit >= 1 && a.nsplit <= 64, "attention decode supports 1..64 splits");
-  const size_t smem = (size_t)(G * D + NW * D + NW * G * TILE + NW * G * D) * sizeof(float);
+  constexpr int NW = 4, TK = 16;
+  const int CL = attn_cluster(a.nsplit);
+  TORCH_CHECK(a.nsplit >= 1 && a.nsplit / CL <= 64, "attention decode: nsplit / cluster size must be <= 64");
+  const size_t smem = (size_t)(G * D + NW * D + NW * TK * G + NW * G * D) * sizeof(float);
   auto k = attn_decode_kernel<D, G>;
   if (smem + 4096 > 48 * 1024) {
     HX_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   }
-  HX_CUDA_CHECK(hx_launch_pdl(k, grid, dim3(NW * 32), smem, s, a));
+  HX_CUDA_CHECK(hx_launch_pdl_cluster(k, grid, dim3(NW * 32), smem, s, CL, a));
 }
 
 template <int D>
@@ -297,6 +472,9 @@ static void launch_g(const AttnDecodeArgs& a, int G, dim3 grid, cudaStream_t s) 
     case 2: launch_dg<D, 2>(a, grid, s); break;
     case 4: launch_dg<D, 4>(a, grid, s); break;
     case 8: launch_dg<D, 8>(a, grid, s); break;
+    case 16:
+      if constexpr (D <= 128) { launch_dg<D, 16>(a, grid, s); break; }
+      [[fallthrough]];
     default: TORCH_CHECK(false, "unsupported GQA group size ", G);
   }
 }
@@ -412,7 +590,10 @@ int na_launch(const hx::AttnDecodeArgs& a, int G, dim3 grid, cudaStream_t st) {
       case 2: hx::launch_dg<D, 2>(a, grid, st); break;
       case 4: hx::launch_dg<D, 4>(a, grid, st); break;
       case 8: hx::launch_dg<D, 8>(a, grid, st); break;
-      default: return na_fail(2, "unsupported GQA group size (Hq / Hkv must be 1, 2, 4 or 8)");
+      case 16:
+        if constexpr (D <= 128) { hx::launch_dg<D, 16>(a, grid, st); break; }
+        [[fallthrough]];
+      default: return na_fail(2, "unsupported GQA group size (Hq / Hkv must be 1, 2, 4, 8, or 16 with head dim <= 128)");
     }
   } catch (const std::exception& ex) {
     return na_fail(7, ex.what());

@@ -120,3 +120,31 @@ static inline cudaError_t hx_launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
+
+// Same, with thread-block clusters of `cluster_x` CTAs along x (grid.x must divide).
+template <typename... KArgs, typename... Args>
+static inline cudaError_t hx_launch_pdl_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                                cudaStream_t st, int cluster_x, Args&&... args) {
+  cudaFuncAttributes fa;
+  cudaError_t e = cudaFuncGetAttributes(&fa, reinterpret_cast<const void*>(kernel));
+  if (e != cudaSuccess) return e;
+  if ((int)(block.x * block.y * block.z) > fa.maxThreadsPerBlock ||
+      (long long)smem > (long long)fa.maxDynamicSharedSizeBytes || cluster_x < 1 || cluster_x > 8 ||
+      grid.x % cluster_x)
+    return cudaErrorInvalidConfiguration;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = hx_pdl_enabled() ? 1 : 0;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = cluster_x;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}

@@ -20,6 +20,7 @@ def main():
     ap.add_argument("--dim", type=int, default=256)
     ap.add_argument("--splits", type=int, default=32)
     ap.add_argument("--iters", type=int, default=50)
+    ap.add_argument("--graph", action="store_true", help="time replays of a CUDA graph of the launches")
     args = ap.parse_args()
     C = ops.C
     D, Hq, Hkv = args.dim, args.hq, args.hkv
@@ -45,15 +46,31 @@ def main():
     for _ in range(5):
         run()
     torch.cuda.synchronize()
+    body = run
+    if args.graph:
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                for _ in range(args.iters):
+                    run()
+        torch.cuda.current_stream().wait_stream(s)
+        g.replay()
+        torch.cuda.synchronize()
+        body = None
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    for _ in range(args.iters):
-        run()
+    if body is None:
+        g.replay()
+    else:
+        for _ in range(args.iters):
+            body()
     e1.record()
     e1.synchronize()
     us = e0.elapsed_time(e1) / args.iters * 1e3
     kv_bytes = 2 * Hkv * (args.context + 1) * D * 2
-    print(json.dumps({"context": args.context, "hq": Hq, "hkv": Hkv, "dim": D, "splits": args.splits,
+    print(json.dumps({"context": args.context, "hq": Hq, "hkv": Hkv, "dim": D, "splits": args.splits, "graph": args.graph,
                       "us": round(us, 2), "kv_MB": round(kv_bytes / 1e6, 2),
                       "GBps": round(kv_bytes / us / 1e3, 1)}))
 

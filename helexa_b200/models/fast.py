@@ -102,9 +102,8 @@ class FastModel:
         self.has_shared = cfg.shared_expert_intermediate_size > 0
         sm = torch.cuda.get_device_properties(device).multi_processor_count if device.type == "cuda" else 1
         self.sms = sm
-        # split-K width of decode attention: about 64 CTAs per sequence in total, so the
-        # per-head merge of the partials stays cheap
-        self.attn_splits = attn_splits or max(4, min(64, 64 // max(1, dims.hkv)))
+        # split-K width of decode attention (None: per batch size, see _splits_for)
+        self.attn_splits = attn_splits
         # ---- state pools -------------------------------------------------
         self.pos = torch.zeros(max_slots, dtype=torch.int32, device=device)
         self.kc: dict[int, torch.Tensor] = {}
@@ -191,6 +190,16 @@ class FastModel:
     # ------------------------------------------------------------------
     # decode
     # ------------------------------------------------------------------
+    def _splits_for(self, B: int) -> int:
+        """Decode-attention split count: about one 128-thread CTA per SM over all
+        (sequence, kv head) pairs (measured best at 8K context: 64-104 splits per kv
+        head for 2 kv heads), a multiple of 8 so the splits form 8-CTA clusters that
+        merge on chip, leaving few partials for the final cross-cluster merge."""
+        if self.attn_splits:
+            return self.attn_splits
+        want = self.sms // max(1, B * max(1, self.dims.hkv))
+        return max(8, min(256, (want + 7) // 8 * 8))
+
     def buffers(self, B: int, out_cap: int = 4096) -> DecodeBuffers:
         if B in self._bufs:
             return self._bufs[B]
@@ -205,8 +214,8 @@ class FastModel:
             gdn_out=z(B, d.gdn_vd) if cfg.num_linear_layers else None,
             proj_attn=z(B, d.qkv_rows) if cfg.num_full_layers else None,
             attn_out=z(B, d.hq * d.D) if cfg.num_full_layers else None,
-            part_o=z(B, d.hq, self.attn_splits, d.D, dt=f32) if cfg.num_full_layers else None,
-            part_ml=z(B, d.hq, self.attn_splits, 2, dt=f32) if cfg.num_full_layers else None,
+            part_o=z(B, d.hq, self._splits_for(B), d.D, dt=f32) if cfg.num_full_layers else None,
+            part_ml=z(B, d.hq, self._splits_for(B), 2, dt=f32) if cfg.num_full_layers else None,
             counters=z(B, max(1, d.hkv), dt=i32) if cfg.num_full_layers else None,
             rlogits=z(B, cfg.num_experts + (1 if self.has_shared else 0), dt=f32) if cfg.num_experts else None,
             ids=z(B, J, dt=i32) if cfg.num_experts else None,

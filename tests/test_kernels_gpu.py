@@ -116,8 +116,12 @@ def test_gdn_decode_matches_recurrent(Dk, Hk, Hv):
         assert torch.equal(ring[s][:, p % K], proj[b, :Cc])
 
 
-@pytest.mark.parametrize("D,Hq,Hkv,gated,L", [(256, 16, 2, True, 700), (128, 32, 8, False, 1500), (64, 4, 2, True, 3)])
-def test_attn_decode(D, Hq, Hkv, gated, L):
+@pytest.mark.parametrize("D,Hq,Hkv,gated,L,ns", [(256, 16, 2, True, 700, 16), (256, 16, 2, True, 1900, 152),
+                                                 (128, 32, 8, False, 1500, 12), (64, 4, 2, True, 3, 5),
+                                                 (128, 64, 4, False, 999, 8), (256, 8, 4, True, 64, 40)])
+def test_attn_decode(D, Hq, Hkv, gated, L, ns):
+    """Split counts cover 8-, 4- and 1-CTA clusters, 19 cluster partials, more splits
+    than keys, and 16 query heads per kv head."""
     C = _C()
     torch.manual_seed(2)
     S, maxlen, B = 2, 2048, 2
@@ -132,7 +136,6 @@ def test_attn_decode(D, Hq, Hkv, gated, L):
     kn = torch.rand(D, device="cuda") + 0.5
     theta = 1e7
     inv = 1.0 / (theta ** (torch.arange(0, rot, 2, dtype=torch.int64).float() / rot)).cuda()
-    ns = 16
     part_o = torch.empty(B, Hq, ns, D, device="cuda")
     part_ml = torch.empty(B, Hq, ns, 2, device="cuda")
     cnt = torch.zeros(B, Hkv, dtype=torch.int32, device="cuda")
