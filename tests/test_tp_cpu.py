@@ -39,7 +39,10 @@ def _worker(rank, ws, port, name, q):
         fm = F.FastModel.from_hf(cfg, w, "cpu", rank=rank, ws=ws, max_slots=1, max_len=128, comm=comm)
         prompt = torch.randint(0, cfg.vocab_size, (70,), generator=torch.Generator().manual_seed(1)).int()
         out = fm.prefill(0, prompt, 0)
-        q.put((rank, out))
+        # a numpy copy travels by value (a tensor would be shared through the child's
+        # resource sharer, which goes away when the child exits)
+        q.put((rank, out.float().numpy()))
+        dist.barrier()  # no rank tears gloo down while a peer's last message is in flight
     finally:
         dist.destroy_process_group()
 
@@ -66,7 +69,7 @@ def test_tp_matches_single_rank(name, ws):
     procs = [ctx.Process(target=_worker, args=(r, ws, port, name, q)) for r in range(ws)]
     for p in procs:
         p.start()
-    res = dict(q.get(timeout=300) for _ in range(ws))
+    res = {r: torch.from_numpy(a) for r, a in (q.get(timeout=300) for _ in range(ws))}
     for p in procs:
         p.join(60)
         assert p.exitcode == 0
