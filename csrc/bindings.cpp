@@ -16,6 +16,11 @@ void attn_decode(torch::Tensor proj, c10::optional<torch::Tensor> q_norm_w, c10:
                  torch::Tensor inv_freq, torch::Tensor kc, torch::Tensor vc, torch::Tensor slots, torch::Tensor pos,
                  torch::Tensor part_o, torch::Tensor part_ml, torch::Tensor counters, torch::Tensor out, int64_t Hq,
                  int64_t Hkv, int64_t D, int64_t rot, bool gated, double eps);
+void gemv_ar(torch::Tensor W, torch::Tensor inp, torch::Tensor x, std::vector<int64_t> bases, int64_t rank,
+             int64_t slot_elems, torch::Tensor epoch, torch::Tensor err, double timeout_s);
+void moe_down_ar(torch::Tensor Wd, torch::Tensor act, torch::Tensor ids, torch::Tensor wts, torch::Tensor x,
+                 std::vector<int64_t> bases, int64_t rank, int64_t slot_elems, torch::Tensor epoch, torch::Tensor err,
+                 double timeout_s);
 void moe_combine(torch::Tensor y, torch::Tensor rows, torch::Tensor wts, torch::Tensor x);
 void moe_route_prefill(torch::Tensor logits, int64_t E, int64_t k, bool has_shared, bool norm_topk, torch::Tensor hn,
                        torch::Tensor ids, torch::Tensor wts, torch::Tensor rows, torch::Tensor counts,
@@ -65,6 +70,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_topk", &moe_topk);
   m.def("moe_down", &moe_down);
   m.def("moe_combine", &moe_combine);
+  m.def("gemv_ar", &gemv_ar);
+  m.def("moe_down_ar", &moe_down_ar);
   m.def("moe_route_prefill", &moe_route_prefill);
   m.def("gemm_grouped_dev", &gemm_grouped_dev);
   m.def("gdn_decode", &gdn_decode);

@@ -22,10 +22,12 @@
 #include <ATen/cuda/CUDAContext.h>
 
 #include "common.cuh"
+#include "tp_fused.cuh"
 
 namespace hx {
 
-enum GemvMode : int { kStoreBf16 = 0, kResidAdd = 1, kSiluPair = 2, kStoreF32 = 3, kRouter = 4, kArgmax = 5 };
+enum GemvMode : int { kStoreBf16 = 0, kResidAdd = 1, kSiluPair = 2, kStoreF32 = 3, kRouter = 4, kArgmax = 5,
+                      kResidAddTP = 6 };
 
 struct GemvArgs {
   const __nv_bfloat16* W;     // [N, K] (or [E, N, K] when ids != nullptr)
@@ -51,6 +53,7 @@ struct GemvArgs {
   int* out_tokens;
   int out_cap;
   int* step;
+  TPPush tp;                  // kResidAddTP: cross-rank reduction fused into the epilogue
 };
 
 // Order-preserving key of a float (larger float -> larger key), index tiebreak to the
@@ -177,6 +180,33 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
 #pragma unroll
     for (int b = 0; b < B; ++b) acc[r][b] = warp_sum(acc[r][b]);
 
+  if constexpr (MODE == kResidAddTP) {
+    // x += sum over ranks of W_r . inp_r: exchange this CTA's rows with the same CTA on
+    // every peer, then add the rank-ordered sum to the residual
+    const unsigned e = tp_epoch(a.tp);
+    const bool pushes = active && lane == 0;
+    if (pushes) {
+#pragma unroll
+      for (int b = 0; b < B; ++b)
+#pragma unroll
+        for (int r = 0; r < RPW; ++r)
+          if (row0 + r < a.N) tp_push(a.tp, e, b * a.N + row0 + r, acc[r][b]);
+    }
+    if (tp_exchange(a.tp, e, blockIdx.x, pushes) && pushes) {
+#pragma unroll
+      for (int b = 0; b < B; ++b)
+#pragma unroll
+        for (int r = 0; r < RPW; ++r) {
+          const int n = row0 + r;
+          if (n >= a.N) break;
+          const long long o = (long long)b * a.ldy + n;
+          const float br = __bfloat162float(__float2bfloat16(tp_sum(a.tp, e, b * a.N + n)));
+          reinterpret_cast<__nv_bfloat16*>(a.y)[o] = __float2bfloat16(__bfloat162float(a.resid[o]) + br);
+        }
+    }
+    tp_finish(a.tp, e, gridDim.x);
+    return;
+  }
   if (active && lane == 0) {
     const int yrow = a.ids ? job : 0;
 #pragma unroll
@@ -358,12 +388,12 @@ static void launch_mode(const GemvArgs& a, int B, cudaStream_t s) {
 // (or partial[b, h] = the sum, for tensor-parallel partial sums).
 // grid (ceil(H / 8), B), 256 threads; VPL = ceil(I / 256) 16-byte vectors per lane and
 // expert row; J <= 16.
-template <int VPL>
+template <int VPL, bool TP>
 __global__ void __launch_bounds__(256) moe_down_kernel(const __nv_bfloat16* __restrict__ Wd,
                                                        const __nv_bfloat16* __restrict__ act,
                                                        const int* __restrict__ ids, const float* __restrict__ wts,
                                                        __nv_bfloat16* x, __nv_bfloat16* partial_out, int H, int I,
-                                                       int J) {
+                                                       int J, TPPush tp) {
   extern __shared__ __align__(16) __nv_bfloat16 acts[];  // [J][I] routing-weight scaled
   pdl_wait_prior();
   pdl_launch_dependents();
@@ -396,11 +426,11 @@ __global__ void __launch_bounds__(256) moe_down_kernel(const __nv_bfloat16* __re
     reinterpret_cast<bf16x8*>(acts)[t] = pack8(f);
   }
   __syncthreads();
-  if (h >= H) return;
+  if (!TP && h >= H) return;
   float acc = 0.f;
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
-    if (j < J) {
+    if (j < J && h < H) {
 #pragma unroll
       for (int q = 0; q < VPL; ++q) {
         if (lane + 32 * q >= I / 8) break;
@@ -413,6 +443,18 @@ __global__ void __launch_bounds__(256) moe_down_kernel(const __nv_bfloat16* __re
     }
   }
   acc = warp_sum(acc);
+  if constexpr (TP) {
+    const unsigned e = tp_epoch(tp);
+    const int cta = blockIdx.y * gridDim.x + blockIdx.x;
+    const bool pushes = lane == 0 && h < H;
+    if (pushes) tp_push(tp, e, b * H + h, acc);
+    if (tp_exchange(tp, e, cta, pushes) && pushes) {
+      const float br = __bfloat162float(__float2bfloat16(tp_sum(tp, e, b * H + h)));
+      x[(long long)b * H + h] = __float2bfloat16(__bfloat162float(x[(long long)b * H + h]) + br);
+    }
+    tp_finish(tp, e, gridDim.x * gridDim.y);
+    return;
+  }
   if (lane == 0) {
     if (partial_out) {
       partial_out[(long long)b * H + h] = __float2bfloat16(acc);
@@ -538,37 +580,97 @@ void gemv_experts(torch::Tensor W, torch::Tensor x, torch::Tensor ids, torch::Te
   else TORCH_CHECK(false, "unsupported expert gemv mode");
 }
 
-void moe_down(torch::Tensor Wd, torch::Tensor act, torch::Tensor ids, torch::Tensor wts, torch::Tensor x,
-              c10::optional<torch::Tensor> partial_out) {
+template <int V, bool TP>
+static void launch_moe_down(dim3 grid, size_t smem, cudaStream_t st, const __nv_bfloat16* wp,
+                            const __nv_bfloat16* ap, const int* ids, const float* wts, __nv_bfloat16* xp,
+                            __nv_bfloat16* pp, int H, int I, int J, const TPPush& tp) {
+  auto k = moe_down_kernel<V, TP>;
+  if (smem + 4096 > 48 * 1024) {
+    HX_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  }
+  HX_CUDA_CHECK(hx_launch_pdl(k, grid, dim3(256), smem, st, wp, ap, ids, wts, xp, pp, H, I, J, tp));
+}
+
+template <bool TP>
+static void moe_down_impl(torch::Tensor Wd, torch::Tensor act, torch::Tensor ids, torch::Tensor wts, torch::Tensor x,
+                          c10::optional<torch::Tensor> partial_out, const TPPush& tp) {
   TORCH_CHECK(Wd.dim() == 3 && Wd.scalar_type() == at::kBFloat16 && Wd.is_contiguous(), "Wd [E,H,I] bf16");
   const int H = Wd.size(1), I = Wd.size(2);
   const int B = x.size(0), J = ids.size(1);
   TORCH_CHECK(J <= 16, "at most 16 experts per token");
   TORCH_CHECK(act.size(-1) == I && act.is_contiguous(), "act [B*J, I] contiguous");
   TORCH_CHECK(x.size(1) == H && x.scalar_type() == at::kBFloat16, "x [B,H] bf16");
+  TORCH_CHECK(I % 8 == 0, "moe_down: expert intermediate size must be a multiple of 8");
   const size_t smem = (size_t)J * I * sizeof(__nv_bfloat16);
   dim3 grid((H + 7) / 8, B);
+  if (TP) {
+    TORCH_CHECK((long long)grid.x * grid.y <= kTPMaxCtas, "moe_down: too many CTAs for the fused reduction");
+    TORCH_CHECK((long long)B * H <= tp.slot_elems, "moe_down: output larger than the receive slot");
+  }
   auto st = at::cuda::getCurrentCUDAStream();
   auto xp = reinterpret_cast<__nv_bfloat16*>(x.data_ptr());
   auto pp = partial_out ? reinterpret_cast<__nv_bfloat16*>(partial_out->data_ptr()) : nullptr;
   auto wp = reinterpret_cast<const __nv_bfloat16*>(Wd.data_ptr());
   auto ap = reinterpret_cast<const __nv_bfloat16*>(act.data_ptr());
-#define HX_MOE_DOWN(V)                                                                                          \
-  {                                                                                                             \
-    auto k = moe_down_kernel<V>;                                                                                \
-    if (smem + 4096 > 48 * 1024) {                                                                                     \
-      HX_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));           \
-    }                                                                                                           \
-    HX_CUDA_CHECK(hx_launch_pdl(k, grid, dim3(256), smem, st, wp, ap, (const int*)ids.data_ptr<int>(),          \
-                                (const float*)wts.data_ptr<float>(), xp, pp, H, I, J));                          \
-  }
-  TORCH_CHECK(I % 8 == 0, "moe_down: expert intermediate size must be a multiple of 8");
+  const int* ip = ids.data_ptr<int>();
+  const float* wtp = wts.data_ptr<float>();
   const int vpl = (I / 8 + 31) / 32;
-  if (vpl == 1) HX_MOE_DOWN(1)
-  else if (vpl == 2) HX_MOE_DOWN(2)
-  else if (vpl == 3) HX_MOE_DOWN(3)
-  else if (vpl == 4) HX_MOE_DOWN(4)
-  else if (vpl <= 6) HX_MOE_DOWN(6)
+  if (vpl == 1) launch_moe_down<1, TP>(grid, smem, st, wp, ap, ip, wtp, xp, pp, H, I, J, tp);
+  else if (vpl == 2) launch_moe_down<2, TP>(grid, smem, st, wp, ap, ip, wtp, xp, pp, H, I, J, tp);
+  else if (vpl == 3) launch_moe_down<3, TP>(grid, smem, st, wp, ap, ip, wtp, xp, pp, H, I, J, tp);
+  else if (vpl == 4) launch_moe_down<4, TP>(grid, smem, st, wp, ap, ip, wtp, xp, pp, H, I, J, tp);
+  else if (vpl <= 6) launch_moe_down<6, TP>(grid, smem, st, wp, ap, ip, wtp, xp, pp, H, I, J, tp);
   else TORCH_CHECK(false, "moe_down: expert intermediate size per rank must be <= 1536");
-#undef HX_MOE_DOWN
+}
+
+void moe_down(torch::Tensor Wd, torch::Tensor act, torch::Tensor ids, torch::Tensor wts, torch::Tensor x,
+              c10::optional<torch::Tensor> partial_out) {
+  moe_down_impl<false>(Wd, act, ids, wts, x, partial_out, TPPush{});
+}
+
+static TPPush make_tp(const std::vector<int64_t>& bases, int64_t rank, int64_t slot_elems, torch::Tensor epoch,
+                      torch::Tensor err, double timeout_s) {
+  TORCH_CHECK(bases.size() >= 1 && bases.size() <= (size_t)kTPMaxRanks, "1..8 ranks");
+  TORCH_CHECK(rank >= 0 && rank < (int64_t)bases.size(), "rank out of range");
+  TORCH_CHECK(epoch.is_cuda() && epoch.scalar_type() == at::kInt && epoch.numel() >= 2, "epoch: int32[2] on device");
+  TORCH_CHECK(err.is_cuda() && err.scalar_type() == at::kInt, "err: int32 on device");
+  TPPush t{};
+  for (size_t r = 0; r < bases.size(); ++r) t.base[r] = reinterpret_cast<char*>(bases[r]);
+  t.rank = (int)rank;
+  t.ws = (int)bases.size();
+  t.slot_elems = (int)slot_elems;
+  t.epoch = reinterpret_cast<unsigned*>(epoch.data_ptr());
+  t.err = err.data_ptr<int>();
+  t.timeout_ns = (unsigned long long)(timeout_s * 1e9);
+  return t;
+}
+
+// MoE down projection of this rank's expert shards, then the cross-rank sum added to
+// the residual, in one launch (peer exchange in the epilogue).
+void moe_down_ar(torch::Tensor Wd, torch::Tensor act, torch::Tensor ids, torch::Tensor wts, torch::Tensor x,
+                 std::vector<int64_t> bases, int64_t rank, int64_t slot_elems, torch::Tensor epoch, torch::Tensor err,
+                 double timeout_s) {
+  moe_down_impl<true>(Wd, act, ids, wts, x, c10::nullopt, make_tp(bases, rank, slot_elems, epoch, err, timeout_s));
+}
+
+// x[B, N] += sum over ranks of W_r[N, K] . inp_r[B, K]: a row-parallel linear, its
+// all-reduce and the residual add in one launch.
+void gemv_ar(torch::Tensor W, torch::Tensor inp, torch::Tensor x, std::vector<int64_t> bases, int64_t rank,
+             int64_t slot_elems, torch::Tensor epoch, torch::Tensor err, double timeout_s) {
+  check_w(W);
+  TORCH_CHECK(inp.scalar_type() == at::kBFloat16 && inp.is_contiguous() && inp.dim() == 2, "inp: [B,K] bf16");
+  const int N = W.size(0), K = W.size(1), B = inp.size(0);
+  TORCH_CHECK(inp.size(1) == K && K % 8 == 0, "K mismatch or not a multiple of 8");
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.is_contiguous() && x.size(0) == B && x.size(1) == N,
+              "x: [B,N] bf16 contiguous");
+  TORCH_CHECK(B >= 1 && B <= 64 && (long long)B * N <= slot_elems, "batch / receive slot size");
+  TORCH_CHECK((N + 15) / 16 <= kTPMaxCtas, "too many CTAs for the fused reduction");
+  GemvArgs a{};
+  a.W = reinterpret_cast<const __nv_bfloat16*>(W.data_ptr());
+  a.x = reinterpret_cast<const __nv_bfloat16*>(inp.data_ptr());
+  a.y = x.data_ptr();
+  a.resid = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
+  a.N = N; a.K = K; a.ldy = N; a.x_row_div = 1;
+  a.tp = make_tp(bases, rank, slot_elems, epoch, err, timeout_s);
+  launch_mode<kResidAddTP>(a, B, at::cuda::getCurrentCUDAStream());
 }

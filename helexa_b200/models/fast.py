@@ -232,6 +232,8 @@ class FastModel:
         """x += W . inp, summed across TP ranks when the layer is sharded."""
         if self.comm is None or self.dims.ws == 1:
             self.C.gemv(W, inp, nb.x, ops.RESID_ADD, nb.x, None, 0.0)
+        elif self.comm.fused:
+            self.C.gemv_ar(W, inp, nb.x, *self.comm.fused_args())
         else:
             self.C.gemv(W, inp, nb.partial, ops.STORE_BF16, None, None, 0.0)
             self.comm.reduce_residual(nb.partial, nb.x)
@@ -285,6 +287,8 @@ class FastModel:
             C.gemv_experts(lw["w_gu"], nb.x, nb.ids.view(-1), nb.act_moe, ops.SILU_PAIR, J, lw["ln2"], eps)
             if self.comm is None or d.ws == 1:
                 C.moe_down(lw["w_d"], nb.act_moe, nb.ids, nb.wts, nb.x, None)
+            elif self.comm.fused:
+                C.moe_down_ar(lw["w_d"], nb.act_moe, nb.ids, nb.wts, nb.x, *self.comm.fused_args())
             else:
                 C.moe_down(lw["w_d"], nb.act_moe, nb.ids, nb.wts, nb.x, nb.partial)
                 self.comm.reduce_residual(nb.partial, nb.x)

@@ -1,13 +1,20 @@
 """Tensor-parallel communicator for one process per GPU.
 
-Two reduction backends for the row-parallel layers (attention o_proj, GDN out_proj,
+Reduction backends for the row-parallel layers (attention o_proj, GDN out_proj,
 MLP down_proj, MoE block end -- the reference's two all-reduces per decoder layer,
 tp/tp_linear.rs:285-293, tp/tp_qwen3_5.rs:1268-1271):
 
-  "p2p"   (default) one-shot reduction over CUDA-IPC peer buffers on NVLink, fused
-          with the residual add, bounded waits, CUDA-graph safe (csrc/allreduce.cu)
+  "p2p"   (default) the reduction runs inside the producing decode kernel: each CTA of
+          the row-parallel GEMV / MoE down pushes its rows into every peer's receive
+          slot over NVLink and sums the peers' rows into the residual
+          (csrc/tp_fused.cuh) -- no separate collective launch; prefill-sized
+          reductions use the one-shot kernel below
+  "p2p1"  a separate one-shot reduction kernel after the GEMV, over CUDA-IPC peer
+          buffers, fused with the residual add (csrc/allreduce.cu)
   "nccl"  the reference-equivalent baseline: ncclAllReduce (through
           torch.distributed) of the row-parallel partial, then the residual add
+
+All device waits are bounded and CUDA-graph safe.
 
 Rendezvous and prefill-size reductions use torch.distributed (NCCL on GPUs, gloo on
 CPU ranks in tests), standing in for the reference's hex-encoded ncclUniqueId sent
@@ -23,6 +30,7 @@ import torch.distributed as dist
 from .. import ops
 
 _FLAG_BYTES = 4096
+_FUSED_FLAG_BYTES = 4096 * 8 * 4  # kTPMaxCtas x kTPMaxRanks u32 (csrc/tp_fused.cuh)
 
 
 class TPError(RuntimeError):
@@ -40,9 +48,14 @@ class TPComm:
         if self.device.type != "cuda":
             self.mode = "host"
         self.timeout_s = timeout_s
-        self.launches_per_reduce = 1
-        if self.mode == "p2p":
+        if self.mode not in ("p2p", "p2p1", "nccl", "host"):
+            raise ValueError(f"unknown TP mode {self.mode!r}")
+        self.fused = self.mode == "p2p"
+        self.launches_per_reduce = 0 if self.fused else 1
+        if self.mode in ("p2p", "p2p1"):
             self._init_p2p(max_elems)
+        if self.fused:
+            self._init_fused(max_elems)
 
     # ---- rendezvous of the IPC regions ----------------------------------
     def _init_p2p(self, max_elems: int):
@@ -65,8 +78,32 @@ class TPComm:
         self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
         dist.barrier(group=self.group)
 
+    def _init_fused(self, max_elems: int):
+        """Receive region of the fused path: per-CTA flags, then f32 slots
+        [parity][source rank][max_elems], exported to and opened by every peer."""
+        C = ops.C
+        self.slot_elems = max_elems
+        region, handle = C.ipc_alloc(_FUSED_FLAG_BYTES + 2 * self.ws * max_elems * 4, self.device.index)
+        self._fused_region = region
+        handles: list = [None] * self.ws
+        dist.all_gather_object(handles, bytes(handle.numpy().tobytes()), group=self.group)
+        self.fused_bases: list[int] = []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                self.fused_bases.append(region.data_ptr())
+            else:
+                p = C.ipc_open(torch.frombuffer(bytearray(h), dtype=torch.uint8), self.device.index)
+                self.fused_bases.append(p)
+                self._opened.append(p)
+        self.fused_epoch = torch.zeros(2, dtype=torch.int32, device=self.device)
+        dist.barrier(group=self.group)
+
+    def fused_args(self) -> tuple:
+        """Trailing arguments of the fused kernels (gemv_ar, moe_down_ar)."""
+        return (self.fused_bases, self.rank, self.slot_elems, self.fused_epoch, self.err, self.timeout_s)
+
     def close(self):
-        if self.mode == "p2p":
+        if self.mode in ("p2p", "p2p1"):
             torch.cuda.synchronize(self.device)
             dist.barrier(group=self.group)
             for p in self._opened:
@@ -75,15 +112,16 @@ class TPComm:
 
     def check(self):
         """Raise TPError if a device-side wait timed out since the last check."""
-        if self.mode == "p2p":
+        if self.mode in ("p2p", "p2p1"):
             e = int(self.err.item())
             if e:
-                raise TPError(f"rank {self.rank}: peer {e - 1000} did not arrive within {self.timeout_s}s")
+                peer = e - 2000 if e >= 2000 else e - 1000
+                raise TPError(f"rank {self.rank}: peer {peer} did not arrive within {self.timeout_s}s")
 
     # ---- reductions -------------------------------------------------------
     def all_reduce_(self, t: torch.Tensor) -> torch.Tensor:
         """Sum in place across ranks (prefill-sized tensors)."""
-        if self.mode == "p2p" and t.numel() * 2 <= self.data_bytes and t.dtype == torch.bfloat16:
+        if self.mode in ("p2p", "p2p1") and t.numel() * 2 <= self.data_bytes and t.dtype == torch.bfloat16:
             flat = t.view(-1)
             ops.C.ar_oneshot(self.bases, self.rank, flat, flat, flat, self.data_bytes, self.epoch, self.err,
                              self._ctas(flat.numel()), self.timeout_s)
@@ -96,7 +134,7 @@ class TPComm:
 
     def reduce_residual(self, partial: torch.Tensor, x: torch.Tensor):
         """x += sum over ranks of `partial` (decode-size [B, hidden] bf16)."""
-        if self.mode == "p2p":
+        if self.mode in ("p2p", "p2p1"):
             ops.C.ar_oneshot(self.bases, self.rank, partial.view(-1), x.view(-1), None, self.data_bytes,
                              self.epoch, self.err, self._ctas(partial.numel()), self.timeout_s)
         else:

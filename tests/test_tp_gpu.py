@@ -1,6 +1,10 @@
-"""Tensor parallelism on 2+ GPUs: the P2P one-shot reduction and the NCCL baseline
-must reproduce the single-GPU model (logits and greedy tokens), including inside a
-captured decode graph. Runs only where the box exposes >= 2 GPUs."""
+"""Tensor parallelism on 2 GPUs: the reduction fused into the decode kernels ("p2p"),
+the separate one-shot kernel ("p2p1") and the NCCL baseline must reproduce the
+single-GPU model. Decode is compared teacher-forced (the same input token at every
+step, logits compared per step), because the MoE router of the test model is sharp
+enough that TP's different bf16 rounding can change a greedy trajectory. Inside a
+captured decode graph the ranks must agree bit for bit. Runs only where the box
+exposes >= 2 GPUs."""
 import os
 import socket
 
@@ -62,6 +66,22 @@ def _run_inner(rank, ws, port, mode, q):
         _log(rank, "prefill done")
         if comm is not None:
             comm.check()
+        # teacher-forced eager decode steps: logits per step for fixed input tokens
+        nb = fm.buffers(1)
+        nb.slots.fill_(0)
+        forced = [int(lg.argmax())] + [int(t) for t in torch.randint(0, cfg.vocab_size, (5,),
+                                                                       generator=torch.Generator().manual_seed(2))]
+        saved = fm._save_slots([0])
+        tf = []
+        for t in forced:
+            nb.tok.fill_(t)
+            fm.decode_step_launch(nb)
+            tf.append(nb.logits[0].float().cpu().clone())
+        torch.cuda.synchronize()
+        fm._restore_slots(saved)
+        if comm is not None:
+            comm.check()
+        _log(rank, "teacher-forced done")
         nb = fm.capture(1, steps=8)
         _log(rank, "captured")
         nb.slots.fill_(0)
@@ -71,7 +91,7 @@ def _run_inner(rank, ws, port, mode, q):
         torch.cuda.synchronize()
         if comm is not None:
             comm.check()
-        q.put((rank, lg.cpu(), nb.out_tokens[0, :16].cpu()))
+        q.put((rank, lg.float().cpu().numpy(), torch.stack(tf).numpy(), nb.out_tokens[0, :16].cpu().numpy()))
         if comm is not None:
             comm.close()
     finally:
@@ -90,8 +110,8 @@ def _launch(ws, mode):
     res, t0 = {}, time.time()
     while len(res) < ws:
         try:
-            r, a, b = q.get(timeout=5)
-            res[r] = (a, b)
+            r, a, t, b = q.get(timeout=5)
+            res[r] = (torch.from_numpy(a), torch.from_numpy(t), torch.from_numpy(b))
         except queue.Empty:
             dead = [p.exitcode for p in ps if p.exitcode not in (None, 0)]
             if dead or time.time() - t0 > 240:
@@ -104,14 +124,39 @@ def _launch(ws, mode):
     return res
 
 
+_cache: dict = {}
+
+
+def _results(ws, mode):
+    key = (ws, mode)
+    if key not in _cache:
+        _cache[key] = _launch(ws, mode)
+    return _cache[key]
+
+
+def _cos(a, b):
+    return torch.nn.functional.cosine_similarity(a.flatten(), b.flatten(), dim=0).item()
+
+
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("mode", ["p2p", "nccl"])
+@pytest.mark.parametrize("mode", ["p2p", "p2p1", "nccl"])
 def test_tp2_matches_single_gpu(mode):
-    single = _launch(1, None)[0]
-    res = _launch(2, mode)
+    single = _results(1, None)[0]
+    res = _results(2, mode)
     for r in range(2):
-        cos = torch.nn.functional.cosine_similarity(res[r][0], single[0], dim=0).item()
-        assert cos > 0.995, cos
-        assert torch.equal(res[r][1], res[0][1])          # ranks agree bit-for-bit
-    agree = (res[0][1] == single[1]).float().mean().item()
-    assert agree >= 0.75, (res[0][1], single[1])
+        assert _cos(res[r][0], single[0]) > 0.995
+        step_cos = [_cos(res[r][1][i], single[1][i]) for i in range(single[1].shape[0])]
+        # one step may route a near-tied token to another expert (bf16 partial sums);
+        # a sharding or reduction error lowers every step
+        assert sorted(step_cos)[len(step_cos) // 2] > 0.99 and min(step_cos) > 0.85, step_cos
+        assert torch.equal(res[r][1], res[0][1])            # ranks agree bit for bit
+        assert torch.equal(res[r][2], res[0][2])
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_tp2_fused_reduction_matches_nccl():
+    """The fused reduction sums f32 partials; NCCL sums bf16 partials: per-step logits
+    must agree closely (only rounding differs)."""
+    fused, nccl = _results(2, "p2p"), _results(2, "nccl")
+    step_cos = [_cos(fused[0][1][i], nccl[0][1][i]) for i in range(fused[0][1].shape[0])]
+    assert sorted(step_cos)[len(step_cos) // 2] > 0.99 and min(step_cos) > 0.85, step_cos
