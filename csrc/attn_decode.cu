@@ -16,6 +16,7 @@
 #include <cooperative_groups.h>
 
 #include "common.cuh"
+#include "mma_frag.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -72,21 +73,6 @@ HX_DEVICE void norm_rope_head(float* xv, const float* w, const float* inv_freq, 
     }
   }
   __syncwarp();
-}
-
-// bf16 m16n8k16 tensor-core MMA (f32 accumulate) used for the score tile.
-HX_DEVICE void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
-                         uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};\n"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-
-HX_DEVICE uint32_t pack_bf16x2(float lo, float hi) {
-  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
-  return *reinterpret_cast<uint32_t*>(&v);
 }
 
 // Per-lane slice of one V row in the PV phase (lanes over head dims).

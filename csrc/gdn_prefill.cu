@@ -7,7 +7,7 @@
 //                g = -exp(A_log) softplus(a + dt_bias); head-major outputs.
 //   gdn_chunk  : one CTA per (value head, chunk): in-chunk cumulative decay, the
 //                strictly-lower system A = -(beta k k^T) * decay, T = (I - A)^-1 by
-//                row-wise forward substitution (linear_attn.rs:566-596), and
+//                forward substitution (linear_attn.rs:566-596), and
 //                u = T (beta v), w = T (beta k exp(gc)), P = (q k^T) * decay (causal).
 //                Chunks are independent here, so this runs over T/64 x Hv CTAs.
 //   gdn_scan   : one CTA per (value head, 32-column V tile) walks the chunks in order
@@ -16,11 +16,15 @@
 //                  S = exp(g_last) S + (k exp(g_last - gc))^T vnew
 //   gdn_onorm  : gated RMSNorm of o with z, bf16 output for out_proj.
 //
-// Math is f32 (SIMT); q/k/v are kept in bf16 between launches like the decode path.
+// The matrix products of gdn_chunk and gdn_scan run on tensor cores (mma.sync
+// m16n8k16, bf16 operands, f32 accumulation -- the operands are bf16 between the
+// launches, like the chunked kernels of flash-linear-attention); cumulative decays,
+// the triangular solve and the carried state are f32.
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 
 #include "common.cuh"
+#include "mma_frag.cuh"
 
 namespace hx {
 
@@ -77,245 +81,348 @@ __global__ void gdn_prep_kernel(const __nv_bfloat16* __restrict__ proj, int ldp,
   }
 }
 
-// grid (nchunks, Hv), block 256. Outputs per (h, chunk): u, w [C, D] f32, P [C, C] f32, gc [C].
+// grid (nchunks, Hv), block 256 (8 warps). Per (value head, chunk) it writes, all bf16
+// except GC: U = T (beta v) and W = T (beta k exp(gc)) [C, D], the causal decayed scores
+// P [C, C], Qg = q exp(gc) and Kd = k exp(g_last - gc) [C, D] (the scan's operands),
+// and GC = the inclusive cumulative log-decay [C] (f32).
+// T = (I - A)^-1 with A = -(beta k k^T) * decay strictly lower (linear_attn.rs:566-596).
+// The k k^T / q k^T tiles and the two T products run on tensor cores (bf16 operands, f32
+// accumulation); the triangular solve is f32: four lanes per column of T, each owning
+// the rows of one residue mod 4 in registers, so the solve needs no block barrier.
 template <int D>
 __global__ void __launch_bounds__(256) gdn_chunk_kernel(const __nv_bfloat16* __restrict__ qn,
                                                         const __nv_bfloat16* __restrict__ kn,
                                                         const __nv_bfloat16* __restrict__ vn,
                                                         const float* __restrict__ g, const float* __restrict__ beta,
-                                                        int Hk, int Hv, int Tp, float* __restrict__ U,
-                                                        float* __restrict__ Wm, float* __restrict__ P,
+                                                        int Hk, int Hv, int Tp, __nv_bfloat16* __restrict__ U,
+                                                        __nv_bfloat16* __restrict__ Wm, __nv_bfloat16* __restrict__ P,
+                                                        __nv_bfloat16* __restrict__ Qg, __nv_bfloat16* __restrict__ Kd,
                                                         float* __restrict__ GC) {
-  extern __shared__ __align__(16) float sm[];
-  float* ks = sm;                    // [C][D+1]
-  float* qs = ks + kGC * (D + 1);    // [C][D+1]
-  float* vs = qs + kGC * (D + 1);    // [C][D+1]
-  float* Am = vs + kGC * (D + 1);    // [C][C+1]  A, then T in place
-  float* gcs = Am + kGC * (kGC + 1); // [C]
-  float* bs = gcs + kGC;             // [C]
-  float* rowA = bs + kGC;            // [C] original row i during substitution
+  constexpr int C = kGC, LDT = D + 8, LDC = C + 8, LDA = C + 1;
+  extern __shared__ __align__(16) unsigned char smraw[];
+  __nv_bfloat16* ks = reinterpret_cast<__nv_bfloat16*>(smraw);  // [C][LDT] k
+  __nv_bfloat16* qs = ks + C * LDT;                              // [C][LDT] q
+  __nv_bfloat16* vs = qs + C * LDT;                              // [C][LDT] v, then beta v
+  __nv_bfloat16* kb = vs + C * LDT;                              // [C][LDT] beta k exp(gc)
+  __nv_bfloat16* Tb = kb + C * LDT;                              // [C][LDC] I + T (bf16)
+  float* Af = reinterpret_cast<float*>(Tb + C * LDC);            // [C][LDA] A (f32)
+  float* gcs = Af + C * LDA;                                     // [C]
+  float* bs = gcs + C;                                           // [C]
   const int c = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
   const int kh = h / (Hv / Hk);
-  const long long t0 = (long long)c * kGC;
-  const int nchunks = gridDim.x;
-  const long long hc = (long long)h * nchunks + c;
-  // load k (f32 in smem), gating
-  for (int i = tid; i < kGC * D; i += 256) {
-    int r = i / D, d = i - r * D;
-    ks[r * (D + 1) + d] = __bfloat162float(kn[((long long)kh * Tp + t0 + r) * D + d]);
-    qs[r * (D + 1) + d] = __bfloat162float(qn[((long long)kh * Tp + t0 + r) * D + d]);
-    vs[r * (D + 1) + d] = __bfloat162float(vn[((long long)h * Tp + t0 + r) * D + d]);
+  const long long t0 = (long long)c * C;
+  const long long hc = (long long)h * gridDim.x + c;
+  constexpr int VPR = D / 8;  // 16-byte pieces per row
+  for (int i = tid; i < C * VPR; i += 256) {
+    const int r = i / VPR, p = i - r * VPR;
+    cp_async16(ks + r * LDT + p * 8, kn + ((long long)kh * Tp + t0 + r) * D + p * 8);
+    cp_async16(qs + r * LDT + p * 8, qn + ((long long)kh * Tp + t0 + r) * D + p * 8);
+    cp_async16(vs + r * LDT + p * 8, vn + ((long long)h * Tp + t0 + r) * D + p * 8);
   }
-  if (tid < kGC) {
-    gcs[tid] = g[(long long)h * Tp + t0 + tid];
-    bs[tid] = beta[(long long)h * Tp + t0 + tid];
+  cp_async_commit();
+  if (warp == 0) {  // inclusive cumulative sum of the log-decay (two values per lane)
+    float a = g[(long long)h * Tp + t0 + lane], b2 = g[(long long)h * Tp + t0 + 32 + lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float x = __shfl_up_sync(0xffffffffu, a, o), y = __shfl_up_sync(0xffffffffu, b2, o);
+      if (lane >= o) { a += x; b2 += y; }
+    }
+    b2 += __shfl_sync(0xffffffffu, a, 31);
+    gcs[lane] = a;
+    gcs[32 + lane] = b2;
+    GC[hc * C + lane] = a;
+    GC[hc * C + 32 + lane] = b2;
+    bs[lane] = beta[(long long)h * Tp + t0 + lane];
+    bs[32 + lane] = beta[(long long)h * Tp + t0 + 32 + lane];
+  }
+  // identity into Tb (the solve fills the strictly lower part)
+  for (int i = tid; i < C * C; i += 256) {
+    const int r = i / C, cc = i - r * C;
+    Tb[r * LDC + cc] = __float2bfloat16(r == cc ? 1.f : 0.f);
+  }
+  cp_async_wait<0>();
+  __syncthreads();
+
+  // ---- k k^T and q k^T: warp -> m-tile (warp & 3), n-tiles 4 * (warp >> 2) .. +3 ----
+  {
+    const int mt = warp & 3, nb = (warp >> 2) * 4;
+    float kk[4][4] = {}, qk[4][4] = {};
+#pragma unroll
+    for (int s = 0; s < D / 16; ++s) {
+      uint32_t ak[4], aq[4];
+      frag_a(ak, ks, LDT, mt * 16, s * 16);
+      frag_a(aq, qs, LDT, mt * 16, s * 16);
+#pragma unroll
+      for (int pr = 0; pr < 2; ++pr) {
+        uint32_t b[4];
+        frag_b2_nk(b, ks, LDT, (nb + 2 * pr) * 8, s * 16);
+        mma_16816(kk[2 * pr], ak[0], ak[1], ak[2], ak[3], b[0], b[1]);
+        mma_16816(kk[2 * pr + 1], ak[0], ak[1], ak[2], ak[3], b[2], b[3]);
+        mma_16816(qk[2 * pr], aq[0], aq[1], aq[2], aq[3], b[0], b[1]);
+        mma_16816(qk[2 * pr + 1], aq[0], aq[1], aq[2], aq[3], b[2], b[3]);
+      }
+    }
+#pragma unroll
+    for (int n = 0; n < 4; ++n)
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const int i = mt * 16 + (lane >> 2) + half * 8;
+        const int j = (nb + n) * 8 + 2 * (lane & 3);
+        float pv[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int jj = j + e;
+          const float dec = jj <= i ? __expf(gcs[i] - gcs[jj]) : 0.f;
+          Af[i * LDA + jj] = jj < i ? -bs[i] * kk[n][half * 2 + e] * dec : 0.f;
+          pv[e] = qk[n][half * 2 + e] * dec;
+        }
+        *reinterpret_cast<uint32_t*>(&P[(hc * C + i) * C + j]) = pack_bf16x2(pv[0], pv[1]);
+      }
   }
   __syncthreads();
-  if (tid == 0) {  // inclusive cumulative sum of the log-decay within the chunk
-    float s = 0.f;
-    for (int i = 0; i < kGC; ++i) { s += gcs[i]; gcs[i] = s; }
+
+  // ---- T (strictly lower) by forward substitution, column j = tid / 4 ---------------
+  // T[i][j] = A[i][j] + sum_{j < m < i} A[i][m] T[m][j]; lane q of the group keeps
+  // T[m][j] for m = 4u + q in tr[u].
+  {
+    const int j = tid >> 2, q = tid & 3;
+    float tr[C / 4];
+#pragma unroll
+    for (int u = 0; u < C / 4; ++u) tr[u] = 0.f;
+#pragma unroll
+    for (int i = 1; i < C; ++i) {
+      float part = 0.f;
+#pragma unroll
+      for (int u = 0; u < C / 4; ++u) {
+        const int m = 4 * u + q;
+        if (4 * u < i && m > j && m < i) part += Af[i * LDA + m] * tr[u];
+      }
+      part += __shfl_xor_sync(0xffffffffu, part, 1);
+      part += __shfl_xor_sync(0xffffffffu, part, 2);
+      const float tij = j < i ? Af[i * LDA + j] + part : 0.f;
+      if (q == (i & 3)) tr[i >> 2] = tij;
+      if (q == 0 && j < i) Tb[i * LDC + j] = __float2bfloat16(tij);
+    }
+  }
+  // ---- operands: beta v, beta k exp(gc) (shared), q exp(gc), k exp(gl - gc) (global)
+  {
+    const float gl = gcs[C - 1];
+    for (int i = tid; i < C * VPR; i += 256) {
+      const int r = i / VPR, p = i - r * VPR;
+      const float b = bs[r], eg = __expf(gcs[r]), ed = __expf(gl - gcs[r]);
+      float fv[8], fk[8], fq[8], o1[8], o2[8], o3[8], o4[8];
+      unpack8(*reinterpret_cast<const bf16x8*>(vs + r * LDT + p * 8), fv);
+      unpack8(*reinterpret_cast<const bf16x8*>(ks + r * LDT + p * 8), fk);
+      unpack8(*reinterpret_cast<const bf16x8*>(qs + r * LDT + p * 8), fq);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        o1[e] = b * fv[e];
+        o2[e] = b * eg * fk[e];
+        o3[e] = fq[e] * eg;
+        o4[e] = fk[e] * ed;
+      }
+      *reinterpret_cast<bf16x8*>(vs + r * LDT + p * 8) = pack8(o1);
+      *reinterpret_cast<bf16x8*>(kb + r * LDT + p * 8) = pack8(o2);
+      *reinterpret_cast<bf16x8*>(Qg + (hc * C + r) * D + p * 8) = pack8(o3);
+      *reinterpret_cast<bf16x8*>(Kd + (hc * C + r) * D + p * 8) = pack8(o4);
+    }
   }
   __syncthreads();
-  if (tid < kGC) GC[hc * kGC + tid] = gcs[tid];
-  // A[i][j] = -beta_i (k_i . k_j) exp(gc_i - gc_j) for j < i; P from q similarly (j <= i)
-  for (int e = tid; e < kGC * kGC; e += 256) {
-    int i = e / kGC, j = e - i * kGC;
-    float a = 0.f;
-    if (j < i) {
-      float dot = 0.f;
-#pragma unroll 8
-      for (int d = 0; d < D; ++d) dot += ks[i * (D + 1) + d] * ks[j * (D + 1) + d];
-      a = -bs[i] * dot * __expf(gcs[i] - gcs[j]);
+  // ---- U = (I + T) (beta v), W = (I + T) (beta k exp(gc)) ------------------------
+  {
+    constexpr int NTW = D / 16;  // n-tiles of 8 columns per warp
+    const int mt = warp & 3, nb = (warp >> 2) * NTW;
+    float au[NTW][4] = {}, aw[NTW][4] = {};
+#pragma unroll
+    for (int s = 0; s < C / 16; ++s) {
+      uint32_t a[4];
+      frag_a(a, Tb, LDC, mt * 16, s * 16);
+#pragma unroll
+      for (int pr = 0; pr < NTW / 2; ++pr) {
+        uint32_t b[4];
+        frag_b2_kn(b, vs, LDT, (nb + 2 * pr) * 8, s * 16);
+        mma_16816(au[2 * pr], a[0], a[1], a[2], a[3], b[0], b[1]);
+        mma_16816(au[2 * pr + 1], a[0], a[1], a[2], a[3], b[2], b[3]);
+        frag_b2_kn(b, kb, LDT, (nb + 2 * pr) * 8, s * 16);
+        mma_16816(aw[2 * pr], a[0], a[1], a[2], a[3], b[0], b[1]);
+        mma_16816(aw[2 * pr + 1], a[0], a[1], a[2], a[3], b[2], b[3]);
+      }
     }
-    Am[i * (kGC + 1) + j] = a;
-  }
-  // P = (q_i . k_j) exp(gc_i - gc_j), j <= i (q already scaled)
-  for (int e = tid; e < kGC * kGC; e += 256) {
-    int i = e / kGC, j = e - i * kGC;
-    float pv = 0.f;
-    if (j <= i) {
-      float dot = 0.f;
-#pragma unroll 8
-      for (int d = 0; d < D; ++d) dot += qs[i * (D + 1) + d] * ks[j * (D + 1) + d];
-      pv = dot * __expf(gcs[i] - gcs[j]);
-    }
-    P[hc * kGC * kGC + e] = pv;
-  }
-  __syncthreads();
-  // forward substitution, row by row: T[i, j] = A[i, j] + sum_{j<m<i} A[i, m] T[m, j]
-  for (int i = 2; i < kGC; ++i) {
-    if (tid < i) rowA[tid] = Am[i * (kGC + 1) + tid];  // the untouched row i of A
-    __syncthreads();
-    if (tid < i - 1) {  // j in [0, i-2]; T[i][i-1] = A[i][i-1]
-      const int j = tid;
-      float s = rowA[j];
-      for (int m = j + 1; m < i; ++m) s += rowA[m] * Am[m * (kGC + 1) + j];
-      Am[i * (kGC + 1) + j] = s;
-    }
-    __syncthreads();
-  }
-  // u = (I + T) (beta v), w = (I + T) (beta k exp(gc)) -- T holds the strictly lower part
-  // fold beta (and exp(gc) for w) into the substitution rows once: tb[i][m] = T[i][m] beta_m
-  if (tid < kGC) rowA[tid] = __expf(gcs[tid]);
-  __syncthreads();
-  for (int e = tid; e < kGC * D; e += 256) {
-    int i = e / D, d = e - i * D;
-    float su = bs[i] * vs[i * (D + 1) + d];
-    float sw = bs[i] * ks[i * (D + 1) + d] * rowA[i];
-    for (int m = 0; m < i; ++m) {
-      const float tm = Am[i * (kGC + 1) + m] * bs[m];
-      su += tm * vs[m * (D + 1) + d];
-      sw += tm * ks[m * (D + 1) + d] * rowA[m];
-    }
-    U[(hc * kGC + i) * D + d] = su;
-    Wm[(hc * kGC + i) * D + d] = sw;
+#pragma unroll
+    for (int n = 0; n < NTW; ++n)
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const int i = mt * 16 + (lane >> 2) + half * 8;
+        const int col = (nb + n) * 8 + 2 * (lane & 3);
+        *reinterpret_cast<uint32_t*>(&U[(hc * C + i) * D + col]) = pack_bf16x2(au[n][half * 2], au[n][half * 2 + 1]);
+        *reinterpret_cast<uint32_t*>(&Wm[(hc * C + i) * D + col]) = pack_bf16x2(aw[n][half * 2], aw[n][half * 2 + 1]);
+      }
   }
 }
 
-// grid (D / 32, Hv), block 256. Walks the chunks in order with the f32 state tile
-// S [D, 32] in shared memory. Every product uses register micro-tiles (4x2 or 8x2
-// outputs per thread with 4-wide vector loads along the reduction), so each
-// shared-memory load feeds several FMAs.
+// grid (D / 32, Hv), block 256 (8 warps). Walks the chunks of one value head in order
+// for a 32-column tile of the state S [D, 32] (the recurrence is independent across
+// value columns). S stays in f32 MMA accumulator fragments for the whole walk (warp w
+// owns state m-tiles w * FPW / 4 ...); per chunk, on tensor cores:
+//   vnew = U - W S;   o = Qg S + P vnew;   S = exp(g_last) S + Kd^T vnew
+// The next chunk's operand tiles stream into the other half of a double buffer with
+// cp.async while the current chunk computes.
 template <int D>
-__global__ void __launch_bounds__(256) gdn_scan_kernel(const __nv_bfloat16* __restrict__ qn,
-                                                       const __nv_bfloat16* __restrict__ kn,
-                                                       const float* __restrict__ U, const float* __restrict__ Wm,
-                                                       const float* __restrict__ P, const float* __restrict__ GC,
-                                                       float* __restrict__ state /* [Hv, D, D] slot slice */, int Hk,
-                                                       int Hv, int Tp, int T, int nchunks,
-                                                       __nv_bfloat16* __restrict__ o /* [T, Hv, D] */) {
-  constexpr int BV = 32;
-  constexpr int LD = D + 4;        // row stride of the [C][D] tiles (16-byte aligned rows)
-  constexpr int LK = kGC + 4;      // row stride of the [D][C] / [C][C] tiles
-  extern __shared__ __align__(16) float sm[];
-  float* S = sm;                     // [D][BV]
-  float* Ws = S + D * BV;            // [C][LD]   w rows
-  float* Qs = Ws + kGC * LD;         // [C][LD]   q * exp(gc)
-  float* KdT = Qs + kGC * LD;        // [D][LK]   (k * exp(glast - gc))^T
-  float* Ps = KdT + D * LK;          // [C][LK]
-  float* Vn = Ps + kGC * LK;         // [C][BV]
-  float* gcs = Vn + kGC * BV;        // [C]
+__global__ void __launch_bounds__(256, 1) gdn_scan_kernel(const __nv_bfloat16* __restrict__ U,
+                                                          const __nv_bfloat16* __restrict__ Wm,
+                                                          const __nv_bfloat16* __restrict__ P,
+                                                          const __nv_bfloat16* __restrict__ Qg,
+                                                          const __nv_bfloat16* __restrict__ Kd,
+                                                          const float* __restrict__ GC,
+                                                          float* __restrict__ state /* [Hv, D, D] slot slice */,
+                                                          int Hv, int T, int nchunks,
+                                                          __nv_bfloat16* __restrict__ o /* [T, Hv, D] */) {
+  constexpr int C = kGC, BV = 32, LDT = D + 8, LDC = C + 8, LDV = BV + 8;
+  constexpr int STAGE = 3 * C * LDT + C * LDC + C * LDV;  // bf16 elements per stage
+  constexpr int FPW = (D / 16) * (BV / 8) / 8;            // state fragments per warp
+  extern __shared__ __align__(16) unsigned char smraw[];
+  __nv_bfloat16* stage0 = reinterpret_cast<__nv_bfloat16*>(smraw);
+  __nv_bfloat16* Sb = stage0 + 2 * STAGE;  // [BV][LDT]  S^T in bf16
+  __nv_bfloat16* VnT = Sb + BV * LDT;      // [BV][LDC]  vnew^T in bf16
   const int vt = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
-  const int kh = h / (Hv / Hk);
-  const int rg = tid >> 4, cp = tid & 15;   // row group (16) x column pair (16)
-  const int c0 = cp * 2;
-  float* Sg = state + (long long)h * D * D;
-  for (int i = tid; i < D * BV; i += 256) {
-    int k = i / BV, vv = i - k * BV;
-    S[i] = Sg[k * D + vt * BV + vv];
-  }
-  for (int c = 0; c < nchunks; ++c) {
+  const int warp = tid >> 5, lane = tid & 31;
+  const int gq = lane >> 2, tq = lane & 3;
+  constexpr int VPR = D / 8, UPR = BV / 8;
+
+  auto load_chunk = [&](int c, __nv_bfloat16* st) {
     const long long hc = (long long)h * nchunks + c;
-    const long long t0 = (long long)c * kGC;
-    __syncthreads();
-    if (tid < kGC) gcs[tid] = GC[hc * kGC + tid];
-    __syncthreads();
-    const float glast = gcs[kGC - 1];
-    for (int i = tid; i < kGC * D / 4; i += 256) {
-      const int r = (i * 4) / D, d = (i * 4) - r * D;
-      *reinterpret_cast<float4*>(&Ws[r * LD + d]) =
-          *reinterpret_cast<const float4*>(&Wm[(hc * kGC + r) * D + d]);
-      const float eq = __expf(gcs[r]), ek = __expf(glast - gcs[r]);
-      const __nv_bfloat16* qr = qn + ((long long)kh * Tp + t0 + r) * D + d;
-      const __nv_bfloat16* kr = kn + ((long long)kh * Tp + t0 + r) * D + d;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        Qs[r * LD + d + j] = __bfloat162float(qr[j]) * eq;
-        KdT[(d + j) * LK + r] = __bfloat162float(kr[j]) * ek;
-      }
+    __nv_bfloat16* Ws = st;
+    __nv_bfloat16* Qs = Ws + C * LDT;
+    __nv_bfloat16* Ks = Qs + C * LDT;
+    __nv_bfloat16* Ps = Ks + C * LDT;
+    __nv_bfloat16* Us = Ps + C * LDC;
+    for (int i = tid; i < C * VPR; i += 256) {
+      const int r = i / VPR, p = i - r * VPR;
+      const long long gofs = (hc * C + r) * D + p * 8;
+      cp_async16(Ws + r * LDT + p * 8, Wm + gofs);
+      cp_async16(Qs + r * LDT + p * 8, Qg + gofs);
+      cp_async16(Ks + r * LDT + p * 8, Kd + gofs);
     }
-    for (int i = tid; i < kGC * kGC / 4; i += 256) {
-      const int r = (i * 4) / kGC, cc = (i * 4) - r * kGC;
-      *reinterpret_cast<float4*>(&Ps[r * LK + cc]) = *reinterpret_cast<const float4*>(&P[hc * kGC * kGC + r * kGC + cc]);
+    for (int i = tid; i < C * (C / 8); i += 256) {
+      const int r = i / (C / 8), p = i - r * (C / 8);
+      cp_async16(Ps + r * LDC + p * 8, P + (hc * C + r) * C + p * 8);
     }
-    __syncthreads();
-    // ---- vnew = u - w S : rows rg*4 .. +3, columns c0, c0+1 ------------------------
-    float acc[4][2];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int r = rg * 4 + i;
-      const float2 u2 = *reinterpret_cast<const float2*>(&U[(hc * kGC + r) * D + vt * BV + c0]);
-      acc[i][0] = u2.x;
-      acc[i][1] = u2.y;
+    for (int i = tid; i < C * UPR; i += 256) {
+      const int r = i / UPR, p = i - r * UPR;
+      cp_async16(Us + r * LDV + p * 8, U + (hc * C + r) * D + vt * BV + p * 8);
     }
-    for (int k = 0; k < D; k += 4) {
-      float2 s2[4];
+    cp_async_commit();
+  };
+
+  // state fragments: f = warp * FPW + i -> m-tile f / 4 (rows of S), n-tile f % 4
+  float S[FPW][4];
+  float* Sg = state + (long long)h * D * D;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) s2[j] = *reinterpret_cast<const float2*>(&S[(k + j) * BV + c0]);
+  for (int i = 0; i < FPW; ++i) {
+    const int f = warp * FPW + i, mt = f >> 2, nt = f & 3;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float4 w4 = *reinterpret_cast<const float4*>(&Ws[(rg * 4 + i) * LD + k]);
-        acc[i][0] -= w4.x * s2[0].x + w4.y * s2[1].x + w4.z * s2[2].x + w4.w * s2[3].x;
-        acc[i][1] -= w4.x * s2[0].y + w4.y * s2[1].y + w4.z * s2[2].y + w4.w * s2[3].y;
-      }
-    }
-#pragma unroll
-    for (int i = 0; i < 4; ++i) *reinterpret_cast<float2*>(&Vn[(rg * 4 + i) * BV + c0]) = make_float2(acc[i][0], acc[i][1]);
-    __syncthreads();
-    // ---- o = (q exp(gc)) S + P vnew ---------------------------------------------
-#pragma unroll
-    for (int i = 0; i < 4; ++i) { acc[i][0] = 0.f; acc[i][1] = 0.f; }
-    for (int k = 0; k < D; k += 4) {
-      float2 s2[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) s2[j] = *reinterpret_cast<const float2*>(&S[(k + j) * BV + c0]);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float4 q4 = *reinterpret_cast<const float4*>(&Qs[(rg * 4 + i) * LD + k]);
-        acc[i][0] += q4.x * s2[0].x + q4.y * s2[1].x + q4.z * s2[2].x + q4.w * s2[3].x;
-        acc[i][1] += q4.x * s2[0].y + q4.y * s2[1].y + q4.z * s2[2].y + q4.w * s2[3].y;
-      }
-    }
-    for (int m = 0; m < kGC; m += 4) {  // P is causal (zero above the diagonal)
-      float2 v2[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) v2[j] = *reinterpret_cast<const float2*>(&Vn[(m + j) * BV + c0]);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float4 p4 = *reinterpret_cast<const float4*>(&Ps[(rg * 4 + i) * LK + m]);
-        acc[i][0] += p4.x * v2[0].x + p4.y * v2[1].x + p4.z * v2[2].x + p4.w * v2[3].x;
-        acc[i][1] += p4.x * v2[0].y + p4.y * v2[1].y + p4.z * v2[2].y + p4.w * v2[3].y;
-      }
-    }
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const long long t = t0 + rg * 4 + i;
-      if (t < T) {
-        __nv_bfloat162 ov = __floats2bfloat162_rn(acc[i][0], acc[i][1]);
-        *reinterpret_cast<__nv_bfloat162*>(&o[(t * Hv + h) * D + vt * BV + c0]) = ov;
-      }
-    }
-    // ---- S = exp(glast) S + KdT vnew : state rows rg*(D/16) .. , columns c0, c0+1 ----
-    {
-      constexpr int RS = D / 16;
-      const float dec = __expf(glast);
-      float sa[RS][2];
-#pragma unroll
-      for (int i = 0; i < RS; ++i) {
-        const float2 s2 = *reinterpret_cast<const float2*>(&S[(rg * RS + i) * BV + c0]);
-        sa[i][0] = s2.x * dec;
-        sa[i][1] = s2.y * dec;
-      }
-      for (int m = 0; m < kGC; m += 4) {
-        float2 v2[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) v2[j] = *reinterpret_cast<const float2*>(&Vn[(m + j) * BV + c0]);
-#pragma unroll
-        for (int i = 0; i < RS; ++i) {
-          const float4 k4 = *reinterpret_cast<const float4*>(&KdT[(rg * RS + i) * LK + m]);
-          sa[i][0] += k4.x * v2[0].x + k4.y * v2[1].x + k4.z * v2[2].x + k4.w * v2[3].x;
-          sa[i][1] += k4.x * v2[0].y + k4.y * v2[1].y + k4.z * v2[2].y + k4.w * v2[3].y;
-        }
-      }
-      __syncthreads();  // all reads of S for this chunk are done
-#pragma unroll
-      for (int i = 0; i < RS; ++i) *reinterpret_cast<float2*>(&S[(rg * RS + i) * BV + c0]) = make_float2(sa[i][0], sa[i][1]);
+    for (int e = 0; e < 4; ++e) {
+      const int row = mt * 16 + gq + (e >> 1) * 8, col = nt * 8 + 2 * tq + (e & 1);
+      S[i][e] = Sg[row * D + vt * BV + col];
     }
   }
-  __syncthreads();
-  for (int i = tid; i < D * BV; i += 256) {
-    int k = i / BV, vv = i - k * BV;
-    Sg[k * D + vt * BV + vv] = S[i];
+  load_chunk(0, stage0);
+  const int mt_o = warp & 3, nb_o = (warp >> 2) * 2;  // output tile: m-tile, n-tiles nb_o, +1
+  for (int c = 0; c < nchunks; ++c) {
+    __nv_bfloat16* cur = stage0 + (c & 1) * STAGE;
+    __syncthreads();  // every warp is done with chunk c-1 (its stage, Sb and VnT)
+    if (c + 1 < nchunks) {
+      load_chunk(c + 1, stage0 + ((c + 1) & 1) * STAGE);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    // S^T (bf16) for this chunk's products
+#pragma unroll
+    for (int i = 0; i < FPW; ++i) {
+      const int f = warp * FPW + i, mt = f >> 2, nt = f & 3;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int row = mt * 16 + gq + (e >> 1) * 8, col = nt * 8 + 2 * tq + (e & 1);
+        Sb[col * LDT + row] = __float2bfloat16(S[i][e]);
+      }
+    }
+    __syncthreads();  // chunk c's tiles and Sb are visible
+    const __nv_bfloat16* Ws = cur;
+    const __nv_bfloat16* Qs = Ws + C * LDT;
+    const __nv_bfloat16* Ks = Qs + C * LDT;
+    const __nv_bfloat16* Ps = Ks + C * LDT;
+    const __nv_bfloat16* Us = Ps + C * LDC;
+    const long long hc = (long long)h * nchunks + c;
+    const float gl = GC[hc * C + C - 1];
+    // ---- W S and Qg S over the [C, BV] output: warp owns m-tile mt_o, n-tiles nb_o, +1
+    float ws[2][4] = {}, ao[2][4] = {};
+#pragma unroll
+    for (int s = 0; s < D / 16; ++s) {
+      uint32_t aw[4], aq[4], b[4];
+      frag_a(aw, Ws, LDT, mt_o * 16, s * 16);
+      frag_a(aq, Qs, LDT, mt_o * 16, s * 16);
+      frag_b2_nk(b, Sb, LDT, nb_o * 8, s * 16);
+      mma_16816(ws[0], aw[0], aw[1], aw[2], aw[3], b[0], b[1]);
+      mma_16816(ws[1], aw[0], aw[1], aw[2], aw[3], b[2], b[3]);
+      mma_16816(ao[0], aq[0], aq[1], aq[2], aq[3], b[0], b[1]);
+      mma_16816(ao[1], aq[0], aq[1], aq[2], aq[3], b[2], b[3]);
+    }
+    // vnew = U - W S  -> VnT (bf16, transposed)
+#pragma unroll
+    for (int n = 0; n < 2; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int row = mt_o * 16 + gq + (e >> 1) * 8, col = (nb_o + n) * 8 + 2 * tq + (e & 1);
+        const float vn = __bfloat162float(Us[row * LDV + col]) - ws[n][e];
+        VnT[col * LDC + row] = __float2bfloat16(vn);
+      }
+    __syncthreads();
+    // ---- o += P vnew (P causal) and store -----------------------------------------
+#pragma unroll
+    for (int s = 0; s < C / 16; ++s) {
+      if (s > mt_o) break;  // P[i][j] = 0 for j > i: k-tiles past the diagonal add nothing
+      uint32_t ap[4], b[4];
+      frag_a(ap, Ps, LDC, mt_o * 16, s * 16);
+      frag_b2_nk(b, VnT, LDC, nb_o * 8, s * 16);
+      mma_16816(ao[0], ap[0], ap[1], ap[2], ap[3], b[0], b[1]);
+      mma_16816(ao[1], ap[0], ap[1], ap[2], ap[3], b[2], b[3]);
+    }
+#pragma unroll
+    for (int n = 0; n < 2; ++n)
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const long long t = (long long)c * C + mt_o * 16 + gq + half * 8;
+        const int col = (nb_o + n) * 8 + 2 * tq;
+        if (t < T)
+          *reinterpret_cast<uint32_t*>(&o[(t * Hv + h) * D + vt * BV + col]) =
+              pack_bf16x2(ao[n][half * 2], ao[n][half * 2 + 1]);
+      }
+    // ---- S = exp(gl) S + Kd^T vnew --------------------------------------------------
+    const float dec = __expf(gl);
+#pragma unroll
+    for (int i = 0; i < FPW; ++i) {
+      const int f = warp * FPW + i, mt = f >> 2, nt = f & 3;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) S[i][e] *= dec;
+#pragma unroll
+      for (int s = 0; s < C / 16; ++s) {
+        uint32_t a[4], b[2];
+        frag_a_t(a, Ks, LDT, mt * 16, s * 16);
+        frag_b1_nk(b, VnT, LDC, nt * 8, s * 16);
+        mma_16816(S[i], a[0], a[1], a[2], a[3], b[0], b[1]);
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < FPW; ++i) {
+    const int f = warp * FPW + i, mt = f >> 2, nt = f & 3;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int row = mt * 16 + gq + (e >> 1) * 8, col = nt * 8 + 2 * tq + (e & 1);
+      Sg[row * D + vt * BV + col] = S[i][e];
+    }
   }
 }
 
@@ -356,8 +463,9 @@ void gdn_prefill(torch::Tensor proj, torch::Tensor conv_w, torch::Tensor ring, t
   auto f32 = proj.options().dtype(at::kFloat);
   auto qn = torch::zeros({Hk, Tp, D}, bfo), kn = torch::zeros({Hk, Tp, D}, bfo), vn = torch::zeros({Hv, Tp, D}, bfo);
   auto g = torch::zeros({Hv, Tp}, f32), beta = torch::zeros({Hv, Tp}, f32);
-  auto U = torch::empty({Hv, nch, kGC, D}, f32), Wm = torch::empty({Hv, nch, kGC, D}, f32);
-  auto P = torch::empty({Hv, nch, kGC, kGC}, f32), GC = torch::empty({Hv, nch, kGC}, f32);
+  auto U = torch::empty({Hv, nch, kGC, D}, bfo), Wm = torch::empty({Hv, nch, kGC, D}, bfo);
+  auto Qg = torch::empty({Hv, nch, kGC, D}, bfo), Kd = torch::empty({Hv, nch, kGC, D}, bfo);
+  auto P = torch::empty({Hv, nch, kGC, kGC}, bfo), GC = torch::empty({Hv, nch, kGC}, f32);
   auto o = torch::empty({T, Hv, D}, bfo);
   auto st = at::cuda::getCurrentCUDAStream();
   const int KC = conv_w.size(1);
@@ -368,18 +476,17 @@ void gdn_prefill(torch::Tensor proj, torch::Tensor conv_w, torch::Tensor ring, t
                                                              (int)p0, A_log.data_ptr<float>(),                      \
                                                              dt_bias.data_ptr<float>(), Hk, Hv, Tp, bp(qn), bp(kn), \
                                                              bp(vn), g.data_ptr<float>(), beta.data_ptr<float>());  \
-    const size_t sm1 = (3 * kGC * (DD + 1) + kGC * (kGC + 1) + 3 * kGC) * 4;                                            \
+    const size_t sm1 = (size_t)(4 * kGC * (DD + 8) + kGC * (kGC + 8)) * 2 + (size_t)(kGC * (kGC + 1) + 2 * kGC) * 4; \
     HX_CUDA_CHECK(cudaFuncSetAttribute(gdn_chunk_kernel<DD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm1)); \
     gdn_chunk_kernel<DD><<<dim3(nch, Hv), 256, sm1, st>>>(bp(qn), bp(kn), bp(vn), g.data_ptr<float>(),             \
-                                                          beta.data_ptr<float>(), Hk, Hv, Tp, U.data_ptr<float>(), \
-                                                          Wm.data_ptr<float>(), P.data_ptr<float>(),               \
-                                                          GC.data_ptr<float>());                                    \
-    const size_t sm2 = (DD * 32 + 2 * kGC * (DD + 4) + DD * (kGC + 4) + kGC * (kGC + 4) + kGC * 32 + kGC) * 4;                       \
+                                                          beta.data_ptr<float>(), Hk, Hv, Tp, bp(U), bp(Wm), bp(P), \
+                                                          bp(Qg), bp(Kd), GC.data_ptr<float>());                    \
+    const size_t sm2 = (size_t)(2 * (3 * kGC * (DD + 8) + kGC * (kGC + 8) + kGC * 40) + 32 * (DD + 8) +          \
+                                32 * (kGC + 8)) * 2;                                                              \
     HX_CUDA_CHECK(cudaFuncSetAttribute(gdn_scan_kernel<DD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm2)); \
-    gdn_scan_kernel<DD><<<dim3(DD / 32, Hv), 256, sm2, st>>>(bp(qn), bp(kn), U.data_ptr<float>(),                 \
-                                                             Wm.data_ptr<float>(), P.data_ptr<float>(),            \
-                                                             GC.data_ptr<float>(), state.data_ptr<float>(), Hk, Hv,\
-                                                             Tp, T, nch, bp(o));                                   \
+    gdn_scan_kernel<DD><<<dim3(DD / 32, Hv), 256, sm2, st>>>(bp(U), bp(Wm), bp(P), bp(Qg), bp(Kd),                \
+                                                             GC.data_ptr<float>(), state.data_ptr<float>(), Hv, T, \
+                                                             nch, bp(o));                                          \
     gdn_onorm_kernel<DD><<<dim3(T, Hv), DD, 0, st>>>(bp(o), bp(proj), ldp, 2 * Hk * DD + Hv * DD,                  \
                                                      norm_w.data_ptr<float>(), (float)eps, Hv, bp(out));            \
   }

@@ -191,7 +191,8 @@ def test_embed_and_argmax():
     assert torch.equal(out[:, 0], tok)
 
 
-@pytest.mark.parametrize("T,p0,D", [(200, 0, 128), (70, 5, 128), (33, 0, 32), (130, 64, 32)])
+@pytest.mark.parametrize("T,p0,D", [(200, 0, 128), (70, 5, 128), (33, 0, 32), (130, 64, 32), (513, 0, 64),
+                                    (1000, 7, 128)])
 def test_gdn_prefill_matches_reference(T, p0, D):
     C = _C()
     torch.manual_seed(7)
