@@ -97,8 +97,14 @@ __global__ void __launch_bounds__(192, 1) gemm_tcgen05_kernel(const __grid_const
   const uint32_t tmem = s->tmem_base;
 
   auto tile_coords = [&](int t, int& a_row, int& b_row, int& rows, int& out_row, int& n_blk) {
-    const int e = t % num_entries;
-    n_blk = t / num_entries;
+    // Grouped (expert) GEMMs walk entry-major: the n-blocks of one A tile and the tiles
+    // of one expert run on neighbouring CTAs at the same time, so each A tile and each
+    // expert's weight block is fetched from DRAM about once and re-read from L2 (the
+    // routed activations and the experts together are far larger than L2). Plain GEMMs
+    // keep n-major order (consecutive CTAs share a weight block).
+    int e;
+    if (p.tiles) { e = t / p.num_n_blocks; n_blk = t - e * p.num_n_blocks; }
+    else { e = t % num_entries; n_blk = t / num_entries; }
     if (p.tiles) {
       const GemmTile g = p.tiles[e];
       a_row = g.a_row0; b_row = g.b_row0 * p.b_rows_per_group + n_blk * BN; rows = g.rows; out_row = g.out_row0;

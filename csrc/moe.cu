@@ -152,26 +152,52 @@ __global__ void moe_route_topk_kernel(const float* __restrict__ logits, int ld, 
   }
 }
 
-// Step 2 (one CTA): exclusive scan of counts -> offsets; grouped-GEMM tile table of
-// 128-row blocks (a_row0, group, rows, out_row0); cursor copy for step 3.
-__global__ void moe_route_plan_kernel(const int* __restrict__ counts, int G, int* __restrict__ offsets,
-                                      int* __restrict__ cursor, int* __restrict__ tiles, int* __restrict__ ntiles,
-                                      int max_tiles) {
-  if (threadIdx.x != 0) return;
-  int off = 0, nt = 0;
-  for (int g = 0; g < G; ++g) {
-    const int c = counts[g];
+// Step 2 (one CTA of 1024 threads, one group per thread): exclusive scans of the
+// counts (-> offsets, cursor) and of the per-group 128-row tile counts (-> where each
+// group writes its tiles); tile table rows are (a_row0, group, rows, out_row0).
+__global__ void __launch_bounds__(1024) moe_route_plan_kernel(const int* __restrict__ counts, int G,
+                                                              int* __restrict__ offsets, int* __restrict__ cursor,
+                                                              int* __restrict__ tiles, int* __restrict__ ntiles,
+                                                              int max_tiles) {
+  __shared__ int wsum[2][32];
+  const int g = threadIdx.x, lane = g & 31, warp = g >> 5;
+  const int c = g < G ? counts[g] : 0;
+  const int nt = (c + 127) / 128;
+  // inclusive warp scans of (count, tiles)
+  int x = c, y = nt;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int xs = __shfl_up_sync(0xffffffffu, x, o), ys = __shfl_up_sync(0xffffffffu, y, o);
+    if (lane >= o) { x += xs; y += ys; }
+  }
+  if (lane == 31) { wsum[0][warp] = x; wsum[1][warp] = y; }
+  __syncthreads();
+  if (warp == 0) {
+    int a = wsum[0][lane], b = wsum[1][lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int as = __shfl_up_sync(0xffffffffu, a, o), bs = __shfl_up_sync(0xffffffffu, b, o);
+      if (lane >= o) { a += as; b += bs; }
+    }
+    wsum[0][lane] = a;  // inclusive totals through warp `lane`
+    wsum[1][lane] = b;
+  }
+  __syncthreads();
+  const int off = x - c + (warp ? wsum[0][warp - 1] : 0);
+  const int t0 = y - nt + (warp ? wsum[1][warp - 1] : 0);
+  if (g < G) {
     offsets[g] = off;
     cursor[g] = off;
-    for (int m0 = 0; m0 < c && nt < max_tiles; m0 += 128, ++nt) {
-      tiles[nt * 4 + 0] = off + m0;
-      tiles[nt * 4 + 1] = g;
-      tiles[nt * 4 + 2] = min(128, c - m0);
-      tiles[nt * 4 + 3] = off + m0;
+    for (int i = 0; i < nt && t0 + i < max_tiles; ++i) {
+      const int m0 = i * 128;
+      int* tr = tiles + (long long)(t0 + i) * 4;
+      tr[0] = off + m0;
+      tr[1] = g;
+      tr[2] = min(128, c - m0);
+      tr[3] = off + m0;
     }
-    off += c;
   }
-  *ntiles = nt;
+  if (g == 1023) *ntiles = min(wsum[1][31], max_tiles);
 }
 
 // Step 3 (one thread per route): claim a row in its expert's segment, record it, and
@@ -238,7 +264,8 @@ void moe_route_prefill(torch::Tensor logits, int64_t E, int64_t k, bool has_shar
   moe_route_topk_kernel<<<(T * 32 + 255) / 256, 256, 0, st>>>(logits.data_ptr<float>(), logits.stride(0), T, E, k,
                                                               has_shared, norm_topk, ids.data_ptr<int>(),
                                                               wts.data_ptr<float>(), counts.data_ptr<int>());
-  moe_route_plan_kernel<<<1, 32, 0, st>>>(counts.data_ptr<int>(), G, offsets.data_ptr<int>(), cursor.data_ptr<int>(),
+  TORCH_CHECK(G <= 1024, "at most 1024 routing groups");
+  moe_route_plan_kernel<<<1, 1024, 0, st>>>(counts.data_ptr<int>(), G, offsets.data_ptr<int>(), cursor.data_ptr<int>(),
                                           tiles.data_ptr<int>(), ntiles.data_ptr<int>(), tiles.size(0));
   moe_route_place_kernel<<<((long long)T * J * 32 + 255) / 256, 256, 0, st>>>(
       ids.data_ptr<int>(), T, J, cursor.data_ptr<int>(), rows.data_ptr<int>(),
