@@ -112,7 +112,7 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(AttnDecodeArgs a) {
   constexpr int S = D / 16;        // MMA k-steps per tile
   constexpr int NT = (G + 7) / 8;  // MMA n-tiles of 8 heads
   constexpr int MAXC = 64;         // most cluster partials the final merge supports
-  constexpr int MAXCL = 8;         // largest cluster
+  constexpr int MAXCL = 16;        // largest cluster
   using VT = typename VSlice<PER>::T;
   extern __shared__ __align__(16) float dsm[];
   float (*qsm)[D] = reinterpret_cast<float (*)[D]>(dsm);                                  // [G][D]
@@ -336,6 +336,9 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(AttnDecodeArgs a) {
     kl[g] = Ls;
   }
   __syncthreads();
+  // One cluster covering every split of this (sequence, kv head) finishes the output
+  // here; otherwise it writes one partial for the cross-cluster merge below.
+  const bool single = (CL == a.nsplit);
   {
     const int cid = split / CL;
     const int per = G * D / CL;
@@ -343,12 +346,21 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(AttnDecodeArgs a) {
       const int g = t / D, d = t - g * D;
       float O = 0.f;
       for (int q = 0; q < CL; ++q) O += pw[g][q] * cluster.map_shared_rank(&wo[0][g][0], q)[d];
+      if (single) {
+        const int hq = kvh * G + g;
+        float o = kl[g] > 0.f ? O / kl[g] : 0.f;
+        o = __bfloat162float(__float2bfloat16(o));
+        if (a.gated) o = o * (1.f / (1.f + __expf(-__bfloat162float(pr[hq * qw + D + d]))));
+        a.out[(long long)b * a.Hq * D + hq * D + d] = __float2bfloat16(o);
+        continue;
+      }
       const long long pi = ((long long)b * a.Hq + kvh * G + g) * a.nsplit + cid;
       a.part_o[pi * D + d] = O;
       if (d == 0) { a.part_ml[pi * 2] = km[g]; a.part_ml[pi * 2 + 1] = kl[g]; }
     }
   }
   cluster.sync();  // peers' shared memory stays alive until every read of it is done
+  if (single) return;
   // ---- last CTA of this (b, kvh) merges the cluster partials --------------------
   __threadfence();
   __syncthreads();
@@ -431,8 +443,11 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(AttnDecodeArgs a) {
   if (threadIdx.x == 0) a.counters[b * a.Hkv + kvh] = 0;
 }
 
-// Cluster size for a split count: the largest of 8, 4, 2, 1 that divides it.
+// Cluster size for a split count: every split in one cluster when there are at most 16
+// and their number is a power of two (the output is finished on chip), else the
+// largest of 8, 4, 2, 1 that divides it.
 static inline int attn_cluster(int nsplit) {
+  if (nsplit <= 16 && (nsplit & (nsplit - 1)) == 0) return nsplit;
   for (int c = 8; c > 1; c >>= 1)
     if (nsplit % c == 0) return c;
   return 1;
@@ -448,6 +463,7 @@ static void launch_dg(const AttnDecodeArgs& a, dim3 grid, cudaStream_t s) {
   if (smem + 4096 > 48 * 1024) {
     HX_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   }
+  if (CL > 8) HX_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
   HX_CUDA_CHECK(hx_launch_pdl_cluster(k, grid, dim3(NW * 32), smem, s, CL, a));
 }
 

@@ -121,7 +121,8 @@ static inline cudaError_t hx_launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
-// Same, with thread-block clusters of `cluster_x` CTAs along x (grid.x must divide).
+// Same, with thread-block clusters of `cluster_x` CTAs along x (grid.x must divide;
+// more than 8 needs the kernel's non-portable cluster size attribute).
 template <typename... KArgs, typename... Args>
 static inline cudaError_t hx_launch_pdl_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
                                                 cudaStream_t st, int cluster_x, Args&&... args) {
@@ -129,7 +130,7 @@ static inline cudaError_t hx_launch_pdl_cluster(void (*kernel)(KArgs...), dim3 g
   cudaError_t e = cudaFuncGetAttributes(&fa, reinterpret_cast<const void*>(kernel));
   if (e != cudaSuccess) return e;
   if ((int)(block.x * block.y * block.z) > fa.maxThreadsPerBlock ||
-      (long long)smem > (long long)fa.maxDynamicSharedSizeBytes || cluster_x < 1 || cluster_x > 8 ||
+      (long long)smem > (long long)fa.maxDynamicSharedSizeBytes || cluster_x < 1 || cluster_x > 16 ||
       grid.x % cluster_x)
     return cudaErrorInvalidConfiguration;
   cudaLaunchConfig_t cfg = {};

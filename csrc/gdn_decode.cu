@@ -1,6 +1,6 @@
 // Gated DeltaNet single-token decode step, fully fused.
 //
-// One CTA per (value head, sequence). From the bf16 in-projection output it
+// VS CTAs (a cluster) per (value head, sequence). From the bf16 in-projection output it
 // performs, without leaving the CTA:
 //   causal conv1d update (K taps, ring-buffer state, SiLU)  -- gdn.cu:488-547 in the ref
 //   gating beta = sigmoid(b), g = -exp(A_log) * softplus(a + dt_bias) -- gdn.cu:658-711
@@ -15,7 +15,11 @@
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 
+#include <cooperative_groups.h>
+
 #include "common.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace hx {
 
@@ -35,25 +39,33 @@ struct GdnDecodeArgs {
   float eps;
 };
 
-template <int DK, int DV>
-__global__ void __launch_bounds__(512) gdn_decode_kernel(GdnDecodeArgs a) {
-  constexpr int NT = 512;
-  constexpr int NKG = NT / DV;       // k-row groups
+// grid (Hv * VS, B) in clusters of VS CTAs: the VS CTAs of one value head each own
+// DV / VS state columns (the delta rule is independent across value columns) and
+// recompute the head's q/k conv and norms; the gated RMSNorm over the head's DV outputs
+// sums the CTAs' partial squares through distributed shared memory.
+template <int DK, int DV, int VS>
+__global__ void __launch_bounds__(256) gdn_decode_kernel(GdnDecodeArgs a) {
+  constexpr int NT = 256;
+  constexpr int DVS = DV / VS;       // value columns of this CTA
+  constexpr int NKG = NT / DVS;      // k-row groups
   constexpr int RK = DK / NKG;       // state rows per thread
-  static_assert(NT % DV == 0 && DK % NKG == 0, "bad tile");
-  __shared__ float qs[DK], ks[DK], vs[DV], zs[DV];
-  __shared__ float red[NKG][DV];
+  static_assert(NT % DVS == 0 && DK % NKG == 0, "bad tile");
+  __shared__ float qs[DK], ks[DK], vs[DVS], zs[DVS];
+  __shared__ float red[NKG][DVS];
   __shared__ float scal[4];
-  __shared__ float wred[16];
+  __shared__ float wred[NT / 32];
+  __shared__ float css;              // this CTA's sum of squared outputs (read by peers)
 
-  const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int vsi = blockIdx.x % VS, h = blockIdx.x / VS, b = blockIdx.y, tid = threadIdx.x;
+  const int col0 = vsi * DVS;
   // slots (host-written before launch) and the recurrent state (last written by this
   // layer's kernel in an earlier step) may be read before the dependency wait; the
   // position may not: with programmatic launch this kernel can start while the
   // previous step's arg-max, which advances it, is still running.
   const int slot = a.slots[b];
-  const int v_ = tid % DV, kg_ = tid / DV;
-  float* S = a.rec + (((long long)slot * a.Hv + h) * DK) * DV;
+  const int v_ = tid % DVS, kg_ = tid / DVS;
+  float* S = a.rec + (((long long)slot * a.Hv + h) * DK) * DV + col0;
   float s[RK];
 #pragma unroll
   for (int i = 0; i < RK; ++i) s[i] = S[(kg_ * RK + i) * DV + v_];
@@ -66,13 +78,13 @@ __global__ void __launch_bounds__(512) gdn_decode_kernel(GdnDecodeArgs a) {
   const __nv_bfloat16* pr = a.proj + (long long)b * a.ldp;
   __nv_bfloat16* ring = a.conv_ring + (long long)slot * C * a.KC;
 
-  // ---- conv update for this head's q, k, v channels -------------------
-  for (int t = tid; t < 2 * DK + DV; t += NT) {
+  // ---- conv update for this head's q, k channels and this CTA's v channels ----
+  for (int t = tid; t < 2 * DK + DVS; t += NT) {
     int c;
     bool owner;
-    if (t < DK) { c = kh * DK + t; owner = (h % r) == 0; }
-    else if (t < 2 * DK) { c = kd + kh * DK + (t - DK); owner = (h % r) == 0; }
-    else { c = 2 * kd + h * DV + (t - 2 * DK); owner = true; }
+    if (t < DK) { c = kh * DK + t; owner = (h % r) == 0 && vsi == 0; }
+    else if (t < 2 * DK) { c = kd + kh * DK + (t - DK); owner = (h % r) == 0 && vsi == 0; }
+    else { c = 2 * kd + h * DV + col0 + (t - 2 * DK); owner = true; }
     __nv_bfloat16 xcur = pr[c];
     float acc = a.conv_w[c * a.KC + a.KC - 1] * __bfloat162float(xcur);
     for (int j = 0; j < a.KC - 1; ++j) {
@@ -86,7 +98,7 @@ __global__ void __launch_bounds__(512) gdn_decode_kernel(GdnDecodeArgs a) {
     else if (t < 2 * DK) ks[t - DK] = y;
     else vs[t - 2 * DK] = y;
   }
-  if (tid < DV) zs[tid] = __bfloat162float(pr[2 * kd + a.Hv * DV + h * DV + tid]);
+  if (tid < DVS) zs[tid] = __bfloat162float(pr[2 * kd + a.Hv * DV + h * DV + col0 + tid]);
   if (tid == 0) {
     float bb = __bfloat162float(pr[2 * kd + 2 * a.Hv * DV + h]);
     float aa = __bfloat162float(pr[2 * kd + 2 * a.Hv * DV + a.Hv + h]);
@@ -134,7 +146,7 @@ __global__ void __launch_bounds__(512) gdn_decode_kernel(GdnDecodeArgs a) {
   __syncthreads();  // everyone has consumed red[] for kv
   red[kg][v] = y;
   __syncthreads();
-  // ---- gated RMSNorm over the head's Dv outputs --------------------------
+  // ---- gated RMSNorm over the head's DV outputs (VS CTAs) ----------------
   float o = 0.f;
   if (kg == 0) {
 #pragma unroll
@@ -145,12 +157,26 @@ __global__ void __launch_bounds__(512) gdn_decode_kernel(GdnDecodeArgs a) {
   ss = warp_sum(ss);
   if ((tid & 31) == 0) wred[tid >> 5] = ss;
   __syncthreads();
-  if (kg == 0) {
+  if (tid == 0) {
     float tot = 0.f;
-    for (int w = 0; w < (DV + 31) / 32; ++w) tot += wred[w];
+#pragma unroll
+    for (int w = 0; w < NT / 32; ++w) tot += wred[w];
+    css = tot;
+  }
+  float tot = 0.f;
+  if constexpr (VS > 1) {
+    cluster.sync();
+#pragma unroll
+    for (int q = 0; q < VS; ++q) tot += *cluster.map_shared_rank(&css, q);
+    cluster.sync();  // peers keep their shared memory until every read is done
+  } else {
+    __syncthreads();
+    tot = css;
+  }
+  if (kg == 0) {
     float inv = rsqrtf(tot / DV + a.eps);
-    float nrm = __bfloat162float(__float2bfloat16(o * inv)) * a.norm_w[v];
-    a.out[(long long)b * a.Hv * DV + h * DV + v] = __float2bfloat16(nrm * silu(zs[v]));
+    float nrm = __bfloat162float(__float2bfloat16(o * inv)) * a.norm_w[col0 + v];
+    a.out[(long long)b * a.Hv * DV + h * DV + col0 + v] = __float2bfloat16(nrm * silu(zs[v]));
   }
 }
 
@@ -179,10 +205,13 @@ void gdn_decode(torch::Tensor proj, torch::Tensor conv_w, torch::Tensor conv_rin
   a.Hk = Hk; a.Hv = Hv; a.KC = conv_w.size(1); a.eps = (float)eps;
   const int B = slots.numel();
   TORCH_CHECK(conv_ring.size(2) == a.KC, "ring slots must equal conv kernel size");
-  dim3 grid(Hv, B);
   auto s = at::cuda::getCurrentCUDAStream();
-  if (Dk == 128 && Dv == 128) HX_CUDA_CHECK(hx_launch_pdl(gdn_decode_kernel<128, 128>, grid, dim3(512), 0, s, a));
-  else if (Dk == 64 && Dv == 64) HX_CUDA_CHECK(hx_launch_pdl(gdn_decode_kernel<64, 64>, grid, dim3(512), 0, s, a));
-  else if (Dk == 32 && Dv == 32) HX_CUDA_CHECK(hx_launch_pdl(gdn_decode_kernel<32, 32>, grid, dim3(512), 0, s, a));
+  // VS CTAs per value head (32 value columns each)
+  if (Dk == 128 && Dv == 128)
+    HX_CUDA_CHECK(hx_launch_pdl_cluster(gdn_decode_kernel<128, 128, 4>, dim3(Hv * 4, B), dim3(256), 0, s, 4, a));
+  else if (Dk == 64 && Dv == 64)
+    HX_CUDA_CHECK(hx_launch_pdl_cluster(gdn_decode_kernel<64, 64, 2>, dim3(Hv * 2, B), dim3(256), 0, s, 2, a));
+  else if (Dk == 32 && Dv == 32)
+    HX_CUDA_CHECK(hx_launch_pdl_cluster(gdn_decode_kernel<32, 32, 1>, dim3(Hv, B), dim3(256), 0, s, 1, a));
   else TORCH_CHECK(false, "unsupported GDN head dims");
 }

@@ -64,13 +64,82 @@ HX_DEVICE unsigned long long argmax_key(float v, int idx) {
   return ((unsigned long long)u << 32) | (unsigned)(0x7fffffff - idx);
 }
 
-template <int B, int RPW, int MODE>
+// Router tail for batch row b (one warp): softmax max / denominator over E logits and
+// top-k selection. Each lane holds experts e = lane + 32 i as 64-bit keys (ordered
+// value bits, then 0x7fffffff - e, so the larger key is the larger logit and, on ties,
+// the lower expert) and its own best key (a tree max). Each round takes the warp's
+// largest key with two hardware max reductions (high word, then the low word among the
+// lanes holding that high word); only the winning lane clears the key and redoes its
+// tree max. The selected logits become softmax probabilities, optionally renormalised.
+template <int PER>
+HX_DEVICE unsigned long long tree_max(const unsigned long long (&k)[PER]) {
+  unsigned long long t[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) t[i] = k[i];
+#pragma unroll
+  for (int w = PER / 2; w > 0; w >>= 1)
+#pragma unroll
+    for (int i = 0; i < w; ++i) t[i] = t[i] > t[i + w] ? t[i] : t[i + w];
+  return t[0];
+}
+
+template <int PER>
+HX_DEVICE void router_tail(const GemvArgs& a, int b, int lane) {
+  const float* lg = reinterpret_cast<const float*>(a.y) + (long long)b * a.ldy;
+  float v[PER];
+  unsigned long long key[PER];
+  float m = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int e = lane + 32 * i;
+    v[i] = e < a.E ? __ldcg(&lg[e]) : -INFINITY;
+    key[i] = e < a.E ? argmax_key(v[i], e) : 0ull;
+    m = fmaxf(m, v[i]);
+  }
+  m = warp_max(m);
+  float den = 0.f;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) den += (lane + 32 * i) < a.E ? expf(v[i] - m) : 0.f;
+  den = warp_sum(den);
+  unsigned long long lbest = tree_max<PER>(key), mine = 0ull;
+  for (int j = 0; j < a.topk; ++j) {
+    const unsigned hi = __reduce_max_sync(0xffffffffu, (unsigned)(lbest >> 32));
+    const unsigned lo = __reduce_max_sync(0xffffffffu, (unsigned)(lbest >> 32) == hi ? (unsigned)lbest : 0u);
+    const unsigned long long win = ((unsigned long long)hi << 32) | lo;
+    if (lane == j) mine = win;
+    if (lbest == win) {
+#pragma unroll
+      for (int i = 0; i < PER; ++i)
+        if (key[i] == win) key[i] = 0ull;
+      lbest = tree_max<PER>(key);
+    }
+  }
+  float pj = 0.f;
+  int id = 0;
+  if (lane < a.topk) {
+    unsigned u = (unsigned)(mine >> 32);
+    u = (u & 0x80000000u) ? (u & 0x7fffffffu) : ~u;  // invert argmax_key's ordering map
+    id = 0x7fffffff - (int)(mine & 0xffffffffu);
+    pj = expf(__uint_as_float(u) - m) / den;
+  }
+  const float sel = warp_sum(pj);
+  const int ldo = a.topk + (a.has_shared ? 1 : 0);
+  if (lane < a.topk) {
+    a.out_ids[b * ldo + lane] = id;
+    a.out_wts[b * ldo + lane] = a.norm_topk ? pj / sel : pj;
+  }
+  if (a.has_shared && lane == 0) {
+    a.out_ids[b * ldo + a.topk] = a.E;
+    a.out_wts[b * ldo + a.topk] = 1.f / (1.f + expf(-__ldcg(&lg[a.E])));
+  }
+}
+
+template <int B, int RPW, int MODE, int U>
 __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem_raw);  // [B][K]
   __shared__ float red[8];
   __shared__ int is_last;
-  constexpr int U = 4;
   const int K = a.K, nvec = K / 8;
   const int job = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -273,7 +342,7 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
   __syncthreads();
   if (!is_last) return;
   __threadfence();
-  if (MODE == kArgmax) {
+  if constexpr (MODE == kArgmax) {
     if (threadIdx.x < B) {
       const int b = threadIdx.x;
       const unsigned long long k = atomicExch(&a.best[b], 0ull);
@@ -287,55 +356,12 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
       }
       if (a.pos) a.pos[a.slots[b]] += 1;
     }
-  } else if (warp < B) {
-    // router: softmax over E, top-k (lowest index on ties), optional renorm, shared expert
-    const int b = warp;
-    const float* lg = reinterpret_cast<const float*>(a.y) + (long long)b * a.ldy;
-    constexpr int PER = 32;  // E <= 1024
-    float v[PER];
-    float m = -INFINITY;
-#pragma unroll
-    for (int i = 0; i < PER; ++i) {
-      int e = lane + 32 * i;
-      v[i] = e < a.E ? __ldcg(&lg[e]) : -INFINITY;
-      m = fmaxf(m, v[i]);
-    }
-    m = warp_max(m);
-    float den = 0.f;
-#pragma unroll
-    for (int i = 0; i < PER; ++i) den += (lane + 32 * i) < a.E ? expf(v[i] - m) : 0.f;
-    den = warp_sum(den);
-    float sel = 0.f, my_p = 0.f;
-    int my_id = -1;
-    for (int j = 0; j < a.topk; ++j) {
-      float bv = -INFINITY;
-      int bi = 0x7fffffff;
-#pragma unroll
-      for (int i = 0; i < PER; ++i) {
-        int e = lane + 32 * i;
-        if (e < a.E && (v[i] > bv || (v[i] == bv && e < bi))) { bv = v[i]; bi = e; }
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
-      }
-      float pj = expf(bv - m) / den;
-      sel += pj;
-      if (lane == j) { my_id = bi; my_p = pj; }
-#pragma unroll
-      for (int i = 0; i < PER; ++i)
-        if (lane + 32 * i == bi) v[i] = -INFINITY;
-    }
-    const int ldo = a.topk + (a.has_shared ? 1 : 0);
-    if (lane < a.topk) {
-      a.out_ids[b * ldo + lane] = my_id;
-      a.out_wts[b * ldo + lane] = a.norm_topk ? my_p / sel : my_p;
-    }
-    if (a.has_shared && lane == 0) {
-      a.out_ids[b * ldo + a.topk] = a.E;
-      a.out_wts[b * ldo + a.topk] = 1.f / (1.f + expf(-__ldcg(&lg[a.E])));
+  } else {
+    // router: softmax over E, top-k (lowest index on ties), optional renorm, shared
+    // expert -- one warp per batch row, no block barriers.
+    if (warp < B) {
+      if (a.E <= 512) router_tail<16>(a, warp, lane);
+      else router_tail<32>(a, warp, lane);
     }
   }
   if (threadIdx.x == 0) *a.counter = 0;
@@ -346,7 +372,13 @@ static void launch_b(const GemvArgs& a, int jobs, cudaStream_t s) {
   constexpr int RPW = 2;
   dim3 grid((a.N + 8 * RPW - 1) / (8 * RPW), jobs);
   size_t smem = (size_t)B * a.K * sizeof(__nv_bfloat16);
-  auto k = gemv_kernel<B, RPW, MODE>;
+  // U = 16-byte loads per lane and row per batch (two batches in flight). Long rows of
+  // the row-parallel projections (K >= 4096, few CTAs) take 8 so that a lane's whole
+  // slice is in flight at once; elsewhere 4 keeps two CTAs per SM (156 vs 90 registers).
+  auto k = gemv_kernel<B, RPW, MODE, 4>;
+  if constexpr (MODE == kResidAdd || MODE == kResidAddTP || MODE == kStoreBf16) {
+    if (a.K >= 4096) k = gemv_kernel<B, RPW, MODE, 8>;
+  }
   if (smem + 4096 > 48 * 1024) {
     HX_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   }

@@ -21,6 +21,8 @@ def main():
     ap.add_argument("--splits", type=int, default=32)
     ap.add_argument("--iters", type=int, default=50)
     ap.add_argument("--graph", action="store_true", help="time replays of a CUDA graph of the launches")
+    ap.add_argument("--cold", action="store_true",
+                    help="write a 256 MB buffer (2x L2) before every launch and subtract the time of the writes alone")
     args = ap.parse_args()
     C = ops.C
     D, Hq, Hkv = args.dim, args.hq, args.hkv
@@ -43,34 +45,43 @@ def main():
         C.attn_decode(proj, qn, qn, inv, kc, vc, slots, pos, part_o, part_ml, cnt, out, Hq, Hkv, D, D // 4, gated,
                       1e-6)
 
-    for _ in range(5):
-        run()
-    torch.cuda.synchronize()
-    body = run
-    if args.graph:
-        g = torch.cuda.CUDAGraph()
-        s = torch.cuda.Stream()
-        s.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(s):
-            with torch.cuda.graph(g, stream=s):
-                for _ in range(args.iters):
-                    run()
-        torch.cuda.current_stream().wait_stream(s)
-        g.replay()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+
+    def timed(fn) -> float:
+        for _ in range(5):
+            fn()
         torch.cuda.synchronize()
-        body = None
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    if body is None:
-        g.replay()
+        body = fn
+        if args.graph:
+            g = torch.cuda.CUDAGraph()
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s):
+                with torch.cuda.graph(g, stream=s):
+                    for _ in range(args.iters):
+                        fn()
+            torch.cuda.current_stream().wait_stream(s)
+            g.replay()
+            torch.cuda.synchronize()
+            body = None
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        if body is None:
+            g.replay()
+        else:
+            for _ in range(args.iters):
+                body()
+        e1.record()
+        e1.synchronize()
+        return e0.elapsed_time(e1)
+
+    if args.cold:
+        ms = timed(lambda: (flush.fill_(1), run())) - timed(lambda: flush.fill_(1))
     else:
-        for _ in range(args.iters):
-            body()
-    e1.record()
-    e1.synchronize()
-    us = e0.elapsed_time(e1) / args.iters * 1e3
+        ms = timed(run)
+    us = ms / args.iters * 1e3
     kv_bytes = 2 * Hkv * (args.context + 1) * D * 2
-    print(json.dumps({"context": args.context, "hq": Hq, "hkv": Hkv, "dim": D, "splits": args.splits, "graph": args.graph,
+    print(json.dumps({"context": args.context, "hq": Hq, "hkv": Hkv, "dim": D, "splits": args.splits, "graph": args.graph, "cold": args.cold,
                       "us": round(us, 2), "kv_MB": round(kv_bytes / 1e6, 2),
                       "GBps": round(kv_bytes / us / 1e3, 1)}))
 
