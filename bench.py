@@ -173,7 +173,7 @@ def main() -> None:
         t1 = e2e.clone()
         dist.all_reduce(t1, op=dist.ReduceOp.MAX)
         e2e = torch.tensor([t0[0], t1[1]])
-    launches = model.launches_per_step() * dec_tokens * args.steps
+    launches = (model.launches_per_step() * dec_tokens + model.prefill_launches()) * args.steps
     if rank == 0:
         line = {
             "metric": "decode tok/s (bs=1) + p50 TTFT, Qwen3-Next-80B-A3B bf16",
@@ -189,7 +189,7 @@ def main() -> None:
             "e2e": {"value": round(float(e2e[0]), 2), "unit": "tok/s",
                     "ttft_p50_ms": round(float(e2e[1]) * 1e3, 2),
                     "h2d_bytes_per_step": args.prompt * 4, "d2h_bytes_per_step": args.decode * 4 + 4},
-            "gpu_launches": launches, "gpu_launches_scope": "decode kernels only (prefill still uses torch ops)",
+            "gpu_launches": launches, "gpu_launches_scope": "this package's kernels per request (prefill + every decode step) x steps; PyTorch ops in prefill (SDPA attention core, RoPE, embedding gather) not counted",
             "clocks": clocks,
         }
         print(json.dumps(line), flush=True)
