@@ -21,6 +21,8 @@ void gemv_ar(torch::Tensor W, torch::Tensor inp, torch::Tensor x, std::vector<in
 void moe_down_ar(torch::Tensor Wd, torch::Tensor act, torch::Tensor ids, torch::Tensor wts, torch::Tensor x,
                  std::vector<int64_t> bases, int64_t rank, int64_t slot_elems, torch::Tensor epoch, torch::Tensor err,
                  double timeout_s);
+void attn_prefill(torch::Tensor q, torch::Tensor kc, torch::Tensor vc, torch::Tensor out, int64_t Hq, int64_t p0,
+                  double scale);
 void moe_combine(torch::Tensor y, torch::Tensor rows, torch::Tensor wts, torch::Tensor x);
 void moe_route_prefill(torch::Tensor logits, int64_t E, int64_t k, bool has_shared, bool norm_topk, torch::Tensor hn,
                        torch::Tensor ids, torch::Tensor wts, torch::Tensor rows, torch::Tensor counts,
@@ -76,6 +78,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_grouped_dev", &gemm_grouped_dev);
   m.def("gdn_decode", &gdn_decode);
   m.def("attn_decode", &attn_decode);
+  m.def("attn_prefill", &attn_prefill);
   m.def("embed", &embed);
   m.def("argmax_step", &argmax_step);
   m.def("ipc_alloc", &ipc_alloc);

@@ -465,6 +465,12 @@ class FastModel:
         self.kc[i][slot, :, p0:p0 + T] = k.transpose(0, 1)
         self.vc[i][slot, :, p0:p0 + T] = v.transpose(0, 1)
         L = p0 + T
+        if self.C is not None:
+            o = torch.empty(T, d.hq * D, dtype=torch.bfloat16, device=h.device)
+            self.C.attn_prefill(q.reshape(T, d.hq * D), self.kc[i][slot], self.vc[i][slot], o, d.hq, p0, D ** -0.5)
+            if gate is not None:
+                o = (o.float() * torch.sigmoid(gate.reshape(T, d.hq * D).float())).to(torch.bfloat16)
+            return self._linear(o, lw["o_w"])
         Kc, Vc = self.kc[i][slot, :, :L], self.vc[i][slot, :, :L]
         if p0 == 0:
             o = torch.nn.functional.scaled_dot_product_attention(

@@ -226,3 +226,30 @@ def test_gdn_prefill_matches_reference(T, p0, D):
     want = R.gated_rms_norm(o, z, nw, 1e-6).reshape(T, vd)
     _close(S, S1, 2e-2)
     _close(out, want, 3e-2)
+
+
+@pytest.mark.parametrize("T,p0,D,Hq,Hkv", [(200, 0, 256, 16, 2), (70, 33, 128, 8, 8), (1, 100, 64, 4, 2),
+                                          (300, 129, 256, 4, 1), (64, 0, 128, 4, 4), (700, 50, 256, 4, 2),
+                                          (1030, 0, 128, 8, 2)])
+def test_attn_prefill_matches_fp32(T, p0, D, Hq, Hkv):
+    """Causal GQA prefill over the cache (keys 0..p0+T-1) against an fp32 softmax of the
+    same bf16 inputs; covers partial query tiles, an earlier prefix (p0 > 0), a single
+    token, grouped query heads and both CTA shapes (4 and 8 warps)."""
+    C = _C()
+    torch.manual_seed(11)
+    L, maxlen = p0 + T, p0 + T + 37
+    q = torch.randn(T, Hq * D, device="cuda").bfloat16()
+    kc = torch.randn(Hkv, maxlen, D, device="cuda").bfloat16()
+    vc = torch.randn(Hkv, maxlen, D, device="cuda").bfloat16()
+    out = torch.empty(T, Hq * D, device="cuda", dtype=torch.bfloat16)
+    C.attn_prefill(q, kc, vc, out, Hq, p0, D ** -0.5)
+    torch.cuda.synchronize()
+    G = Hq // Hkv
+    qf = q.float().view(T, Hq, D).transpose(0, 1)                       # [Hq, T, D]
+    kf = kc[:, :L].float().repeat_interleave(G, 0)                       # [Hq, L, D]
+    vf = vc[:, :L].float().repeat_interleave(G, 0)
+    sc = torch.einsum("htd,hld->htl", qf, kf) * D ** -0.5
+    mask = torch.arange(L, device="cuda")[None, :] <= (p0 + torch.arange(T, device="cuda"))[:, None]
+    sc = sc.masked_fill(~mask[None], float("-inf"))
+    want = torch.einsum("htl,hld->htd", torch.softmax(sc, -1), vf).transpose(0, 1).reshape(T, Hq * D)
+    _close(out, want, 2e-2)
