@@ -314,12 +314,12 @@ class FastModel:
         return n
 
     def prefill_launches(self) -> int:
-        """Kernels of this package one prefill launches (PyTorch ops such as the SDPA
-        attention core, RoPE and embedding gather are not counted)."""
+        """Kernels of this package one prefill launches (PyTorch ops such as RoPE, the
+        output gate and the embedding gather are not counted)."""
         cfg = self.cfg
         n = 1  # lm_head GEMM of the last token
         for i in range(cfg.num_hidden_layers):
-            n += 5 + 2 if cfg.is_linear(i) else 2          # in_proj, prep, chunk, scan, onorm, out | qkv, o
+            n += 5 + 2 if cfg.is_linear(i) else 3          # in_proj, prep, chunk, scan, onorm, out | qkv, attn, o
             n += 7 if cfg.layer_uses_moe(i) else 2          # router, topk, plan, place, 2 grouped, combine | 2 GEMMs
         return n
 
