@@ -64,6 +64,7 @@ torch::Tensor gguf_quant_host(torch::Tensor x, int64_t type);
 void gguf_gemv(torch::Tensor W, int64_t type, int64_t K, torch::Tensor x, torch::Tensor y, int64_t mode,
                c10::optional<torch::Tensor> resid, c10::optional<torch::Tensor> norm_w, double eps);
 void gguf_dequant(torch::Tensor W, int64_t type, int64_t K, torch::Tensor out);
+torch::Tensor gguf_quant(torch::Tensor W, int64_t type);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("set_pdl", [](bool on) { hx_pdl_enabled() = on; });
@@ -90,6 +91,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gguf_quant_host", &gguf_quant_host);
   m.def("gguf_gemv", &gguf_gemv);
   m.def("gguf_dequant", &gguf_dequant);
+  m.def("gguf_quant", &gguf_quant);
   m.def("gdn_prefill", &gdn_prefill);
   m.def("gemv_router", &gemv_router);
   m.def("gemv_argmax", &gemv_argmax);

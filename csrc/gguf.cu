@@ -215,6 +215,121 @@ static void block_of(int t, int& bb, int& bv) {
   else TORCH_CHECK(false, "unsupported GGUF type ", t);
 }
 
+// ---- in-situ quantization on the device (the reference's parallel ISQ,
+// tp/isq.rs:252-326): the same direct min/max fits as the host codecs in
+// gguf_host.cpp (round-to-nearest-even everywhere), so the bytes match the host
+// quantizer's; one thread per block.
+// Every f16 field of the three block formats sits at an even offset of an even-sized
+// row, so it is stored as one 16-bit write.
+HX_DEVICE void put_half(uint8_t* p, __half h) { *reinterpret_cast<unsigned short*>(p) = __half_as_ushort(h); }
+
+HX_DEVICE void quant_q8_0_dev(const float* x, uint8_t* b) {
+  float amax = 0.f;
+  for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(x[i]));
+  const __half dh = __float2half_rn(amax / 127.f);
+  put_half(b, dh);
+  const float dq = __half2float(dh);
+  const float id = amax / 127.f > 0.f ? 1.f / dq : 0.f;
+  for (int i = 0; i < 32; ++i) b[2 + i] = (uint8_t)(int8_t)max(-127, min(127, __float2int_rn(x[i] * id)));
+}
+
+HX_DEVICE void quant_q4_k_dev(const float* x, uint8_t* b) {
+  float scale[8], minv[8], ms = 0.f, mm = 0.f;
+  for (int j = 0; j < 8; ++j) {
+    float lo = x[j * 32], hi = x[j * 32];
+    for (int l = 1; l < 32; ++l) { lo = fminf(lo, x[j * 32 + l]); hi = fmaxf(hi, x[j * 32 + l]); }
+    lo = fminf(lo, 0.f);
+    scale[j] = (hi - lo) / 15.f;
+    minv[j] = -lo;
+    ms = fmaxf(ms, scale[j]);
+    mm = fmaxf(mm, minv[j]);
+  }
+  const __half dh = __float2half_rn(ms / 63.f), mh = __float2half_rn(mm / 63.f);
+  put_half(b, dh);
+  put_half(b + 2, mh);
+  const float dq = __half2float(dh), mq = __half2float(mh);
+  int sc[8], m[8];
+  for (int j = 0; j < 8; ++j) {
+    sc[j] = dq > 0.f ? min(63, __float2int_rn(scale[j] / dq)) : 0;
+    m[j] = mq > 0.f ? min(63, __float2int_rn(minv[j] / mq)) : 0;
+  }
+  uint8_t* q = b + 4;
+  for (int i = 0; i < 12; ++i) q[i] = 0;
+  for (int j = 0; j < 8; ++j) {
+    if (j < 4) {
+      q[j] = (uint8_t)(sc[j] & 63);
+      q[j + 4] = (uint8_t)(m[j] & 63);
+    } else {
+      q[j + 4] = (uint8_t)((sc[j] & 0xF) | ((m[j] & 0xF) << 4));
+      q[j - 4] |= (uint8_t)((sc[j] >> 4) << 6);
+      q[j] |= (uint8_t)((m[j] >> 4) << 6);
+    }
+  }
+  uint8_t* qs = b + 16;
+  for (int g = 0; g < 4; ++g)
+    for (int l = 0; l < 32; ++l) {
+      int qq[2];
+      for (int h = 0; h < 2; ++h) {
+        const int j = 2 * g + h;
+        const float step = dq * sc[j];
+        const float v = x[j * 32 + l] + mq * m[j];
+        qq[h] = step > 0.f ? max(0, min(15, __float2int_rn(v / step))) : 0;
+      }
+      qs[g * 32 + l] = (uint8_t)(qq[0] | (qq[1] << 4));
+    }
+}
+
+HX_DEVICE void quant_q6_k_dev(const float* x, uint8_t* b) {
+  float s[16], smax = 0.f;
+  for (int j = 0; j < 16; ++j) {
+    float amax = 0.f, v = 0.f;
+    for (int l = 0; l < 16; ++l) {
+      const float a = x[j * 16 + l];
+      if (fabsf(a) > amax) { amax = fabsf(a); v = a; }
+    }
+    s[j] = amax > 0.f ? -v / 32.f : 0.f;  // the largest value maps to -32 exactly
+    smax = fmaxf(smax, fabsf(s[j]));
+  }
+  const __half dh = __float2half_rn(smax / 127.f);
+  const float dq = __half2float(dh);
+  int8_t sc[16];
+  for (int j = 0; j < 16; ++j) sc[j] = dq > 0.f ? (int8_t)max(-128, min(127, __float2int_rn(s[j] / dq))) : 0;
+  uint8_t* ql = b;
+  uint8_t* qh = b + 128;
+  for (int half = 0; half < 2; ++half)
+    for (int l = 0; l < 32; ++l) {
+      int q[4];
+      for (int k = 0; k < 4; ++k) {
+        const int idx = 128 * half + l + 32 * k, j = idx / 16;
+        const float step = dq * sc[j];
+        const int v = step != 0.f ? __float2int_rn(x[idx] / step) : 0;
+        q[k] = max(-32, min(31, v)) + 32;
+      }
+      ql[64 * half + l] = (uint8_t)((q[0] & 0xF) | ((q[2] & 0xF) << 4));
+      ql[64 * half + l + 32] = (uint8_t)((q[1] & 0xF) | ((q[3] & 0xF) << 4));
+      qh[32 * half + l] = (uint8_t)((q[0] >> 4) | ((q[1] >> 4) << 2) | ((q[2] >> 4) << 4) | ((q[3] >> 4) << 6));
+    }
+  for (int j = 0; j < 16; ++j) b[192 + j] = (uint8_t)sc[j];
+  put_half(b + 208, dh);
+}
+
+template <int T>
+__global__ void gguf_quant_kernel(const __nv_bfloat16* __restrict__ W, int N, int K, uint8_t* __restrict__ out,
+                                  long long row_bytes) {
+  constexpr int BV = GgufBlock<T>::vals, BB = GgufBlock<T>::bytes;
+  const int nb = K / BV;
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long long)N * nb) return;
+  const int r = (int)(i / nb), blk = (int)(i - (long long)r * nb);
+  float x[BV];
+  const __nv_bfloat16* src = W + (long long)r * K + (long long)blk * BV;
+  for (int v = 0; v < BV; ++v) x[v] = __bfloat162float(src[v]);
+  uint8_t* b = out + (long long)r * row_bytes + (long long)blk * BB;
+  if (T == kQ8_0) quant_q8_0_dev(x, b);
+  else if (T == kQ4_K) quant_q4_k_dev(x, b);
+  else quant_q6_k_dev(x, b);
+}
+
 }  // namespace hx
 
 using namespace hx;
@@ -253,4 +368,24 @@ void gguf_dequant(torch::Tensor W, int64_t type, int64_t K, torch::Tensor out) {
   else if (type == kQ4_K) gguf_dequant_kernel<kQ4_K><<<grid, 256, 0, st>>>(W.data_ptr<uint8_t>(), W.size(1), op, N, (int)K);
   else gguf_dequant_kernel<kQ6_K><<<grid, 256, 0, st>>>(W.data_ptr<uint8_t>(), W.size(1), op, N, (int)K);
   HX_CUDA_CHECK(cudaGetLastError());
+}
+
+// bf16 [N, K] -> GGUF block rows uint8 [N, K / vals * bytes] on the device.
+torch::Tensor gguf_quant(torch::Tensor W, int64_t type) {
+  int bb, bv;
+  block_of((int)type, bb, bv);
+  TORCH_CHECK(W.is_cuda() && W.scalar_type() == at::kBFloat16 && W.dim() == 2 && W.is_contiguous(), "W [N, K] bf16");
+  const int N = W.size(0), K = W.size(1);
+  TORCH_CHECK(K % bv == 0, "K must be a multiple of the block size");
+  auto out = torch::empty({N, (int64_t)K / bv * bb}, W.options().dtype(at::kByte));
+  const long long nblk = (long long)N * (K / bv);
+  if (nblk == 0) return out;
+  const int grid = (int)((nblk + 127) / 128);
+  auto st = at::cuda::getCurrentCUDAStream();
+  auto wp = reinterpret_cast<const __nv_bfloat16*>(W.data_ptr());
+  if (type == kQ8_0) gguf_quant_kernel<kQ8_0><<<grid, 128, 0, st>>>(wp, N, K, out.data_ptr<uint8_t>(), out.size(1));
+  else if (type == kQ4_K) gguf_quant_kernel<kQ4_K><<<grid, 128, 0, st>>>(wp, N, K, out.data_ptr<uint8_t>(), out.size(1));
+  else gguf_quant_kernel<kQ6_K><<<grid, 128, 0, st>>>(wp, N, K, out.data_ptr<uint8_t>(), out.size(1));
+  HX_CUDA_CHECK(cudaGetLastError());
+  return out;
 }

@@ -84,6 +84,45 @@ class DecodeBuffers:
     graph_steps: int = 0
 
 
+# GGUF type ids (ggml): the block formats the kernels read
+GGUF_Q8_0, GGUF_Q4_K, GGUF_Q6_K = 8, 12, 14
+_GGUF_BLOCK = {GGUF_Q8_0: (34, 32), GGUF_Q4_K: (144, 256), GGUF_Q6_K: (210, 256)}
+# quantization schemes -> type per fused weight (Q4_K_M: ffn_down in Q6_K, the rest Q4_K;
+# the fused [q|k|v] projection keeps one type, so attn_v is Q4_K here)
+QUANT_SCHEMES = {
+    "Q8_0": {"*": GGUF_Q8_0},
+    "Q6_K": {"*": GGUF_Q6_K},
+    "Q4_K": {"*": GGUF_Q4_K},
+    "Q4_K_M": {"*": GGUF_Q4_K, "w_d": GGUF_Q6_K},
+}
+
+
+class QWeight:
+    """One linear weight held as GGUF block rows on the device (uint8 [N, row_bytes]):
+    decode reads it through the fused-dequant GEMV, prefill dequantizes it to bf16
+    for the tensor-core GEMM (the reference's QMatMul / dequant-then-GEMM switch,
+    tp/tp_linear.rs:76-139)."""
+
+    def __init__(self, raw: torch.Tensor, gtype: int, K: int):
+        self.raw, self.type, self.K = raw, gtype, K
+
+    @property
+    def shape(self):
+        return (self.raw.shape[0], self.K)
+
+    def nbytes(self) -> int:
+        return self.raw.numel()
+
+    def dequant(self, C) -> torch.Tensor:
+        out = torch.empty(self.raw.shape[0], self.K, dtype=torch.bfloat16, device=self.raw.device)
+        C.gguf_dequant(self.raw, self.type, self.K, out)
+        return out
+
+
+def _tbytes(t) -> int:
+    return t.nbytes() if isinstance(t, QWeight) else t.numel() * t.element_size()
+
+
 class FastModel:
     """CUDA inference model for Qwen3 / Qwen3-MoE / Qwen3-Next on one rank."""
 
@@ -171,7 +210,7 @@ class FastModel:
         return cls(cfg, layers, embed, lm, fn, dims, device, **kw)
 
     def weight_bytes(self) -> int:
-        n = sum(t.numel() * t.element_size() for lw in self.layers for t in lw.values())
+        n = sum(_tbytes(t) for lw in self.layers for t in lw.values())
         n += self.embed_w.numel() * 2 + (0 if self.lm_head is self.embed_w else self.lm_head.numel() * 2)
         return n
 
@@ -184,7 +223,7 @@ class FastModel:
                     per = t[0].numel() * t.element_size()
                     n += per * (cfg.num_experts_per_tok + (1 if self.has_shared else 0))
                 else:
-                    n += t.numel() * t.element_size()
+                    n += _tbytes(t)
         return n + self.lm_head.numel() * 2 + self.cfg.hidden_size * 2
 
     # ------------------------------------------------------------------
@@ -231,11 +270,11 @@ class FastModel:
     def _row_parallel(self, W, inp, nb: DecodeBuffers):
         """x += W . inp, summed across TP ranks when the layer is sharded."""
         if self.comm is None or self.dims.ws == 1:
-            self.C.gemv(W, inp, nb.x, ops.RESID_ADD, nb.x, None, 0.0)
-        elif self.comm.fused:
+            self._gemv(W, inp, nb.x, ops.RESID_ADD, nb.x, None, 0.0)
+        elif self.comm.fused and not isinstance(W, QWeight):
             self.C.gemv_ar(W, inp, nb.x, *self.comm.fused_args())
         else:
-            self.C.gemv(W, inp, nb.partial, ops.STORE_BF16, None, None, 0.0)
+            self._gemv(W, inp, nb.partial, ops.STORE_BF16, None, None, 0.0)
             self.comm.reduce_residual(nb.partial, nb.x)
 
     def _decode_layer(self, i: int, nb: DecodeBuffers):
@@ -246,14 +285,14 @@ class FastModel:
             if cfg.is_linear(i) and "gdn" in skip or not cfg.is_linear(i) and "attn" in skip:
                 pass
             elif cfg.is_linear(i):
-                C.gemv(lw["w_in"], nb.x, nb.proj_gdn, ops.STORE_BF16, None, lw["ln1"], eps)
+                self._gemv(lw["w_in"], nb.x, nb.proj_gdn, ops.STORE_BF16, None, lw["ln1"], eps)
                 if "gdn_core" not in skip:
                     C.gdn_decode(nb.proj_gdn, lw["conv_w"], self.conv[i], self.rec[i], lw["A_log"],
                                  lw["dt_bias"], lw["gnorm"], nb.slots, self.pos, nb.gdn_out, d.hk, d.hv, d.dk, d.dv,
                                  eps)
                 self._row_parallel(lw["out_w"], nb.gdn_out, nb)
             else:
-                C.gemv(lw["w_qkv"], nb.x, nb.proj_attn, ops.STORE_BF16, None, lw["ln1"], eps)
+                self._gemv(lw["w_qkv"], nb.x, nb.proj_attn, ops.STORE_BF16, None, lw["ln1"], eps)
                 if "attn_core" not in skip:
                     C.attn_decode(nb.proj_attn, lw.get("q_norm"), lw.get("k_norm"), self.inv_freq, self.kc[i],
                                   self.vc[i], nb.slots, self.pos, nb.part_o, nb.part_ml, nb.counters, nb.attn_out,
@@ -269,12 +308,12 @@ class FastModel:
                     C.moe_down(lw["w_d"], nb.act_moe, nb.ids, nb.wts, nb.x, None)
             return
         if cfg.is_linear(i):
-            C.gemv(lw["w_in"], nb.x, nb.proj_gdn, ops.STORE_BF16, None, lw["ln1"], eps)
+            self._gemv(lw["w_in"], nb.x, nb.proj_gdn, ops.STORE_BF16, None, lw["ln1"], eps)
             C.gdn_decode(nb.proj_gdn, lw["conv_w"], self.conv[i], self.rec[i], lw["A_log"], lw["dt_bias"],
                          lw["gnorm"], nb.slots, self.pos, nb.gdn_out, d.hk, d.hv, d.dk, d.dv, eps)
             self._row_parallel(lw["out_w"], nb.gdn_out, nb)
         else:
-            C.gemv(lw["w_qkv"], nb.x, nb.proj_attn, ops.STORE_BF16, None, lw["ln1"], eps)
+            self._gemv(lw["w_qkv"], nb.x, nb.proj_attn, ops.STORE_BF16, None, lw["ln1"], eps)
             C.attn_decode(nb.proj_attn, lw.get("q_norm"), lw.get("k_norm"), self.inv_freq, self.kc[i], self.vc[i],
                           nb.slots, self.pos, nb.part_o, nb.part_ml, nb.counters, nb.attn_out, d.hq, d.hkv, d.D,
                           cfg.rotary_dim, cfg.attn_output_gate, eps)
@@ -293,7 +332,7 @@ class FastModel:
                 C.moe_down(lw["w_d"], nb.act_moe, nb.ids, nb.wts, nb.x, nb.partial)
                 self.comm.reduce_residual(nb.partial, nb.x)
         else:
-            C.gemv(lw["w_gu"], nb.x, nb.act_mlp, ops.SILU_PAIR, None, lw["ln2"], eps)
+            self._gemv(lw["w_gu"], nb.x, nb.act_mlp, ops.SILU_PAIR, None, lw["ln2"], eps)
             self._row_parallel(lw["w_d"], nb.act_mlp, nb)
 
     def decode_step_launch(self, nb: DecodeBuffers):
@@ -312,6 +351,41 @@ class FastModel:
             if self.comm is not None and self.dims.ws > 1:
                 n += self.comm.launches_per_reduce * 2
         return n
+
+    def quantize_(self, scheme: str) -> None:
+        """In-situ quantization (the reference's ISQ, tp/isq.rs:252-326) of the dense
+        linear projections into GGUF k-quant blocks on the device: GDN in/out, attention
+        qkv/o and dense-MLP gate-up/down. Router, stacked experts, embedding and lm_head
+        stay bf16. Weights whose input width is not a multiple of the block size stay
+        bf16 too (a tensor-parallel shard must hold whole superblocks)."""
+        if scheme not in QUANT_SCHEMES:
+            raise ValueError(f"unknown quantization {scheme!r}; one of {sorted(QUANT_SCHEMES)}")
+        if self.C is None:
+            raise RuntimeError("quantized serving needs the CUDA extension")
+        rule = QUANT_SCHEMES[scheme]
+        for i, lw in enumerate(self.layers):
+            keys = ["w_in", "out_w", "w_qkv", "o_w"]
+            if not self.cfg.layer_uses_moe(i):
+                keys += ["w_gu", "w_d"]
+            for k in keys:
+                w = lw.get(k)
+                if w is None or isinstance(w, QWeight) or w.dim() != 2:
+                    continue
+                gt = rule.get(k, rule["*"])
+                if w.shape[1] % _GGUF_BLOCK[gt][1]:
+                    continue
+                lw[k] = QWeight(self.C.gguf_quant(w.contiguous(), gt), gt, w.shape[1])
+                del w
+        self.quant = scheme
+        for nb in self._bufs.values():  # captured graphs refer to the old weights
+            nb.graph = None
+        torch.cuda.empty_cache()
+
+    def _gemv(self, W, x, y, mode: int, resid=None, norm=None, eps: float = 0.0):
+        if isinstance(W, QWeight):
+            self.C.gguf_gemv(W.raw, W.type, W.K, x, y, mode, resid, norm, eps)
+        else:
+            self.C.gemv(W, x, y, mode, resid, norm, eps)
 
     def prefill_launches(self) -> int:
         """Kernels of this package one prefill launches (PyTorch ops such as RoPE, the
@@ -383,6 +457,8 @@ class FastModel:
                 y = (torch.nn.functional.silu(y[:, 0::2].float()).to(torch.bfloat16).float()
                      * y[:, 1::2].float()).to(torch.bfloat16)
             return y
+        if isinstance(W, QWeight):
+            W = W.dequant(self.C)
         N = W.shape[0] // 2 if epi == 1 else W.shape[0]
         Np = (N + 7) // 8 * 8  # keep output rows 16-byte aligned for the vector epilogue
         out = torch.empty(x.shape[0], Np, dtype=torch.float32 if epi == 2 else torch.bfloat16, device=x.device)

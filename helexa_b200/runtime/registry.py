@@ -79,6 +79,8 @@ def build_served_model(spec: ModelSpec) -> ServedModel:
             from ..weights.loader import SafetensorsDir
             st = SafetensorsDir(src.path)
             model = FastModel.from_hf(cfg, st.get, dev, **kw)
+        if spec.quant:  # in-situ quantization of the dense projections (ISQ)
+            model.quantize_(spec.quant.upper())
         runner = FastRunner(model)
         kv_bpt = cfg.kv_bytes_per_token()
     else:

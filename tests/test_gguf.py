@@ -97,3 +97,61 @@ def test_gguf_gemv_and_dequant(gt, B, mode):
     torch.cuda.synchronize()
     err = (y.float() - want).abs().max().item()
     assert err <= 2e-2 * want.abs().max().item() + 1e-3, err
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("gt,tol", [(G.Q8_0, 0.01), (G.Q4_K, 0.12), (G.Q6_K, 0.03)])
+def test_device_quantizer_matches_host_codec(gt, tol):
+    """In-situ quantization on the GPU writes the host codec's block bytes, and the
+    decoded weights stay within the codec tolerance of the input."""
+    C = _C()
+    torch.manual_seed(4)
+    N, K = 96, 1024
+    w = (torch.randn(N, K) * 0.03).bfloat16()
+    host = C.gguf_quant_host(w.float().view(-1), gt).view(N, -1)
+    dev = C.gguf_quant(w.cuda(), gt).cpu()
+    assert dev.shape == host.shape
+    wd = C.gguf_dequant_host(dev.reshape(-1), gt, N * K).view(N, K)
+    wh = C.gguf_dequant_host(host.reshape(-1), gt, N * K).view(N, K)
+    rel = (wd - w.float()).norm() / w.float().norm()
+    assert rel < tol, rel
+    assert torch.equal(wd, wh)
+    assert torch.equal(dev, host)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name,scheme", [("tiny-qwen3", "Q8_0"), ("tiny-qwen3", "Q4_K_M"),
+                                         ("tiny-qwen3-next", "Q6_K")])
+def test_quantized_model_matches_dequantized_weights(name, scheme):
+    """A quantized FastModel (fused-dequant decode GEMVs, dequant-then-GEMM prefill)
+    against the same model holding the dequantized bf16 weights: prefill logits and
+    teacher-forced graph decode logits agree."""
+    from helexa_b200.config import get_preset
+    from helexa_b200.models.fast import FastModel, QWeight
+    from helexa_b200.weights.random_init import random_weights
+    cfg = get_preset(name)
+    w = random_weights(cfg, seed=0, std=0.05)
+    dev = torch.device("cuda", 0)
+    q = FastModel.from_hf(cfg, w, dev, max_slots=1, max_len=128)
+    q.quantize_(scheme)
+    nq = sum(isinstance(t, QWeight) for lw in q.layers for t in lw.values())
+    assert nq > 0
+    ref = FastModel.from_hf(cfg, w, dev, max_slots=1, max_len=128)
+    for lq, lr in zip(q.layers, ref.layers):
+        for k, t in lq.items():
+            if isinstance(t, QWeight):
+                lr[k] = t.dequant(q.C)
+    prompt = torch.randint(0, cfg.vocab_size, (40,), generator=torch.Generator().manual_seed(1)).int().to(dev)
+    out = []
+    for m in (q, ref):
+        lg = m.prefill(0, prompt, 0).float()
+        nb = m.capture(1, steps=4)
+        nb.slots.fill_(0)
+        nb.tok.fill_(int(lg.argmax()))
+        m.replay(nb)
+        torch.cuda.synchronize()
+        out.append((lg, nb.logits[0].float().clone(), nb.out_tokens[0, :4].clone()))
+    cos = torch.nn.functional.cosine_similarity
+    assert cos(out[0][0], out[1][0], dim=0).item() > 0.999
+    assert cos(out[0][1], out[1][1], dim=0).item() > 0.995
+    assert q.weight_bytes() < ref.weight_bytes()
