@@ -9,6 +9,7 @@ the 126 MB L2, so every step streams them from HBM (no flush needed).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl helexa|reference]
   python bench.py --model qwen3-8b --prompt 2048 --decode 256     # BASELINE's Qwen3-8B config
+  python bench.py --model qwen3-32b --prompt 4096 --decode 256 --quant Q4_K_M
 """
 from __future__ import annotations
 
@@ -78,6 +79,7 @@ def main() -> None:
     ap.add_argument("--prompt", type=int, default=8192)
     ap.add_argument("--decode", type=int, default=512)
     ap.add_argument("--graph-steps", type=int, default=16)
+    ap.add_argument("--quant", default=None, help="in-situ quantization of the dense projections (Q8_0, Q6_K, Q4_K, Q4_K_M)")
     args = ap.parse_args()
     if args.impl == "reference":
         reference_arm(args)
@@ -103,6 +105,8 @@ def main() -> None:
     cfg = get_preset(args.model)
     max_len = args.prompt + args.decode + 64
     model = FastModel.random(cfg, dev, seed=0, rank=rank, ws=world, max_slots=1, max_len=max_len, comm=comm)
+    if args.quant:
+        model.quantize_(args.quant.upper())
     gen = Generator(model, slot=0, graph_steps=args.graph_steps, prefill_chunk=args.prompt)
     g = torch.Generator().manual_seed(1234)
     prompts = [torch.randint(0, cfg.vocab_size, (args.prompt,), generator=g, dtype=torch.int32).pin_memory()
@@ -177,7 +181,7 @@ def main() -> None:
     launches = (model.launches_per_step() * dec_tokens + model.prefill_launches()) * args.steps
     if rank == 0:
         line = {
-            "metric": f"decode tok/s (bs=1) + p50 TTFT, {cfg.name} bf16",
+            "metric": f"decode tok/s (bs=1) + p50 TTFT, {cfg.name} " + (args.quant or "bf16"),
             "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round((dec_ms + ttft_sum) / args.steps, 3),
             "higher_is_better": True, "scaling": "strong",
