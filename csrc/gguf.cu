@@ -86,6 +86,23 @@ __global__ void __launch_bounds__(256) gguf_gemv_kernel(const uint8_t* __restric
                                                         int N, int K) {
   extern __shared__ __align__(16) float xs[];  // [B][K] f32
   __shared__ float red[8];
+  constexpr int RPW = 2;
+  constexpr int U = 4;  // 8-value groups per lane decoded ahead (all their loads in flight)
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row0 = (blockIdx.x * 8 + warp) * RPW;
+  const int nvec = K / 8;
+  const bool active = row0 < N;
+  float wf[U][RPW][8];
+  auto decode_batch = [&](int v0) {
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int v = min(v0 + 32 * u, nvec - 1);
+#pragma unroll
+      for (int r = 0; r < RPW; ++r) dequant8<T>(W + (long long)min(row0 + r, N - 1) * row_bytes, v, wf[u][r]);
+    }
+  };
+  // weights never depend on the previous kernel: decode the first batch before the wait
+  if (active) decode_batch(lane);
   pdl_wait_prior();
   pdl_launch_dependents();
   for (int b = 0; b < B; ++b) {
@@ -106,29 +123,29 @@ __global__ void __launch_bounds__(256) gguf_gemv_kernel(const uint8_t* __restric
     }
   }
   __syncthreads();
-  constexpr int RPW = 2;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row0 = (blockIdx.x * 8 + warp) * RPW;
-  if (row0 >= N) return;
+  if (!active) return;
   float acc[RPW][B];
 #pragma unroll
   for (int r = 0; r < RPW; ++r)
 #pragma unroll
     for (int b = 0; b < B; ++b) acc[r][b] = 0.f;
-  const int nvec = K / 8;
-  for (int v = lane; v < nvec; v += 32) {
+  for (int v0 = lane; v0 < nvec; v0 += 32 * U) {
 #pragma unroll
-    for (int r = 0; r < RPW; ++r) {
-      const int row = min(row0 + r, N - 1);
-      float wf[8];
-      dequant8<T>(W + (long long)row * row_bytes, v, wf);
+    for (int u = 0; u < U; ++u) {
+      const int v = v0 + 32 * u;
+      if (v >= nvec) break;
 #pragma unroll
       for (int b = 0; b < B; ++b) {
-        const float* xv = xs + b * K + v * 8;
+        const float4* xv = reinterpret_cast<const float4*>(xs + b * K + v * 8);
+        const float4 x0 = xv[0], x1 = xv[1];
+        const float xf[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
 #pragma unroll
-        for (int i = 0; i < 8; ++i) acc[r][b] = fmaf(wf[i], xv[i], acc[r][b]);
+        for (int r = 0; r < RPW; ++r)
+#pragma unroll
+          for (int i = 0; i < 8; ++i) acc[r][b] = fmaf(wf[u][r][i], xf[i], acc[r][b]);
       }
     }
+    if (v0 + 32 * U < nvec) decode_batch(v0 + 32 * U);
   }
 #pragma unroll
   for (int r = 0; r < RPW; ++r)

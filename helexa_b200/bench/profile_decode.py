@@ -29,6 +29,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--eager", action="store_true")
+    ap.add_argument("--quant", default=None, help="in-situ quantization (Q8_0, Q6_K, Q4_K, Q4_K_M)")
     ap.add_argument("--no-pdl", action="store_true", help="launch without programmatic dependent launch")
     ap.add_argument("--skip", default="", help="profiling only: comma list of gdn,attn,gdn_core,attn_core,ffn,experts")
     args = ap.parse_args()
@@ -41,6 +42,8 @@ def main():
     dev = torch.device("cuda", 0)
     fm = FastModel.random(cfg, dev, max_slots=args.batch, max_len=args.context + args.steps * 4 + 64)
     B = args.batch
+    if args.quant:
+        fm.quantize_(args.quant.upper())
     fm.profile_skip = set(x for x in args.skip.split(",") if x)
     if args.eager:
         nb = fm.buffers(B)
