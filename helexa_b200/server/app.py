@@ -79,6 +79,16 @@ def create_app(registry: ModelRegistry | None = None, default_models: list[dict]
     app = FastAPI(title="helexa-b200 node")
     app.state.registry = reg
     app.state.activation = {"pending": [], "failed": {}, "ready": []}
+    app.state.shutting_down = False
+
+    @app.middleware("http")
+    async def _refuse_while_shutting_down(request, call_next):
+        # graceful shutdown (the reference's SHUTTING_DOWN flag): admission closes first,
+        # in-flight requests finish, then every model unloads
+        if app.state.shutting_down and request.url.path.startswith("/v1/"):
+            return JSONResponse(wire.error_body("node is shutting down", "shutting_down"), 503,
+                                headers={"Retry-After": "5"})
+        return await call_next(request)
 
     @app.on_event("startup")
     async def _prewarm():
@@ -86,6 +96,8 @@ def create_app(registry: ModelRegistry | None = None, default_models: list[dict]
 
         async def load_defaults():
             for d in default_models or []:
+                if app.state.shutting_down:
+                    break
                 spec = ModelSpec.from_dict(d)
                 app.state.activation["pending"].append(spec.model_id)
                 for attempt in range(3):
@@ -102,6 +114,7 @@ def create_app(registry: ModelRegistry | None = None, default_models: list[dict]
 
     @app.on_event("shutdown")
     async def _shutdown():
+        app.state.shutting_down = True
         await reg.unload_all()
 
     # ---- node surface ---------------------------------------------------------

@@ -53,3 +53,22 @@ def test_settings_env_override(tmp_path):
     s = load_settings(str(f), env={"HELEXA_PORT": "8080", "HELEXA_ADMISSION__MAX_QUEUE_DEPTH": "9",
                                    "OTHER": "x"})
     assert s == {"port": 8080, "admission": {"max_in_flight": 2, "max_queue_depth": 9}}
+
+
+def test_tp_smoke_cli_gloo():
+    """The TP smoke check spawns ranks, pings them and verifies a sanity all-reduce."""
+    from helexa_b200.parallel.smoke import run
+    ok, line = run(2, cpu=True, timeout_s=120)
+    assert ok, line
+    assert line.startswith("status=ok ranks=2 backend=gloo")
+
+
+def test_node_refuses_requests_while_shutting_down():
+    from fastapi.testclient import TestClient
+    from helexa_b200.server.app import create_app
+    app = create_app()
+    with TestClient(app) as c:
+        app.state.shutting_down = True
+        r = c.post("/v1/chat/completions", json={"model": "x", "messages": []})
+        assert r.status_code == 503 and r.headers.get("retry-after") == "5"
+        assert c.get("/version").status_code == 200
