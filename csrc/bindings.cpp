@@ -23,11 +23,16 @@ void moe_down_ar(torch::Tensor Wd, torch::Tensor act, torch::Tensor ids, torch::
                  double timeout_s);
 void attn_prefill(torch::Tensor q, torch::Tensor kc, torch::Tensor vc, torch::Tensor out, int64_t Hq, int64_t p0,
                   double scale);
+void gemv_experts_ep(torch::Tensor W, torch::Tensor x, torch::Tensor ids, torch::Tensor y, int64_t mode,
+                     int64_t x_row_div, c10::optional<torch::Tensor> norm_w, double eps, int64_t e_base);
+void moe_down_ar_ep(torch::Tensor Wd, torch::Tensor act, torch::Tensor ids, torch::Tensor wts, torch::Tensor x,
+                    std::vector<int64_t> bases, int64_t rank, int64_t slot_elems, torch::Tensor epoch,
+                    torch::Tensor err, double timeout_s, int64_t e_base);
 void moe_combine(torch::Tensor y, torch::Tensor rows, torch::Tensor wts, torch::Tensor x);
 void moe_route_prefill(torch::Tensor logits, int64_t E, int64_t k, bool has_shared, bool norm_topk, torch::Tensor hn,
                        torch::Tensor ids, torch::Tensor wts, torch::Tensor rows, torch::Tensor counts,
                        torch::Tensor offsets, torch::Tensor cursor, torch::Tensor tiles, torch::Tensor ntiles,
-                       torch::Tensor A);
+                       torch::Tensor A, int64_t e_base, int64_t e_count);
 void gemm_grouped_dev(torch::Tensor A, torch::Tensor B, torch::Tensor C, torch::Tensor tiles, torch::Tensor ntiles,
                       int64_t n, int64_t epi, torch::Tensor err);
 void embed(torch::Tensor E, torch::Tensor tok, torch::Tensor x);
@@ -75,6 +80,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_combine", &moe_combine);
   m.def("gemv_ar", &gemv_ar);
   m.def("moe_down_ar", &moe_down_ar);
+  m.def("gemv_experts_ep", &gemv_experts_ep);
+  m.def("moe_down_ar_ep", &moe_down_ar_ep);
   m.def("moe_route_prefill", &moe_route_prefill);
   m.def("gemm_grouped_dev", &gemm_grouped_dev);
   m.def("gdn_decode", &gdn_decode);

@@ -54,6 +54,7 @@ struct GemvArgs {
   int out_cap;
   int* step;
   TPPush tp;                  // kResidAddTP: cross-rank reduction fused into the epilogue
+  int e_base, e_count;        // expert mode under expert parallelism: this rank's experts (count 0: all)
 };
 
 // Order-preserving key of a float (larger float -> larger key), index tiebreak to the
@@ -144,7 +145,7 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
   const int job = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row0 = (blockIdx.x * 8 + warp) * RPW;
-  const bool active = row0 < a.N;
+  bool active = row0 < a.N;
 
   const bf16x8* wrow[RPW];
   bf16x8 cur[RPW][U];
@@ -174,8 +175,13 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
   const __nv_bfloat16* xsrc = a.x;
   if (!static_w) {
     xsrc += (long long)(job / a.x_row_div) * K;
+    int e = a.ids[job];
+    if (a.e_count) {  // expert parallel: jobs routed to another rank's experts do nothing
+      e -= a.e_base;
+      if (e < 0 || e >= a.e_count) active = false;
+    }
     if (active) {
-      set_rows(a.W + (long long)a.ids[job] * a.w_expert_stride);
+      set_rows(a.W + (long long)e * a.w_expert_stride);
       load_batch(cur, lane);
     }
   }
@@ -425,7 +431,7 @@ __global__ void __launch_bounds__(256) moe_down_kernel(const __nv_bfloat16* __re
                                                        const __nv_bfloat16* __restrict__ act,
                                                        const int* __restrict__ ids, const float* __restrict__ wts,
                                                        __nv_bfloat16* x, __nv_bfloat16* partial_out, int H, int I,
-                                                       int J, TPPush tp) {
+                                                       int J, TPPush tp, int e_base, int e_count) {
   extern __shared__ __align__(16) __nv_bfloat16 acts[];  // [J][I] routing-weight scaled
   pdl_wait_prior();
   pdl_launch_dependents();
@@ -437,8 +443,8 @@ __global__ void __launch_bounds__(256) moe_down_kernel(const __nv_bfloat16* __re
   if (h < H) {
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
-      if (j < J) {
-        const long long e = ids[b * J + j];
+      const long long e = j < J ? (long long)ids[b * J + j] - e_base : -1;
+      if (j < J && (e_count == 0 || (e >= 0 && e < e_count))) {
         const bf16x8* row = reinterpret_cast<const bf16x8*>(Wd + (e * H + h) * (long long)I);
 #pragma unroll
         for (int q = 0; q < VPL; ++q) {
@@ -462,7 +468,8 @@ __global__ void __launch_bounds__(256) moe_down_kernel(const __nv_bfloat16* __re
   float acc = 0.f;
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
-    if (j < J && h < H) {
+    const int el = j < J ? ids[b * J + j] - e_base : -1;
+    if (j < J && h < H && (e_count == 0 || (el >= 0 && el < e_count))) {
 #pragma unroll
       for (int q = 0; q < VPL; ++q) {
         if (lane + 32 * q >= I / 8) break;
@@ -615,17 +622,18 @@ void gemv_experts(torch::Tensor W, torch::Tensor x, torch::Tensor ids, torch::Te
 template <int V, bool TP>
 static void launch_moe_down(dim3 grid, size_t smem, cudaStream_t st, const __nv_bfloat16* wp,
                             const __nv_bfloat16* ap, const int* ids, const float* wts, __nv_bfloat16* xp,
-                            __nv_bfloat16* pp, int H, int I, int J, const TPPush& tp) {
+                            __nv_bfloat16* pp, int H, int I, int J, const TPPush& tp, int e_base, int e_count) {
   auto k = moe_down_kernel<V, TP>;
   if (smem + 4096 > 48 * 1024) {
     HX_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   }
-  HX_CUDA_CHECK(hx_launch_pdl(k, grid, dim3(256), smem, st, wp, ap, ids, wts, xp, pp, H, I, J, tp));
+  HX_CUDA_CHECK(hx_launch_pdl(k, grid, dim3(256), smem, st, wp, ap, ids, wts, xp, pp, H, I, J, tp, e_base, e_count));
 }
 
 template <bool TP>
 static void moe_down_impl(torch::Tensor Wd, torch::Tensor act, torch::Tensor ids, torch::Tensor wts, torch::Tensor x,
-                          c10::optional<torch::Tensor> partial_out, const TPPush& tp) {
+                          c10::optional<torch::Tensor> partial_out, const TPPush& tp, int e_base = 0,
+                          int e_count = 0) {
   TORCH_CHECK(Wd.dim() == 3 && Wd.scalar_type() == at::kBFloat16 && Wd.is_contiguous(), "Wd [E,H,I] bf16");
   const int H = Wd.size(1), I = Wd.size(2);
   const int B = x.size(0), J = ids.size(1);
@@ -647,11 +655,11 @@ static void moe_down_impl(torch::Tensor Wd, torch::Tensor act, torch::Tensor ids
   const int* ip = ids.data_ptr<int>();
   const float* wtp = wts.data_ptr<float>();
   const int vpl = (I / 8 + 31) / 32;
-  if (vpl == 1) launch_moe_down<1, TP>(grid, smem, st, wp, ap, ip, wtp, xp, pp, H, I, J, tp);
-  else if (vpl == 2) launch_moe_down<2, TP>(grid, smem, st, wp, ap, ip, wtp, xp, pp, H, I, J, tp);
-  else if (vpl == 3) launch_moe_down<3, TP>(grid, smem, st, wp, ap, ip, wtp, xp, pp, H, I, J, tp);
-  else if (vpl == 4) launch_moe_down<4, TP>(grid, smem, st, wp, ap, ip, wtp, xp, pp, H, I, J, tp);
-  else if (vpl <= 6) launch_moe_down<6, TP>(grid, smem, st, wp, ap, ip, wtp, xp, pp, H, I, J, tp);
+  if (vpl == 1) launch_moe_down<1, TP>(grid, smem, st, wp, ap, ip, wtp, xp, pp, H, I, J, tp, e_base, e_count);
+  else if (vpl == 2) launch_moe_down<2, TP>(grid, smem, st, wp, ap, ip, wtp, xp, pp, H, I, J, tp, e_base, e_count);
+  else if (vpl == 3) launch_moe_down<3, TP>(grid, smem, st, wp, ap, ip, wtp, xp, pp, H, I, J, tp, e_base, e_count);
+  else if (vpl == 4) launch_moe_down<4, TP>(grid, smem, st, wp, ap, ip, wtp, xp, pp, H, I, J, tp, e_base, e_count);
+  else if (vpl <= 6) launch_moe_down<6, TP>(grid, smem, st, wp, ap, ip, wtp, xp, pp, H, I, J, tp, e_base, e_count);
   else TORCH_CHECK(false, "moe_down: expert intermediate size per rank must be <= 1536");
 }
 
@@ -705,4 +713,37 @@ void gemv_ar(torch::Tensor W, torch::Tensor inp, torch::Tensor x, std::vector<in
   a.N = N; a.K = K; a.ldy = N; a.x_row_div = 1;
   a.tp = make_tp(bases, rank, slot_elems, epoch, err, timeout_s);
   launch_mode<kResidAddTP>(a, B, at::cuda::getCurrentCUDAStream());
+}
+
+// Expert parallelism: W holds this rank's experts e_base .. e_base + W.size(0) - 1; ids
+// are global. Routes to other ranks' experts are skipped (their rows stay unwritten
+// and the matching moe_down_ar_ep skips them too); the cross-rank sum of moe_down_ar_ep
+// combines every rank's experts.
+void gemv_experts_ep(torch::Tensor W, torch::Tensor x, torch::Tensor ids, torch::Tensor y, int64_t mode,
+                     int64_t x_row_div, c10::optional<torch::Tensor> norm_w, double eps, int64_t e_base) {
+  TORCH_CHECK(W.dim() == 3, "W: [E_local, N, K]");
+  check_w(W);
+  TORCH_CHECK(ids.scalar_type() == at::kInt && ids.is_contiguous(), "ids int32");
+  const int N = W.size(1), K = W.size(2), jobs = ids.numel();
+  TORCH_CHECK(x.size(-1) == K && K % 8 == 0, "K mismatch");
+  GemvArgs a{};
+  a.W = reinterpret_cast<const __nv_bfloat16*>(W.data_ptr());
+  a.x = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
+  a.y = y.data_ptr();
+  a.ids = ids.data_ptr<int>();
+  a.N = N; a.K = K; a.ldy = y.stride(0); a.eps = (float)eps;
+  a.w_expert_stride = (long long)N * K; a.x_row_div = (int)x_row_div;
+  a.e_base = (int)e_base; a.e_count = (int)W.size(0);
+  if (norm_w) a.norm_w = norm_w->data_ptr<float>();
+  auto s = at::cuda::getCurrentCUDAStream();
+  if (mode == kSiluPair) launch_b<1, kSiluPair>(a, jobs, s);
+  else if (mode == kStoreBf16) launch_b<1, kStoreBf16>(a, jobs, s);
+  else TORCH_CHECK(false, "unsupported expert gemv mode");
+}
+
+void moe_down_ar_ep(torch::Tensor Wd, torch::Tensor act, torch::Tensor ids, torch::Tensor wts, torch::Tensor x,
+                    std::vector<int64_t> bases, int64_t rank, int64_t slot_elems, torch::Tensor epoch,
+                    torch::Tensor err, double timeout_s, int64_t e_base) {
+  moe_down_impl<true>(Wd, act, ids, wts, x, c10::nullopt, make_tp(bases, rank, slot_elems, epoch, err, timeout_s),
+                      (int)e_base, (int)Wd.size(0));
 }

@@ -78,9 +78,11 @@ __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ y, const in
   for (int v = threadIdx.x; v < H / 8; v += blockDim.x) {
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     for (int j = 0; j < J; ++j) {
+      const int row = rows[(long long)t * J + j];
+      if (row < 0) continue;  // routed to another rank's expert
       const float w = wts[(long long)t * J + j];
       float f[8];
-      unpack8(reinterpret_cast<const bf16x8*>(y + (long long)rows[(long long)t * J + j] * H)[v], f);
+      unpack8(reinterpret_cast<const bf16x8*>(y + (long long)row * H)[v], f);
 #pragma unroll
       for (int i = 0; i < 8; ++i) acc[i] = fmaf(w, f[i], acc[i]);
     }
@@ -98,7 +100,7 @@ __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ y, const in
 // expert E with sigmoid(logits[t, E]) when has_shared), and per-expert counts.
 __global__ void moe_route_topk_kernel(const float* __restrict__ logits, int ld, int T, int E, int k, int has_shared,
                                       int norm_topk, int* __restrict__ ids, float* __restrict__ wts,
-                                      int* __restrict__ counts) {
+                                      int* __restrict__ counts, int e_base, int e_count) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= T) return;
   const int J = k + (has_shared ? 1 : 0);
@@ -141,9 +143,13 @@ __global__ void moe_route_topk_kernel(const float* __restrict__ logits, int ld, 
       if (lane + 32 * i == bi) v[i] = -INFINITY;
   }
   if (lane < k) {
-    ids[(long long)warp * J + lane] = my_id;
+    // expert parallel (e_count > 0): keep this rank's experts as local ids, mark the
+    // rest -1 (their routes are computed by the ranks that own them)
+    int id = my_id;
+    if (e_count) id = (my_id >= e_base && my_id < e_base + e_count) ? my_id - e_base : -1;
+    ids[(long long)warp * J + lane] = id;
     wts[(long long)warp * J + lane] = norm_topk ? my_p / sel : my_p;
-    atomicAdd(&counts[my_id], 1);
+    if (id >= 0) atomicAdd(&counts[id], 1);
   }
   if (has_shared && lane == 0) {
     ids[(long long)warp * J + k] = E;
@@ -207,8 +213,13 @@ __global__ void moe_route_place_kernel(const int* __restrict__ ids, int T, int J
                                        __nv_bfloat16* __restrict__ A, int H) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= T * J) return;
+  const int id = ids[warp];
+  if (id < 0) {  // another rank's expert
+    if (lane == 0) rows[warp] = -1;
+    return;
+  }
   int r = 0;
-  if (lane == 0) r = atomicAdd(&cursor[ids[warp]], 1);
+  if (lane == 0) r = atomicAdd(&cursor[id], 1);
   r = __shfl_sync(0xffffffffu, r, 0);
   if (lane == 0) rows[warp] = r;
   const int t = warp / J;
@@ -253,9 +264,10 @@ void moe_topk(torch::Tensor logits, int64_t E, int64_t k, bool has_shared, bool 
 void moe_route_prefill(torch::Tensor logits, int64_t E, int64_t k, bool has_shared, bool norm_topk, torch::Tensor hn,
                        torch::Tensor ids, torch::Tensor wts, torch::Tensor rows, torch::Tensor counts,
                        torch::Tensor offsets, torch::Tensor cursor, torch::Tensor tiles, torch::Tensor ntiles,
-                       torch::Tensor A) {
+                       torch::Tensor A, int64_t e_base, int64_t e_count) {
   const int T = logits.size(0), H = hn.size(1);
-  const int J = k + (has_shared ? 1 : 0), G = E + (has_shared ? 1 : 0);
+  const int J = k + (has_shared ? 1 : 0), G = e_count ? (int)e_count : E + (has_shared ? 1 : 0);
+  TORCH_CHECK(!(e_count && has_shared), "expert parallelism needs a model without a shared expert");
   TORCH_CHECK(E <= 1024 && k <= 32 && H % 8 == 0, "routing limits");
   TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.stride(1) == 1 && hn.is_contiguous(), "logits f32 rows");
   TORCH_CHECK(ids.size(0) == T && ids.size(1) == J && rows.sizes() == ids.sizes() && A.size(0) >= (long long)T * J,
@@ -263,7 +275,8 @@ void moe_route_prefill(torch::Tensor logits, int64_t E, int64_t k, bool has_shar
   auto st = at::cuda::getCurrentCUDAStream();
   moe_route_topk_kernel<<<(T * 32 + 255) / 256, 256, 0, st>>>(logits.data_ptr<float>(), logits.stride(0), T, E, k,
                                                               has_shared, norm_topk, ids.data_ptr<int>(),
-                                                              wts.data_ptr<float>(), counts.data_ptr<int>());
+                                                              wts.data_ptr<float>(), counts.data_ptr<int>(), (int)e_base,
+                                                              (int)e_count);
   TORCH_CHECK(G <= 1024, "at most 1024 routing groups");
   moe_route_plan_kernel<<<1, 1024, 0, st>>>(counts.data_ptr<int>(), G, offsets.data_ptr<int>(), cursor.data_ptr<int>(),
                                           tiles.data_ptr<int>(), ntiles.data_ptr<int>(), tiles.size(0));

@@ -168,12 +168,13 @@ class FastModel:
     # ------------------------------------------------------------------
     @classmethod
     def from_hf(cls, cfg: ModelConfig, get: Callable[[str], torch.Tensor] | dict, device,
-                rank: int = 0, ws: int = 1, **kw) -> "FastModel":
-        """Load from HF-layout tensors (a dict or a name -> tensor callable)."""
+                rank: int = 0, ws: int = 1, ep: bool = False, **kw) -> "FastModel":
+        """Load from HF-layout tensors (a dict or a name -> tensor callable). `ep`: the
+        MoE layers are expert-parallel over the ranks (whole experts per rank)."""
         if isinstance(get, dict):
             get = get.__getitem__
         device = torch.device(device)
-        dims = layout.local_dims(cfg, rank, ws)
+        dims = layout.local_dims(cfg, rank, ws, ep)
         layers = []
         for i in range(cfg.num_hidden_layers):
             fl = layout.fuse_layer(cfg, dims, i, get)
@@ -185,10 +186,10 @@ class FastModel:
 
     @classmethod
     def random(cls, cfg: ModelConfig, device, seed: int = 0, rank: int = 0, ws: int = 1, std: float = 0.02,
-               **kw) -> "FastModel":
+               ep: bool = False, **kw) -> "FastModel":
         """Random-init N(0, std) directly in the fused layout on the device (large models)."""
         device = torch.device(device)
-        dims = layout.local_dims(cfg, rank, ws)
+        dims = layout.local_dims(cfg, rank, ws, ep)
         g = torch.Generator(device=device).manual_seed(seed + 7919 * rank)
 
         def mk(shape, dtype):
@@ -323,6 +324,15 @@ class FastModel:
             J = k + (1 if self.has_shared else 0)
             C.gemv_router(lw["router"], nb.x, nb.rlogits, lw["ln2"], eps, E, k, self.has_shared,
                           cfg.norm_topk_prob, nb.ids, nb.wts, nb.counter)
+            if d.ep:
+                # expert parallel: this rank runs the routes to its own experts; the fused
+                # cross-rank sum in the down kernel combines every rank's experts
+                if not self.comm.fused:
+                    raise RuntimeError("expert parallelism needs the fused p2p reduction (HELEXA_TP_MODE=p2p)")
+                C.gemv_experts_ep(lw["w_gu"], nb.x, nb.ids.view(-1), nb.act_moe, ops.SILU_PAIR, J, lw["ln2"], eps,
+                                  d.e0)
+                C.moe_down_ar_ep(lw["w_d"], nb.act_moe, nb.ids, nb.wts, nb.x, *self.comm.fused_args(), d.e0)
+                return
             C.gemv_experts(lw["w_gu"], nb.x, nb.ids.view(-1), nb.act_moe, ops.SILU_PAIR, J, lw["ln2"], eps)
             if self.comm is None or d.ws == 1:
                 C.moe_down(lw["w_d"], nb.act_moe, nb.ids, nb.wts, nb.x, None)
@@ -579,11 +589,13 @@ class FastModel:
         order = torch.argsort(flat, stable=True)
         tok_of, w_of = order // k, topv.view(-1)[order]
         counts = torch.bincount(flat, minlength=E).tolist()
+        d = self.dims
         start = 0
         for e, c in enumerate(counts):
-            if c:
+            le = e - d.e0 if d.ep else e  # expert parallel: only this rank's experts
+            if c and 0 <= le < lw["w_gu"].shape[0]:
                 t = tok_of[start:start + c]
-                y = self._linear(self._linear(hn[t], lw["w_gu"][e], 1), lw["w_d"][e])
+                y = self._linear(self._linear(hn[t], lw["w_gu"][le], 1), lw["w_d"][le])
                 out.index_add_(0, t, y.float() * w_of[start:start + c, None])
             start += c
         if self.has_shared:
@@ -596,7 +608,8 @@ class FastModel:
         cfg, dev = self.cfg, hn.device
         T, H = hn.shape
         shared = self.has_shared
-        J, G = k + int(shared), E + int(shared)
+        d = self.dims
+        J, G = k + int(shared), (d.e_local if d.ep else E + int(shared))
         i32 = torch.int32
         ids = torch.empty(T, J, dtype=i32, device=dev)
         wts = torch.empty(T, J, dtype=torch.float32, device=dev)
@@ -608,7 +621,7 @@ class FastModel:
         ntiles = torch.empty(1, dtype=i32, device=dev)
         A = torch.empty(T * J, H, dtype=torch.bfloat16, device=dev)
         self.C.moe_route_prefill(logits, E, k, shared, cfg.norm_topk_prob, hn.contiguous(), ids, wts, rows, counts,
-                                 offsets, cursor, tiles, ntiles, A)
+                                 offsets, cursor, tiles, ntiles, A, d.e0 if d.ep else 0, d.e_local if d.ep else 0)
         I2 = lw["w_gu"].shape[1]
         act = torch.empty(T * J, I2 // 2, dtype=torch.bfloat16, device=dev)
         self.C.gemm_grouped_dev(A, lw["w_gu"].view(-1, H), act, tiles, ntiles, I2, 1, self._gemm_err())

@@ -50,6 +50,9 @@ class LocalDims:
     inter: int = 0        # dense MLP shard
     moe_inter: int = 0    # per-expert shard
     shared_inter: int = 0
+    ep: bool = False      # expert parallel: whole experts e0 .. e0 + e_local - 1 on this rank
+    e0: int = 0
+    e_local: int = 0
 
     @property
     def gdn_kd(self) -> int:
@@ -72,7 +75,10 @@ class LocalDims:
         return self.hq * self.qw + 2 * self.hkv * self.D
 
 
-def local_dims(cfg: ModelConfig, rank: int = 0, ws: int = 1) -> LocalDims:
+def local_dims(cfg: ModelConfig, rank: int = 0, ws: int = 1, ep: bool = False) -> LocalDims:
+    """Per-rank shard sizes. With `ep` (expert parallelism, ws > 1) each rank holds
+    whole experts E/ws .. instead of an intermediate slice of every expert; attention,
+    GDN and dense layers stay tensor-parallel."""
     d = LocalDims(ws=ws, rank=rank, H=cfg.hidden_size)
     if cfg.num_full_layers:
         if cfg.num_attention_heads % ws:
@@ -98,7 +104,15 @@ def local_dims(cfg: ModelConfig, rank: int = 0, ws: int = 1) -> LocalDims:
         d.dk, d.dv = cfg.linear_key_head_dim, cfg.linear_value_head_dim
     if cfg.intermediate_size and cfg.intermediate_size % ws == 0:
         d.inter = cfg.intermediate_size // ws
-    if cfg.num_experts:
+    if cfg.num_experts and ep and ws > 1:
+        if cfg.num_experts % ws:
+            raise ValueError(f"{cfg.num_experts} experts do not split over {ws} ranks")
+        if cfg.shared_expert_intermediate_size:
+            raise ValueError("expert parallelism needs a model without a shared expert")
+        d.ep, d.e_local = True, cfg.num_experts // ws
+        d.e0 = rank * d.e_local
+        d.moe_inter = cfg.moe_intermediate_size
+    elif cfg.num_experts:
         if cfg.moe_intermediate_size % ws:
             raise ValueError("moe_intermediate_size does not split")
         d.moe_inter = cfg.moe_intermediate_size // ws
@@ -185,11 +199,13 @@ def fuse_layer(cfg: ModelConfig, dims: LocalDims, i: int, get, dtype=torch.bfloa
             rw.append(get(m + "shared_expert_gate.weight"))
         out["router"] = torch.cat(rw, 0).to(dtype).contiguous()
         gus, ds = [], []
-        for e in range(E):
+        # expert parallel: this rank's whole experts; tensor parallel: a slice of each
+        experts, es, er = (range(dims.e0, dims.e0 + dims.e_local), 1, 0) if dims.ep else (range(E), ws, r)
+        for e in experts:
             pre = m + f"experts.{e}."
-            gus.append(interleave_rows(_rows(get(pre + "gate_proj.weight"), ws, r),
-                                       _rows(get(pre + "up_proj.weight"), ws, r)))
-            ds.append(_cols(get(pre + "down_proj.weight"), ws, r))
+            gus.append(interleave_rows(_rows(get(pre + "gate_proj.weight"), es, er),
+                                       _rows(get(pre + "up_proj.weight"), es, er)))
+            ds.append(_cols(get(pre + "down_proj.weight"), es, er))
         if has_shared:
             if cfg.shared_expert_intermediate_size != cfg.moe_intermediate_size:
                 raise ValueError("the fused expert stack needs shared_expert_intermediate_size == "
@@ -222,9 +238,10 @@ def layer_shapes(cfg: ModelConfig, dims: LocalDims, i: int) -> dict[str, tuple[t
             s.update(q_norm=((dims.D,), f32), k_norm=((dims.D,), f32))
     if cfg.layer_uses_moe(i):
         extra = 1 if cfg.shared_expert_intermediate_size else 0
+        ne = dims.e_local if dims.ep else cfg.num_experts + extra
         s.update(router=((cfg.num_experts + extra, H), bf),
-                 w_gu=((cfg.num_experts + extra, 2 * dims.moe_inter, H), bf),
-                 w_d=((cfg.num_experts + extra, H, dims.moe_inter), bf))
+                 w_gu=((ne, 2 * dims.moe_inter, H), bf),
+                 w_d=((ne, H, dims.moe_inter), bf))
     else:
         s.update(w_gu=((2 * dims.inter, H), bf), w_d=((H, dims.inter), bf))
     return s

@@ -92,7 +92,8 @@ def test_moe_route_prefill_and_grouped_dev(shared):
     counts, offsets, cursor = torch.zeros(G, **i32), torch.empty(G, **i32), torch.empty(G, **i32)
     tiles, ntiles = torch.empty((T * J + 127) // 128 + G, 4, **i32), torch.empty(1, **i32)
     A = torch.empty(T * J, H, device="cuda", dtype=torch.bfloat16)
-    C.moe_route_prefill(logits, E, k, shared, True, hn, ids, wts, rows, counts, offsets, cursor, tiles, ntiles, A)
+    C.moe_route_prefill(logits, E, k, shared, True, hn, ids, wts, rows, counts, offsets, cursor, tiles, ntiles, A,
+                        0, 0)
     act = torch.empty(T * J, I, device="cuda", dtype=torch.bfloat16)
     e = _err()
     C.gemm_grouped_dev(A, w_gu.view(-1, H), act, tiles, ntiles, 2 * I, 1, e)

@@ -22,7 +22,7 @@ def _free_port():
     return p
 
 
-def _worker(rank, ws, port, name, q):
+def _worker(rank, ws, port, name, q, ep=False):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=ws)
     try:
@@ -36,7 +36,7 @@ def _worker(rank, ws, port, name, q):
         torch.manual_seed(0)
         w = _realistic(cfg, random_weights(cfg, seed=0, std=0.05))
         comm = TPComm(device=torch.device("cpu"))
-        fm = F.FastModel.from_hf(cfg, w, "cpu", rank=rank, ws=ws, max_slots=1, max_len=128, comm=comm)
+        fm = F.FastModel.from_hf(cfg, w, "cpu", rank=rank, ws=ws, max_slots=1, max_len=128, comm=comm, ep=ep)
         prompt = torch.randint(0, cfg.vocab_size, (70,), generator=torch.Generator().manual_seed(1)).int()
         out = fm.prefill(0, prompt, 0)
         # a numpy copy travels by value (a tensor would be shared through the child's
@@ -47,8 +47,12 @@ def _worker(rank, ws, port, name, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("name,ws", [("tiny-qwen3-next", 2), ("tiny-qwen3-next", 4), ("tiny-qwen3-moe", 2)])
-def test_tp_matches_single_rank(name, ws):
+@pytest.mark.parametrize("name,ws,ep", [("tiny-qwen3-next", 2, False), ("tiny-qwen3-next", 4, False),
+                                        ("tiny-qwen3-moe", 2, False), ("tiny-qwen3-moe", 2, True),
+                                        ("tiny-qwen3-moe", 4, True)])
+def test_tp_matches_single_rank(name, ws, ep):
+    """Tensor-parallel (and, with ep, expert-parallel MoE) prefill on gloo ranks against
+    the single-rank model."""
     import helexa_b200.models.fast as F
     from helexa_b200.config import get_preset
     from helexa_b200.weights.random_init import random_weights
@@ -66,7 +70,7 @@ def test_tp_matches_single_rank(name, ws):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, ws, port, name, q)) for r in range(ws)]
+    procs = [ctx.Process(target=_worker, args=(r, ws, port, name, q, ep)) for r in range(ws)]
     for p in procs:
         p.start()
     res = {r: torch.from_numpy(a) for r, a in (q.get(timeout=300) for _ in range(ws))}

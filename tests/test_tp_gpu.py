@@ -30,18 +30,18 @@ def _log(rank, msg):
             f.write(msg + "\n")
 
 
-def _run(rank, ws, port, mode, q):
+def _run(rank, ws, port, mode, q, name="tiny-qwen3-next", ep=False):
     import torch.distributed as dist
     _log(rank, f"start ws={ws} mode={mode}")
     try:
-        _run_inner(rank, ws, port, mode, q)
+        _run_inner(rank, ws, port, mode, q, name, ep)
     except BaseException as e:  # surface the failure in the log before dying
         import traceback
         _log(rank, "FAILED: " + "".join(traceback.format_exception(e)))
         raise
 
 
-def _run_inner(rank, ws, port, mode, q):
+def _run_inner(rank, ws, port, mode, q, name, ep):
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
@@ -53,13 +53,13 @@ def _run_inner(rank, ws, port, mode, q):
         from helexa_b200.parallel.tp import TPComm
         from helexa_b200.weights.random_init import random_weights
         from test_fast_model_gpu import _realistic
-        cfg = get_preset("tiny-qwen3-next")
+        cfg = get_preset(name)
         torch.manual_seed(0)
         w = _realistic(cfg, random_weights(cfg, seed=0, std=0.05))
         _log(rank, "pg up")
         comm = TPComm(device=dev, mode=mode) if ws > 1 else None
         _log(rank, "comm up")
-        fm = FastModel.from_hf(cfg, w, dev, rank=rank, ws=ws, max_slots=1, max_len=256, comm=comm)
+        fm = FastModel.from_hf(cfg, w, dev, rank=rank, ws=ws, max_slots=1, max_len=256, comm=comm, ep=ep)
         prompt = torch.randint(0, cfg.vocab_size, (60,), generator=torch.Generator().manual_seed(1)).int().to(dev)
         lg = fm.prefill(0, prompt, 0)
         torch.cuda.synchronize()
@@ -98,11 +98,11 @@ def _run_inner(rank, ws, port, mode, q):
         dist.destroy_process_group()
 
 
-def _launch(ws, mode):
+def _launch(ws, mode, name="tiny-qwen3-next", ep=False):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    ps = [ctx.Process(target=_run, args=(r, ws, port, mode, q)) for r in range(ws)]
+    ps = [ctx.Process(target=_run, args=(r, ws, port, mode, q, name, ep)) for r in range(ws)]
     for p in ps:
         p.start()
     import queue
@@ -127,10 +127,10 @@ def _launch(ws, mode):
 _cache: dict = {}
 
 
-def _results(ws, mode):
-    key = (ws, mode)
+def _results(ws, mode, name="tiny-qwen3-next", ep=False):
+    key = (ws, mode, name, ep)
     if key not in _cache:
-        _cache[key] = _launch(ws, mode)
+        _cache[key] = _launch(ws, mode, name, ep)
     return _cache[key]
 
 
@@ -160,3 +160,16 @@ def test_tp2_fused_reduction_matches_nccl():
     fused, nccl = _results(2, "p2p"), _results(2, "nccl")
     step_cos = [_cos(fused[0][1][i], nccl[0][1][i]) for i in range(fused[0][1].shape[0])]
     assert sorted(step_cos)[len(step_cos) // 2] > 0.99 and min(step_cos) > 0.85, step_cos
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ep2_matches_single_gpu():
+    """Expert-parallel MoE over 2 GPUs (whole experts per rank, routes to the other rank's
+    experts skipped, combine through the fused reduction) against the single GPU."""
+    single = _results(1, None, "tiny-qwen3-moe")[0]
+    res = _results(2, "p2p", "tiny-qwen3-moe", True)
+    for r in range(2):
+        assert _cos(res[r][0], single[0]) > 0.995
+        step_cos = [_cos(res[r][1][i], single[1][i]) for i in range(single[1].shape[0])]
+        assert sorted(step_cos)[len(step_cos) // 2] > 0.99 and min(step_cos) > 0.85, step_cos
+        assert torch.equal(res[r][2], res[0][2])
