@@ -33,10 +33,18 @@ class Metrics:
         self.tokens = Counter("cortex_completion_tokens_total", "completion tokens", ["model"], registry=self.reg)
         self.cold = Counter("cortex_cold_starts_total", "cold loads", ["model"], registry=self.reg)
         self.evictions = Counter("cortex_evictions_total", "evictions", ["model"], registry=self.reg)
+        self.principal_requests = Counter("cortex_principal_requests_total", "requests per principal",
+                                          ["principal", "model"], registry=self.reg)
+        self.principal_tokens = Counter("cortex_principal_tokens_total", "tokens per principal",
+                                        ["principal", "model", "kind"], registry=self.reg)
 
 
 def create_gateway(catalogue: Catalogue, nodes: list[NodeState], api_keys: dict[str, str] | None = None,
-                   require_auth: bool = False, poll_interval_s: float = 10.0, transport=None) -> FastAPI:
+                   require_auth: bool = False, poll_interval_s: float = 10.0, transport=None,
+                   entitlements: dict[str, set[str]] | None = None) -> FastAPI:
+    """`entitlements`: principal -> models it may use (a principal absent from the map,
+    and anonymous callers, may use every model). Usage is metered per principal
+    (anonymous callers as "anonymous") into `/metrics` and `GET /usage`."""
     app = FastAPI(title="helexa-b200 gateway")
     router = Router(catalogue, nodes)
     metrics = Metrics()
@@ -44,6 +52,21 @@ def create_gateway(catalogue: Catalogue, nodes: list[NodeState], api_keys: dict[
     app.state.router = router
     app.state.metrics = metrics
     app.state.client = client
+    usage: dict[str, dict[str, int]] = {}
+    app.state.usage = usage
+
+    def _meter(principal: str | None, model: str, prompt: int = 0, completion: int = 0, request: bool = False):
+        who = principal or "anonymous"
+        u = usage.setdefault(who, {"requests": 0, "prompt_tokens": 0, "completion_tokens": 0})
+        if request:
+            u["requests"] += 1
+            metrics.principal_requests.labels(who, model).inc()
+        u["prompt_tokens"] += prompt
+        u["completion_tokens"] += completion
+        if prompt:
+            metrics.principal_tokens.labels(who, model, "prompt").inc(prompt)
+        if completion:
+            metrics.principal_tokens.labels(who, model, "completion").inc(completion)
 
     async def poll_once():
         for n in list(router.nodes.values()):
@@ -86,6 +109,11 @@ def create_gateway(catalogue: Catalogue, nodes: list[NodeState], api_keys: dict[
         if err is not None:
             return err
         requested = body.get("model", "")
+        if principal and entitlements and principal in entitlements:
+            target = catalogue.resolve(requested)
+            if requested not in entitlements[principal] and target not in entitlements[principal]:
+                return JSONResponse(error_body(f"principal is not entitled to model {requested!r}",
+                                               "model_not_entitled"), 403)
         t0 = time.monotonic()
         try:
             dec = router.route(requested)
@@ -107,6 +135,7 @@ def create_gateway(catalogue: Catalogue, nodes: list[NodeState], api_keys: dict[
                 return JSONResponse(r.json(), r.status_code)
             dec.node.models[dec.model_id] = {"id": dec.model_id, "status": "loaded"}
         body["model"] = dec.model_id
+        _meter(principal, dec.model_id, request=True)
         headers = {k: v for k, v in request.headers.items()
                    if not k.lower().startswith("x-helexa-") and k.lower() not in ("host", "content-length",
                                                                                    "authorization")}
@@ -132,6 +161,7 @@ def create_gateway(catalogue: Catalogue, nodes: list[NodeState], api_keys: dict[
                     metrics.requests.labels(dec.model_id, str(resp.status_code)).inc()
                     metrics.duration.labels(dec.model_id).observe(time.monotonic() - t0)
                     metrics.tokens.labels(dec.model_id).inc(ntok)
+                    _meter(principal, dec.model_id, completion=ntok)
             return StreamingResponse(relay(), status_code=resp.status_code,
                                      media_type=resp.headers.get("content-type", "text/event-stream"))
         r = await client.post(url, json=body, headers=headers)
@@ -139,8 +169,10 @@ def create_gateway(catalogue: Catalogue, nodes: list[NodeState], api_keys: dict[
         metrics.duration.labels(dec.model_id).observe(time.monotonic() - t0)
         try:
             j = r.json()
-            usage = j.get("usage") or {}
-            metrics.tokens.labels(dec.model_id).inc(usage.get("completion_tokens", usage.get("output_tokens", 0)))
+            rep = j.get("usage") or {}
+            metrics.tokens.labels(dec.model_id).inc(rep.get("completion_tokens", rep.get("output_tokens", 0)))
+            _meter(principal, dec.model_id, prompt=int(rep.get("prompt_tokens", rep.get("input_tokens", 0)) or 0),
+                   completion=int(rep.get("completion_tokens", rep.get("output_tokens", 0)) or 0))
             if requested != dec.model_id and isinstance(j, dict) and "model" in j:
                 j["model"] = requested
             return JSONResponse(j, r.status_code, headers={k: v for k, v in r.headers.items()
@@ -163,6 +195,10 @@ def create_gateway(catalogue: Catalogue, nodes: list[NodeState], api_keys: dict[
             data.append({"id": mid, "object": "model", "owned_by": "helexa", "aliases": e.aliases,
                          "loaded_on": loaded, "limit": lim})
         return {"object": "list", "data": data}
+
+    @app.get("/usage")
+    async def usage_report():
+        return {"principals": usage}
 
     @app.get("/health")
     async def health():

@@ -113,3 +113,21 @@ def test_recovering_hold_and_debounced_unhealthy():
     for _ in range(3):
         r.observe("a", None, None)
     assert not r.nodes["a"].healthy
+
+
+def test_entitlements_and_per_principal_metering():
+    """A principal limited to m1 (reached through its alias too) is refused m2; usage is
+    metered per principal into /usage and /metrics."""
+    fleet = MockFleet()
+    app = _app(fleet, api_keys={"k1": "acct-1", "k2": "acct-2"}, entitlements={"acct-1": {"m1"}})
+    with TestClient(app) as c:
+        h1, h2 = {"authorization": "Bearer k1"}, {"authorization": "Bearer k2"}
+        assert c.post("/v1/chat/completions", json={"model": "m2"}, headers=h1).status_code == 403
+        assert c.post("/v1/chat/completions", json={"model": "fast"}, headers=h1).status_code == 200
+        assert c.post("/v1/chat/completions", json={"model": "m2"}, headers=h2).status_code == 200
+        c.post("/v1/chat/completions", json={"model": "m1"})
+        u = c.get("/usage").json()["principals"]
+        assert u["acct-1"] == {"requests": 1, "prompt_tokens": 0, "completion_tokens": 2}
+        assert u["acct-2"]["requests"] == 1 and u["anonymous"]["requests"] == 1
+        m = c.get("/metrics").text
+        assert 'cortex_principal_tokens_total{kind="completion",model="m1",principal="acct-1"} 2.0' in m
