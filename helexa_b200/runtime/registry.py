@@ -113,6 +113,8 @@ def build_served_model(spec: ModelSpec) -> ServedModel:
     if use_cuda:
         free, _ = torch.cuda.mem_get_info(sm.devices[0])
         adm.set_kv_budget_mb(max(0, free - (1500 << 20)) >> 20)
+        devs = list(sm.devices)
+        sm.free_vram_mb = lambda: min(torch.cuda.mem_get_info(d)[0] for d in devs) >> 20
     return sm
 
 

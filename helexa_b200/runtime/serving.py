@@ -109,6 +109,11 @@ class ServedModel:
     spec: dict = field(default_factory=dict)
     ema: ThroughputEma = field(default_factory=ThroughputEma)
     kv_bytes_per_token: int = 0
+    # refuse new requests while the tightest device has less free memory than this floor
+    # (prefill activations come from the caching allocator); the reference's
+    # NEURON_MIN_FREE_VRAM_MB guard
+    min_free_vram_mb: int = int(os.environ.get("HELEXA_MIN_FREE_VRAM_MB", "1500"))
+    free_vram_mb: object = None  # callable -> MiB free on the tightest device, or None (no check)
 
     @property
     def limits(self) -> ModelLimits:
@@ -130,6 +135,11 @@ class ServedModel:
         return self.tokenizer.encode(text), starts_in_think
 
     def _validate(self, ids: list[int], params: SamplingParams):
+        if self.free_vram_mb is not None:
+            free = self.free_vram_mb()
+            if free is not None and free < self.min_free_vram_mb:
+                raise RequestError(f"only {int(free)} MiB of device memory free (floor {self.min_free_vram_mb} MiB)",
+                                   503, "insufficient_vram")
         lim = self.limits
         if len(ids) > lim.input:
             raise RequestError(f"prompt has {len(ids)} tokens; this model accepts at most {lim.input}",

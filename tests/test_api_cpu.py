@@ -85,3 +85,19 @@ def test_errors(client):
     assert r.status_code == 400
     r = client.post("/models/unload", json={"model_id": "nope"})
     assert r.status_code == 404
+
+
+def test_refuses_below_free_memory_floor(client):
+    """Below the free-device-memory floor new requests get 503 insufficient_vram."""
+    sm = client.app.state.registry.models["tiny"]
+    old = sm.free_vram_mb
+    try:
+        sm.free_vram_mb = lambda: sm.min_free_vram_mb - 1
+        r = client.post("/v1/chat/completions", json={"model": "tiny", "max_tokens": 2,
+                                                      "messages": [{"role": "user", "content": "hi"}]})
+        assert r.status_code == 503 and r.json()["error"]["code"] == "insufficient_vram", r.text
+    finally:
+        sm.free_vram_mb = old
+    r = client.post("/v1/chat/completions", json={"model": "tiny", "max_tokens": 2,
+                                                  "messages": [{"role": "user", "content": "hi"}]})
+    assert r.status_code == 200
