@@ -126,6 +126,15 @@ def create_app(registry: ModelRegistry | None = None, default_models: list[dict]
     async def discovery():
         return discover_devices()
 
+    @app.get("/capabilities")
+    async def capabilities_of_source(source: str):
+        """Capabilities of an unloaded model directory, from its files alone."""
+        from ..weights.loader import discover_capabilities
+        path = source.split(":", 1)[1] if source.startswith("dir:") else source
+        if not os.path.isdir(path):
+            return _err(404, f"{path} is not a directory on this node", "not_found")
+        return {"source": source, "capabilities": discover_capabilities(path)}
+
     @app.get("/health")
     async def health():
         models = {}

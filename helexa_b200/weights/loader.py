@@ -133,3 +133,22 @@ def classify_dir(path: str) -> str:
     if has_st:
         return "dense"
     return "empty"
+
+
+def discover_capabilities(path: str) -> list[str]:
+    """Capabilities of a model directory from its files alone, without loading it (the
+    reference derives image / vision capability from the local HF cache the same way):
+    a diffusers pipeline -> ["image"]; a config with a vision tower or vision token ids ->
+    chat + vision (this node serves the text path only); otherwise chat + completion."""
+    import json
+    kind = classify_dir(path)
+    if kind == "diffusers":
+        return ["image"]
+    caps = ["chat", "completion"]
+    cfgp = os.path.join(path, "config.json")
+    if os.path.exists(cfgp):
+        with open(cfgp) as f:
+            raw = json.load(f)
+        if "vision_config" in raw or "image_token_id" in raw or "vision_start_token_id" in raw:
+            caps.append("vision")
+    return caps

@@ -72,3 +72,30 @@ def test_node_refuses_requests_while_shutting_down():
         r = c.post("/v1/chat/completions", json={"model": "x", "messages": []})
         assert r.status_code == 503 and r.headers.get("retry-after") == "5"
         assert c.get("/version").status_code == 200
+
+
+def test_capability_discovery_from_files(tmp_path):
+    import json
+    from helexa_b200.weights.loader import discover_capabilities
+    text = tmp_path / "text"
+    text.mkdir()
+    (text / "config.json").write_text(json.dumps({"model_type": "qwen3"}))
+    (text / "model.safetensors").write_bytes(b"")
+    assert discover_capabilities(str(text)) == ["chat", "completion"]
+    vis = tmp_path / "vis"
+    vis.mkdir()
+    (vis / "config.json").write_text(json.dumps({"model_type": "qwen3_5", "vision_config": {}}))
+    assert "vision" in discover_capabilities(str(vis))
+    img = tmp_path / "img"
+    img.mkdir()
+    (img / "model_index.json").write_text("{}")
+    assert discover_capabilities(str(img)) == ["image"]
+
+
+def test_capabilities_endpoint(tmp_path):
+    from fastapi.testclient import TestClient
+    from helexa_b200.server.app import create_app
+    (tmp_path / "model_index.json").write_text("{}")
+    with TestClient(create_app()) as c:
+        assert c.get("/capabilities", params={"source": str(tmp_path)}).json()["capabilities"] == ["image"]
+        assert c.get("/capabilities", params={"source": str(tmp_path / "nope")}).status_code == 404
