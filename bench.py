@@ -24,8 +24,9 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-# Published reference number this metric is compared against (the only
-# Qwen3-Next-80B bf16 decode figure the reference publishes, host-scatter MoE path).
+# Published reference number this metric is compared against: the only Qwen3-Next-80B
+# bf16 decode figure the reference publishes (4.3 tok/s on its host-scatter MoE path,
+# on other hardware).
 BASELINE_DECODE_TOK_S = 4.3
 
 

@@ -595,10 +595,10 @@ int na_launch(const hx::AttnDecodeArgs& a, int G, dim3 grid, cudaStream_t st) {
       case 16:
         if constexpr (D <= 128) { hx::launch_dg<D, 16>(a, grid, st); break; }
         [[fallthrough]];
-      default: return na_fail(2, "unsupported GQA group size (Hq / Hkv must be 1, 2, 4, 8, or 16 with head dim <= 128)");
+      default: return na_fail(HX_NOALLOC_E_GQA, "unsupported GQA group size (Hq / Hkv must be 1, 2, 4, 8, or 16 with head dim <= 128)");
     }
   } catch (const std::exception& ex) {
-    return na_fail(7, ex.what());
+    return na_fail(HX_NOALLOC_E_LAUNCH, ex.what());
   }
   return 0;
 }
@@ -612,18 +612,18 @@ extern "C" int hx_attn_decode_noalloc(const void* proj, int ldp, const float* q_
                                       const int* pos, void* out, int B, int Hq, int Hkv, int D, int rot, int gated,
                                       float eps, int nsplit, cudaStream_t stream) {
   g_na_err[0] = 0;
-  if (B < 1 || Hq < 1 || Hkv < 1 || nsplit < 1 || Hq % Hkv) return na_fail(3, "invalid B / Hq / Hkv / nsplit");
+  if (B < 1 || Hq < 1 || Hkv < 1 || nsplit < 1 || Hq % Hkv) return na_fail(HX_NOALLOC_E_ARGS, "invalid B / Hq / Hkv / nsplit");
   if ((long long)B * Hq * nsplit * D > HX_NOALLOC_MAX_PART_O || (long long)B * Hq * nsplit > HX_NOALLOC_MAX_ROWS ||
       (long long)B * Hkv > HX_NOALLOC_MAX_COUNTERS) {
     snprintf(g_na_err, sizeof(g_na_err),
              "scratch too small: needs B*Hq*nsplit*D=%lld (max %d), B*Hq*nsplit=%lld (max %d), B*Hkv=%lld (max %d)",
              (long long)B * Hq * nsplit * D, HX_NOALLOC_MAX_PART_O, (long long)B * Hq * nsplit, HX_NOALLOC_MAX_ROWS,
              (long long)B * Hkv, HX_NOALLOC_MAX_COUNTERS);
-    return 4;
+    return HX_NOALLOC_E_SCRATCH;
   }
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices) return na_fail(5, "cudaGetDevice failed");
+  if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices) return na_fail(HX_NOALLOC_E_DEVICE, "cudaGetDevice failed");
   NoAllocScratch* s = nullptr;
   int rc = na_setup(dev, &s);
   if (rc) return rc;
@@ -650,7 +650,7 @@ extern "C" int hx_attn_decode_noalloc(const void* proj, int ldp, const float* q_
   if (D == 256) rc = na_launch<256>(a, G, grid, stream);
   else if (D == 128) rc = na_launch<128>(a, G, grid, stream);
   else if (D == 64) rc = na_launch<64>(a, G, grid, stream);
-  else return na_fail(6, "unsupported head dim (64, 128 or 256)");
+  else return na_fail(HX_NOALLOC_E_HEAD_DIM, "unsupported head dim (64, 128 or 256)");
   if (rc) return rc;
   e = cudaGetLastError();
   if (e != cudaSuccess) return na_fail((int)e, cudaGetErrorString(e));

@@ -24,7 +24,15 @@ extern "C" {
 #define HX_NOALLOC_MAX_ROWS (1 << 15)
 #define HX_NOALLOC_MAX_COUNTERS 1024
 
-// Returns 0 on success, otherwise a non-zero code; hx_noalloc_error() describes it.
+// Return codes: 0 on success; a cudaError_t value (below 1000) when a CUDA call failed;
+// otherwise one of the HX_NOALLOC_E_* codes below, which start at 1000 so they never
+// collide with a cudaError_t. hx_noalloc_error() describes the last failure.
+#define HX_NOALLOC_E_GQA 1002      // Hq / Hkv is not a supported GQA group size
+#define HX_NOALLOC_E_ARGS 1003     // B, Hq, Hkv or nsplit invalid
+#define HX_NOALLOC_E_SCRATCH 1004  // request exceeds the fixed scratch limits above
+#define HX_NOALLOC_E_DEVICE 1005   // no current device
+#define HX_NOALLOC_E_HEAD_DIM 1006 // head dim not 64, 128 or 256
+#define HX_NOALLOC_E_LAUNCH 1007   // the launch helper threw
 // See attn_decode.cu for the argument layout, set-up and concurrency rules.
 int hx_attn_decode_noalloc(const void* proj, int ldp, const float* q_norm_w, const float* k_norm_w,
                            const float* inv_freq, void* kc, void* vc, int maxlen, const int* slots, const int* pos,

@@ -16,8 +16,45 @@ import json
 
 import torch
 
+from .. import ops
 from ..config import get_preset
 from ..models.fast import FastModel
+
+
+class SkippingModel(FastModel):
+    """FastModel whose decode layer leaves named components out (single rank), so a
+    replayed step measures their share of the step time. Profiling only."""
+
+    skip: frozenset = frozenset()
+
+    def _decode_layer(self, i, nb):
+        C, cfg, d, lw, skip = self.C, self.cfg, self.dims, self.layers[i], self.skip
+        eps = cfg.rms_norm_eps
+        if not skip:
+            return super()._decode_layer(i, nb)
+        if cfg.is_linear(i) and "gdn" in skip or not cfg.is_linear(i) and "attn" in skip:
+            pass
+        elif cfg.is_linear(i):
+            self._gemv(lw["w_in"], nb.x, nb.proj_gdn, ops.STORE_BF16, None, lw["ln1"], eps)
+            if "gdn_core" not in skip:
+                C.gdn_decode(nb.proj_gdn, lw["conv_w"], self.conv[i], self.rec[i], lw["A_log"], lw["dt_bias"],
+                             lw["gnorm"], nb.slots, self.pos, nb.gdn_out, d.hk, d.hv, d.dk, d.dv, eps)
+            self._row_parallel(lw["out_w"], nb.gdn_out, nb)
+        else:
+            self._gemv(lw["w_qkv"], nb.x, nb.proj_attn, ops.STORE_BF16, None, lw["ln1"], eps)
+            if "attn_core" not in skip:
+                C.attn_decode(nb.proj_attn, lw.get("q_norm"), lw.get("k_norm"), self.inv_freq, self.kc[i],
+                              self.vc[i], nb.slots, self.pos, nb.part_o, nb.part_ml, nb.counters, nb.attn_out,
+                              d.hq, d.hkv, d.D, cfg.rotary_dim, cfg.attn_output_gate, eps)
+            self._row_parallel(lw["o_w"], nb.attn_out, nb)
+        if "ffn" not in skip and cfg.layer_uses_moe(i):
+            E, k = cfg.num_experts, cfg.num_experts_per_tok
+            J = k + (1 if self.has_shared else 0)
+            C.gemv_router(lw["router"], nb.x, nb.rlogits, lw["ln2"], eps, E, k, self.has_shared,
+                          cfg.norm_topk_prob, nb.ids, nb.wts, nb.counter)
+            if "experts" not in skip:
+                C.gemv_experts(lw["w_gu"], nb.x, nb.ids.view(-1), nb.act_moe, ops.SILU_PAIR, J, lw["ln2"], eps)
+                C.moe_down(lw["w_d"], nb.act_moe, nb.ids, nb.wts, nb.x, None)
 
 
 def main():
@@ -44,7 +81,9 @@ def main():
     B = args.batch
     if args.quant:
         fm.quantize_(args.quant.upper())
-    fm.profile_skip = set(x for x in args.skip.split(",") if x)
+    if args.skip:
+        fm.__class__ = SkippingModel
+        fm.skip = frozenset(x for x in args.skip.split(",") if x)
     if args.eager:
         nb = fm.buffers(B)
     else:

@@ -1,0 +1,122 @@
+"""Command line: run a node, run the gateway, print fleet status.
+
+  python -m helexa_b200.cli node   [--host H] [--port P] [--config node.toml]
+  python -m helexa_b200.cli serve  [--config cortex.toml]
+  python -m helexa_b200.cli status [--endpoint http://localhost:31313]
+
+`serve` and `status` are the reference's `cortex serve|status` (cortex-cli/src/main.rs:
+15-111). The gateway config is TOML:
+
+  [gateway]
+  listen = "0.0.0.0:31313"
+  poll_interval_s = 10
+  require_auth = false
+
+  [[neurons]]                       # one per node
+  name = "gpu-box-1"
+  url = "http://10.0.0.5:13131"
+
+  [[models]]                        # catalogue entries (CatalogueEntry fields)
+  model_id = "qwen3-8b"
+  source = "preset:qwen3-8b"
+  aliases = ["fast"]
+  tensor_parallel = 2
+
+  [auth.keys]                       # bearer key -> principal
+  "sk-abc" = "acct-1"
+
+  [entitlements]                    # principal -> models it may use
+  "acct-1" = ["qwen3-8b"]
+
+  [budgets."acct-1"]                # token cap; window_s = 0 is a hard balance
+  hard_cap = 1000000
+  window_s = 0
+
+`HELEXA_`-prefixed environment variables override keys (`__` separates levels).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import sys
+
+
+def _gateway_from_config(cfg: dict):
+    from .gateway.app import create_gateway
+    from .gateway.budget import Cap
+    from .gateway.core import Catalogue, CatalogueEntry, NodeState
+
+    cat = Catalogue()
+    for m in cfg.get("models", []):
+        cat.add(CatalogueEntry(**{k: v for k, v in m.items() if k in CatalogueEntry.__dataclass_fields__}))
+    nodes = [NodeState(n["name"], n["url"].rstrip("/")) for n in cfg.get("neurons", [])]
+    if not nodes:
+        raise SystemExit("config has no [[neurons]] entries")
+    gw = cfg.get("gateway", {})
+    keys = cfg.get("auth", {}).get("keys") or None
+    ents = {p: set(ms) for p, ms in (cfg.get("entitlements") or {}).items()} or None
+    budgets = {p: Cap(b.get("hard_cap"), int(b.get("window_s", 0))) for p, b in (cfg.get("budgets") or {}).items()}
+    return create_gateway(cat, nodes, api_keys=keys, require_auth=bool(gw.get("require_auth", False)),
+                          poll_interval_s=float(gw.get("poll_interval_s", 10.0)), entitlements=ents,
+                          budgets=budgets or None)
+
+
+def _listen(s: str) -> tuple[str, int]:
+    host, _, port = s.rpartition(":")
+    return host or "0.0.0.0", int(port)
+
+
+def status_report(endpoint: str, get=None) -> str:
+    """Fleet health and the models with their node placements, as printed by `status`."""
+    if get is None:
+        import httpx
+
+        def get(url):
+            r = httpx.get(url, timeout=10.0)
+            r.raise_for_status()
+            return r.json()
+    endpoint = endpoint.rstrip("/")
+    health = get(endpoint + "/health")
+    models = get(endpoint + "/v1/models")
+    lines = ["Fleet health: " + json.dumps(health, indent=2, sort_keys=True), "", "Models:"]
+    for m in models.get("data", []):
+        where = ", ".join(f"{n}(loaded)" for n in m.get("loaded_on") or []) or "-"
+        lim = m.get("limit") or {}
+        ctx = f"ctx={lim['context']}" if lim.get("context") else ""
+        lines.append(f"  {m.get('id', '?'):40} {where} {ctx}".rstrip())
+    return "\n".join(lines)
+
+
+def main(argv: list[str] | None = None) -> int:
+    ap = argparse.ArgumentParser(prog="helexa", description="helexa-b200 serving engine")
+    sub = ap.add_subparsers(dest="cmd", required=True)
+    n = sub.add_parser("node", help="run a node daemon (the serving engine)")
+    n.add_argument("--host", default="127.0.0.1")
+    n.add_argument("--port", type=int, default=13131)
+    n.add_argument("--config")
+    s = sub.add_parser("serve", help="run the gateway in front of a fleet of nodes")
+    s.add_argument("-c", "--config", default="cortex.toml")
+    st = sub.add_parser("status", help="print fleet health and model placements")
+    st.add_argument("-e", "--endpoint", default="http://localhost:31313")
+    args = ap.parse_args(argv)
+    if args.cmd == "node":
+        from .server.app import main as node_main
+        sys.argv = [sys.argv[0], "--host", args.host, "--port", str(args.port)] + \
+            (["--config", args.config] if args.config else [])
+        node_main()
+        return 0
+    if args.cmd == "serve":
+        import uvicorn
+
+        from .config.settings import load_settings
+        cfg = load_settings(args.config)
+        app = _gateway_from_config(cfg)
+        host, port = _listen(cfg.get("gateway", {}).get("listen", "0.0.0.0:31313"))
+        uvicorn.run(app, host=host, port=port)
+        return 0
+    print(status_report(args.endpoint))
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

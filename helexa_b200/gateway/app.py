@@ -20,6 +20,7 @@ from fastapi.responses import JSONResponse, Response, StreamingResponse
 from prometheus_client import CollectorRegistry, Counter, Histogram, generate_latest
 
 from ..server.wire import error_body
+from .budget import BudgetExceeded, BudgetLedger, Cap, SSEUsage, estimate_prompt_tokens, reservation_estimate
 from .core import Catalogue, NodeState, NoRoute, Router
 
 
@@ -41,10 +42,12 @@ class Metrics:
 
 def create_gateway(catalogue: Catalogue, nodes: list[NodeState], api_keys: dict[str, str] | None = None,
                    require_auth: bool = False, poll_interval_s: float = 10.0, transport=None,
-                   entitlements: dict[str, set[str]] | None = None) -> FastAPI:
+                   entitlements: dict[str, set[str]] | None = None,
+                   budgets: dict[str, Cap] | None = None) -> FastAPI:
     """`entitlements`: principal -> models it may use (a principal absent from the map,
     and anonymous callers, may use every model). Usage is metered per principal
-    (anonymous callers as "anonymous") into `/metrics` and `GET /usage`."""
+    (anonymous callers as "anonymous") into `/metrics` and `GET /usage`. `budgets`:
+    principal -> token cap, enforced by reserve -> settle (`gateway/budget.py`)."""
     app = FastAPI(title="helexa-b200 gateway")
     router = Router(catalogue, nodes)
     metrics = Metrics()
@@ -54,6 +57,8 @@ def create_gateway(catalogue: Catalogue, nodes: list[NodeState], api_keys: dict[
     app.state.client = client
     usage: dict[str, dict[str, int]] = {}
     app.state.usage = usage
+    ledger = BudgetLedger(budgets)
+    app.state.ledger = ledger
 
     def _meter(principal: str | None, model: str, prompt: int = 0, completion: int = 0, request: bool = False):
         who = principal or "anonymous"
@@ -121,6 +126,28 @@ def create_gateway(catalogue: Catalogue, nodes: list[NodeState], api_keys: dict[
             metrics.requests.labels(requested, str(e.status)).inc()
             h = {"Retry-After": str(e.retry_after)} if e.retry_after else None
             return JSONResponse(error_body(str(e), e.code), e.status, headers=h)
+        # fail-fast prompt pre-validation against the advertised context (the node stays
+        # the exact limit; the estimate under-counts, so only gross overages stop here)
+        lim = (dec.node.models.get(dec.model_id) or {}).get("limit") or {}
+        est = estimate_prompt_tokens(body)
+        if isinstance(lim.get("context"), int) and est > lim["context"]:
+            metrics.requests.labels(dec.model_id, "400").inc()
+            return JSONResponse(error_body(f"prompt is about {est} tokens; {dec.model_id} accepts at most "
+                                           f"{lim['context']}", "context_length_exceeded"), 400)
+        try:
+            resv = ledger.reserve(principal, reservation_estimate(body, lim.get("output")))
+        except BudgetExceeded as e:
+            metrics.requests.labels(dec.model_id, "429").inc()
+            h = {"Retry-After": str(e.retry_after)} if e.retry_after else None
+            return JSONResponse(error_body(str(e), e.code), 429, headers=h)
+        handoff = {"stream": False}
+        try:
+            return await _dispatch(request, path, body, principal, requested, dec, t0, resv, handoff)
+        finally:
+            if not handoff["stream"]:  # a streamed response settles when its relay ends
+                ledger.release(resv)  # no-op once settled
+
+    async def _dispatch(request, path, body, principal, requested, dec, t0, resv, handoff):
         if dec.action == "cold_load":
             for victim in dec.evict:
                 await client.post(dec.node.url + "/models/unload", json={"model_id": victim})
@@ -148,20 +175,25 @@ def create_gateway(catalogue: Catalogue, nodes: list[NodeState], api_keys: dict[
 
             async def relay():
                 first = True
-                ntok = 0
+                seen = SSEUsage()
                 try:
                     async for chunk in resp.aiter_bytes():
                         if first:
                             metrics.ttft.labels(dec.model_id).observe(time.monotonic() - t0)
                             first = False
-                        ntok += chunk.count(b'"content"')
+                        seen.feed(chunk)
                         yield chunk
                 finally:
                     await resp.aclose()
                     metrics.requests.labels(dec.model_id, str(resp.status_code)).inc()
                     metrics.duration.labels(dec.model_id).observe(time.monotonic() - t0)
-                    metrics.tokens.labels(dec.model_id).inc(ntok)
-                    _meter(principal, dec.model_id, completion=ntok)
+                    metrics.tokens.labels(dec.model_id).inc(seen.completion)
+                    _meter(principal, dec.model_id, prompt=seen.prompt, completion=seen.completion)
+                    if seen.seen:
+                        ledger.settle(resv, seen.prompt + seen.completion)
+                    else:
+                        ledger.release(resv)
+            handoff["stream"] = True
             return StreamingResponse(relay(), status_code=resp.status_code,
                                      media_type=resp.headers.get("content-type", "text/event-stream"))
         r = await client.post(url, json=body, headers=headers)
@@ -171,8 +203,11 @@ def create_gateway(catalogue: Catalogue, nodes: list[NodeState], api_keys: dict[
             j = r.json()
             rep = j.get("usage") or {}
             metrics.tokens.labels(dec.model_id).inc(rep.get("completion_tokens", rep.get("output_tokens", 0)))
-            _meter(principal, dec.model_id, prompt=int(rep.get("prompt_tokens", rep.get("input_tokens", 0)) or 0),
-                   completion=int(rep.get("completion_tokens", rep.get("output_tokens", 0)) or 0))
+            pt = int(rep.get("prompt_tokens", rep.get("input_tokens", 0)) or 0)
+            ct = int(rep.get("completion_tokens", rep.get("output_tokens", 0)) or 0)
+            _meter(principal, dec.model_id, prompt=pt, completion=ct)
+            if rep:
+                ledger.settle(resv, pt + ct)
             if requested != dec.model_id and isinstance(j, dict) and "model" in j:
                 j["model"] = requested
             return JSONResponse(j, r.status_code, headers={k: v for k, v in r.headers.items()
@@ -198,7 +233,11 @@ def create_gateway(catalogue: Catalogue, nodes: list[NodeState], api_keys: dict[
 
     @app.get("/usage")
     async def usage_report():
-        return {"principals": usage}
+        out = {}
+        for who, u in usage.items():
+            b = ledger.snapshot(who)
+            out[who] = dict(u, budget=b) if b else u
+        return {"principals": out}
 
     @app.get("/health")
     async def health():

@@ -161,7 +161,6 @@ class FastModel:
                 self.vc[i] = torch.zeros(shp, dtype=torch.bfloat16, device=device)
         self._bufs: dict[int, DecodeBuffers] = {}
         self.prefill_timer = None  # optional PhaseTimer (CUDA events per prefill phase)
-        self.profile_skip: set[str] = set()  # profiling only (see _decode_layer)
 
     # ------------------------------------------------------------------
     # construction
@@ -281,33 +280,6 @@ class FastModel:
     def _decode_layer(self, i: int, nb: DecodeBuffers):
         C, cfg, d, lw = self.C, self.cfg, self.dims, self.layers[i]
         eps = cfg.rms_norm_eps
-        skip = self.profile_skip
-        if skip:  # profiling only: leave components out to measure their share of a step
-            if cfg.is_linear(i) and "gdn" in skip or not cfg.is_linear(i) and "attn" in skip:
-                pass
-            elif cfg.is_linear(i):
-                self._gemv(lw["w_in"], nb.x, nb.proj_gdn, ops.STORE_BF16, None, lw["ln1"], eps)
-                if "gdn_core" not in skip:
-                    C.gdn_decode(nb.proj_gdn, lw["conv_w"], self.conv[i], self.rec[i], lw["A_log"],
-                                 lw["dt_bias"], lw["gnorm"], nb.slots, self.pos, nb.gdn_out, d.hk, d.hv, d.dk, d.dv,
-                                 eps)
-                self._row_parallel(lw["out_w"], nb.gdn_out, nb)
-            else:
-                self._gemv(lw["w_qkv"], nb.x, nb.proj_attn, ops.STORE_BF16, None, lw["ln1"], eps)
-                if "attn_core" not in skip:
-                    C.attn_decode(nb.proj_attn, lw.get("q_norm"), lw.get("k_norm"), self.inv_freq, self.kc[i],
-                                  self.vc[i], nb.slots, self.pos, nb.part_o, nb.part_ml, nb.counters, nb.attn_out,
-                                  d.hq, d.hkv, d.D, cfg.rotary_dim, cfg.attn_output_gate, eps)
-                self._row_parallel(lw["o_w"], nb.attn_out, nb)
-            if "ffn" not in skip and cfg.layer_uses_moe(i):
-                E, k = cfg.num_experts, cfg.num_experts_per_tok
-                J = k + (1 if self.has_shared else 0)
-                C.gemv_router(lw["router"], nb.x, nb.rlogits, lw["ln2"], eps, E, k, self.has_shared,
-                              cfg.norm_topk_prob, nb.ids, nb.wts, nb.counter)
-                if "experts" not in skip:
-                    C.gemv_experts(lw["w_gu"], nb.x, nb.ids.view(-1), nb.act_moe, ops.SILU_PAIR, J, lw["ln2"], eps)
-                    C.moe_down(lw["w_d"], nb.act_moe, nb.ids, nb.wts, nb.x, None)
-            return
         if cfg.is_linear(i):
             self._gemv(lw["w_in"], nb.x, nb.proj_gdn, ops.STORE_BF16, None, lw["ln1"], eps)
             C.gdn_decode(nb.proj_gdn, lw["conv_w"], self.conv[i], self.rec[i], lw["A_log"], lw["dt_bias"],

@@ -18,6 +18,8 @@ import torch
 
 from ..weights.loader import resolve_source
 from .admission import AdmissionConfig, AdmissionController
+from .context_limit import ContextProfile, derive_limit
+from .preflight import PreflightError, preflight
 from .engine import Engine
 from .prefix_cache import PrefixCache
 from .runner import FastRunner, RefRunner
@@ -54,18 +56,61 @@ class ModelSpec:
 
 
 class LoadError(RuntimeError):
-    pass
+    def __init__(self, message: str, code: str = "load_failed", hint: str = ""):
+        super().__init__(message)
+        self.code, self.hint = code, hint
+
+
+# free device memory kept back from the KV sizing (activations, graphs, workspace)
+FLOOR_BYTES = int(os.environ.get("HELEXA_VRAM_FLOOR_MB", "1500")) << 20
+
+
+def free_device_bytes(dev: int) -> int:
+    """Free memory of a device including what PyTorch's caching allocator holds but is
+    not using (that memory is reusable by the next allocation, so it is not "used")."""
+    free, _ = torch.cuda.mem_get_info(dev)
+    return free + max(0, torch.cuda.memory_reserved(dev) - torch.cuda.memory_allocated(dev))
+
+
+def plan_max_len(cfg, spec: "ModelSpec", free_bytes: int, weight_bytes: int) -> int:
+    """KV length per slot that fits the tightest device after the weights, for the
+    spec's slot count (context_limit.rs: free memory -> context)."""
+    tp = max(1, spec.tensor_parallel)
+    prof = ContextProfile.from_config(cfg, tp)
+    lim = derive_limit(prof, max(0, free_bytes - weight_bytes), floor_bytes=FLOOR_BYTES,
+                       concurrent=spec.max_batch + 1)
+    return max(0, min(spec.max_len, cfg.max_position_embeddings, lim.context))
 
 
 def build_served_model(spec: ModelSpec) -> ServedModel:
     src = resolve_source(spec.source)
     cfg = src.config
     use_cuda = (spec.device or ("cuda" if torch.cuda.is_available() else "cpu")) == "cuda"
+    devs_free = None
+    if use_cuda:
+        ids = spec.devices or list(range(spec.tensor_parallel))
+        devs_free = [free_device_bytes(d) for d in ids]
+    try:
+        kind = src.kind
+        if kind == "dir":
+            from ..weights.loader import classify_dir
+            kind = classify_dir(src.path)
+        preflight(kind, cfg, spec.tensor_parallel, spec.quant, devs_free)
+    except PreflightError as e:
+        raise LoadError(e.message, e.code, e.hint) from e
     if spec.tensor_parallel > 1:
-        raise LoadError("tensor_parallel > 1 is served by the rank worker pool (helexa_b200.runtime.worker)")
+        if not use_cuda:
+            return _build_tp_cpu(spec, src, cfg)
+        return _build_tp(spec, src, cfg, devs_free)
     tok = load_tokenizer(src.path, cfg.vocab_size)
     max_len = min(spec.max_len, cfg.max_position_embeddings)
     if use_cuda:
+        bpp = {"Q4_K": 0.5625, "Q4_K_M": 0.6, "Q6_K": 0.82, "Q8_0": 1.0625}.get((spec.quant or "").upper(), 2.0)
+        # bf16 weights exist before in-situ quantization, so size KV for the bf16 load
+        max_len = plan_max_len(cfg, spec, devs_free[0], int(cfg.param_count() * max(bpp, 2.0)))
+        if max_len < 256:
+            raise LoadError(f"only {max_len} tokens of KV fit beside the weights", "insufficient_memory",
+                            "lower max_batch or use more tensor-parallel ranks")
         from ..models.fast import FastModel
         dev = torch.device("cuda", (spec.devices or [0])[0])
         kw = dict(max_slots=spec.max_batch + 1, max_len=max_len)
@@ -111,11 +156,35 @@ def build_served_model(spec: ModelSpec) -> ServedModel:
                      defaults=defaults, devices=spec.devices or ([0] if use_cuda else []),
                      tensor_parallel=spec.tensor_parallel, spec=asdict(spec), kv_bytes_per_token=kv_bpt)
     if use_cuda:
-        free, _ = torch.cuda.mem_get_info(sm.devices[0])
-        adm.set_kv_budget_mb(max(0, free - (1500 << 20)) >> 20)
+        # KV pools are preallocated for every slot at max_len, so the admission budget is
+        # that pool (a request reserves its prompt + output tokens against it)
+        adm.set_kv_budget_mb((kv_bpt * max_len * spec.max_batch) >> 20)
         devs = list(sm.devices)
-        sm.free_vram_mb = lambda: min(torch.cuda.mem_get_info(d)[0] for d in devs) >> 20
+        sm.free_vram_mb = lambda: min(free_device_bytes(d) for d in devs) >> 20
     return sm
+
+
+def _build_tp(spec, src, cfg, devs_free):
+    from .tp_pool import build_tp_served_model
+    return build_tp_served_model(spec, src, cfg, devs_free)
+
+
+def _build_tp_cpu(spec, src, cfg):
+    """tensor_parallel > 1 without GPUs: gloo rank processes that each run the full
+    fp32 reference model of a preset (the pool's host logic, no sharding). The
+    `HELEXA_DEBUG_TP_FAIL=<rank>:<prefill length>` hook makes that rank raise on such a
+    prefill (host-side fault injection for recovery tests)."""
+    from .tp_pool import serve_runner, spawn_pool
+    if src.kind != "preset":
+        raise LoadError("tensor_parallel > 1 on the CPU serves presets only", "bad_tensor_parallel")
+    args = {"preset": src.preset, "max_slots": spec.max_batch + 1, "max_len": min(spec.max_len, 4096)}
+    fail = os.environ.get("HELEXA_DEBUG_TP_FAIL")
+    if fail:
+        r, n = fail.split(":")
+        args.update(fail_rank=int(r), fail_prefill_len=int(n))
+    runner = spawn_pool(spec.tensor_parallel, "helexa_b200.runtime.tp_pool:cpu_ref_runner", args, backend="gloo",
+                        init_timeout_s=300)
+    return serve_runner(spec, src, cfg, runner, [], runner.max_len)
 
 
 def _hf(gname: str):
@@ -169,9 +238,12 @@ class ModelRegistry:
             fut.set_result(sm)
             return sm
         except Exception as e:
-            fut.set_exception(LoadError(str(e)))
+            err = e if isinstance(e, LoadError) else LoadError(str(e))
+            fut.set_exception(err)
             fut.exception()  # mark retrieved
-            raise LoadError(str(e)) from e
+            if err is e:
+                raise
+            raise err from e
         finally:
             self.loading.pop(spec.model_id, None)
 
@@ -184,6 +256,9 @@ class ModelRegistry:
         m.admission.close()
         m.status = "unloading"
         await asyncio.to_thread(m.engine.shutdown)
+        close = getattr(m.engine.runner, "close", None)
+        if close is not None:  # tensor-parallel pool: stop the rank processes
+            await asyncio.to_thread(close)
         self.models.pop(model_id, None)
         del m
         if torch.cuda.is_available():

@@ -115,10 +115,18 @@ class ServedModel:
     min_free_vram_mb: int = int(os.environ.get("HELEXA_MIN_FREE_VRAM_MB", "1500"))
     free_vram_mb: object = None  # callable -> MiB free on the tightest device, or None (no check)
 
+    # prompts must prefill within this many seconds at the measured prefill rate
+    max_prefill_s: float = float(os.environ.get("HELEXA_MAX_PREFILL_S", "120"))
+
     @property
     def limits(self) -> ModelLimits:
+        """Context = the KV length the runner was sized for (derived from free device
+        memory at load); input additionally bounded by the prompt cap and by the
+        prefill-time budget at the EMA prefill rate (harness/context_limit.rs)."""
         ctx = self.engine.runner.max_len
         inp = min(self.max_prompt_tokens, ctx - 1)
+        if self.ema.prefill_tok_s > 0:
+            inp = max(1, min(inp, int(self.ema.prefill_tok_s * self.max_prefill_s)))
         return ModelLimits(context=ctx, input=inp, output=max(1, ctx - 1))
 
     # ---- prompt -------------------------------------------------------------

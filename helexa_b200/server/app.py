@@ -165,7 +165,10 @@ def create_app(registry: ModelRegistry | None = None, default_models: list[dict]
         try:
             spec = ModelSpec.from_dict(body)
             m = await reg.load(spec)
-        except (LoadError, ValueError, FileNotFoundError, KeyError) as e:
+        except LoadError as e:
+            return _err(422, str(e) + (f" ({e.hint})" if e.hint else ""),
+                        "model_load_failed" if e.code == "load_failed" else e.code)
+        except (ValueError, FileNotFoundError, KeyError) as e:
             return _err(422, str(e), "model_load_failed")
         return {"status": "loaded", "model_id": m.model_id, "limit": m.limits.__dict__}
 

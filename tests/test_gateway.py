@@ -131,3 +131,103 @@ def test_entitlements_and_per_principal_metering():
         assert u["acct-2"]["requests"] == 1 and u["anonymous"]["requests"] == 1
         m = c.get("/metrics").text
         assert 'cortex_principal_tokens_total{kind="completion",model="m1",principal="acct-1"} 2.0' in m
+
+
+def test_streamed_usage_metered_from_final_usage_chunk():
+    """Streamed usage comes from the usage the node reports in its final SSE event, even
+    when the bytes arrive split at arbitrary points."""
+    from helexa_b200.gateway.budget import SSEUsage
+    body = (b'data: {"choices":[{"delta":{"content":"a"}}]}\n\n'
+            b'data: {"choices":[{"delta":{"content":"\\"content\\""}}]}\n\n'
+            b'data: {"choices":[],"usage":{"prompt_tokens":7,"completion_tokens":3}}\n\ndata: [DONE]\n\n')
+    for cut in range(1, len(body), 5):
+        u = SSEUsage()
+        u.feed(body[:cut])
+        u.feed(body[cut:])
+        assert (u.prompt, u.completion, u.seen) == (7, 3, True)
+    a = SSEUsage()
+    a.feed(b'event: message_start\ndata: {"type":"message_start","message":{"usage":{"input_tokens":5,'
+           b'"output_tokens":0}}}\n\nevent: message_delta\ndata: {"type":"message_delta","usage":'
+           b'{"output_tokens":4}}\n\n')
+    assert (a.prompt, a.completion) == (5, 4)
+
+    fleet = MockFleet()
+    orig = fleet.handler
+
+    def handler(req):
+        if req.url.path == "/v1/chat/completions" and json.loads(req.content).get("stream"):
+            return httpx.Response(200, content=body, headers={"content-type": "text/event-stream"})
+        return orig(req)
+    nodes = [NodeState("a", "http://a.node"), NodeState("b", "http://b.node")]
+    app = create_gateway(_cat(), nodes, transport=httpx.MockTransport(handler), poll_interval_s=3600,
+                         api_keys={"k1": "acct-1"})
+    with TestClient(app) as c:
+        c.post("/v1/chat/completions", json={"model": "m1", "stream": True}, headers={"authorization": "Bearer k1"})
+        u = c.get("/usage").json()["principals"]["acct-1"]
+        assert (u["prompt_tokens"], u["completion_tokens"]) == (7, 3)
+
+
+def test_prompt_prevalidation_against_advertised_context():
+    fleet = MockFleet()
+    with TestClient(_app(fleet)) as c:
+        c.app.state.router.observe("a", [{"id": "m1", "status": "loaded", "limit": {"context": 100, "output": 50}}],
+                                   {}, 1000)
+        c.app.state.router.observe("b", [{"id": "m2", "status": "loaded"}], {}, 1000)
+        n0 = len(fleet.calls)
+        r = c.post("/v1/chat/completions", json={"model": "m1", "messages": [{"role": "user", "content": "x" * 2000}]})
+        assert r.status_code == 400 and r.json()["error"]["code"] == "context_length_exceeded"
+        assert len(fleet.calls) == n0  # refused before dispatch
+        r = c.post("/v1/chat/completions", json={"model": "m1", "messages": [{"role": "user", "content": "hi"}]})
+        assert r.status_code == 200
+
+
+def test_budget_reserve_settle_and_rejection_codes():
+    from helexa_b200.gateway.budget import BudgetExceeded, BudgetLedger, Cap
+    t = [0.0]
+    led = BudgetLedger({"bal": Cap(100), "win": Cap(50, window_s=60)}, clock=lambda: t[0])
+    r1 = led.reserve("bal", 60)
+    with pytest.raises(BudgetExceeded) as e:   # outstanding reservations count against the cap
+        led.reserve("bal", 50)
+    assert e.value.code == "insufficient_quota" and e.value.retry_after == 0
+    led.settle(r1, 20)                          # the unused 40 come back
+    led.settle(r1, 999)                         # a reservation resolves once
+    assert led.snapshot("bal") == {"hard_cap": 100, "spent": 20, "reserved": 0, "window_s": 0}
+    led.release(led.reserve("bal", 80))
+    assert led.snapshot("bal")["reserved"] == 0
+    led.settle(led.reserve("win", 50), 50)
+    with pytest.raises(BudgetExceeded) as e:
+        led.reserve("win", 1)
+    assert e.value.code == "rate_limit_exceeded" and e.value.retry_after > 0
+    t[0] = 61.0                                 # the rolling window resets
+    assert led.reserve("win", 10) is not None
+    assert led.reserve("nobody", 10**9) is None  # uncapped principals are not reserved
+
+    fleet = MockFleet()
+    app = _app(fleet, api_keys={"k1": "acct-1"}, budgets={"acct-1": Cap(4200)})
+    with TestClient(app) as c:
+        h = {"authorization": "Bearer k1"}
+        # reservation = prompt estimate + max_tokens; the mock reports 2 completion tokens
+        assert c.post("/v1/chat/completions", json={"model": "m1", "max_tokens": 4000}, headers=h).status_code == 200
+        b = c.get("/usage").json()["principals"]["acct-1"]["budget"]
+        assert b["spent"] == 2 and b["reserved"] == 0
+        r = c.post("/v1/chat/completions", json={"model": "m1", "max_tokens": 5000}, headers=h)
+        assert r.status_code == 429 and r.json()["error"]["code"] == "insufficient_quota"
+
+
+def test_cli_gateway_config_and_status(tmp_path):
+    """`helexa serve` builds the gateway from a TOML config; `helexa status` prints the
+    fleet health and model placements the gateway reports."""
+    from helexa_b200.cli import _gateway_from_config, status_report
+    from helexa_b200.config.settings import load_settings
+    p = tmp_path / "cortex.toml"
+    p.write_text('[gateway]\nlisten = "127.0.0.1:31999"\npoll_interval_s = 3600\n'
+                 '[[neurons]]\nname = "a"\nurl = "http://a.node/"\n'
+                 '[[models]]\nmodel_id = "m1"\nsource = "preset:x"\naliases = ["fast"]\n'
+                 '[auth.keys]\n"k1" = "acct-1"\n[budgets."acct-1"]\nhard_cap = 10\n')
+    app = _gateway_from_config(load_settings(str(p), env={}))
+    assert app.state.router.nodes["a"].url == "http://a.node"
+    assert app.state.ledger.snapshot("acct-1")["hard_cap"] == 10
+    replies = {"http://gw/health": {"status": "ok", "nodes": {"a": {"healthy": True, "models": ["m1"]}}},
+               "http://gw/v1/models": {"data": [{"id": "m1", "loaded_on": ["a"], "limit": {"context": 4096}}]}}
+    out = status_report("http://gw/", get=replies.__getitem__)
+    assert "Fleet health" in out and "m1" in out and "a(loaded)" in out and "ctx=4096" in out

@@ -73,5 +73,5 @@ def test_noalloc_rejects_oversized_request():
     z = ctypes.c_void_p(0)
     # B*Hq*nsplit*D far beyond the fixed scratch: refused before any launch
     rc = f(z, 0, z, z, z, z, z, 16, z, z, z, 64, 64, 8, 256, 64, 1, 1e-6, 256, z)
-    assert rc != 0
+    assert rc == 1004  # HX_NOALLOC_E_SCRATCH: never a cudaError_t value
     assert b"scratch too small" in lib.hx_noalloc_error()
