@@ -162,6 +162,12 @@ def main() -> None:
     if world > 1:
         dist.all_reduce(stats, op=dist.ReduceOp.MAX)
     dec_ms, ttft_p50, ttft_sum = stats.tolist()
+    # a bounded device wait that ran out makes every later output invalid: report it and
+    # fail instead of printing a throughput of wrong tokens
+    dev_err = torch.tensor([model.device_error()], dtype=torch.int64, device=dev)
+    if world > 1:
+        dist.all_reduce(dev_err, op=dist.ReduceOp.MAX)
+    device_errors = int(dev_err.item())
     value = dec_tokens * args.steps / (dec_ms / 1e3)
     # ---- end to end through the public API (Generator.generate) --------------
     barrier()
@@ -198,8 +204,11 @@ def main() -> None:
                     "h2d_bytes_per_step": args.prompt * 4, "d2h_bytes_per_step": args.decode * 4 + 4},
             "gpu_launches": launches, "gpu_launches_scope": "this package's kernels per request (prefill + every decode step) x steps; PyTorch ops in prefill (RoPE, gate, embedding gather) not counted",
             "clocks": clocks,
+            "device_errors": device_errors,
         }
         print(json.dumps(line), flush=True)
+    if device_errors:
+        sys.exit(3)
     if world > 1:
         dist.destroy_process_group()
 

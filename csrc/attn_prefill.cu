@@ -28,7 +28,9 @@ __global__ void __launch_bounds__(NW * 32, 1) attn_prefill_kernel(const __nv_bfl
                                                                   const __nv_bfloat16* __restrict__ kc,
                                                                   const __nv_bfloat16* __restrict__ vc,
                                                                   long long ld_head, __nv_bfloat16* __restrict__ o,
-                                                                  int ldo_t, int T, int p0, int G, float scale_log2) {
+                                                                  int ldo_t, int T, int p0, int G, float scale_log2,
+                                                                  const __nv_bfloat16* __restrict__ gate, int ldg_t,
+                                                                  int ldg_h) {
   constexpr int LD = D + 8;       // padded row (bf16 elements): conflict-free ldmatrix
   constexpr int NT = D / 8;       // output n-tiles per warp
   constexpr int BM = NW * 16;     // query rows per CTA
@@ -175,13 +177,22 @@ __global__ void __launch_bounds__(NW * 32, 1) attn_prefill_kernel(const __nv_bfl
   // ---- normalise and store ---------------------------------------------------------
   const float inv0 = l[0] > 0.f ? 1.f / l[0] : 0.f, inv1 = l[1] > 0.f ? 1.f / l[1] : 0.f;
   const int ta = t0 + warp * 16 + g, tb = ta + 8;
+  // optional sigmoid output gate (Qwen3-Next gated attention): o = bf16(o) * sigmoid(gate)
+  auto gated = [&](int t, int d, float v) {
+    if (!gate) return v;
+    const float gv = __bfloat162float(gate[(long long)t * ldg_t + (long long)h * ldg_h + d]);
+    return __bfloat162float(__float2bfloat16(v)) / (1.f + __expf(-gv));
+  };
 #pragma unroll
   for (int n = 0; n < NT; ++n) {
-    const int col = h * D + n * 8 + 2 * tq;
+    const int d = n * 8 + 2 * tq;
+    const int col = h * D + d;
     if (ta < T)
-      *reinterpret_cast<uint32_t*>(&o[(long long)ta * ldo_t + col]) = pack_bf16x2(acc[n][0] * inv0, acc[n][1] * inv0);
+      *reinterpret_cast<uint32_t*>(&o[(long long)ta * ldo_t + col]) =
+          pack_bf16x2(gated(ta, d, acc[n][0] * inv0), gated(ta, d + 1, acc[n][1] * inv0));
     if (tb < T)
-      *reinterpret_cast<uint32_t*>(&o[(long long)tb * ldo_t + col]) = pack_bf16x2(acc[n][2] * inv1, acc[n][3] * inv1);
+      *reinterpret_cast<uint32_t*>(&o[(long long)tb * ldo_t + col]) =
+          pack_bf16x2(gated(tb, d, acc[n][2] * inv1), gated(tb, d + 1, acc[n][3] * inv1));
   }
 }
 
@@ -191,8 +202,10 @@ using namespace hx;
 
 // q: [T, Hq*D] (row stride >= Hq*D) bf16, already normed and rotated; kc/vc: the slot's
 // caches [Hkv, maxlen, D] with keys 0 .. p0+T-1 written; out: [T, Hq*D] bf16.
+// gate (optional): [T, *] bf16 view whose head h starts at column h * gate_head_stride
+// (the output gate columns of the fused q projection); out = attention * sigmoid(gate).
 void attn_prefill(torch::Tensor q, torch::Tensor kc, torch::Tensor vc, torch::Tensor out, int64_t Hq, int64_t p0,
-                  double scale) {
+                  double scale, c10::optional<torch::Tensor> gate, int64_t gate_head_stride) {
   TORCH_CHECK(q.is_cuda() && q.scalar_type() == at::kBFloat16 && q.dim() == 2 && q.stride(1) == 1, "q [T, Hq*D] bf16");
   TORCH_CHECK(kc.scalar_type() == at::kBFloat16 && kc.dim() == 3 && kc.is_contiguous() && vc.sizes() == kc.sizes() &&
                   vc.is_contiguous(),
@@ -203,6 +216,13 @@ void attn_prefill(torch::Tensor q, torch::Tensor kc, torch::Tensor vc, torch::Te
               "out [T, Hq*D] bf16");
   TORCH_CHECK(p0 >= 0 && p0 + T <= kc.size(1), "keys past the cache");
   TORCH_CHECK(q.stride(0) % 8 == 0 && out.stride(0) % 2 == 0, "row strides must keep 16-byte rows");
+  const __nv_bfloat16* gp = nullptr;
+  int ldg = 0;
+  if (gate) {
+    TORCH_CHECK(gate->scalar_type() == at::kBFloat16 && gate->stride(1) == 1 && gate->size(0) == T, "gate [T, *] bf16");
+    gp = reinterpret_cast<const __nv_bfloat16*>(gate->data_ptr());
+    ldg = gate->stride(0);
+  }
   if (T == 0) return;
   const float sl2 = (float)scale * 1.4426950408889634f;
   auto st = at::cuda::getCurrentCUDAStream();
@@ -219,7 +239,7 @@ void attn_prefill(torch::Tensor q, torch::Tensor kc, torch::Tensor vc, torch::Te
         reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), (int)q.stride(0),                                    \
         reinterpret_cast<const __nv_bfloat16*>(kc.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(vc.data_ptr()), \
         (long long)kc.stride(0), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), (int)out.stride(0), T, (int)p0,  \
-        (int)(Hq / Hkv), sl2);                                                                                     \
+        (int)(Hq / Hkv), sl2, gp, ldg, (int)gate_head_stride);                                                     \
   }
   if (D == 256) { if (nw == 8) HX_ATTN_PF(256, 8) else HX_ATTN_PF(256, 4) }
   else if (D == 128) { if (nw == 8) HX_ATTN_PF(128, 8) else HX_ATTN_PF(128, 4) }

@@ -22,7 +22,12 @@ void moe_down_ar(torch::Tensor Wd, torch::Tensor act, torch::Tensor ids, torch::
                  std::vector<int64_t> bases, int64_t rank, int64_t slot_elems, torch::Tensor epoch, torch::Tensor err,
                  double timeout_s);
 void attn_prefill(torch::Tensor q, torch::Tensor kc, torch::Tensor vc, torch::Tensor out, int64_t Hq, int64_t p0,
-                  double scale);
+                  double scale, c10::optional<torch::Tensor> gate, int64_t gate_head_stride);
+void add_rmsnorm(torch::Tensor x, c10::optional<torch::Tensor> o, torch::Tensor w, torch::Tensor h, double eps);
+void qk_rope_kv(torch::Tensor qkv, int64_t Hq, int64_t Hkv, int64_t D, int64_t qw, c10::optional<torch::Tensor> q_norm,
+                c10::optional<torch::Tensor> k_norm, torch::Tensor inv_freq, int64_t rot, torch::Tensor kc,
+                torch::Tensor vc, int64_t p0, torch::Tensor q_out, double eps);
+void conv_ring_update(torch::Tensor proj, torch::Tensor ring, int64_t p0);
 void gemv_experts_ep(torch::Tensor W, torch::Tensor x, torch::Tensor ids, torch::Tensor y, int64_t mode,
                      int64_t x_row_div, c10::optional<torch::Tensor> norm_w, double eps, int64_t e_base);
 void moe_down_ar_ep(torch::Tensor Wd, torch::Tensor act, torch::Tensor ids, torch::Tensor wts, torch::Tensor x,
@@ -57,6 +62,11 @@ void gemv_argmax(torch::Tensor W, torch::Tensor x, c10::optional<torch::Tensor> 
                  double eps, torch::Tensor best, torch::Tensor counter, torch::Tensor tok,
                  c10::optional<torch::Tensor> slots, c10::optional<torch::Tensor> pos,
                  c10::optional<torch::Tensor> out_tokens, c10::optional<torch::Tensor> step);
+void gemv_argmax_tp(torch::Tensor W, torch::Tensor x, c10::optional<torch::Tensor> logits, torch::Tensor norm_w,
+                    double eps, torch::Tensor best, torch::Tensor counter, torch::Tensor tok, torch::Tensor slots,
+                    torch::Tensor pos, torch::Tensor out_tokens, torch::Tensor step, int64_t v_off,
+                    std::vector<int64_t> bases, int64_t rank, int64_t slot_elems, torch::Tensor epoch,
+                    torch::Tensor err, double timeout_s);
 
 void gdn_prefill(torch::Tensor proj, torch::Tensor conv_w, torch::Tensor ring, torch::Tensor A_log,
                  torch::Tensor dt_bias, torch::Tensor norm_w, torch::Tensor state, torch::Tensor out, int64_t Hk,
@@ -86,7 +96,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_grouped_dev", &gemm_grouped_dev);
   m.def("gdn_decode", &gdn_decode);
   m.def("attn_decode", &attn_decode);
-  m.def("attn_prefill", &attn_prefill);
+  m.def("attn_prefill", &attn_prefill, py::arg("q"), py::arg("kc"), py::arg("vc"), py::arg("out"), py::arg("Hq"),
+        py::arg("p0"), py::arg("scale"), py::arg("gate") = py::none(), py::arg("gate_head_stride") = 0);
+  m.def("add_rmsnorm", &add_rmsnorm);
+  m.def("qk_rope_kv", &qk_rope_kv);
+  m.def("conv_ring_update", &conv_ring_update);
   m.def("embed", &embed);
   m.def("argmax_step", &argmax_step);
   m.def("ipc_alloc", &ipc_alloc);
@@ -102,5 +116,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gdn_prefill", &gdn_prefill);
   m.def("gemv_router", &gemv_router);
   m.def("gemv_argmax", &gemv_argmax);
+  m.def("gemv_argmax_tp", &gemv_argmax_tp);
   m.def("gemm_grouped", &gemm_grouped);
 }

@@ -55,6 +55,7 @@ struct GemvArgs {
   int* step;
   TPPush tp;                  // kResidAddTP: cross-rank reduction fused into the epilogue
   int e_base, e_count;        // expert mode under expert parallelism: this rank's experts (count 0: all)
+  int v_off;                  // arg-max: global index of row 0 (vocab-parallel lm_head slice)
 };
 
 // Order-preserving key of a float (larger float -> larger key), index tiebreak to the
@@ -256,18 +257,19 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
     for (int b = 0; b < B; ++b) acc[r][b] = warp_sum(acc[r][b]);
 
   if constexpr (MODE == kResidAddTP) {
-    // x += sum over ranks of W_r . inp_r: exchange this CTA's rows with the same CTA on
-    // every peer, then add the rank-ordered sum to the residual
+    // x += sum over ranks of W_r . inp_r: the warp exchanges its rows with the warps of
+    // the same rows on every peer, then adds the rank-ordered sum to the residual
     const unsigned e = tp_epoch(a.tp);
-    const bool pushes = active && lane == 0;
-    if (pushes) {
+    int idx[RPW * B];
+    float v[RPW * B];
 #pragma unroll
-      for (int b = 0; b < B; ++b)
+    for (int b = 0; b < B; ++b)
 #pragma unroll
-        for (int r = 0; r < RPW; ++r)
-          if (row0 + r < a.N) tp_push(a.tp, e, b * a.N + row0 + r, acc[r][b]);
-    }
-    if (tp_exchange(a.tp, e, blockIdx.x, pushes) && pushes) {
+      for (int r = 0; r < RPW; ++r) {
+        idx[b * RPW + r] = (active && row0 + r < a.N) ? b * a.N + row0 + r : -1;
+        v[b * RPW + r] = acc[r][b];
+      }
+    if (tp_warp_allreduce<RPW * B>(a.tp, e, idx, v) && active && lane == 0) {
 #pragma unroll
       for (int b = 0; b < B; ++b)
 #pragma unroll
@@ -275,7 +277,7 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
           const int n = row0 + r;
           if (n >= a.N) break;
           const long long o = (long long)b * a.ldy + n;
-          const float br = __bfloat162float(__float2bfloat16(tp_sum(a.tp, e, b * a.N + n)));
+          const float br = __bfloat162float(__float2bfloat16(v[b * RPW + r]));
           reinterpret_cast<__nv_bfloat16*>(a.y)[o] = __float2bfloat16(__bfloat162float(a.resid[o]) + br);
         }
     }
@@ -331,7 +333,7 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
       if (active && lane == 0) {
 #pragma unroll
         for (int r = 0; r < RPW; ++r)
-          if (row0 + r < a.N) k = max(k, argmax_key(acc[r][b], row0 + r));
+          if (row0 + r < a.N) k = max(k, argmax_key(acc[r][b], a.v_off + row0 + r));
       }
       if (lane == 0) wbest[warp][b] = k;
     }
@@ -349,9 +351,26 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
   if (!is_last) return;
   __threadfence();
   if constexpr (MODE == kArgmax) {
+    __shared__ unsigned long long kbest[B];
+    if (threadIdx.x < B) kbest[threadIdx.x] = atomicExch(&a.best[threadIdx.x], 0ull);
+    if (a.tp.ws > 1) {
+      // vocab-parallel lm_head: every rank holds a slice of the vocabulary; the maximum
+      // key over ranks (value, then lowest global index) is the token on every rank
+      __syncthreads();
+      const unsigned e = tp_epoch(a.tp);
+      if (warp == 0) {
+        unsigned long long keys[B];
+#pragma unroll
+        for (int b = 0; b < B; ++b) keys[b] = kbest[b];
+        tp_warp_max_u64(a.tp, e, keys, B);
+        if (lane < B) kbest[lane] = keys[lane];
+      }
+      tp_finish(a.tp, e, 1);
+    }
+    __syncthreads();
     if (threadIdx.x < B) {
       const int b = threadIdx.x;
-      const unsigned long long k = atomicExch(&a.best[b], 0ull);
+      const unsigned long long k = kbest[b];
       int t = 0x7fffffff - (int)(k & 0xffffffffu);
       if (k == 0) t = 0;
       a.tok[b] = t;
@@ -484,11 +503,10 @@ __global__ void __launch_bounds__(256) moe_down_kernel(const __nv_bfloat16* __re
   acc = warp_sum(acc);
   if constexpr (TP) {
     const unsigned e = tp_epoch(tp);
-    const int cta = blockIdx.y * gridDim.x + blockIdx.x;
-    const bool pushes = lane == 0 && h < H;
-    if (pushes) tp_push(tp, e, b * H + h, acc);
-    if (tp_exchange(tp, e, cta, pushes) && pushes) {
-      const float br = __bfloat162float(__float2bfloat16(tp_sum(tp, e, b * H + h)));
+    int idx[1] = {h < H ? b * H + h : -1};
+    float v[1] = {acc};
+    if (tp_warp_allreduce<1>(tp, e, idx, v) && h < H && lane == 0) {
+      const float br = __bfloat162float(__float2bfloat16(v[0]));
       x[(long long)b * H + h] = __float2bfloat16(__bfloat162float(x[(long long)b * H + h]) + br);
     }
     tp_finish(tp, e, gridDim.x * gridDim.y);
@@ -570,11 +588,41 @@ void gemv_router(torch::Tensor W, torch::Tensor x, torch::Tensor logits, torch::
   launch_mode<kRouter>(a, B, at::cuda::getCurrentCUDAStream());
 }
 
+static TPPush make_tp(const std::vector<int64_t>& bases, int64_t rank, int64_t slot_elems, torch::Tensor epoch,
+                      torch::Tensor err, double timeout_s);
+
+static void gemv_argmax_impl(torch::Tensor W, torch::Tensor x, c10::optional<torch::Tensor> logits,
+                             torch::Tensor norm_w, double eps, torch::Tensor best, torch::Tensor counter,
+                             torch::Tensor tok, c10::optional<torch::Tensor> slots, c10::optional<torch::Tensor> pos,
+                             c10::optional<torch::Tensor> out_tokens, c10::optional<torch::Tensor> step,
+                             const TPPush& tp, int v_off);
+
 // lm_head GEMV with fused arg-max and decode-step bookkeeping.
 void gemv_argmax(torch::Tensor W, torch::Tensor x, c10::optional<torch::Tensor> logits, torch::Tensor norm_w,
                  double eps, torch::Tensor best, torch::Tensor counter, torch::Tensor tok,
                  c10::optional<torch::Tensor> slots, c10::optional<torch::Tensor> pos,
                  c10::optional<torch::Tensor> out_tokens, c10::optional<torch::Tensor> step) {
+  gemv_argmax_impl(W, x, logits, norm_w, eps, best, counter, tok, slots, pos, out_tokens, step, TPPush{}, 0);
+}
+
+// Vocab-parallel lm_head: W holds rows v_off .. v_off + W.size(0) - 1 of the vocabulary;
+// the per-rank arg-max keys are exchanged over the fused-reduction region and every
+// rank advances with the same global token.
+void gemv_argmax_tp(torch::Tensor W, torch::Tensor x, c10::optional<torch::Tensor> logits, torch::Tensor norm_w,
+                    double eps, torch::Tensor best, torch::Tensor counter, torch::Tensor tok, torch::Tensor slots,
+                    torch::Tensor pos, torch::Tensor out_tokens, torch::Tensor step, int64_t v_off,
+                    std::vector<int64_t> bases, int64_t rank, int64_t slot_elems, torch::Tensor epoch,
+                    torch::Tensor err, double timeout_s) {
+  TORCH_CHECK(x.size(0) * 4 <= slot_elems, "receive slot too small");
+  gemv_argmax_impl(W, x, logits, norm_w, eps, best, counter, tok, slots, pos, out_tokens, step,
+                   make_tp(bases, rank, slot_elems, epoch, err, timeout_s), (int)v_off);
+}
+
+static void gemv_argmax_impl(torch::Tensor W, torch::Tensor x, c10::optional<torch::Tensor> logits,
+                             torch::Tensor norm_w, double eps, torch::Tensor best, torch::Tensor counter,
+                             torch::Tensor tok, c10::optional<torch::Tensor> slots, c10::optional<torch::Tensor> pos,
+                             c10::optional<torch::Tensor> out_tokens, c10::optional<torch::Tensor> step,
+                             const TPPush& tp, int v_off) {
   check_w(W);
   const int B = x.size(0);
   TORCH_CHECK(best.scalar_type() == at::kLong && best.numel() >= B, "best: int64 [B] zero-initialised");
@@ -593,6 +641,8 @@ void gemv_argmax(torch::Tensor W, torch::Tensor x, c10::optional<torch::Tensor> 
   a.step = step ? step->data_ptr<int>() : nullptr;
   TORCH_CHECK(!a.pos || a.slots, "pos needs slots");
   TORCH_CHECK(!a.out_tokens || a.step, "out_tokens needs step");
+  a.tp = tp;
+  a.v_off = v_off;
   launch_mode<kArgmax>(a, B, at::cuda::getCurrentCUDAStream());
 }
 
@@ -672,14 +722,15 @@ static TPPush make_tp(const std::vector<int64_t>& bases, int64_t rank, int64_t s
                       torch::Tensor err, double timeout_s) {
   TORCH_CHECK(bases.size() >= 1 && bases.size() <= (size_t)kTPMaxRanks, "1..8 ranks");
   TORCH_CHECK(rank >= 0 && rank < (int64_t)bases.size(), "rank out of range");
-  TORCH_CHECK(epoch.is_cuda() && epoch.scalar_type() == at::kInt && epoch.numel() >= 2, "epoch: int32[2] on device");
+  TORCH_CHECK(epoch.is_cuda() && epoch.scalar_type() == at::kInt && epoch.numel() >= 2,
+              "epoch: int32[2] on device (last completed epoch, completion count)");
   TORCH_CHECK(err.is_cuda() && err.scalar_type() == at::kInt, "err: int32 on device");
   TPPush t{};
   for (size_t r = 0; r < bases.size(); ++r) t.base[r] = reinterpret_cast<char*>(bases[r]);
   t.rank = (int)rank;
   t.ws = (int)bases.size();
   t.slot_elems = (int)slot_elems;
-  t.epoch = reinterpret_cast<unsigned*>(epoch.data_ptr());
+  t.ctr = reinterpret_cast<unsigned*>(epoch.data_ptr());
   t.err = err.data_ptr<int>();
   t.timeout_ns = (unsigned long long)(timeout_s * 1e9);
   return t;

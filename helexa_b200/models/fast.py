@@ -97,6 +97,16 @@ QUANT_SCHEMES = {
 }
 
 
+class DeviceError(RuntimeError):
+    """A kernel's bounded wait ran out (code 1000+peer / 2000+peer: a tensor-parallel
+    peer never arrived; other codes: a GEMM pipeline wait)."""
+
+    def __init__(self, code: int):
+        what = f"tensor-parallel peer {code % 1000} never arrived" if code >= 1000 else "GEMM pipeline wait ran out"
+        super().__init__(f"device error {code}: {what}")
+        self.code = code
+
+
 class QWeight:
     """One linear weight held as GGUF block rows on the device (uint8 [N, row_bytes]):
     decode reads it through the fused-dequant GEMV, prefill dequantizes it to bf16
@@ -137,6 +147,18 @@ class FastModel:
         self.max_slots, self.max_len = max_slots, max_len
         self.comm = comm  # parallel.TPComm or None (single rank)
         self.C = ops.C if device.type == "cuda" else None
+        # vocab-parallel lm_head under the fused TP path: each rank streams V / ws rows per
+        # decode step and the arg-max keys are exchanged (instead of every rank streaming
+        # the whole 151936 x hidden matrix)
+        V = cfg.vocab_size
+        self.vocab_parallel = bool(comm is not None and dims.ws > 1 and getattr(comm, "fused", False)
+                                   and V % dims.ws == 0)
+        self.v_off = 0
+        if self.vocab_parallel:
+            vl = V // dims.ws
+            self.v_off = dims.rank * vl
+            self.lm_head = lm_head[self.v_off:self.v_off + vl].contiguous()
+        self.v_local = self.lm_head.shape[0]
         self.inv_freq = cfg.rope_inv_freq().to(device)
         self.has_shared = cfg.shared_expert_intermediate_size > 0
         sm = torch.cuda.get_device_properties(device).multi_processor_count if device.type == "cuda" else 1
@@ -262,7 +284,7 @@ class FastModel:
             act_moe=z(B * J, d.moe_inter) if cfg.num_experts else None,
             act_mlp=z(B, d.inter) if any_mlp else None,
             partial=z(B, d.H),
-            logits=z(B, cfg.vocab_size, dt=f32), out_tokens=z(B, out_cap, dt=i32), step=z(B, dt=i32),
+            logits=z(B, self.v_local, dt=f32), out_tokens=z(B, out_cap, dt=i32), step=z(B, dt=i32),
             best=z(B, dt=torch.int64), counter=z(1, dt=i32), err=z(1, dt=i32))
         self._bufs[B] = nb
         return nb
@@ -322,8 +344,13 @@ class FastModel:
         self.C.embed(self.embed_w, nb.tok, nb.x)
         for i in range(self.cfg.num_hidden_layers):
             self._decode_layer(i, nb)
-        self.C.gemv_argmax(self.lm_head, nb.x, nb.logits, self.final_norm, self.cfg.rms_norm_eps, nb.best,
-                           nb.counter, nb.tok, nb.slots, self.pos, nb.out_tokens, nb.step)
+        if self.vocab_parallel:
+            self.C.gemv_argmax_tp(self.lm_head, nb.x, nb.logits, self.final_norm, self.cfg.rms_norm_eps, nb.best,
+                                  nb.counter, nb.tok, nb.slots, self.pos, nb.out_tokens, nb.step, self.v_off,
+                                  *self.comm.fused_args())
+        else:
+            self.C.gemv_argmax(self.lm_head, nb.x, nb.logits, self.final_norm, self.cfg.rms_norm_eps, nb.best,
+                               nb.counter, nb.tok, nb.slots, self.pos, nb.out_tokens, nb.step)
 
     def launches_per_step(self) -> int:
         cfg = self.cfg
@@ -452,10 +479,24 @@ class FastModel:
             self._gerr = torch.zeros(1, dtype=torch.int32, device=self.device)
         return self._gerr
 
+    def device_error(self) -> int:
+        """First nonzero device error word (GEMM bounded waits, TP exchange), else 0.
+        Reading it synchronizes the device."""
+        words = [self._gemm_err()]
+        if self.comm is not None and getattr(self.comm, "err", None) is not None:
+            words.append(self.comm.err)
+        for v in torch.cat([w.view(-1)[:1] for w in words]).tolist():
+            if v:
+                return int(v)
+        return 0
+
     def check_errors(self):
-        """Raise if a device-side bounded wait gave up since the model was built."""
-        if hasattr(self, "_gerr") and int(self._gerr.item()):
-            raise RuntimeError(f"GEMM kernel reported error code {int(self._gerr.item())}")
+        """Raise DeviceError if a device-side bounded wait gave up since the model was
+        built: the kernels return instead of hanging, so their outputs after that point
+        are not valid and must not be served."""
+        code = self.device_error()
+        if code:
+            raise DeviceError(code)
 
     def _reduce(self, t: torch.Tensor) -> torch.Tensor:
         if self.comm is not None and self.dims.ws > 1:
@@ -633,4 +674,10 @@ class FastModel:
             tm.mark("head")
         last = self._rms(x[-1:], self.final_norm)
         self.pos[slot] = p0 + T
-        return self._linear(last, self.lm_head, 2)[0]
+        return self.full_logits(self._linear(last, self.lm_head, 2))[0]
+
+    def full_logits(self, local: torch.Tensor) -> torch.Tensor:
+        """[n, V_local] logits of this rank's vocabulary slice -> [n, V] on every rank."""
+        if not self.vocab_parallel:
+            return local
+        return self.comm.all_gather_rows(local)

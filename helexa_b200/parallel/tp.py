@@ -30,7 +30,6 @@ import torch.distributed as dist
 from .. import ops
 
 _FLAG_BYTES = 4096
-_FUSED_FLAG_BYTES = 4096 * 8 * 4  # kTPMaxCtas x kTPMaxRanks u32 (csrc/tp_fused.cuh)
 
 
 class TPError(RuntimeError):
@@ -79,11 +78,12 @@ class TPComm:
         dist.barrier(group=self.group)
 
     def _init_fused(self, max_elems: int):
-        """Receive region of the fused path: per-CTA flags, then f32 slots
-        [parity][source rank][max_elems], exported to and opened by every peer."""
+        """Receive region of the fused path: 8-byte (epoch, value) words
+        [parity][source rank][max_elems], exported to and opened by every peer
+        (csrc/tp_fused.cuh)."""
         C = ops.C
         self.slot_elems = max_elems
-        region, handle = C.ipc_alloc(_FUSED_FLAG_BYTES + 2 * self.ws * max_elems * 4, self.device.index)
+        region, handle = C.ipc_alloc(2 * self.ws * max_elems * 8, self.device.index)
         self._fused_region = region
         handles: list = [None] * self.ws
         dist.all_gather_object(handles, bytes(handle.numpy().tobytes()), group=self.group)
@@ -110,13 +110,22 @@ class TPComm:
                 ops.C.ipc_close(p)
             self._opened = []
 
+    def error_code(self) -> int:
+        """The device error word (0 = healthy); reading it synchronizes the device."""
+        return int(self.err.item()) if self.mode in ("p2p", "p2p1") else 0
+
     def check(self):
         """Raise TPError if a device-side wait timed out since the last check."""
-        if self.mode in ("p2p", "p2p1"):
-            e = int(self.err.item())
-            if e:
-                peer = e - 2000 if e >= 2000 else e - 1000
-                raise TPError(f"rank {self.rank}: peer {peer} did not arrive within {self.timeout_s}s")
+        e = self.error_code()
+        if e:
+            peer = e - 2000 if e >= 2000 else e - 1000
+            raise TPError(f"rank {self.rank}: peer {peer} did not arrive within {self.timeout_s}s (code {e})")
+
+    def all_gather_rows(self, t: torch.Tensor) -> torch.Tensor:
+        """Concatenate every rank's `t` along dim -1 (vocab-parallel logits)."""
+        parts = [torch.empty_like(t) for _ in range(self.ws)]
+        dist.all_gather(parts, t.contiguous(), group=self.group)
+        return torch.cat(parts, -1)
 
     # ---- reductions -------------------------------------------------------
     def all_reduce_(self, t: torch.Tensor) -> torch.Tensor:

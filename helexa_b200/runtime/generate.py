@@ -73,6 +73,7 @@ class Generator:
         finish = "length"
         eos = set(eos_ids)
         if not ignore_eos and first in eos:
+            m.check_errors()
             return GenerateResult(out, prompt.numel(), ttft, 0.0, "stop")
         produced = 0
         t1 = time.perf_counter()
@@ -98,6 +99,7 @@ class Generator:
         ev[2].record(stream)
         ev[2].synchronize()
         decode_s = time.perf_counter() - t1
+        m.check_errors()  # tokens produced after a timed-out wait are not valid
         # The slot's state has advanced over the whole last graph chunk, including any
         # tokens discarded after a stop; callers that continue a sequence restore a
         # prefix snapshot instead of reusing this state.

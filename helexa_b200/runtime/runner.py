@@ -72,6 +72,7 @@ class FastRunner:
         for s in range(0, len(tokens), self.prefill_chunk):
             logits = self.m.prefill(slot, toks[s:s + self.prefill_chunk], p0 + s)
         self.host_pos[slot] = p0 + len(tokens)
+        self.m.check_errors()  # a timed-out wait makes the outputs invalid: poison, don't serve
         return logits
 
     def decode(self, slots: list[int], tokens: list[int], steps: int) -> list[list[int]]:
@@ -89,6 +90,7 @@ class FastRunner:
         m.pos[self.pad_slot] = 0
         m.replay(nb)
         out = nb.out_tokens[:len(slots), :steps].cpu().tolist()
+        m.check_errors()
         for s in slots:
             self.host_pos[s] += steps
         return out
@@ -105,7 +107,9 @@ class FastRunner:
         m.decode_step_launch(nb)
         for s in slots:
             self.host_pos[s] += 1
-        return nb.logits[:len(slots)].float().cpu()
+        lg = m.full_logits(nb.logits[:len(slots)].float()).cpu()
+        m.check_errors()
+        return lg
 
     def snapshot(self, slot: int, length: int) -> Snapshot:
         m = self.m
