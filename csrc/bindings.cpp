@@ -28,6 +28,9 @@ void qk_rope_kv(torch::Tensor qkv, int64_t Hq, int64_t Hkv, int64_t D, int64_t q
                 c10::optional<torch::Tensor> k_norm, torch::Tensor inv_freq, int64_t rot, torch::Tensor kc,
                 torch::Tensor vc, int64_t p0, torch::Tensor q_out, double eps);
 void conv_ring_update(torch::Tensor proj, torch::Tensor ring, int64_t p0);
+void rs_norm_ag(std::vector<int64_t> bases, int64_t rank, int64_t stage_off, int64_t h_off, torch::Tensor x,
+                torch::Tensor w, double eps, torch::Tensor ctr, torch::Tensor err, double timeout_s, int64_t ctas);
+int64_t rs_norm_ag_flag_bytes();
 void gemv_experts_ep(torch::Tensor W, torch::Tensor x, torch::Tensor ids, torch::Tensor y, int64_t mode,
                      int64_t x_row_div, c10::optional<torch::Tensor> norm_w, double eps, int64_t e_base);
 void moe_down_ar_ep(torch::Tensor Wd, torch::Tensor act, torch::Tensor ids, torch::Tensor wts, torch::Tensor x,
@@ -101,6 +104,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("add_rmsnorm", &add_rmsnorm);
   m.def("qk_rope_kv", &qk_rope_kv);
   m.def("conv_ring_update", &conv_ring_update);
+  m.def("rs_norm_ag", &rs_norm_ag);
+  m.def("rs_norm_ag_flag_bytes", &rs_norm_ag_flag_bytes);
   m.def("embed", &embed);
   m.def("argmax_step", &argmax_step);
   m.def("ipc_alloc", &ipc_alloc);

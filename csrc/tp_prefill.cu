@@ -1,0 +1,185 @@
+// Prefill tensor-parallel reduction fused with the residual add and the next RMSNorm:
+//
+//   reduce-scatter  rank r owns the token rows [r*T/ws, (r+1)*T/ws); for each owned
+//                   row the kernel loads the row-parallel partial of every rank
+//                   straight out of that rank's staging buffer (plain 16-byte P2P loads
+//                   over NVLink), sums them in rank order 0..ws-1 (bit-identical on
+//                   every rank), rounds to bf16 and adds the residual row;
+//   RMSNorm         h = RMSNorm(x) * w of the updated row (the next layer's input norm,
+//                   or the final norm after the last layer);
+//   all-gather      the normalised row is stored into every rank's `h` buffer (plain
+//                   16-byte P2P stores), where the next GEMM's TMA reads it locally.
+//
+// This replaces the reference's ncclAllReduce of the row-parallel output followed by a
+// separate residual add and norm (tp/tp_linear.rs:285-293, tp/tp_qwen3_5.rs:1268-1271).
+// The residual stream x stays row-sharded: a rank keeps only its owned rows of x
+// current, which is all the next fused step reads. Bytes over NVLink per rank are those
+// of one all-reduce ((ws-1)/ws of the activation in, the same out); the norm, the add
+// and two launches are gone.
+//
+// Synchronisation, per CTA index c (every rank launches the same grid, small enough to
+// be co-resident): after griddepcontrol.wait each CTA release-stores this call's epoch
+// into flag1[c][me] of every rank and waits for flag1[c][*] (every rank's row-parallel
+// GEMM, which precedes this kernel in its stream, has finished: its staging buffer is
+// complete). After its rows are stored, each CTA fences at system scope and release-
+// stores flag2[c][me] everywhere, then waits for flag2[c][*]: when every CTA of a rank
+// returns, every rank has both finished reading that rank's staging buffer (so the
+// next GEMM may overwrite it) and delivered all of its h rows. Dependents are launched
+// only at the very end, so a PDL-launched successor never takes the slots this grid's
+// CTAs need. Epochs are per call (ctr[0], published by the last CTA). Every wait is
+// bounded: on expiry the kernel records 3000 + peer in `err` and returns.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+
+#include "common.cuh"
+
+namespace hx {
+
+constexpr int kPFMaxRanks = 8;
+constexpr int kPFMaxCtas = 1024;
+constexpr size_t kPFFlagBytes = 2ull * kPFMaxCtas * kPFMaxRanks * sizeof(unsigned);
+
+struct TPPrefill {
+  char* base[kPFMaxRanks];  // each rank's region: [flags1][flags2][stage T_max x H][h T_max x H]
+  int rank, ws;
+  long long stage_off, h_off;  // byte offsets of the staging and h buffers in a region
+  unsigned* ctr;             // local [2]: last completed epoch, CTA completion count
+  int* err;
+  unsigned long long timeout_ns;
+};
+
+HX_DEVICE unsigned* pf_flag(const TPPrefill& p, int dst, int which, int cta, int src) {
+  return reinterpret_cast<unsigned*>(p.base[dst]) + ((size_t)which * kPFMaxCtas + cta) * kPFMaxRanks + src;
+}
+
+HX_DEVICE void pf_st_release(unsigned* f, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(v) : "memory");
+}
+HX_DEVICE unsigned pf_ld_acquire(const unsigned* f) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+  return v;
+}
+
+// Threads 0..ws-1 signal every rank and wait for every rank; false if a wait ran out.
+HX_DEVICE bool pf_barrier(const TPPrefill& p, int which, unsigned e) {
+  __shared__ int bad;
+  if (threadIdx.x == 0) bad = 0;
+  __syncthreads();
+  const int r = threadIdx.x;
+  if (r < p.ws) {
+    __threadfence_system();
+    pf_st_release(pf_flag(p, r, which, blockIdx.x, p.rank), e);
+    const unsigned* mine = pf_flag(p, p.rank, which, blockIdx.x, r);
+    const unsigned long long t0 = globaltimer_ns();
+    while ((int)(pf_ld_acquire(mine) - e) < 0) {
+      if (*((volatile int*)p.err) != 0 || globaltimer_ns() - t0 > p.timeout_ns) {
+        atomicCAS(p.err, 0, 3000 + r);
+        bad = 1;
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  return !bad;
+}
+
+template <int VPT>
+__global__ void __launch_bounds__(256) rs_norm_ag_kernel(TPPrefill p, __nv_bfloat16* __restrict__ x,
+                                                        const float* __restrict__ w, int T, int H, float eps) {
+  __shared__ float red[8];
+  pdl_wait_prior();
+  const unsigned e = *((volatile unsigned*)p.ctr) + 1;
+  const bool healthy = *((volatile int*)p.err) == 0;
+  if (healthy && pf_barrier(p, 0, e)) {
+    const int per = (T + p.ws - 1) / p.ws;
+    const int r0 = p.rank * per, r1 = min(T, r0 + per);
+    const int nv = H / 8;
+    for (int t = r0 + blockIdx.x; t < r1; t += gridDim.x) {
+      float f[VPT][8];
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) {
+        const int v = threadIdx.x + 256 * i;
+        if (v < nv) {
+          float s[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+          for (int src = 0; src < p.ws; ++src) {
+            const bf16x8* part =
+                reinterpret_cast<const bf16x8*>(p.base[src] + p.stage_off) + (long long)t * nv + v;
+            float q[8];
+            unpack8(*part, q);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) s[j] += q[j];
+          }
+          bf16x8* xp = reinterpret_cast<bf16x8*>(x + (long long)t * H) + v;
+          float xv[8];
+          unpack8(*xp, xv);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) xv[j] += __bfloat162float(__float2bfloat16(s[j]));
+          const bf16x8 nx = pack8(xv);
+          *xp = nx;
+          unpack8(nx, f[i]);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) ss += f[i][j] * f[i][j];
+        }
+      }
+      ss = block_sum(ss, red);
+      const float inv = rsqrtf(ss / H + eps);
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) {
+        const int v = threadIdx.x + 256 * i;
+        if (v < nv) {
+          float g[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) g[j] = f[i][j] * inv * w[v * 8 + j];
+          const bf16x8 hv = pack8(g);
+          for (int dst = 0; dst < p.ws; ++dst)
+            reinterpret_cast<bf16x8*>(p.base[dst] + p.h_off)[(long long)t * nv + v] = hv;
+        }
+      }
+    }
+    __threadfence_system();  // this thread's h stores reach every rank before the signal
+    pf_barrier(p, 1, e);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && atomicAdd(p.ctr + 1, 1u) + 1 == gridDim.x) {
+    p.ctr[1] = 0;
+    p.ctr[0] = e;
+  }
+  pdl_launch_dependents();
+}
+
+}  // namespace hx
+
+using namespace hx;
+
+// Regions: every rank's [flags][stage][h] base pointers (this rank's own at `rank`);
+// the staging buffer holds this rank's row-parallel partial [T, H] bf16; x [T, H] bf16
+// (owned rows updated); w f32 [H]; h rows land in every rank's h buffer.
+void rs_norm_ag(std::vector<int64_t> bases, int64_t rank, int64_t stage_off, int64_t h_off, torch::Tensor x,
+                torch::Tensor w, double eps, torch::Tensor ctr, torch::Tensor err, double timeout_s, int64_t ctas) {
+  const int ws = bases.size();
+  TORCH_CHECK(ws >= 1 && ws <= kPFMaxRanks && rank >= 0 && rank < ws, "1..8 ranks");
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.is_contiguous() && x.dim() == 2, "x [T,H] bf16");
+  const int T = x.size(0), H = x.size(1);
+  TORCH_CHECK(H % 8 == 0 && H <= 256 * 8 * 4, "hidden must be a multiple of 8 and <= 8192");
+  TORCH_CHECK(w.scalar_type() == at::kFloat && w.numel() == H, "w f32 [H]");
+  TORCH_CHECK(stage_off % 16 == 0 && h_off % 16 == 0 && stage_off >= (int64_t)kPFFlagBytes, "region layout");
+  TORCH_CHECK(ctr.scalar_type() == at::kInt && ctr.numel() >= 2 && err.scalar_type() == at::kInt, "ctr / err");
+  TORCH_CHECK(ctas >= 1 && ctas <= kPFMaxCtas, "ctas in [1, 1024]");
+  TPPrefill p{};
+  for (int r = 0; r < ws; ++r) p.base[r] = reinterpret_cast<char*>(bases[r]);
+  p.rank = rank; p.ws = ws; p.stage_off = stage_off; p.h_off = h_off;
+  p.ctr = reinterpret_cast<unsigned*>(ctr.data_ptr());
+  p.err = err.data_ptr<int>();
+  p.timeout_ns = (unsigned long long)(timeout_s * 1e9);
+  auto st = at::cuda::getCurrentCUDAStream();
+  auto xp = reinterpret_cast<__nv_bfloat16*>(x.data_ptr());
+  const int vpt = (H / 8 + 255) / 256;
+  const dim3 grid((unsigned)ctas);
+  if (vpt == 1) HX_CUDA_CHECK(hx_launch_pdl(rs_norm_ag_kernel<1>, grid, dim3(256), 0, st, p, xp, w.data_ptr<float>(), T, H, (float)eps));
+  else if (vpt == 2) HX_CUDA_CHECK(hx_launch_pdl(rs_norm_ag_kernel<2>, grid, dim3(256), 0, st, p, xp, w.data_ptr<float>(), T, H, (float)eps));
+  else HX_CUDA_CHECK(hx_launch_pdl(rs_norm_ag_kernel<4>, grid, dim3(256), 0, st, p, xp, w.data_ptr<float>(), T, H, (float)eps));
+}
+
+int64_t rs_norm_ag_flag_bytes() { return (int64_t)kPFFlagBytes; }

@@ -397,13 +397,15 @@ class FastModel:
             self.C.gemv(W, x, y, mode, resid, norm, eps)
 
     def prefill_launches(self) -> int:
-        """Kernels of this package one prefill launches (PyTorch ops such as RoPE, the
-        output gate and the embedding gather are not counted)."""
+        """Kernels of this package one prefill chunk launches (the MoE combine's output
+        memset and the vocab-parallel logits gather are library calls, not counted)."""
         cfg = self.cfg
-        n = 1  # lm_head GEMM of the last token
+        n = 3  # embedding, first norm, lm_head GEMM of the last token
         for i in range(cfg.num_hidden_layers):
-            n += 5 + 2 if cfg.is_linear(i) else 3          # in_proj, prep, chunk, scan, onorm, out | qkv, attn, o
+            # in_proj, prep, chunk, scan, onorm, out, conv ring | qkv, q/k-norm+rope+KV, attn, o
+            n += 5 + 3 if cfg.is_linear(i) else 4
             n += 7 if cfg.layer_uses_moe(i) else 2          # router, topk, plan, place, 2 grouped, combine | 2 GEMMs
+            n += 2                                          # two fused (reduce +) residual + norm kernels
         return n
 
     def capture(self, B: int, steps: int = 1) -> DecodeBuffers:
@@ -457,22 +459,33 @@ class FastModel:
         xf = x.float()
         return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.cfg.rms_norm_eps) * w).to(torch.bfloat16)
 
-    def _linear(self, x: torch.Tensor, W: torch.Tensor, epi: int = 0) -> torch.Tensor:
-        """x [T, K] @ W[N, K]^T on the tcgen05 GEMM (epi 1: SwiGLU on interleaved rows)."""
+    def _linear(self, x: torch.Tensor, W: torch.Tensor, epi: int = 0, out: torch.Tensor | None = None) -> torch.Tensor:
+        """x [T, K] @ W[N, K]^T on the tcgen05 GEMM (epi 1: SwiGLU on interleaved rows;
+        epi 2: f32 output). `out`: a caller-provided contiguous [T, N] destination."""
         x = x.contiguous()
         if self.C is None:  # CPU layout tests only
             y = x @ W.t()
             if epi == 1:
                 y = (torch.nn.functional.silu(y[:, 0::2].float()).to(torch.bfloat16).float()
                      * y[:, 1::2].float()).to(torch.bfloat16)
+            if out is not None:
+                out.copy_(y)
+                return out
             return y
         if isinstance(W, QWeight):
             W = W.dequant(self.C)
         N = W.shape[0] // 2 if epi == 1 else W.shape[0]
+        if out is not None and N % 8 == 0:
+            self.C.gemm(x, W, out, epi, self._gemm_err())
+            return out
         Np = (N + 7) // 8 * 8  # keep output rows 16-byte aligned for the vector epilogue
-        out = torch.empty(x.shape[0], Np, dtype=torch.float32 if epi == 2 else torch.bfloat16, device=x.device)
-        self.C.gemm(x, W, out, epi, self._gemm_err())
-        return out if Np == N else out[:, :N]
+        y = torch.empty(x.shape[0], Np, dtype=torch.float32 if epi == 2 else torch.bfloat16, device=x.device)
+        self.C.gemm(x, W, y, epi, self._gemm_err())
+        y = y if Np == N else y[:, :N]
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
 
     def _gemm_err(self) -> torch.Tensor:
         if not hasattr(self, "_gerr"):
@@ -498,12 +511,52 @@ class FastModel:
         if code:
             raise DeviceError(code)
 
-    def _reduce(self, t: torch.Tensor) -> torch.Tensor:
-        if self.comm is not None and self.dims.ws > 1:
-            self.comm.all_reduce_(t)
-        return t
+    # ------------------------------------------------------------------
+    # prefill plumbing: residual + norm, reductions, buffers
+    # ------------------------------------------------------------------
+    def _tp(self) -> bool:
+        return self.comm is not None and self.dims.ws > 1
 
-    def _gdn_prefill(self, i: int, h: torch.Tensor, slot: int, p0: int) -> torch.Tensor:
+    def _fused_prefill_tp(self) -> bool:
+        return self._tp() and self.C is not None and getattr(self.comm, "fused", False)
+
+    def _add_norm(self, x: torch.Tensor, o: torch.Tensor | None, w: torch.Tensor, h: torch.Tensor):
+        """x += o (o already summed over ranks, or None), h = RMSNorm(x) * w."""
+        if self.C is None:
+            if o is not None:
+                x.copy_(x + o)
+            h.copy_(self._rms(x, w))
+            return
+        self.C.add_rmsnorm(x, o, w, h, self.cfg.rms_norm_eps)
+
+    def _reduce_add_norm(self, x: torch.Tensor, o: torch.Tensor, w: torch.Tensor, h: torch.Tensor):
+        """x += sum over ranks of the row-parallel partial o; h = RMSNorm(x) * w.
+
+        Fused TP (p2p): o lives in this rank's exported staging buffer and one kernel
+        reduce-scatters it, adds the residual, normalises and all-gathers h over peer
+        memory. Other modes: all-reduce (NCCL or the one-shot kernel), then the fused
+        add + norm kernel."""
+        if self._fused_prefill_tp():
+            self.comm.rs_norm_ag(x, w, self.cfg.rms_norm_eps)
+            return
+        if self._tp():
+            self.comm.all_reduce_(o)
+        self._add_norm(x, o, w, h)
+
+    def _prefill_bufs(self, T: int):
+        """(row-parallel output destination or None, h) for a chunk of T tokens."""
+        H = self.cfg.hidden_size
+        if self._fused_prefill_tp():
+            stage, h = self.comm.prefill_region(self.prefill_cap, H)
+            return stage[:T * H].view(T, H), h[:T * H].view(T, H)
+        return None, torch.empty(T, H, dtype=torch.bfloat16, device=self.device)
+
+    @property
+    def prefill_cap(self) -> int:
+        """Largest prefill chunk (tokens) one pass handles; longer prompts are chunked."""
+        return min(8192, self.max_len)
+
+    def _gdn_prefill(self, i: int, h: torch.Tensor, slot: int, p0: int, out=None) -> torch.Tensor:
         from .reference import causal_conv1d, delta_rule_chunked, delta_rule_recurrent, gdn_gating, l2norm
         d, lw, cfg = self.dims, self.layers[i], self.cfg
         T = h.shape[0]
@@ -514,11 +567,9 @@ class FastModel:
             o = torch.empty(T, vd, dtype=torch.bfloat16, device=h.device)
             self.C.gdn_prefill(proj, lw["conv_w"], ring, lw["A_log"], lw["dt_bias"], lw["gnorm"], self.rec[i][slot],
                                o, d.hk, d.hv, d.dk, p0, cfg.rms_norm_eps)
-            # advance the conv ring to the last K inputs (slot = position % K)
-            lo = max(p0, p0 + T - K)
-            idx = torch.arange(lo, p0 + T, device=h.device)
-            ring[:, idx % K] = proj[idx - p0, :2 * kd + vd].t()
-            return self._linear(o, lw["out_w"])
+            # the ring keeps the last K conv inputs (slot = position % K) for decode
+            self.C.conv_ring_update(proj, ring, p0)
+            return self._linear(o, lw["out_w"], out=out)
         mixed = proj[:, :2 * kd + vd]
         z = proj[:, 2 * kd + vd:2 * kd + 2 * vd]
         bb = proj[:, 2 * kd + 2 * vd:2 * kd + 2 * vd + d.hv]
@@ -544,13 +595,23 @@ class FastModel:
         o = o * torch.rsqrt(o.pow(2).mean(-1, keepdim=True) + cfg.rms_norm_eps)
         o = o.to(torch.bfloat16).float() * lw["gnorm"]
         o = (o * torch.nn.functional.silu(z.float().view(T, d.hv, d.dv))).to(torch.bfloat16)
-        return self._linear(o.reshape(T, vd), lw["out_w"])
+        return self._linear(o.reshape(T, vd), lw["out_w"], out=out)
 
-    def _attn_prefill(self, i: int, h: torch.Tensor, slot: int, p0: int) -> torch.Tensor:
-        from .reference import apply_rope, rope_cos_sin
+    def _attn_prefill(self, i: int, h: torch.Tensor, slot: int, p0: int, out=None) -> torch.Tensor:
         d, lw, cfg = self.dims, self.layers[i], self.cfg
         T, D = h.shape[0], d.D
         qkv = self._linear(h, lw["w_qkv"])
+        if self.C is not None:
+            # q/k-norm + partial RoPE + KV-cache append in one kernel; the sigmoid output
+            # gate is applied in the attention kernel's epilogue
+            q = torch.empty(T, d.hq * D, dtype=torch.bfloat16, device=h.device)
+            self.C.qk_rope_kv(qkv, d.hq, d.hkv, D, d.qw, lw.get("q_norm"), lw.get("k_norm"), self.inv_freq,
+                              cfg.rotary_dim, self.kc[i][slot], self.vc[i][slot], p0, q, cfg.rms_norm_eps)
+            o = torch.empty(T, d.hq * D, dtype=torch.bfloat16, device=h.device)
+            gate = qkv[:, D:] if cfg.attn_output_gate else None
+            self.C.attn_prefill(q, self.kc[i][slot], self.vc[i][slot], o, d.hq, p0, D ** -0.5, gate, d.qw)
+            return self._linear(o, lw["o_w"], out=out)
+        from .reference import apply_rope, rope_cos_sin
         qp = qkv[:, :d.hq * d.qw].view(T, d.hq, d.qw)
         q, gate = qp[..., :D], (qp[..., D:] if cfg.attn_output_gate else None)
         k = qkv[:, d.hq * d.qw:d.hq * d.qw + d.hkv * D].view(T, d.hkv, D)
@@ -564,12 +625,6 @@ class FastModel:
         self.kc[i][slot, :, p0:p0 + T] = k.transpose(0, 1)
         self.vc[i][slot, :, p0:p0 + T] = v.transpose(0, 1)
         L = p0 + T
-        if self.C is not None:
-            o = torch.empty(T, d.hq * D, dtype=torch.bfloat16, device=h.device)
-            self.C.attn_prefill(q.reshape(T, d.hq * D), self.kc[i][slot], self.vc[i][slot], o, d.hq, p0, D ** -0.5)
-            if gate is not None:
-                o = (o.float() * torch.sigmoid(gate.reshape(T, d.hq * D).float())).to(torch.bfloat16)
-            return self._linear(o, lw["o_w"])
         Kc, Vc = self.kc[i][slot, :, :L], self.vc[i][slot, :, :L]
         if p0 == 0:
             o = torch.nn.functional.scaled_dot_product_attention(
@@ -581,23 +636,23 @@ class FastModel:
         o = o.transpose(0, 1).reshape(T, d.hq * D)
         if gate is not None:
             o = (o.float() * torch.sigmoid(gate.reshape(T, d.hq * D).float())).to(torch.bfloat16)
-        return self._linear(o, lw["o_w"])
+        return self._linear(o, lw["o_w"], out=out)
 
-    def _ffn_prefill(self, i: int, hn: torch.Tensor) -> torch.Tensor:
+    def _ffn_prefill(self, i: int, hn: torch.Tensor, out=None) -> torch.Tensor:
         cfg, lw = self.cfg, self.layers[i]
         if not cfg.layer_uses_moe(i):
-            return self._linear(self._linear(hn, lw["w_gu"], 1), lw["w_d"])
+            return self._linear(self._linear(hn, lw["w_gu"], 1), lw["w_d"], out=out)
         E, k = cfg.num_experts, cfg.num_experts_per_tok
         T = hn.shape[0]
         logits = self._linear(hn, lw["router"], 2)
         if self.C is not None:
-            return self._moe_prefill_device(lw, hn, logits, E, k)
+            return self._moe_prefill_device(lw, hn, logits, E, k, out)
         # CPU path (tests without the extension): per-expert loops over sorted routes
         probs = torch.softmax(logits[:, :E].float(), -1)
         topv, topi = torch.topk(probs, k, -1)
         if cfg.norm_topk_prob:
             topv = topv / topv.sum(-1, keepdim=True)
-        out = torch.zeros(T, cfg.hidden_size, dtype=torch.float32, device=hn.device)
+        acc = torch.zeros(T, cfg.hidden_size, dtype=torch.float32, device=hn.device)
         flat = topi.view(-1)
         order = torch.argsort(flat, stable=True)
         tok_of, w_of = order // k, topv.view(-1)[order]
@@ -609,14 +664,17 @@ class FastModel:
             if c and 0 <= le < lw["w_gu"].shape[0]:
                 t = tok_of[start:start + c]
                 y = self._linear(self._linear(hn[t], lw["w_gu"][le], 1), lw["w_d"][le])
-                out.index_add_(0, t, y.float() * w_of[start:start + c, None])
+                acc.index_add_(0, t, y.float() * w_of[start:start + c, None])
             start += c
         if self.has_shared:
             y = self._linear(self._linear(hn, lw["w_gu"][E], 1), lw["w_d"][E])
-            out += y.float() * torch.sigmoid(logits[:, E:E + 1].float())
-        return out.to(torch.bfloat16)
+            acc += y.float() * torch.sigmoid(logits[:, E:E + 1].float())
+        if out is not None:
+            out.copy_(acc)
+            return out
+        return acc.to(torch.bfloat16)
 
-    def _moe_prefill_device(self, lw, hn, logits, E: int, k: int) -> torch.Tensor:
+    def _moe_prefill_device(self, lw, hn, logits, E: int, k: int, out=None) -> torch.Tensor:
         """Routing, grouped expert GEMMs and combine with no host synchronisation."""
         cfg, dev = self.cfg, hn.device
         T, H = hn.shape
@@ -641,7 +699,9 @@ class FastModel:
         y = torch.empty(T * J, H, dtype=torch.bfloat16, device=dev)
         self.C.gemm_grouped_dev(act, lw["w_d"].view(-1, lw["w_d"].shape[-1]), y, tiles, ntiles, H, 0,
                                 self._gemm_err())
-        out = torch.zeros(T, H, dtype=torch.bfloat16, device=dev)
+        if out is None:
+            out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+        out.zero_()  # the combine accumulates into its output
         self.C.moe_combine(y, rows, wts, out)
         return out
 
@@ -650,31 +710,48 @@ class FastModel:
         """Run `tokens` (device int tensor [T]) for `slot` starting at position p0.
 
         Updates the slot's KV / GDN state and position; returns the last token's
-        f32 logits [V].
+        f32 logits [V]. Prompts longer than `prefill_cap` run as consecutive chunks.
         """
-        cfg = self.cfg
         T = tokens.shape[0]
         if p0 + T > self.max_len:
             raise ValueError(f"sequence of {p0 + T} tokens exceeds max_len {self.max_len}")
-        x = self.embed_w[tokens.long()]
+        cap = self.prefill_cap
+        logits = None
+        for s in range(0, T, cap):
+            logits = self._prefill_chunk(slot, tokens[s:s + cap], p0 + s)
+        return logits
+
+    def _prefill_chunk(self, slot: int, tokens: torch.Tensor, p0: int) -> torch.Tensor:
+        cfg = self.cfg
+        T = tokens.shape[0]
+        H = cfg.hidden_size
+        L = cfg.num_hidden_layers
+        if self.C is not None:
+            x = torch.empty(T, H, dtype=torch.bfloat16, device=self.device)
+            self.C.embed(self.embed_w, tokens.to(torch.int32).contiguous(), x)
+        else:
+            x = self.embed_w[tokens.long()].clone()
+        out, h = self._prefill_bufs(T)
+        # every rank computes all rows of the first norm itself (the embedding is replicated)
+        self._add_norm(x, None, self.layers[0]["ln1"], h)
         tm = self.prefill_timer
-        for i in range(cfg.num_hidden_layers):
+        for i in range(L):
             lw = self.layers[i]
-            kind = "gdn" if cfg.is_linear(i) else "attn"
             if tm is not None:
-                tm.mark(kind)
-            h = self._rms(x, lw["ln1"])
-            o = self._gdn_prefill(i, h, slot, p0) if cfg.is_linear(i) else self._attn_prefill(i, h, slot, p0)
-            x = x + self._reduce(o)
+                tm.mark("gdn" if cfg.is_linear(i) else "attn")
+            o = self._gdn_prefill(i, h, slot, p0, out) if cfg.is_linear(i) else \
+                self._attn_prefill(i, h, slot, p0, out)
+            self._reduce_add_norm(x, o, lw["ln2"], h)
             if tm is not None:
                 tm.mark("moe" if cfg.layer_uses_moe(i) else "mlp")
-            o = self._ffn_prefill(i, self._rms(x, lw["ln2"]))
-            x = x + self._reduce(o)
+            o = self._ffn_prefill(i, h, out)
+            nxt = self.layers[i + 1]["ln1"] if i + 1 < L else self.final_norm
+            self._reduce_add_norm(x, o, nxt, h)
         if tm is not None:
             tm.mark("head")
-        last = self._rms(x[-1:], self.final_norm)
         self.pos[slot] = p0 + T
-        return self.full_logits(self._linear(last, self.lm_head, 2))[0]
+        # h holds the final-normed rows (all-gathered under TP): the lm_head reads the last
+        return self.full_logits(self._linear(h[-1:], self.lm_head, 2))[0]
 
     def full_logits(self, local: torch.Tensor) -> torch.Tensor:
         """[n, V_local] logits of this rank's vocabulary slice -> [n, V] on every rank."""

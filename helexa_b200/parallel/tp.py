@@ -4,11 +4,13 @@ Reduction backends for the row-parallel layers (attention o_proj, GDN out_proj,
 MLP down_proj, MoE block end -- the reference's two all-reduces per decoder layer,
 tp/tp_linear.rs:285-293, tp/tp_qwen3_5.rs:1268-1271):
 
-  "p2p"   (default) the reduction runs inside the producing decode kernel: each CTA of
-          the row-parallel GEMV / MoE down pushes its rows into every peer's receive
-          slot over NVLink and sums the peers' rows into the residual
-          (csrc/tp_fused.cuh) -- no separate collective launch; prefill-sized
-          reductions use the one-shot kernel below
+  "p2p"   (default) decode: the reduction runs inside the producing kernel: each warp
+          of the row-parallel GEMV / MoE down stores its rows as (epoch, value) words
+          into every peer's receive slot over NVLink and sums the peers' rows into the
+          residual (csrc/tp_fused.cuh) -- no separate collective launch; prefill: the
+          row-parallel GEMM writes into an exported staging buffer and one kernel does
+          reduce-scatter + residual + RMSNorm + all-gather over peer memory
+          (csrc/tp_prefill.cu)
   "p2p1"  a separate one-shot reduction kernel after the GEMV, over CUDA-IPC peer
           buffers, fused with the residual add (csrc/allreduce.cu)
   "nccl"  the reference-equivalent baseline: ncclAllReduce (through
@@ -98,6 +100,60 @@ class TPComm:
         self.fused_epoch = torch.zeros(2, dtype=torch.int32, device=self.device)
         dist.barrier(group=self.group)
 
+    # ---- prefill: fused reduce-scatter + residual + RMSNorm + all-gather --------------
+    def prefill_region(self, max_tokens: int, hidden: int):
+        """Lazily (collectively: every rank calls it at the same prefill) export the
+        prefill region [flags | stage T x H | h T x H] (bf16) and open the peers'. Returns
+        (stage, h) local views of `max_tokens * hidden` elements each."""
+        need = max_tokens * hidden
+        if getattr(self, "_pf_elems", 0) >= need and self._pf_hidden == hidden:
+            return self._pf_stage, self._pf_h
+        C = ops.C
+        flag = C.rs_norm_ag_flag_bytes()
+        nbytes = need * 2
+        self._pf_stage_off = flag
+        self._pf_h_off = flag + nbytes
+        region, handle = C.ipc_alloc(flag + 2 * nbytes, self.device.index)
+        handles: list = [None] * self.ws
+        dist.all_gather_object(handles, bytes(handle.numpy().tobytes()), group=self.group)
+        old = getattr(self, "_pf_opened", [])
+        if old:
+            torch.cuda.synchronize(self.device)
+            for p in old:
+                ops.C.ipc_close(p)
+        self._pf_opened = []
+        self.pf_bases: list[int] = []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                self.pf_bases.append(region.data_ptr())
+            else:
+                p = C.ipc_open(torch.frombuffer(bytearray(h), dtype=torch.uint8), self.device.index)
+                self.pf_bases.append(p)
+                self._pf_opened.append(p)
+        self._pf_region = region
+        self._pf_elems, self._pf_hidden = need, hidden
+        self.pf_ctr = torch.zeros(2, dtype=torch.int32, device=self.device)
+        bf = region[flag:flag + 2 * nbytes].view(torch.bfloat16)
+        self._pf_stage, self._pf_h = bf[:need], bf[need:]
+        dist.barrier(group=self.group)
+        return self._pf_stage, self._pf_h
+
+    def rs_norm_ag(self, x: torch.Tensor, w: torch.Tensor, eps: float):
+        """x[own rows] += sum over ranks of the staged partials; every rank's h buffer
+        receives RMSNorm(x) * w for all rows (csrc/tp_prefill.cu)."""
+        T, H = x.shape
+        if T * H > self._pf_elems:
+            raise ValueError("prefill chunk larger than the exported region")
+        ctas = max(1, min(self.sms_hint, (T + self.ws - 1) // self.ws))
+        ops.C.rs_norm_ag(self.pf_bases, self.rank, self._pf_stage_off, self._pf_h_off, x, w, eps, self.pf_ctr,
+                         self.err, self.timeout_s, ctas)
+
+    @property
+    def sms_hint(self) -> int:
+        if not hasattr(self, "_sms"):
+            self._sms = torch.cuda.get_device_properties(self.device).multi_processor_count
+        return self._sms
+
     def fused_args(self) -> tuple:
         """Trailing arguments of the fused kernels (gemv_ar, moe_down_ar)."""
         return (self.fused_bases, self.rank, self.slot_elems, self.fused_epoch, self.err, self.timeout_s)
@@ -106,9 +162,9 @@ class TPComm:
         if self.mode in ("p2p", "p2p1"):
             torch.cuda.synchronize(self.device)
             dist.barrier(group=self.group)
-            for p in self._opened:
+            for p in self._opened + getattr(self, "_pf_opened", []):
                 ops.C.ipc_close(p)
-            self._opened = []
+            self._opened, self._pf_opened = [], []
 
     def error_code(self) -> int:
         """The device error word (0 = healthy); reading it synchronizes the device."""
