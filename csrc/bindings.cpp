@@ -31,6 +31,23 @@ void conv_ring_update(torch::Tensor proj, torch::Tensor ring, int64_t p0);
 void rs_norm_ag(std::vector<int64_t> bases, int64_t rank, int64_t stage_off, int64_t h_off, torch::Tensor x,
                 torch::Tensor w, double eps, torch::Tensor ctr, torch::Tensor err, double timeout_s, int64_t ctas);
 int64_t rs_norm_ag_flag_bytes();
+void gemv_tma(torch::Tensor W, torch::Tensor x, torch::Tensor y, int64_t mode, c10::optional<torch::Tensor> resid,
+              c10::optional<torch::Tensor> norm_w, double eps, torch::Tensor err);
+void gemv_tma_ar(torch::Tensor W, torch::Tensor inp, torch::Tensor x, std::vector<int64_t> bases, int64_t rank,
+                 int64_t slot_elems, torch::Tensor ctr, torch::Tensor err, double timeout_s);
+void gemv_tma_experts(torch::Tensor W, torch::Tensor x, torch::Tensor ids, torch::Tensor y, int64_t mode,
+                      int64_t x_row_div, c10::optional<torch::Tensor> norm_w, double eps, int64_t e_base,
+                      int64_t e_count, torch::Tensor err);
+void moe_down_tma(torch::Tensor Wd, torch::Tensor act, torch::Tensor ids, torch::Tensor wts, torch::Tensor x,
+                  c10::optional<torch::Tensor> partial_out, int64_t e_base, int64_t e_count, torch::Tensor err,
+                  c10::optional<std::vector<int64_t>> bases, int64_t rank, int64_t slot_elems,
+                  c10::optional<torch::Tensor> ctr, double timeout_s);
+void gemv_tma_argmax(torch::Tensor W, torch::Tensor x, c10::optional<torch::Tensor> logits, torch::Tensor norm_w,
+                     double eps, torch::Tensor best, torch::Tensor counter, torch::Tensor tok, torch::Tensor slots,
+                     torch::Tensor pos, torch::Tensor out_tokens, torch::Tensor step, int64_t v_off, torch::Tensor err,
+                     c10::optional<std::vector<int64_t>> bases, int64_t rank, int64_t slot_elems,
+                     c10::optional<torch::Tensor> ctr, double timeout_s);
+bool gemv_tma_ok(int64_t N, int64_t K, int64_t x_rows, int64_t groups_per_rb);
 void gemv_experts_ep(torch::Tensor W, torch::Tensor x, torch::Tensor ids, torch::Tensor y, int64_t mode,
                      int64_t x_row_div, c10::optional<torch::Tensor> norm_w, double eps, int64_t e_base);
 void moe_down_ar_ep(torch::Tensor Wd, torch::Tensor act, torch::Tensor ids, torch::Tensor wts, torch::Tensor x,
@@ -106,6 +123,17 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("conv_ring_update", &conv_ring_update);
   m.def("rs_norm_ag", &rs_norm_ag);
   m.def("rs_norm_ag_flag_bytes", &rs_norm_ag_flag_bytes);
+  m.def("gemv_tma", &gemv_tma);
+  m.def("gemv_tma_ar", &gemv_tma_ar);
+  m.def("gemv_tma_experts", &gemv_tma_experts);
+  m.def("moe_down_tma", &moe_down_tma, py::arg("Wd"), py::arg("act"), py::arg("ids"), py::arg("wts"), py::arg("x"),
+        py::arg("partial_out"), py::arg("e_base"), py::arg("e_count"), py::arg("err"), py::arg("bases") = py::none(),
+        py::arg("rank") = 0, py::arg("slot_elems") = 0, py::arg("ctr") = py::none(), py::arg("timeout_s") = 5.0);
+  m.def("gemv_tma_argmax", &gemv_tma_argmax, py::arg("W"), py::arg("x"), py::arg("logits"), py::arg("norm_w"),
+        py::arg("eps"), py::arg("best"), py::arg("counter"), py::arg("tok"), py::arg("slots"), py::arg("pos"),
+        py::arg("out_tokens"), py::arg("step"), py::arg("v_off"), py::arg("err"), py::arg("bases") = py::none(),
+        py::arg("rank") = 0, py::arg("slot_elems") = 0, py::arg("ctr") = py::none(), py::arg("timeout_s") = 5.0);
+  m.def("gemv_tma_ok", &gemv_tma_ok);
   m.def("embed", &embed);
   m.def("argmax_step", &argmax_step);
   m.def("ipc_alloc", &ipc_alloc);

@@ -84,59 +84,79 @@ HX_DEVICE bool pf_barrier(const TPPrefill& p, int which, unsigned e) {
   return !bad;
 }
 
-template <int VPT>
+// One warp per owned row (8 rows in flight per CTA); lane l handles the 16-byte pieces
+// l, l+32, ... of the row, in chunks of 8 per lane (all loads of a chunk and source in
+// flight at once). The updated bf16 row is kept in shared memory for the normalisation
+// pass, so no block barrier is needed per row.
 __global__ void __launch_bounds__(256) rs_norm_ag_kernel(TPPrefill p, __nv_bfloat16* __restrict__ x,
                                                         const float* __restrict__ w, int T, int H, float eps) {
-  __shared__ float red[8];
+  constexpr int CH = 8;
+  extern __shared__ __align__(16) unsigned char smraw[];
   pdl_wait_prior();
   const unsigned e = *((volatile unsigned*)p.ctr) + 1;
   const bool healthy = *((volatile int*)p.err) == 0;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nv = H / 8;
+  bf16x8* rowbuf = reinterpret_cast<bf16x8*>(smraw) + (size_t)warp * nv;
   if (healthy && pf_barrier(p, 0, e)) {
     const int per = (T + p.ws - 1) / p.ws;
     const int r0 = p.rank * per, r1 = min(T, r0 + per);
-    const int nv = H / 8;
-    for (int t = r0 + blockIdx.x; t < r1; t += gridDim.x) {
-      float f[VPT][8];
+    for (int t = r0 + blockIdx.x * 8 + warp; t < r1; t += gridDim.x * 8) {
+      bf16x8* xr = reinterpret_cast<bf16x8*>(x + (long long)t * H);
       float ss = 0.f;
+      for (int c0 = 0; c0 < nv; c0 += 32 * CH) {
+        float s[CH][8];
 #pragma unroll
-      for (int i = 0; i < VPT; ++i) {
-        const int v = threadIdx.x + 256 * i;
-        if (v < nv) {
-          float s[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-          for (int src = 0; src < p.ws; ++src) {
-            const bf16x8* part =
-                reinterpret_cast<const bf16x8*>(p.base[src] + p.stage_off) + (long long)t * nv + v;
-            float q[8];
-            unpack8(*part, q);
+        for (int i = 0; i < CH; ++i)
 #pragma unroll
-            for (int j = 0; j < 8; ++j) s[j] += q[j];
+          for (int j = 0; j < 8; ++j) s[i][j] = 0.f;
+        for (int src = 0; src < p.ws; ++src) {  // rank order: identical sums on every rank
+          const bf16x8* part = reinterpret_cast<const bf16x8*>(p.base[src] + p.stage_off) + (long long)t * nv;
+          bf16x8 q[CH];
+#pragma unroll
+          for (int i = 0; i < CH; ++i) {
+            const int v = c0 + lane + 32 * i;
+            if (v < nv) q[i] = part[v];
           }
-          bf16x8* xp = reinterpret_cast<bf16x8*>(x + (long long)t * H) + v;
-          float xv[8];
-          unpack8(*xp, xv);
 #pragma unroll
-          for (int j = 0; j < 8; ++j) xv[j] += __bfloat162float(__float2bfloat16(s[j]));
-          const bf16x8 nx = pack8(xv);
-          *xp = nx;
-          unpack8(nx, f[i]);
+          for (int i = 0; i < CH; ++i) {
+            if (c0 + lane + 32 * i < nv) {
+              float f[8];
+              unpack8(q[i], f);
 #pragma unroll
-          for (int j = 0; j < 8; ++j) ss += f[i][j] * f[i][j];
+              for (int j = 0; j < 8; ++j) s[i][j] += f[j];
+            }
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < CH; ++i) {
+          const int v = c0 + lane + 32 * i;
+          if (v < nv) {
+            float xv[8];
+            unpack8(xr[v], xv);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) xv[j] += __bfloat162float(__float2bfloat16(s[i][j]));
+            const bf16x8 nx = pack8(xv);
+            xr[v] = nx;
+            rowbuf[v] = nx;
+            unpack8(nx, xv);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) ss += xv[j] * xv[j];
+          }
         }
       }
-      ss = block_sum(ss, red);
+      ss = warp_sum(ss);  // also orders this warp's row-buffer stores before the reads
       const float inv = rsqrtf(ss / H + eps);
+      for (int v = lane; v < nv; v += 32) {
+        float g[8];
+        unpack8(rowbuf[v], g);
 #pragma unroll
-      for (int i = 0; i < VPT; ++i) {
-        const int v = threadIdx.x + 256 * i;
-        if (v < nv) {
-          float g[8];
-#pragma unroll
-          for (int j = 0; j < 8; ++j) g[j] = f[i][j] * inv * w[v * 8 + j];
-          const bf16x8 hv = pack8(g);
-          for (int dst = 0; dst < p.ws; ++dst)
-            reinterpret_cast<bf16x8*>(p.base[dst] + p.h_off)[(long long)t * nv + v] = hv;
-        }
+        for (int j = 0; j < 8; ++j) g[j] = g[j] * inv * w[v * 8 + j];
+        const bf16x8 hv = pack8(g);
+        for (int dst = 0; dst < p.ws; ++dst)
+          reinterpret_cast<bf16x8*>(p.base[dst] + p.h_off)[(long long)t * nv + v] = hv;
       }
+      __syncwarp();
     }
     __threadfence_system();  // this thread's h stores reach every rank before the signal
     pf_barrier(p, 1, e);
@@ -175,11 +195,11 @@ void rs_norm_ag(std::vector<int64_t> bases, int64_t rank, int64_t stage_off, int
   p.timeout_ns = (unsigned long long)(timeout_s * 1e9);
   auto st = at::cuda::getCurrentCUDAStream();
   auto xp = reinterpret_cast<__nv_bfloat16*>(x.data_ptr());
-  const int vpt = (H / 8 + 255) / 256;
-  const dim3 grid((unsigned)ctas);
-  if (vpt == 1) HX_CUDA_CHECK(hx_launch_pdl(rs_norm_ag_kernel<1>, grid, dim3(256), 0, st, p, xp, w.data_ptr<float>(), T, H, (float)eps));
-  else if (vpt == 2) HX_CUDA_CHECK(hx_launch_pdl(rs_norm_ag_kernel<2>, grid, dim3(256), 0, st, p, xp, w.data_ptr<float>(), T, H, (float)eps));
-  else HX_CUDA_CHECK(hx_launch_pdl(rs_norm_ag_kernel<4>, grid, dim3(256), 0, st, p, xp, w.data_ptr<float>(), T, H, (float)eps));
+  const size_t smem = (size_t)8 * H * sizeof(__nv_bfloat16);  // one row per warp
+  if (smem > 48 * 1024)
+    HX_CUDA_CHECK(cudaFuncSetAttribute(rs_norm_ag_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  HX_CUDA_CHECK(hx_launch_pdl(rs_norm_ag_kernel, dim3((unsigned)ctas), dim3(256), smem, st, p, xp, w.data_ptr<float>(),
+                              T, H, (float)eps));
 }
 
 int64_t rs_norm_ag_flag_bytes() { return (int64_t)kPFFlagBytes; }

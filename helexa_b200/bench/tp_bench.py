@@ -1,6 +1,8 @@
-"""Two-or-more-rank microbenchmark of the decode reductions (CUDA events in graphs, max over
-ranks): the plain residual GEMV, the GEMV with the cross-rank reduction fused into its
-epilogue, and the separate one-shot P2P reduction kernel.
+"""Two-or-more-rank microbenchmark of the tensor-parallel reductions (CUDA events, max
+over ranks). Decode (in CUDA graphs): the plain residual GEMV, the GEMV with the
+cross-rank reduction fused into its epilogue, and the separate one-shot P2P kernel.
+Prefill (T=8192 x H=2048 bf16, one row-parallel output): the fused reduce-scatter +
+residual + RMSNorm + all-gather kernel against NCCL all-reduce + the add/norm kernel.
 
   python -m torch.distributed.run --nnodes=1 --nproc-per-node 2 --master-addr 127.0.0.1 \\
       -m helexa_b200.bench.tp_bench
@@ -37,6 +39,25 @@ for N, K in [(2048, 4096 // ws), (2048, 2048)]:
     res[f"gemv_ar_{N}x{K}"] = t(lambda: C.gemv_ar(W, inp, x, *comm.fused_args()))
     part = torch.zeros(1, N, device=dev).bfloat16()
     res[f"ar_oneshot_{N}"] = t(lambda: C.ar_oneshot(comm.bases, rank, part.view(-1), x.view(-1), None, comm.data_bytes, comm.epoch, comm.err, 1, 5.0))
+def t_eager(fn, n=20):
+    for _ in range(3): fn()
+    torch.cuda.synchronize(); dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(n): fn()
+    e1.record(); e1.synchronize()
+    return e0.elapsed_time(e1) / n * 1e3
+T, H = 8192, 2048
+stage, hbuf = comm.prefill_region(T, H)
+stage.copy_(torch.randn(T * H, device=dev).bfloat16())
+xs = torch.randn(T, H, device=dev).bfloat16(); w = torch.rand(H, device=dev) + 0.5
+res[f"prefill_rs_norm_ag_{T}x{H}"] = t_eager(lambda: comm.rs_norm_ag(xs, w, 1e-6))
+o = torch.randn(T, H, device=dev).bfloat16(); hh = torch.empty_like(o)
+def nccl_path():
+    dist.all_reduce(o)
+    C.add_rmsnorm(xs, o, w, hh, 1e-6)
+res[f"prefill_nccl_allreduce_add_norm_{T}x{H}"] = t_eager(nccl_path)
+res["prefill_bytes_over_nvlink_per_rank_MB"] = 2 * (ws - 1) / ws * T * H * 2 / 1e6
 comm.check()
 r = torch.tensor(list(res.values()), device=dev); dist.all_reduce(r, op=dist.ReduceOp.MAX)
 if rank == 0: print(json.dumps({k: round(v, 2) for k, v in zip(res, r.tolist())}))

@@ -182,6 +182,13 @@ class FastModel:
                 self.kc[i] = torch.zeros(shp, dtype=torch.bfloat16, device=device)
                 self.vc[i] = torch.zeros(shp, dtype=torch.bfloat16, device=device)
         self._bufs: dict[int, DecodeBuffers] = {}
+        # decode GEMV engine: "tma" (bulk-copy ring, csrc/gemv_tma.cu) or "ld" (register-
+        # staged loads, csrc/gemv.cu); shapes the TMA engine does not take use "ld"
+        import os
+        self.gemv_engine = os.environ.get("HELEXA_GEMV", "tma")
+        self._tma_ok_cache: dict = {}
+        if self.C is not None:
+            self._gemm_err()  # allocated before any graph capture
         self.prefill_timer = None  # optional PhaseTimer (CUDA events per prefill phase)
 
     # ------------------------------------------------------------------
@@ -289,12 +296,23 @@ class FastModel:
         self._bufs[B] = nb
         return nb
 
+    def _tma(self, N: int, K: int, x_rows: int, groups: int = 1) -> bool:
+        if self.gemv_engine != "tma" or self.C is None:
+            return False
+        key = (N, K, x_rows, groups)
+        if key not in self._tma_ok_cache:
+            self._tma_ok_cache[key] = bool(self.C.gemv_tma_ok(N, K, x_rows, groups))
+        return self._tma_ok_cache[key]
+
     def _row_parallel(self, W, inp, nb: DecodeBuffers):
         """x += W . inp, summed across TP ranks when the layer is sharded."""
         if self.comm is None or self.dims.ws == 1:
             self._gemv(W, inp, nb.x, ops.RESID_ADD, nb.x, None, 0.0)
         elif self.comm.fused and not isinstance(W, QWeight):
-            self.C.gemv_ar(W, inp, nb.x, *self.comm.fused_args())
+            if self._tma(W.shape[0], W.shape[1], nb.B):
+                self.C.gemv_tma_ar(W, inp, nb.x, *self.comm.fused_args())
+            else:
+                self.C.gemv_ar(W, inp, nb.x, *self.comm.fused_args())
         else:
             self._gemv(W, inp, nb.partial, ops.STORE_BF16, None, None, 0.0)
             self.comm.reduce_residual(nb.partial, nb.x)
@@ -318,16 +336,36 @@ class FastModel:
             J = k + (1 if self.has_shared else 0)
             C.gemv_router(lw["router"], nb.x, nb.rlogits, lw["ln2"], eps, E, k, self.has_shared,
                           cfg.norm_topk_prob, nb.ids, nb.wts, nb.counter)
+            Wgu, Wd = lw["w_gu"], lw["w_d"]
+            tma_gu = self._tma(Wgu.shape[1], Wgu.shape[2], nb.B, nb.B * J)
+            tma_d = self._tma(Wd.shape[1], Wd.shape[2], nb.B * J, nb.B)
+            e_base, e_count = (d.e0, Wgu.shape[0]) if d.ep else (0, 0)
+            if tma_gu:
+                C.gemv_tma_experts(Wgu, nb.x, nb.ids.view(-1), nb.act_moe, ops.SILU_PAIR, J, lw["ln2"], eps, e_base,
+                                   e_count, self._gemm_err())
+            elif d.ep:
+                C.gemv_experts_ep(Wgu, nb.x, nb.ids.view(-1), nb.act_moe, ops.SILU_PAIR, J, lw["ln2"], eps, d.e0)
+            else:
+                C.gemv_experts(Wgu, nb.x, nb.ids.view(-1), nb.act_moe, ops.SILU_PAIR, J, lw["ln2"], eps)
             if d.ep:
                 # expert parallel: this rank runs the routes to its own experts; the fused
                 # cross-rank sum in the down kernel combines every rank's experts
                 if not self.comm.fused:
                     raise RuntimeError("expert parallelism needs the fused p2p reduction (HELEXA_TP_MODE=p2p)")
-                C.gemv_experts_ep(lw["w_gu"], nb.x, nb.ids.view(-1), nb.act_moe, ops.SILU_PAIR, J, lw["ln2"], eps,
-                                  d.e0)
-                C.moe_down_ar_ep(lw["w_d"], nb.act_moe, nb.ids, nb.wts, nb.x, *self.comm.fused_args(), d.e0)
+                if tma_d:
+                    bases, rank, slots_, ctr, err, tmo = self.comm.fused_args()
+                    C.moe_down_tma(Wd, nb.act_moe, nb.ids, nb.wts, nb.x, None, e_base, e_count, err, bases, rank,
+                                   slots_, ctr, tmo)
+                else:
+                    C.moe_down_ar_ep(Wd, nb.act_moe, nb.ids, nb.wts, nb.x, *self.comm.fused_args(), d.e0)
                 return
-            C.gemv_experts(lw["w_gu"], nb.x, nb.ids.view(-1), nb.act_moe, ops.SILU_PAIR, J, lw["ln2"], eps)
+            if tma_d and (self.comm is None or d.ws == 1):
+                C.moe_down_tma(Wd, nb.act_moe, nb.ids, nb.wts, nb.x, None, 0, 0, self._gemm_err())
+                return
+            if tma_d and self.comm.fused:
+                bases, rank, slots_, ctr, err, tmo = self.comm.fused_args()
+                C.moe_down_tma(Wd, nb.act_moe, nb.ids, nb.wts, nb.x, None, 0, 0, err, bases, rank, slots_, ctr, tmo)
+                return
             if self.comm is None or d.ws == 1:
                 C.moe_down(lw["w_d"], nb.act_moe, nb.ids, nb.wts, nb.x, None)
             elif self.comm.fused:
@@ -344,7 +382,15 @@ class FastModel:
         self.C.embed(self.embed_w, nb.tok, nb.x)
         for i in range(self.cfg.num_hidden_layers):
             self._decode_layer(i, nb)
-        if self.vocab_parallel:
+        if self._tma(self.lm_head.shape[0], self.lm_head.shape[1], nb.B):
+            tp = {}
+            if self.vocab_parallel:
+                bases, rank, slots_, ctr, _, tmo = self.comm.fused_args()
+                tp = dict(bases=bases, rank=rank, slot_elems=slots_, ctr=ctr, timeout_s=tmo)
+            self.C.gemv_tma_argmax(self.lm_head, nb.x, nb.logits, self.final_norm, self.cfg.rms_norm_eps, nb.best,
+                                   nb.counter, nb.tok, nb.slots, self.pos, nb.out_tokens, nb.step, self.v_off,
+                                   self.comm.err if self.vocab_parallel else self._gemm_err(), **tp)
+        elif self.vocab_parallel:
             self.C.gemv_argmax_tp(self.lm_head, nb.x, nb.logits, self.final_norm, self.cfg.rms_norm_eps, nb.best,
                                   nb.counter, nb.tok, nb.slots, self.pos, nb.out_tokens, nb.step, self.v_off,
                                   *self.comm.fused_args())
@@ -393,6 +439,8 @@ class FastModel:
     def _gemv(self, W, x, y, mode: int, resid=None, norm=None, eps: float = 0.0):
         if isinstance(W, QWeight):
             self.C.gguf_gemv(W.raw, W.type, W.K, x, y, mode, resid, norm, eps)
+        elif x.shape[0] <= 8 and self._tma(W.shape[0], W.shape[1], x.shape[0]):
+            self.C.gemv_tma(W, x, y, mode, resid, norm, eps, self._gemm_err())
         else:
             self.C.gemv(W, x, y, mode, resid, norm, eps)
 

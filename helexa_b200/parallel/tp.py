@@ -144,7 +144,9 @@ class TPComm:
         T, H = x.shape
         if T * H > self._pf_elems:
             raise ValueError("prefill chunk larger than the exported region")
-        ctas = max(1, min(self.sms_hint, (T + self.ws - 1) // self.ws))
+        # one warp per owned row, 8 per CTA, two CTAs per SM (all co-resident)
+        rows = (T + self.ws - 1) // self.ws
+        ctas = max(1, min(2 * self.sms_hint, (rows + 7) // 8))
         ops.C.rs_norm_ag(self.pf_bases, self.rank, self._pf_stage_off, self._pf_h_off, x, w, eps, self.pf_ctr,
                          self.err, self.timeout_s, ctas)
 

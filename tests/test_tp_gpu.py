@@ -76,7 +76,7 @@ def _run_inner(rank, ws, port, mode, q, name, ep):
         for t in forced:
             nb.tok.fill_(t)
             fm.decode_step_launch(nb)
-            tf.append(nb.logits[0].float().cpu().clone())
+            tf.append(fm.full_logits(nb.logits[:1].float())[0].cpu().clone())
         torch.cuda.synchronize()
         fm._restore_slots(saved)
         if comm is not None:
