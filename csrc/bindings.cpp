@@ -48,6 +48,8 @@ void gemv_tma_argmax(torch::Tensor W, torch::Tensor x, c10::optional<torch::Tens
                      c10::optional<std::vector<int64_t>> bases, int64_t rank, int64_t slot_elems,
                      c10::optional<torch::Tensor> ctr, double timeout_s);
 bool gemv_tma_ok(int64_t N, int64_t K, int64_t x_rows, int64_t groups_per_rb);
+void attn_prefill_tc(torch::Tensor q, torch::Tensor kc, torch::Tensor vc, torch::Tensor out, int64_t Hq, int64_t p0,
+                     double scale, c10::optional<torch::Tensor> gate, int64_t gate_head_stride, torch::Tensor err);
 void gemv_experts_ep(torch::Tensor W, torch::Tensor x, torch::Tensor ids, torch::Tensor y, int64_t mode,
                      int64_t x_row_div, c10::optional<torch::Tensor> norm_w, double eps, int64_t e_base);
 void moe_down_ar_ep(torch::Tensor Wd, torch::Tensor act, torch::Tensor ids, torch::Tensor wts, torch::Tensor x,
@@ -134,6 +136,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("out_tokens"), py::arg("step"), py::arg("v_off"), py::arg("err"), py::arg("bases") = py::none(),
         py::arg("rank") = 0, py::arg("slot_elems") = 0, py::arg("ctr") = py::none(), py::arg("timeout_s") = 5.0);
   m.def("gemv_tma_ok", &gemv_tma_ok);
+  m.def("attn_prefill_tc", &attn_prefill_tc);
   m.def("embed", &embed);
   m.def("argmax_step", &argmax_step);
   m.def("ipc_alloc", &ipc_alloc);

@@ -370,14 +370,14 @@ __global__ void __launch_bounds__(kGtThreads, 1) gemv_tma_kernel(GtArgs a) {
   if (a.mode != kGtArgmax) return;
   // ---- arg-max tail: CTA best -> global best; the last CTA does the step bookkeeping
   consumer_sync();
-  if (threadIdx.x < B) atomicMax(&a.best[threadIdx.x], kbest[threadIdx.x]);
+  if (threadIdx.x < a.B) atomicMax(&a.best[threadIdx.x], kbest[threadIdx.x]);
   __threadfence();
   consumer_sync();
   if (threadIdx.x == 0) is_last = (atomicAdd(a.counter, 1) == (int)gridDim.x - 1);
   consumer_sync();
   if (!is_last) return;
   __threadfence();
-  if (threadIdx.x < B) kbest[threadIdx.x] = atomicExch(&a.best[threadIdx.x], 0ull);
+  if (threadIdx.x < a.B) kbest[threadIdx.x] = atomicExch(&a.best[threadIdx.x], 0ull);
   consumer_sync();
   if (a.tp.ws > 1) {
     const unsigned e = tp_epoch(a.tp);
@@ -385,13 +385,13 @@ __global__ void __launch_bounds__(kGtThreads, 1) gemv_tma_kernel(GtArgs a) {
       unsigned long long keys[B];
 #pragma unroll
       for (int b = 0; b < B; ++b) keys[b] = kbest[b];
-      tp_warp_max_u64(a.tp, e, keys, B);
-      if (lane < B) kbest[lane] = keys[lane];
+      tp_warp_max_u64(a.tp, e, keys, a.B);
+      if (lane < a.B) kbest[lane] = keys[lane];
     }
     consumer_sync();
     if (threadIdx.x == 0) a.tp.ctr[0] = e;
   }
-  if (threadIdx.x < B) {
+  if (threadIdx.x < a.B) {  // a.B: the real batch (the template B may be rounded up)
     const int b = threadIdx.x;
     const unsigned long long k = kbest[b];
     const int t = k == 0 ? 0 : 0x7fffffff - (int)(k & 0xffffffffu);
@@ -423,7 +423,23 @@ int sms() {
   return g_sms;
 }
 
-constexpr size_t kSmemBudget = 200 * 1024;
+// Shared memory per CTA (weight ring + activations) and the largest weight tile. Kept
+// under half of the SM's shared memory by default so the next kernel's CTA can become
+// resident and start streaming its weights (PDL) while this one drains.
+size_t smem_budget() {
+  static size_t v = [] {
+    const char* e = getenv("HELEXA_GEMV_SMEM_KB");
+    return (size_t)(e ? atoi(e) : 100) * 1024;
+  }();
+  return v;
+}
+size_t max_tile() {
+  static size_t v = [] {
+    const char* e = getenv("HELEXA_GEMV_TILE_KB");
+    return (size_t)(e ? atoi(e) : 16) * 1024;
+  }();
+  return v;
+}
 
 // Tile shape: RT rows per tile (multiple of 8 -> warp-per-row(s); 1, 2 or 4 -> warps
 // split K), at most 64 KB per tile, small enough that every SM gets a row block.
@@ -435,20 +451,21 @@ void choose_tiles(GtArgs& a, int groups_per_rb, size_t xbytes) {
 }
 
 bool choose_tiles_ok(GtArgs& a, int groups_per_rb, size_t xbytes) {
-  const int by_bytes = (int)std::max<long long>(1, 65536 / ((long long)a.K * 2));
+  const int by_bytes = (int)std::max<long long>(1, (long long)max_tile() / ((long long)a.K * 2));
   int want = (int)std::max<long long>(1, ((long long)a.N * groups_per_rb + sms() - 1) / sms());
   int cap = std::min(std::min(by_bytes, kGtMaxRT), want < 8 ? 8 : want);
   int rt = 1;
   while (rt * 2 <= cap) rt *= 2;
-  if (rt < 8 && by_bytes >= 8) rt = 8;  // short rows: keep warp-per-row tiles
+
   if (a.mode == kGtSilu && rt < 2) rt = 2;
   a.RT = rt;
   a.WPR = rt >= 8 ? 1 : 8 / rt;
   a.nrb = (a.N + rt - 1) / rt;
   const size_t tile = (size_t)rt * a.K * 2;
   const size_t outb = 2ull * rt * 8 * sizeof(float);
-  if (xbytes + outb + 2 * tile > kSmemBudget) return false;
-  long long st = (long long)((kSmemBudget - xbytes - outb) / tile);
+  const size_t budget = std::max(smem_budget(), xbytes + outb + 2 * tile);
+  if (budget > 200 * 1024) return false;
+  long long st = (long long)((budget - xbytes - outb) / tile);
   a.stages = (int)std::min<long long>(st, kGtMaxStages);
   return true;
 }

@@ -41,11 +41,15 @@ def main():
             e1.synchronize()
             return e0.elapsed_time(e1) / args.iters * 1e3  # us
 
+        err = torch.zeros(1, dtype=torch.int32, device="cuda")
         us = run(lambda W: C.gemv(W, x, y, ops.STORE_BF16, None, None, 0.0))
+        us_tma = run(lambda W: C.gemv_tma(W, x, y, ops.STORE_BF16, None, None, 0.0, err)) \
+            if C.gemv_tma_ok(N, K, args.batch, 1) else float("nan")
         us_ref = run(lambda W: torch.matmul(x, W.t()))
-        print(json.dumps({"N": N, "K": K, "batch": args.batch, "MB": round(nbytes / 1e6, 1), "us": round(us, 2),
-                          "GBps": round(nbytes / us / 1e3, 1), "cublas_us": round(us_ref, 2),
-                          "cublas_GBps": round(nbytes / us_ref / 1e3, 1)}))
+        print(json.dumps({"N": N, "K": K, "batch": args.batch, "MB": round(nbytes / 1e6, 1), "ld_us": round(us, 2),
+                          "ld_GBps": round(nbytes / us / 1e3, 1), "tma_us": round(us_tma, 2),
+                          "tma_GBps": round(nbytes / us_tma / 1e3, 1), "cublas_us": round(us_ref, 2),
+                          "cublas_GBps": round(nbytes / us_ref / 1e3, 1), "err": int(err.item())}))
         del Ws
         torch.cuda.empty_cache()
 

@@ -182,10 +182,14 @@ class FastModel:
                 self.kc[i] = torch.zeros(shp, dtype=torch.bfloat16, device=device)
                 self.vc[i] = torch.zeros(shp, dtype=torch.bfloat16, device=device)
         self._bufs: dict[int, DecodeBuffers] = {}
-        # decode GEMV engine: "tma" (bulk-copy ring, csrc/gemv_tma.cu) or "ld" (register-
-        # staged loads, csrc/gemv.cu); shapes the TMA engine does not take use "ld"
+        # decode GEMV engine: "ld" (register-staged loads, csrc/gemv.cu; default: measured
+        # 3.9-5.5 TB/s on the 80B shapes in isolation) or "tma" (bulk-copy ring,
+        # csrc/gemv_tma.cu; 1.4-3.0 TB/s on the same shapes, kept as an option)
         import os
-        self.gemv_engine = os.environ.get("HELEXA_GEMV", "tma")
+        self.gemv_engine = os.environ.get("HELEXA_GEMV", "ld")
+        # attention prefill: "tc" (tcgen05/TMEM, csrc/attn_prefill_tc.cu) or "mma"
+        # (mma.sync tiles, csrc/attn_prefill.cu)
+        self.attn_engine = os.environ.get("HELEXA_ATTN_PREFILL", "tc")
         self._tma_ok_cache: dict = {}
         if self.C is not None:
             self._gemm_err()  # allocated before any graph capture
@@ -657,7 +661,11 @@ class FastModel:
                               cfg.rotary_dim, self.kc[i][slot], self.vc[i][slot], p0, q, cfg.rms_norm_eps)
             o = torch.empty(T, d.hq * D, dtype=torch.bfloat16, device=h.device)
             gate = qkv[:, D:] if cfg.attn_output_gate else None
-            self.C.attn_prefill(q, self.kc[i][slot], self.vc[i][slot], o, d.hq, p0, D ** -0.5, gate, d.qw)
+            if self.attn_engine == "tc":
+                self.C.attn_prefill_tc(q, self.kc[i][slot], self.vc[i][slot], o, d.hq, p0, D ** -0.5, gate, d.qw,
+                                       self._gemm_err())
+            else:
+                self.C.attn_prefill(q, self.kc[i][slot], self.vc[i][slot], o, d.hq, p0, D ** -0.5, gate, d.qw)
             return self._linear(o, lw["o_w"], out=out)
         from .reference import apply_rope, rope_cos_sin
         qp = qkv[:, :d.hq * d.qw].view(T, d.hq, d.qw)
