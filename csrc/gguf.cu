@@ -359,6 +359,7 @@ void gguf_gemv(torch::Tensor W, int64_t type, int64_t K, torch::Tensor x, torch:
   TORCH_CHECK(W.scalar_type() == at::kByte && W.dim() == 2 && W.is_contiguous() && W.is_cuda(), "W uint8 [N, bytes]");
   TORCH_CHECK(K % bv == 0 && W.size(1) == K / bv * bb, "row bytes do not match K");
   TORCH_CHECK(x.size(1) == K && x.scalar_type() == at::kBFloat16, "x [B, K] bf16");
+  TORCH_CHECK(y.stride(-1) == 1, "y rows must be contiguous (a column view of a wider buffer is fine)");
   const int N = W.size(0), B = x.size(0);
   if (type == kQ4_K) TORCH_CHECK(reinterpret_cast<uintptr_t>(W.data_ptr()) % 16 == 0, "Q4_K rows need 16-byte alignment");
   auto st = at::cuda::getCurrentCUDAStream();
@@ -366,9 +367,9 @@ void gguf_gemv(torch::Tensor W, int64_t type, int64_t K, torch::Tensor x, torch:
   auto rp = resid ? reinterpret_cast<const __nv_bfloat16*>(resid->data_ptr()) : nullptr;
   auto np = norm_w ? norm_w->data_ptr<float>() : nullptr;
   const long long rb = W.size(1);
-  if (type == kQ8_0) gg_mode<kQ8_0>((int)mode, wp, rb, x, y.data_ptr(), y.size(1), rp, np, (float)eps, N, (int)K, B, st);
-  else if (type == kQ4_K) gg_mode<kQ4_K>((int)mode, wp, rb, x, y.data_ptr(), y.size(1), rp, np, (float)eps, N, (int)K, B, st);
-  else gg_mode<kQ6_K>((int)mode, wp, rb, x, y.data_ptr(), y.size(1), rp, np, (float)eps, N, (int)K, B, st);
+  if (type == kQ8_0) gg_mode<kQ8_0>((int)mode, wp, rb, x, y.data_ptr(), y.stride(0), rp, np, (float)eps, N, (int)K, B, st);
+  else if (type == kQ4_K) gg_mode<kQ4_K>((int)mode, wp, rb, x, y.data_ptr(), y.stride(0), rp, np, (float)eps, N, (int)K, B, st);
+  else gg_mode<kQ6_K>((int)mode, wp, rb, x, y.data_ptr(), y.stride(0), rp, np, (float)eps, N, (int)K, B, st);
 }
 
 void gguf_dequant(torch::Tensor W, int64_t type, int64_t K, torch::Tensor out) {

@@ -129,8 +129,29 @@ class QWeight:
         return out
 
 
+class QWeightCat:
+    """Row segments of different GGUF block types forming one projection (Q4_K_M keeps
+    attn_v in Q6_K beside Q4_K q/k): the decode GEMV runs once per segment into a
+    column slice of the output; prefill dequantizes and concatenates."""
+
+    def __init__(self, parts: list):
+        self.parts = parts
+
+    @property
+    def shape(self):
+        return (sum(p.shape[0] for p in self.parts), self.parts[0].shape[1])
+
+    def nbytes(self) -> int:
+        return sum(_tbytes(p) for p in self.parts)
+
+    def dequant(self, C) -> torch.Tensor:
+        return torch.cat([p.dequant(C) if isinstance(p, QWeight) else p for p in self.parts], 0)
+
+
 def _tbytes(t) -> int:
-    return t.nbytes() if isinstance(t, QWeight) else t.numel() * t.element_size()
+    if isinstance(t, (QWeight, QWeightCat)):
+        return t.nbytes()
+    return t.numel() * t.element_size()
 
 
 class FastModel:
@@ -215,6 +236,45 @@ class FastModel:
         lm = embed if cfg.tie_word_embeddings else get("lm_head.weight").to(device=device, dtype=torch.bfloat16)
         fn = layout.norm_f32(cfg, get("model.norm.weight")).to(device)
         return cls(cfg, layers, embed, lm.contiguous(), fn, dims, device, **kw)
+
+    @classmethod
+    def from_gguf(cls, cfg: ModelConfig, g, device, rank: int = 0, ws: int = 1, **kw) -> "FastModel":
+        """Serve a GGUF file as GGUF: quantized projections go to the device as their
+        block rows (no host dequantization, no re-quantization) and run through the
+        fused-dequant GEMVs at decode and dequant-then-tcgen05-GEMM at prefill; tensor
+        parallel shards are cut on block boundaries (weights/gguf.py QuantLayer)."""
+        from ..weights.gguf import QuantLayer, QuantRows, quant_block_of
+        if cfg.family not in ("qwen3", "llama") or cfg.num_experts:
+            # MoE / hybrid GGUF files: dequantize on load (quantized experts are not served
+            # natively yet)
+            return cls.from_hf(cfg, g.hf_get, device, rank=rank, ws=ws, **kw)
+        device = torch.device(device)
+        blk = max(quant_block_of(g, f"blk.{i}.ffn_down.weight") for i in range(cfg.num_hidden_layers))
+        dims = layout.local_dims(cfg, rank, ws, inter_block=blk)
+        ql = QuantLayer(g)
+
+        def dev(t):
+            if isinstance(t, QuantRows):
+                return QWeight(t.raw.contiguous().to(device), t.gtype, t.K)
+            if isinstance(t, list):
+                return QWeightCat([dev(p) for p in t])
+            return t.to(device=device, dtype=torch.float32 if t.dtype == torch.float32 and t.dim() == 1
+                        else torch.bfloat16).contiguous()
+        layers = [{k: dev(v) for k, v in ql.layer(cfg, dims, i).items()} for i in range(cfg.num_hidden_layers)]
+        C = ops.C
+
+        def table(name):  # embedding / lm_head: dequantized to bf16 on the device
+            t = g.tensors[name]
+            if t.gtype in (8, 12, 14):
+                q = ql._raw2d(name)
+                return QWeight(q.raw.contiguous().to(device), q.gtype, q.K).dequant(C)
+            return g.tensor(name).to(device=device, dtype=torch.bfloat16).contiguous()
+        embed = table("token_embd.weight")
+        lm = embed if "output.weight" not in g.tensors else table("output.weight")
+        fn = layout.norm_f32(cfg, g.tensor("output_norm.weight")).to(device)
+        m = cls(cfg, layers, embed, lm.contiguous(), fn, dims, device, **kw)
+        m.quant = "gguf"
+        return m
 
     @classmethod
     def random(cls, cfg: ModelConfig, device, seed: int = 0, rank: int = 0, ws: int = 1, std: float = 0.02,
@@ -312,7 +372,7 @@ class FastModel:
         """x += W . inp, summed across TP ranks when the layer is sharded."""
         if self.comm is None or self.dims.ws == 1:
             self._gemv(W, inp, nb.x, ops.RESID_ADD, nb.x, None, 0.0)
-        elif self.comm.fused and not isinstance(W, QWeight):
+        elif self.comm.fused and not isinstance(W, (QWeight, QWeightCat)):
             if self._tma(W.shape[0], W.shape[1], nb.B):
                 self.C.gemv_tma_ar(W, inp, nb.x, *self.comm.fused_args())
             else:
@@ -428,7 +488,7 @@ class FastModel:
                 keys += ["w_gu", "w_d"]
             for k in keys:
                 w = lw.get(k)
-                if w is None or isinstance(w, QWeight) or w.dim() != 2:
+                if w is None or isinstance(w, (QWeight, QWeightCat)) or w.dim() != 2:
                     continue
                 gt = rule.get(k, rule["*"])
                 if w.shape[1] % _GGUF_BLOCK[gt][1]:
@@ -441,6 +501,15 @@ class FastModel:
         torch.cuda.empty_cache()
 
     def _gemv(self, W, x, y, mode: int, resid=None, norm=None, eps: float = 0.0):
+        if isinstance(W, QWeightCat):
+            if mode != ops.STORE_BF16:
+                raise ValueError("segmented quantized weights support the plain store epilogue only")
+            off = 0
+            for p in W.parts:
+                n = p.shape[0]
+                self._gemv(p, x, y[:, off:off + n], mode, None, norm, eps)
+                off += n
+            return
         if isinstance(W, QWeight):
             self.C.gguf_gemv(W.raw, W.type, W.K, x, y, mode, resid, norm, eps)
         elif x.shape[0] <= 8 and self._tma(W.shape[0], W.shape[1], x.shape[0]):
@@ -524,7 +593,7 @@ class FastModel:
                 out.copy_(y)
                 return out
             return y
-        if isinstance(W, QWeight):
+        if isinstance(W, (QWeight, QWeightCat)):
             W = W.dequant(self.C)
         N = W.shape[0] // 2 if epi == 1 else W.shape[0]
         if out is not None and N % 8 == 0:

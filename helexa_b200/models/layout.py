@@ -48,6 +48,7 @@ class LocalDims:
     dk: int = 0
     dv: int = 0
     inter: int = 0        # dense MLP shard
+    inter0: int = 0       # first intermediate column of this rank's shard
     moe_inter: int = 0    # per-expert shard
     shared_inter: int = 0
     ep: bool = False      # expert parallel: whole experts e0 .. e0 + e_local - 1 on this rank
@@ -75,10 +76,23 @@ class LocalDims:
         return self.hq * self.qw + 2 * self.hkv * self.D
 
 
-def local_dims(cfg: ModelConfig, rank: int = 0, ws: int = 1, ep: bool = False) -> LocalDims:
+def block_split(n: int, block: int, ws: int, rank: int) -> tuple[int, int]:
+    """(start, size) of rank's share of n columns split on `block` boundaries: whole
+    blocks, as even as possible (the first n/block mod ws ranks get one block more).
+    With block = 1 and n divisible by ws this is the even Megatron split."""
+    nb = n // block
+    lo = rank * nb // ws
+    hi = (rank + 1) * nb // ws
+    return lo * block, (hi - lo) * block
+
+
+def local_dims(cfg: ModelConfig, rank: int = 0, ws: int = 1, ep: bool = False, inter_block: int = 1) -> LocalDims:
     """Per-rank shard sizes. With `ep` (expert parallelism, ws > 1) each rank holds
     whole experts E/ws .. instead of an intermediate slice of every expert; attention,
-    GDN and dense layers stay tensor-parallel."""
+    GDN and dense layers stay tensor-parallel. `inter_block`: the dense MLP's
+    intermediate dim splits on multiples of this (256 for k-quant GGUF weights, whose
+    row-parallel down projection must hold whole superblocks: Qwen3-32B's 25600 over 8
+    ranks gives 12 or 13 superblocks per rank)."""
     d = LocalDims(ws=ws, rank=rank, H=cfg.hidden_size)
     if cfg.num_full_layers:
         if cfg.num_attention_heads % ws:
@@ -102,8 +116,10 @@ def local_dims(cfg: ModelConfig, rank: int = 0, ws: int = 1, ep: bool = False) -
         d.hk = cfg.linear_num_key_heads // ws
         d.hv = cfg.linear_num_value_heads // ws
         d.dk, d.dv = cfg.linear_key_head_dim, cfg.linear_value_head_dim
-    if cfg.intermediate_size and cfg.intermediate_size % ws == 0:
-        d.inter = cfg.intermediate_size // ws
+    if cfg.intermediate_size:
+        if cfg.intermediate_size % inter_block:
+            raise ValueError(f"intermediate {cfg.intermediate_size} is not a multiple of {inter_block}")
+        d.inter0, d.inter = block_split(cfg.intermediate_size, inter_block, ws, rank)
     if cfg.num_experts and ep and ws > 1:
         if cfg.num_experts % ws:
             raise ValueError(f"{cfg.num_experts} experts do not split over {ws} ranks")
@@ -217,9 +233,10 @@ def fuse_layer(cfg: ModelConfig, dims: LocalDims, i: int, get, dtype=torch.bfloa
         out["w_gu"] = torch.stack(gus).to(dtype).contiguous()
         out["w_d"] = torch.stack(ds).to(dtype).contiguous()
     else:
-        out["w_gu"] = interleave_rows(_rows(get(m + "gate_proj.weight"), ws, r),
-                                      _rows(get(m + "up_proj.weight"), ws, r)).to(dtype).contiguous()
-        out["w_d"] = _cols(get(m + "down_proj.weight"), ws, r).to(dtype).contiguous()
+        i0, i1 = dims.inter0, dims.inter0 + dims.inter
+        out["w_gu"] = interleave_rows(get(m + "gate_proj.weight")[i0:i1],
+                                      get(m + "up_proj.weight")[i0:i1]).to(dtype).contiguous()
+        out["w_d"] = get(m + "down_proj.weight")[:, i0:i1].to(dtype).contiguous()
     return out
 
 

@@ -39,12 +39,18 @@ def check_tp(cfg: ModelConfig, tp: int, quant: str | None = None) -> None:
         raise PreflightError("tp_indivisible", f"{cfg.linear_num_key_heads} GDN key heads over {tp} ranks")
     if cfg.num_experts and cfg.moe_intermediate_size % tp:
         raise PreflightError("tp_indivisible", f"expert intermediate {cfg.moe_intermediate_size} over {tp} ranks")
-    if quant and quant.upper().endswith("_K") and cfg.intermediate_size:
-        # row-parallel shards of down_proj must hold whole 256-value superblocks
-        if (cfg.intermediate_size // tp) % 256:
+    if quant and "_K" in quant.upper():
+        # row-parallel shards must hold whole 256-value superblocks: down_proj splits
+        # unevenly on superblock boundaries (Qwen3-32B: 12 or 13 of 100 per rank at TP8),
+        # so only a too-narrow intermediate or o_proj head slice refuses
+        if cfg.intermediate_size and (cfg.intermediate_size % 256 or cfg.intermediate_size // 256 < tp):
             raise PreflightError("quant_shard_misaligned",
-                                 f"{quant} down_proj shard {cfg.intermediate_size // tp} is not a multiple of 256",
-                                 "use a smaller tensor_parallel or a non-k-quant format")
+                                 f"{quant} down_proj ({cfg.intermediate_size} columns) cannot give each of {tp} "
+                                 "ranks whole 256-value superblocks", "use a smaller tensor_parallel")
+        if cfg.num_full_layers and (cfg.num_attention_heads // tp * cfg.head_dim) % 256:
+            raise PreflightError("quant_shard_misaligned",
+                                 f"{quant} o_proj shard of {cfg.num_attention_heads // tp} heads is not a whole "
+                                 "number of superblocks", "use a smaller tensor_parallel")
 
 
 def check_memory(cfg: ModelConfig, tp: int, free_bytes_per_device: list[int], bytes_per_param: float = 2.0,

@@ -119,7 +119,7 @@ def build_served_model(spec: ModelSpec) -> ServedModel:
         elif src.kind == "gguf":
             from ..weights.gguf import GGUFFile
             g = GGUFFile(src.path)
-            model = FastModel.from_hf(cfg, g.hf_get, dev, **kw)
+            model = FastModel.from_gguf(cfg, g, dev, **kw)
         else:
             from ..weights.loader import SafetensorsDir
             st = SafetensorsDir(src.path)

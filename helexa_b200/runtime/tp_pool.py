@@ -83,7 +83,7 @@ def cuda_fast_runner(rank: int, ws: int, cfg_args: dict):
         model = FastModel.random(cfg, dev, seed=0, **kw)
     elif src.kind == "gguf":
         from ..weights.gguf import GGUFFile
-        model = FastModel.from_hf(cfg, GGUFFile(src.path).hf_get, dev, **kw)
+        model = FastModel.from_gguf(cfg, GGUFFile(src.path), dev, **kw)
     else:
         from ..weights.loader import SafetensorsDir
         model = FastModel.from_hf(cfg, SafetensorsDir(src.path).get, dev, **kw)

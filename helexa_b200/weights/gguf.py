@@ -250,3 +250,130 @@ def write_gguf(path: str, meta: dict, tensors: list[tuple[str, torch.Tensor, int
         for (_, _, _, data) in blobs:
             f.write(data)
             f.write(b"\0" * ((align - len(data) % align) % align))
+
+
+# ---------------------------------------------------------------------------
+# native quantized layout: block rows straight to the device, no host dequantization
+# ---------------------------------------------------------------------------
+@dataclass
+class QuantRows:
+    """A quantized weight as GGUF block rows (uint8 [N, row_bytes], host mmap view)."""
+    raw: torch.Tensor
+    gtype: int
+    K: int
+
+    @property
+    def rows(self) -> int:
+        return self.raw.shape[0]
+
+
+def _blocks(gt: int) -> tuple[int, int]:
+    return BLOCK[gt]
+
+
+class QuantLayer:
+    """Builds one decoder layer of a dense Qwen3 / Llama GGUF file in the fused per-rank
+    layout of models/layout.py, keeping quantized projections as block rows:
+
+      w_qkv  q|k|v rows of this rank's heads (one QuantRows when the three share a
+             block type, else a list of segments -- Q4_K_M stores attn_v as Q6_K);
+      o_w    row-parallel: this rank's head columns, whole blocks;
+      w_gu   gate/up rows of the rank's intermediate shard, interleaved row by row;
+      w_d    row-parallel: the shard's columns on superblock boundaries (uneven shards
+             when the intermediate size does not split evenly into whole superblocks).
+    Tensors stored unquantized (norms, F16/BF16/F32 projections) come back as floats.
+    """
+
+    def __init__(self, g: "GGUFFile"):
+        self.g = g
+
+    def _raw2d(self, name: str) -> QuantRows:
+        t = self.g.tensors[name]
+        bb, bv = _blocks(t.gtype)
+        N, K = t.shape
+        return QuantRows(self.g.raw(name).view(N, K // bv * bb), t.gtype, K)
+
+    def is_quant(self, name: str) -> bool:
+        return self.g.tensors[name].gtype in (Q8_0, Q4_K, Q6_K)
+
+    def rows(self, name: str, r0: int, r1: int):
+        if not self.is_quant(name):
+            return self.g.tensor(name)[r0:r1]
+        q = self._raw2d(name)
+        return QuantRows(q.raw[r0:r1], q.gtype, q.K)
+
+    def cols(self, name: str, c0: int, c1: int):
+        if not self.is_quant(name):
+            return self.g.tensor(name)[:, c0:c1]
+        q = self._raw2d(name)
+        bb, bv = _blocks(q.gtype)
+        if c0 % bv or c1 % bv:
+            # not on block boundaries: this shard cannot stay quantized
+            return self.g.tensor(name)[:, c0:c1]
+        nblk = q.K // bv
+        part = q.raw.view(q.rows, nblk, bb)[:, c0 // bv:c1 // bv].reshape(q.rows, -1)
+        return QuantRows(part, q.gtype, c1 - c0)
+
+    @staticmethod
+    def cat_rows(parts: list):
+        """Row concatenation; same-type quantized parts merge into one weight."""
+        if all(isinstance(p, QuantRows) for p in parts) and len({(p.gtype, p.K) for p in parts}) == 1:
+            return QuantRows(torch.cat([p.raw for p in parts], 0), parts[0].gtype, parts[0].K)
+        if any(isinstance(p, QuantRows) for p in parts):
+            # segments of different block types: merge runs of adjacent same-type parts
+            segs: list = []
+            for p in parts:
+                last = segs[-1] if segs else None
+                if isinstance(p, QuantRows) and isinstance(last, QuantRows) and (last.gtype, last.K) == (p.gtype, p.K):
+                    segs[-1] = QuantRows(torch.cat([last.raw, p.raw], 0), p.gtype, p.K)
+                elif isinstance(p, torch.Tensor) and isinstance(last, torch.Tensor):
+                    segs[-1] = torch.cat([last, p], 0)
+                else:
+                    segs.append(p)
+            return segs
+        return torch.cat(parts, 0)
+
+    @staticmethod
+    def interleave(gt, up):
+        if isinstance(gt, QuantRows) and isinstance(up, QuantRows) and gt.gtype == up.gtype:
+            raw = torch.stack([gt.raw, up.raw], 1).reshape(-1, gt.raw.shape[1])
+            return QuantRows(raw, gt.gtype, gt.K)
+        return None
+
+    def layer(self, cfg: ModelConfig, dims, i: int) -> dict:
+        from ..models.layout import interleave_rows, norm_f32
+        p = f"blk.{i}."
+        g = self.g
+        out: dict = {"ln1": norm_f32(cfg, g.tensor(p + "attn_norm.weight")),
+                     "ln2": norm_f32(cfg, g.tensor(p + "ffn_norm.weight"))}
+        D = cfg.head_dim
+        hq0 = dims.rank * dims.hq
+        q = self.rows(p + "attn_q.weight", hq0 * D, (hq0 + dims.hq) * D)
+        k0, k1 = dims.kv_head0 * D, (dims.kv_head0 + dims.hkv) * D
+        k = self.rows(p + "attn_k.weight", k0, k1)
+        v = self.rows(p + "attn_v.weight", k0, k1)
+        out["w_qkv"] = self.cat_rows([q, k, v])
+        out["o_w"] = self.cols(p + "attn_output.weight", hq0 * D, (hq0 + dims.hq) * D)
+        if cfg.qk_norm:
+            out["q_norm"] = norm_f32(cfg, g.tensor(p + "attn_q_norm.weight"))
+            out["k_norm"] = norm_f32(cfg, g.tensor(p + "attn_k_norm.weight"))
+        i0, i1 = dims.inter0, dims.inter0 + dims.inter
+        gate = self.rows(p + "ffn_gate.weight", i0, i1)
+        up = self.rows(p + "ffn_up.weight", i0, i1)
+        gu = self.interleave(gate, up)
+        if gu is None:  # mixed block types: the fused SwiGLU rows fall back to bf16
+            deq = lambda t: t if isinstance(t, torch.Tensor) else _dequant_rows(t)  # noqa: E731
+            gu = interleave_rows(deq(gate), deq(up))
+        out["w_gu"] = gu
+        out["w_d"] = self.cols(p + "ffn_down.weight", i0, i1)
+        return out
+
+
+def _dequant_rows(q: QuantRows) -> torch.Tensor:
+    from .. import ops
+    return ops.C.gguf_dequant_host(q.raw.contiguous().view(-1).clone(), q.gtype, q.rows * q.K).view(q.rows, q.K)
+
+
+def quant_block_of(g: "GGUFFile", name: str) -> int:
+    """Values per block of a tensor (1 for unquantized types)."""
+    return BLOCK[g.tensors[name].gtype][1]

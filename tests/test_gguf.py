@@ -155,3 +155,100 @@ def test_quantized_model_matches_dequantized_weights(name, scheme):
     assert cos(out[0][0], out[1][0], dim=0).item() > 0.999
     assert cos(out[0][1], out[1][1], dim=0).item() > 0.995
     assert q.weight_bytes() < ref.weight_bytes()
+
+
+def _write_tiny_gguf(path, inter=768, layers=2):
+    """A Q4_K_M-style dense Qwen3 file: q/k/o/gate/up Q4_K, v/down Q6_K, f32 norms,
+    Q8_0 embedding, Q6_K output. hidden 256, 4 heads of 64 (2 kv heads)."""
+    import dataclasses
+
+    from helexa_b200.config import get_preset
+    from helexa_b200.weights.random_init import random_weights
+    cfg = dataclasses.replace(get_preset("tiny-qwen3"), intermediate_size=inter, num_hidden_layers=layers,
+                              layer_types=None, tie_word_embeddings=False)
+    w = random_weights(cfg, seed=2, std=0.05)
+    types = {"attn_q": G.Q4_K, "attn_k": G.Q4_K, "attn_v": G.Q6_K, "attn_output": G.Q4_K, "ffn_gate": G.Q4_K,
+             "ffn_up": G.Q4_K, "ffn_down": G.Q6_K}
+    tensors = []
+    for hf, t in w.items():
+        gname = G.hf_to_gguf_name(hf)
+        kind = gname.split(".")[-2] if gname.startswith("blk.") else gname
+        if t.dim() == 1:
+            gt = G.F32
+        elif gname == "token_embd.weight":
+            gt = G.Q8_0
+        elif gname == "output.weight":
+            gt = G.Q6_K
+        else:
+            gt = types[kind]
+        tensors.append((gname, t, gt))
+    meta = {"general.architecture": "qwen3", "general.name": "tiny-gguf", "qwen3.block_count": layers,
+            "qwen3.embedding_length": cfg.hidden_size, "qwen3.attention.head_count": cfg.num_attention_heads,
+            "qwen3.attention.head_count_kv": cfg.num_key_value_heads, "qwen3.attention.key_length": cfg.head_dim,
+            "qwen3.feed_forward_length": inter, "qwen3.context_length": 4096, "qwen3.vocab_size": cfg.vocab_size,
+            "qwen3.attention.layer_norm_rms_epsilon": cfg.rms_norm_eps, "qwen3.rope.freq_base": cfg.rope_theta}
+    G.write_gguf(path, meta, tensors)
+    return cfg
+
+
+@pytest.mark.parametrize("ws", [1, 2])
+def test_native_gguf_layout_matches_dequantized(tmp_path, ws):
+    """QuantLayer keeps block rows (no host dequantization): dequantizing its per-rank
+    pieces gives exactly the fused layout built from the dequantized checkpoint,
+    including the uneven superblock split of down_proj (3 superblocks over 2 ranks) and
+    the segmented q|k|v (Q4_K q/k, Q6_K v)."""
+    from helexa_b200.models import layout
+    path = os.path.join(tmp_path, "m.gguf")
+    _write_tiny_gguf(path)
+    g = G.GGUFFile(path)
+    cfg = g.model_config()
+    ql = G.QuantLayer(g)
+
+    def deq(t):
+        if isinstance(t, G.QuantRows):
+            return G._dequant_rows(t)
+        if isinstance(t, list):
+            return torch.cat([deq(p) for p in t], 0)
+        return t.float()
+    sizes = []
+    for r in range(ws):
+        dims = layout.local_dims(cfg, r, ws, inter_block=256)
+        sizes.append(dims.inter)
+        want = layout.fuse_layer(cfg, dims, 1, g.hf_get, dtype=torch.float32)
+        got = ql.layer(cfg, dims, 1)
+        assert isinstance(got["w_gu"], G.QuantRows) and isinstance(got["w_d"], G.QuantRows)
+        assert isinstance(got["w_qkv"], list) and len(got["w_qkv"]) == 2  # q|k Q4_K, v Q6_K
+        for k, t in want.items():
+            assert torch.equal(deq(got[k]), t.float()), (r, k)
+    assert sum(sizes) == 768 and all(s % 256 == 0 for s in sizes)
+    g.close()
+
+
+@pytest.mark.gpu
+def test_native_gguf_model_matches_dequantized(tmp_path):
+    """FastModel.from_gguf serves the block rows (fused-dequant decode GEMVs, segmented
+    q|k|v) and matches the model built from the dequantized checkpoint."""
+    from helexa_b200.models.fast import FastModel, QWeight, QWeightCat
+    path = os.path.join(tmp_path, "m.gguf")
+    _write_tiny_gguf(path)
+    g = G.GGUFFile(path)
+    cfg = g.model_config()
+    dev = torch.device("cuda", 0)
+    q = FastModel.from_gguf(cfg, g, dev, max_slots=1, max_len=128)
+    assert isinstance(q.layers[0]["w_qkv"], QWeightCat) and isinstance(q.layers[0]["w_d"], QWeight)
+    ref = FastModel.from_hf(cfg, g.hf_get, dev, max_slots=1, max_len=128)
+    prompt = torch.randint(0, cfg.vocab_size, (40,), generator=torch.Generator().manual_seed(1)).int().to(dev)
+    out = []
+    for m in (q, ref):
+        lg = m.prefill(0, prompt, 0).float()
+        nb = m.capture(1, steps=4)
+        nb.slots.fill_(0)
+        nb.tok.fill_(int(lg.argmax()))
+        m.replay(nb)
+        torch.cuda.synchronize()
+        out.append((lg, nb.logits[0].float().clone()))
+    cos = torch.nn.functional.cosine_similarity
+    assert cos(out[0][0], out[1][0], dim=0).item() > 0.999
+    assert cos(out[0][1], out[1][1], dim=0).item() > 0.995
+    assert q.weight_bytes() < ref.weight_bytes()
+    g.close()

@@ -39,8 +39,10 @@ def test_preflight():
     assert e.value.code == "wrong_modality"
     q32 = get_preset("qwen3-32b")
     preflight("gguf", q32, tp=4, quant="Q4_K")
+    preflight("gguf", q32, tp=8, quant="Q4_K_M")     # uneven superblock split of down_proj
+    tiny = get_preset("tiny-qwen3")
     with pytest.raises(PreflightError) as e:
-        preflight("gguf", q32, tp=8, quant="Q4_K")
+        preflight("gguf", tiny, tp=4, quant="Q4_K")   # fewer superblocks than ranks
     assert e.value.code == "quant_shard_misaligned"
     with pytest.raises(PreflightError) as e:
         preflight("dense", nxt, tp=1, free_bytes_per_device=[80 << 30])
