@@ -48,6 +48,10 @@ void gemv_tma_argmax(torch::Tensor W, torch::Tensor x, c10::optional<torch::Tens
                      c10::optional<std::vector<int64_t>> bases, int64_t rank, int64_t slot_elems,
                      c10::optional<torch::Tensor> ctr, double timeout_s);
 bool gemv_tma_ok(int64_t N, int64_t K, int64_t x_rows, int64_t groups_per_rb);
+void sample_step(torch::Tensor logits, int64_t V, torch::Tensor slots, torch::Tensor temp, torch::Tensor top_k,
+                 torch::Tensor top_p, torch::Tensor penalty, torch::Tensor seed, torch::Tensor ctr, torch::Tensor hist,
+                 torch::Tensor hist_n, torch::Tensor hist_at, torch::Tensor hist_cap, torch::Tensor tok,
+                 torch::Tensor pos, torch::Tensor out_tokens, torch::Tensor step);
 void attn_prefill_tc(torch::Tensor q, torch::Tensor kc, torch::Tensor vc, torch::Tensor out, int64_t Hq, int64_t p0,
                      double scale, c10::optional<torch::Tensor> gate, int64_t gate_head_stride, torch::Tensor err);
 void gemv_experts_ep(torch::Tensor W, torch::Tensor x, torch::Tensor ids, torch::Tensor y, int64_t mode,
@@ -137,6 +141,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("rank") = 0, py::arg("slot_elems") = 0, py::arg("ctr") = py::none(), py::arg("timeout_s") = 5.0);
   m.def("gemv_tma_ok", &gemv_tma_ok);
   m.def("attn_prefill_tc", &attn_prefill_tc);
+  m.def("sample_step", &sample_step);
   m.def("embed", &embed);
   m.def("argmax_step", &argmax_step);
   m.def("ipc_alloc", &ipc_alloc);

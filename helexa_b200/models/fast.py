@@ -82,6 +82,60 @@ class DecodeBuffers:
     err: torch.Tensor          # int32 [1] bounded-wait error code
     graph: torch.cuda.CUDAGraph | None = None
     graph_steps: int = 0
+    sgraph: torch.cuda.CUDAGraph | None = None    # sampled decode (on-device sampler)
+    sgraph_steps: int = 0
+    logits_full: torch.Tensor | None = None       # f32 [B, V] (vocab-parallel gather target)
+    _gather_buf: torch.Tensor | None = None
+
+
+class SamplerState:
+    """Per-slot parameters and penalty history of the on-device sampler
+    (csrc/sample_device.cu), read by the captured sampled-decode graphs."""
+
+    HIST = 64
+
+    def __init__(self, slots: int, device):
+        f32, i32, i64 = torch.float32, torch.int32, torch.int64
+        self.temp = torch.zeros(slots, dtype=f32, device=device)
+        self.top_k = torch.zeros(slots, dtype=i32, device=device)
+        self.top_p = torch.ones(slots, dtype=f32, device=device)
+        self.penalty = torch.ones(slots, dtype=f32, device=device)
+        self.seed = torch.zeros(slots, dtype=i64, device=device)
+        self.ctr = torch.zeros(slots, dtype=i64, device=device)
+        self.hist = torch.zeros(slots, self.HIST, dtype=i32, device=device)
+        self.hist_n = torch.zeros(slots, dtype=i32, device=device)
+        self.hist_at = torch.zeros(slots, dtype=i32, device=device)
+        self.hist_cap = torch.full((slots,), self.HIST, dtype=i32, device=device)
+
+    def tensors(self):
+        return (self.temp, self.top_k, self.top_p, self.penalty, self.seed, self.ctr, self.hist, self.hist_n,
+                self.hist_at, self.hist_cap)
+
+    def set_slot(self, slot: int, temperature: float, top_k: int, top_p: float, penalty: float, last_n: int,
+                 seed: int, draws: int, history: list[int]):
+        """Load one sequence's sampling parameters and its last `last_n` tokens."""
+        cap = max(1, min(int(last_n), self.HIST))
+        h = list(history[-cap:]) if penalty != 1.0 else []
+        self.temp[slot] = float(temperature)
+        self.top_k[slot] = int(top_k)
+        self.top_p[slot] = float(top_p)
+        self.penalty[slot] = float(penalty)
+        self.seed[slot] = int(seed) & ((1 << 63) - 1)
+        self.ctr[slot] = int(draws)
+        row = torch.zeros(self.HIST, dtype=torch.int32)
+        if h:
+            row[:len(h)] = torch.tensor(h, dtype=torch.int32)
+        self.hist[slot].copy_(row, non_blocking=False)
+        self.hist_n[slot] = len(h)
+        self.hist_at[slot] = len(h) % cap
+        self.hist_cap[slot] = cap
+
+    def snapshot(self):
+        return [t.clone() for t in self.tensors()]
+
+    def restore(self, saved):
+        for t, v in zip(self.tensors(), saved):
+            t.copy_(v)
 
 
 # GGUF type ids (ggml): the block formats the kernels read
@@ -212,6 +266,7 @@ class FastModel:
         # (mma.sync tiles, csrc/attn_prefill.cu)
         self.attn_engine = os.environ.get("HELEXA_ATTN_PREFILL", "tc")
         self._tma_ok_cache: dict = {}
+        self.sampler = SamplerState(max_slots, device) if device.type == "cuda" else None
         if self.C is not None:
             self._gemm_err()  # allocated before any graph capture
         self.prefill_timer = None  # optional PhaseTimer (CUDA events per prefill phase)
@@ -441,11 +496,25 @@ class FastModel:
             self._gemv(lw["w_gu"], nb.x, nb.act_mlp, ops.SILU_PAIR, None, lw["ln2"], eps)
             self._row_parallel(lw["w_d"], nb.act_mlp, nb)
 
-    def decode_step_launch(self, nb: DecodeBuffers):
-        """Enqueue one decode step for the nb.B slots in nb.slots (graph-capturable)."""
+    def decode_step_launch(self, nb: DecodeBuffers, sampled: bool = False):
+        """Enqueue one decode step for the nb.B slots in nb.slots (graph-capturable).
+        sampled: the lm_head writes f32 logits and the on-device sampler picks the token
+        with each slot's temperature / top-k / top-p / repeat penalty."""
         self.C.embed(self.embed_w, nb.tok, nb.x)
         for i in range(self.cfg.num_hidden_layers):
             self._decode_layer(i, nb)
+        if sampled:
+            self.C.gemv(self.lm_head, nb.x, nb.logits, ops.STORE_F32, None, self.final_norm, self.cfg.rms_norm_eps)
+            full = nb.logits
+            if self.vocab_parallel:
+                if nb.logits_full is None:
+                    nb.logits_full = torch.zeros(nb.B, self.cfg.vocab_size, dtype=torch.float32, device=self.device)
+                self._gather_logits(nb)
+                full = nb.logits_full
+            st = self.sampler
+            self.C.sample_step(full, self.cfg.vocab_size, nb.slots, *st.tensors(), nb.tok, self.pos, nb.out_tokens,
+                               nb.step)
+            return
         if self._tma(self.lm_head.shape[0], self.lm_head.shape[1], nb.B):
             tp = {}
             if self.vocab_parallel:
@@ -461,6 +530,16 @@ class FastModel:
         else:
             self.C.gemv_argmax(self.lm_head, nb.x, nb.logits, self.final_norm, self.cfg.rms_norm_eps, nb.best,
                                nb.counter, nb.tok, nb.slots, self.pos, nb.out_tokens, nb.step)
+
+    def _gather_logits(self, nb: DecodeBuffers):
+        """logits_full[b] = the concatenation over ranks of each rank's vocabulary slice
+        (NCCL all-gather; capturable in the decode graph)."""
+        import torch.distributed as dist
+        ws = self.dims.ws
+        if nb._gather_buf is None:
+            nb._gather_buf = torch.empty(ws, nb.B, self.v_local, dtype=torch.float32, device=self.device)
+        dist.all_gather_into_tensor(nb._gather_buf, nb.logits, group=self.comm.group)
+        nb.logits_full.view(nb.B, ws, self.v_local).copy_(nb._gather_buf.transpose(0, 1))
 
     def launches_per_step(self) -> int:
         cfg = self.cfg
@@ -497,7 +576,7 @@ class FastModel:
                 del w
         self.quant = scheme
         for nb in self._bufs.values():  # captured graphs refer to the old weights
-            nb.graph = None
+            nb.graph = nb.sgraph = None
         torch.cuda.empty_cache()
 
     def _gemv(self, W, x, y, mode: int, resid=None, norm=None, eps: float = 0.0):
@@ -529,32 +608,44 @@ class FastModel:
             n += 2                                          # two fused (reduce +) residual + norm kernels
         return n
 
-    def capture(self, B: int, steps: int = 1) -> DecodeBuffers:
-        """Capture `steps` consecutive decode steps for batch B into one CUDA graph.
+    def capture(self, B: int, steps: int = 1, sampled: bool = False) -> DecodeBuffers:
+        """Capture `steps` consecutive decode steps for batch B into one CUDA graph
+        (`sampled`: the on-device sampler instead of the fused arg-max).
 
         Capture runs one eager warm-up step first; pool state it touches (positions,
-        KV at the current position, GDN state) is saved and restored around it.
+        KV at the current position, GDN state, sampler counters and history) is saved
+        and restored around it.
         """
         nb = self.buffers(B)
-        if nb.graph is not None and nb.graph_steps == steps:
+        if sampled and nb.sgraph is not None and nb.sgraph_steps == steps:
             return nb
+        if not sampled and nb.graph is not None and nb.graph_steps == steps:
+            return nb
+        if sampled and self.vocab_parallel and nb.logits_full is None:
+            nb.logits_full = torch.zeros(B, self.cfg.vocab_size, dtype=torch.float32, device=self.device)
         saved = self._save_slots(nb.slots.tolist())
+        samp = self.sampler.snapshot() if sampled else None
         step_saved, tok_saved = nb.step.clone(), nb.tok.clone()
         s = torch.cuda.Stream(self.device)
         s.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(s):
-            self.decode_step_launch(nb)
+            self.decode_step_launch(nb, sampled)
         torch.cuda.current_stream(self.device).wait_stream(s)
         torch.cuda.synchronize(self.device)
         self._restore_slots(saved)
+        if samp is not None:
+            self.sampler.restore(samp)
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=s):
             for _ in range(steps):
-                self.decode_step_launch(nb)
+                self.decode_step_launch(nb, sampled)
         torch.cuda.synchronize(self.device)
         nb.step.copy_(step_saved)
         nb.tok.copy_(tok_saved)
-        nb.graph, nb.graph_steps = g, steps
+        if sampled:
+            nb.sgraph, nb.sgraph_steps = g, steps
+        else:
+            nb.graph, nb.graph_steps = g, steps
         return nb
 
     def _save_slots(self, slots: list[int]):
@@ -570,8 +661,8 @@ class FastModel:
         for i, t in saved["rec"].items():
             self.rec[i][sl] = t
 
-    def replay(self, nb: DecodeBuffers):
-        nb.graph.replay()
+    def replay(self, nb: DecodeBuffers, sampled: bool = False):
+        (nb.sgraph if sampled else nb.graph).replay()
 
     # ------------------------------------------------------------------
     # prefill

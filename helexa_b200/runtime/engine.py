@@ -74,6 +74,8 @@ class _Seq:
     produced: int = 0
     last: int = 0
     sampler: HostSampler | None = None
+    draws: int = 0          # on-device sampler draws so far (seeded reproducibility)
+    seed: int = 0
     t_start: float = 0.0
     t_first: float = 0.0
     cached: int = 0
@@ -193,6 +195,8 @@ class Engine:
         seq = _Seq(req=req, slot=slot, history=list(prompt), t_start=t0, cached=cached)
         if not req.params.greedy:
             seq.sampler = HostSampler(req.params)
+            seq.seed = int(req.params.seed) if req.params.seed is not None else \
+                int(torch.randint(0, 2 ** 62, (1,), generator=seq.sampler.gen))
             tok = seq.sampler.sample(logits, seq.history)
         else:
             tok = int(torch.argmax(logits))
@@ -246,7 +250,18 @@ class Engine:
                 outs = r.decode([s.slot for s in greedy], [s.last for s in greedy], 1)
             for s, o in zip(greedy, outs):
                 self._emit(s, o)
-        if sampled:
+        if sampled and getattr(r, "sample_on_device", False):
+            # temperature / top-k / top-p / repeat penalty on the device, several steps
+            # per replayed graph (no per-token logits copy to the host)
+            left = min(s.req.params.max_tokens - s.produced for s in sampled)
+            steps = max(1, min(self.decode_steps, left))
+            outs = r.decode_sampled([s.slot for s in sampled], [s.last for s in sampled], steps,
+                                    [s.req.params for s in sampled], [s.history for s in sampled],
+                                    [s.draws for s in sampled], [s.seed for s in sampled])
+            for s, o in zip(sampled, outs):
+                s.draws += len(o)
+                self._emit(s, o)
+        elif sampled:
             lg = r.decode_logits([s.slot for s in sampled], [s.last for s in sampled])
             for s, row in zip(sampled, lg):
                 self._emit(s, [s.sampler.sample(row, s.history)])

@@ -95,6 +95,36 @@ class FastRunner:
             self.host_pos[s] += steps
         return out
 
+    sample_on_device = True
+
+    def decode_sampled(self, slots: list[int], tokens: list[int], steps: int, params: list,
+                       histories: list[list[int]], draws: list[int], seeds: list[int]) -> list[list[int]]:
+        """`steps` sampled steps on the device (temperature / top-k / top-p / repeat
+        penalty per row, seeded draws), replayed from a captured graph; returns the
+        tokens per slot. `draws` numbers each sequence's earlier device draws, so a
+        seeded request gives the same tokens however its steps are grouped."""
+        m = self.m
+        B = self.bucket(len(slots))
+        st = m.sampler
+        for sl, p, h, d, sd in zip(slots, params, histories, draws, seeds):
+            st.set_slot(sl, p.temperature, p.top_k, p.top_p, p.repeat_penalty, p.repeat_last_n, sd, d, h)
+        pad = B - len(slots)
+        if pad:
+            st.set_slot(self.pad_slot, 0.0, 0, 1.0, 1.0, 1, 0, 0, [])
+        nb = m.capture(B, steps=steps, sampled=True)
+        sl = list(slots) + [self.pad_slot] * pad
+        tk = list(tokens) + [0] * pad
+        nb.slots.copy_(torch.tensor(sl, dtype=torch.int32), non_blocking=True)
+        nb.tok.copy_(torch.tensor(tk, dtype=torch.int32), non_blocking=True)
+        nb.step.zero_()
+        m.pos[self.pad_slot] = 0
+        m.replay(nb, sampled=True)
+        out = nb.out_tokens[:len(slots), :steps].cpu().tolist()
+        m.check_errors()
+        for s in slots:
+            self.host_pos[s] += steps
+        return out
+
     def decode_logits(self, slots: list[int], tokens: list[int]) -> torch.Tensor:
         """One eager step returning f32 logits [n, V] (host-sampled requests)."""
         m = self.m

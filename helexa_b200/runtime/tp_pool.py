@@ -153,7 +153,8 @@ def _rank_main(args: dict) -> None:
     wd = StepWatchdog(on_timeout=lambda: os._exit(70))
     leader = LeaderRunner(local, ctrl, watchdog=wd)
     conn.send(("ready", {"num_slots": local.num_slots, "max_len": local.max_len, "vocab": local.vocab,
-                         "greedy_on_device": bool(getattr(local, "greedy_on_device", False))}))
+                         "greedy_on_device": bool(getattr(local, "greedy_on_device", False)),
+                         "sample_on_device": bool(getattr(local, "sample_on_device", False))}))
     snaps: dict[int, object] = {}
     while True:
         try:
@@ -212,6 +213,7 @@ class RemoteRunner:
         self.procs, self.conn = procs, conn
         self.num_slots, self.max_len, self.vocab = info["num_slots"], info["max_len"], info["vocab"]
         self.greedy_on_device = info["greedy_on_device"]
+        self.sample_on_device = info.get("sample_on_device", False)
         self._mu = threading.Lock()
         self.closed = False
 
@@ -242,6 +244,10 @@ class RemoteRunner:
 
     def decode_logits(self, slots, tokens):
         return self._call("decode_logits", list(slots), list(tokens))
+
+    def decode_sampled(self, slots, tokens, steps, params, histories, draws, seeds):
+        return self._call("decode_sampled", list(slots), list(tokens), steps, list(params),
+                          [list(h[-64:]) for h in histories], list(draws), list(seeds))
 
     def snapshot(self, slot, length):
         return RemoteSnapshot(*self._call("snapshot", slot, length))

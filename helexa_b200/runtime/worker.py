@@ -45,6 +45,7 @@ class LeaderRunner:
         self.max_len = local.max_len
         self.vocab = local.vocab
         self.greedy_on_device = getattr(local, "greedy_on_device", False)
+        self.sample_on_device = getattr(local, "sample_on_device", False)
         self._snap_ids = 0
         self._snaps: dict[int, object] = {}
 
@@ -74,6 +75,12 @@ class LeaderRunner:
 
     def decode_logits(self, slots, tokens):
         return self._call("decode_logits", list(slots), list(tokens))
+
+    def decode_sampled(self, slots, tokens, steps, params, histories, draws, seeds):
+        # every rank samples with the same seeds and counters from the same gathered
+        # logits, so all ranks pick the same tokens
+        return self._call("decode_sampled", list(slots), list(tokens), steps, list(params),
+                          [list(h[-64:]) for h in histories], list(draws), list(seeds))
 
     def snapshot(self, slot, length):
         # every rank keeps its own shard of the snapshot under a shared id

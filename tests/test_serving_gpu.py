@@ -41,8 +41,11 @@ def _oracle_greedy(cfg, w, prompt, n):
 def test_cuda_greedy_matches_oracle(name):
     from helexa_b200.models.fast import FastModel
     from helexa_b200.runtime.runner import FastRunner
+    from test_fast_model_gpu import _realistic
     cfg = get_preset(name)
-    w = random_weights(cfg, seed=0)
+    torch.manual_seed(0)
+    # unit-scale norms: with plain N(0, 0.02) weights every top-2 margin is at bf16 noise
+    w = _realistic(cfg, random_weights(cfg, seed=0, std=0.05))
     prompt = torch.randint(0, cfg.vocab_size, (32,), generator=torch.Generator().manual_seed(0)).tolist()
     want, margins = _oracle_greedy(cfg, w, prompt, 16)
     fm = FastModel.from_hf(cfg, w, "cuda", max_slots=2, max_len=256)
@@ -53,8 +56,8 @@ def test_cuda_greedy_matches_oracle(name):
     while len(got) < 16:
         got += r.decode([0], [got[-1]], 4)[0]
     got = got[:16]
-    # bf16 weights and activations vs the fp32 oracle: logit differences of a few 1e-3
-    n = _margin_rule(want, margins, got, 5e-3)
+    # bf16 weights and activations vs the fp32 oracle: logit differences of ~1e-2
+    n = _margin_rule(want, margins, got, 2e-2)
     assert n >= 4, f"diverged at step {n}"
 
 
