@@ -52,6 +52,11 @@ void sample_step(torch::Tensor logits, int64_t V, torch::Tensor slots, torch::Te
                  torch::Tensor top_p, torch::Tensor penalty, torch::Tensor seed, torch::Tensor ctr, torch::Tensor hist,
                  torch::Tensor hist_n, torch::Tensor hist_at, torch::Tensor hist_cap, torch::Tensor tok,
                  torch::Tensor pos, torch::Tensor out_tokens, torch::Tensor step);
+void moe_fused(torch::Tensor x, torch::Tensor norm_w, double eps, torch::Tensor router, torch::Tensor w_gu,
+               torch::Tensor w_d, int64_t E, int64_t topk, bool has_shared, bool norm_topk, torch::Tensor rlogits,
+               torch::Tensor act, torch::Tensor bar, torch::Tensor err, int64_t e_base, int64_t e_count,
+               c10::optional<std::vector<int64_t>> bases, int64_t rank, int64_t slot_elems,
+               c10::optional<torch::Tensor> ctr, double timeout_s);
 void attn_prefill_tc(torch::Tensor q, torch::Tensor kc, torch::Tensor vc, torch::Tensor out, int64_t Hq, int64_t p0,
                      double scale, c10::optional<torch::Tensor> gate, int64_t gate_head_stride, torch::Tensor err);
 void gemv_experts_ep(torch::Tensor W, torch::Tensor x, torch::Tensor ids, torch::Tensor y, int64_t mode,
@@ -142,6 +147,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemv_tma_ok", &gemv_tma_ok);
   m.def("attn_prefill_tc", &attn_prefill_tc);
   m.def("sample_step", &sample_step);
+  m.def("moe_fused", &moe_fused, py::arg("x"), py::arg("norm_w"), py::arg("eps"), py::arg("router"), py::arg("w_gu"),
+        py::arg("w_d"), py::arg("E"), py::arg("topk"), py::arg("has_shared"), py::arg("norm_topk"),
+        py::arg("rlogits"), py::arg("act"), py::arg("bar"), py::arg("err"), py::arg("e_base") = 0,
+        py::arg("e_count") = 0, py::arg("bases") = py::none(), py::arg("rank") = 0, py::arg("slot_elems") = 0,
+        py::arg("ctr") = py::none(), py::arg("timeout_s") = 5.0);
   m.def("embed", &embed);
   m.def("argmax_step", &argmax_step);
   m.def("ipc_alloc", &ipc_alloc);

@@ -22,6 +22,7 @@
 #include <ATen/cuda/CUDAContext.h>
 
 #include "common.cuh"
+#include "moe_route.cuh"
 #include "tp_fused.cuh"
 
 namespace hx {
@@ -58,82 +59,11 @@ struct GemvArgs {
   int v_off;                  // arg-max: global index of row 0 (vocab-parallel lm_head slice)
 };
 
-// Order-preserving key of a float (larger float -> larger key), index tiebreak to the
-// smallest index (torch.argmax semantics).
-HX_DEVICE unsigned long long argmax_key(float v, int idx) {
-  unsigned u = __float_as_uint(v);
-  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-  return ((unsigned long long)u << 32) | (unsigned)(0x7fffffff - idx);
-}
-
-// Router tail for batch row b (one warp): softmax max / denominator over E logits and
-// top-k selection. Each lane holds experts e = lane + 32 i as 64-bit keys (ordered
-// value bits, then 0x7fffffff - e, so the larger key is the larger logit and, on ties,
-// the lower expert) and its own best key (a tree max). Each round takes the warp's
-// largest key with two hardware max reductions (high word, then the low word among the
-// lanes holding that high word); only the winning lane clears the key and redoes its
-// tree max. The selected logits become softmax probabilities, optionally renormalised.
-template <int PER>
-HX_DEVICE unsigned long long tree_max(const unsigned long long (&k)[PER]) {
-  unsigned long long t[PER];
-#pragma unroll
-  for (int i = 0; i < PER; ++i) t[i] = k[i];
-#pragma unroll
-  for (int w = PER / 2; w > 0; w >>= 1)
-#pragma unroll
-    for (int i = 0; i < w; ++i) t[i] = t[i] > t[i + w] ? t[i] : t[i + w];
-  return t[0];
-}
-
 template <int PER>
 HX_DEVICE void router_tail(const GemvArgs& a, int b, int lane) {
   const float* lg = reinterpret_cast<const float*>(a.y) + (long long)b * a.ldy;
-  float v[PER];
-  unsigned long long key[PER];
-  float m = -INFINITY;
-#pragma unroll
-  for (int i = 0; i < PER; ++i) {
-    const int e = lane + 32 * i;
-    v[i] = e < a.E ? __ldcg(&lg[e]) : -INFINITY;
-    key[i] = e < a.E ? argmax_key(v[i], e) : 0ull;
-    m = fmaxf(m, v[i]);
-  }
-  m = warp_max(m);
-  float den = 0.f;
-#pragma unroll
-  for (int i = 0; i < PER; ++i) den += (lane + 32 * i) < a.E ? expf(v[i] - m) : 0.f;
-  den = warp_sum(den);
-  unsigned long long lbest = tree_max<PER>(key), mine = 0ull;
-  for (int j = 0; j < a.topk; ++j) {
-    const unsigned hi = __reduce_max_sync(0xffffffffu, (unsigned)(lbest >> 32));
-    const unsigned lo = __reduce_max_sync(0xffffffffu, (unsigned)(lbest >> 32) == hi ? (unsigned)lbest : 0u);
-    const unsigned long long win = ((unsigned long long)hi << 32) | lo;
-    if (lane == j) mine = win;
-    if (lbest == win) {
-#pragma unroll
-      for (int i = 0; i < PER; ++i)
-        if (key[i] == win) key[i] = 0ull;
-      lbest = tree_max<PER>(key);
-    }
-  }
-  float pj = 0.f;
-  int id = 0;
-  if (lane < a.topk) {
-    unsigned u = (unsigned)(mine >> 32);
-    u = (u & 0x80000000u) ? (u & 0x7fffffffu) : ~u;  // invert argmax_key's ordering map
-    id = 0x7fffffff - (int)(mine & 0xffffffffu);
-    pj = expf(__uint_as_float(u) - m) / den;
-  }
-  const float sel = warp_sum(pj);
   const int ldo = a.topk + (a.has_shared ? 1 : 0);
-  if (lane < a.topk) {
-    a.out_ids[b * ldo + lane] = id;
-    a.out_wts[b * ldo + lane] = a.norm_topk ? pj / sel : pj;
-  }
-  if (a.has_shared && lane == 0) {
-    a.out_ids[b * ldo + a.topk] = a.E;
-    a.out_wts[b * ldo + a.topk] = 1.f / (1.f + expf(-__ldcg(&lg[a.E])));
-  }
+  moe_topk_warp<PER>(lg, a.E, a.topk, a.has_shared, a.norm_topk, a.out_ids + b * ldo, a.out_wts + b * ldo, lane);
 }
 
 template <int B, int RPW, int MODE, int U>

@@ -252,7 +252,8 @@ void sample_step(torch::Tensor logits, int64_t V, torch::Tensor slots, torch::Te
   a.slots = slots.data_ptr<int>();
   a.temp = temp.data_ptr<float>(); a.top_k = top_k.data_ptr<int>(); a.top_p = top_p.data_ptr<float>();
   a.penalty = penalty.data_ptr<float>();
-  a.seed = seed.data_ptr<long long>(); a.ctr = ctr.data_ptr<long long>();
+  a.seed = reinterpret_cast<const long long*>(seed.data_ptr<int64_t>());
+  a.ctr = reinterpret_cast<long long*>(ctr.data_ptr<int64_t>());
   a.hist = hist.data_ptr<int>(); a.hist_n = hist_n.data_ptr<int>(); a.hist_at = hist_at.data_ptr<int>();
   a.hist_cap = hist_cap.data_ptr<int>();
   a.tok = tok.data_ptr<int>(); a.pos = pos.data_ptr<int>();

@@ -20,6 +20,7 @@ is captured once per batch size and replayed.
 """
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass
 from typing import Callable
 
@@ -260,13 +261,16 @@ class FastModel:
         # decode GEMV engine: "ld" (register-staged loads, csrc/gemv.cu; default: measured
         # 3.9-5.5 TB/s on the 80B shapes in isolation) or "tma" (bulk-copy ring,
         # csrc/gemv_tma.cu; 1.4-3.0 TB/s on the same shapes, kept as an option)
-        import os
         self.gemv_engine = os.environ.get("HELEXA_GEMV", "ld")
         # attention prefill: "tc" (tcgen05/TMEM, csrc/attn_prefill_tc.cu) or "mma"
         # (mma.sync tiles, csrc/attn_prefill.cu)
         self.attn_engine = os.environ.get("HELEXA_ATTN_PREFILL", "tc")
         self._tma_ok_cache: dict = {}
         self.sampler = SamplerState(max_slots, device) if device.type == "cuda" else None
+        # decode MoE block as one persistent kernel (router, top-k, experts, down and the TP
+        # exchange with grid barriers, csrc/moe_fused.cu) instead of three launches
+        self.moe_fused = os.environ.get("HELEXA_MOE_FUSED", "1") == "1" and cfg.num_experts > 0
+        self._moe_bar = torch.zeros(4, dtype=torch.int32, device=device) if device.type == "cuda" else None
         if self.C is not None:
             self._gemm_err()  # allocated before any graph capture
         self.prefill_timer = None  # optional PhaseTimer (CUDA events per prefill phase)
@@ -415,6 +419,21 @@ class FastModel:
         self._bufs[B] = nb
         return nb
 
+    _moe_fused_ok = False
+
+    def _moe_fused_call(self, lw, nb: DecodeBuffers, E: int, k: int, J: int):
+        d, cfg = self.dims, self.cfg
+        e_base, e_count = (d.e0, lw["w_gu"].shape[0]) if d.ep else (0, 0)
+        tp = {}
+        err = self._gemm_err()
+        if self.comm is not None and d.ws > 1:
+            bases, rank, slots_, ctr, err, tmo = self.comm.fused_args()
+            tp = dict(bases=bases, rank=rank, slot_elems=slots_, ctr=ctr, timeout_s=tmo)
+        self.C.moe_fused(nb.x, lw["ln2"], cfg.rms_norm_eps, lw["router"], lw["w_gu"], lw["w_d"], E, k,
+                         self.has_shared, cfg.norm_topk_prob, nb.rlogits, nb.act_moe, self._moe_bar, err,
+                         e_base, e_count, **tp)
+        self._moe_fused_ok = True
+
     def _tma(self, N: int, K: int, x_rows: int, groups: int = 1) -> bool:
         if self.gemv_engine != "tma" or self.C is None:
             return False
@@ -456,6 +475,14 @@ class FastModel:
             C.gemv_router(lw["router"], nb.x, nb.rlogits, lw["ln2"], eps, E, k, self.has_shared,
                           cfg.norm_topk_prob, nb.ids, nb.wts, nb.counter)
             Wgu, Wd = lw["w_gu"], lw["w_d"]
+            if self.moe_fused and nb.B <= 8 and not (d.ep and not self.comm.fused):
+                try:
+                    self._moe_fused_call(lw, nb, E, k, J)
+                    return
+                except RuntimeError:
+                    if self._moe_fused_ok:
+                        raise
+                    self.moe_fused = False  # refused on this device: three-kernel path
             tma_gu = self._tma(Wgu.shape[1], Wgu.shape[2], nb.B, nb.B * J)
             tma_d = self._tma(Wd.shape[1], Wd.shape[2], nb.B * J, nb.B)
             e_base, e_count = (d.e0, Wgu.shape[0]) if d.ep else (0, 0)
@@ -545,7 +572,7 @@ class FastModel:
         cfg = self.cfg
         n = 2  # embed, lm_head(+arg-max)
         for i in range(cfg.num_hidden_layers):
-            n += 3 + (3 if cfg.layer_uses_moe(i) else 2)
+            n += 3 + ((1 if self.moe_fused else 3) if cfg.layer_uses_moe(i) else 2)
             if self.comm is not None and self.dims.ws > 1:
                 n += self.comm.launches_per_reduce * 2
         return n
