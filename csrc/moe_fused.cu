@@ -409,13 +409,16 @@ void moe_fused(torch::Tensor x, torch::Tensor norm_w, double eps, torch::Tensor 
     a.tpp = t;
     a.timeout_ns = t.timeout_ns;
   }
-  const size_t smem = (size_t)B * H * 2 + (size_t)B * J * I * 2;
+  // the kernel places the activations after Bt rows of normalised x, where Bt is the
+  // template batch (B rounded up to 1, 2, 4 or 8), so size the smem with Bt
+  const int Bt = B <= 2 ? B : (B <= 4 ? 4 : 8);
+  const size_t smem = (size_t)Bt * H * 2 + (size_t)B * J * I * 2;
   TORCH_CHECK(smem <= 200 * 1024, "moe_fused: activations exceed shared memory");
   auto st = at::cuda::getCurrentCUDAStream();
-  switch (B) {
+  switch (Bt) {
     case 1: launch_moe_fused<1>(a, smem, st); break;
     case 2: launch_moe_fused<2>(a, smem, st); break;
-    case 3: case 4: launch_moe_fused<4>(a, smem, st); break;
+    case 4: launch_moe_fused<4>(a, smem, st); break;
     default: launch_moe_fused<8>(a, smem, st);
   }
 }

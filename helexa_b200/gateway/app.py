@@ -227,8 +227,11 @@ def create_gateway(catalogue: Catalogue, nodes: list[NodeState], api_keys: dict[
         for mid, e in catalogue.entries.items():
             loaded = [n.name for n in router.nodes.values() if n.models.get(mid, {}).get("status") == "loaded"]
             lim = next((n.models[mid].get("limit") for n in router.nodes.values() if mid in n.models), None)
-            data.append({"id": mid, "object": "model", "owned_by": "helexa", "aliases": e.aliases,
-                         "loaded_on": loaded, "limit": lim})
+            item = {"id": mid, "object": "model", "owned_by": "helexa", "aliases": e.aliases,
+                    "loaded_on": loaded, "limit": lim}
+            if e.cost_input_per_mtok is not None or e.cost_output_per_mtok is not None:
+                item["cost"] = {"input_per_mtok": e.cost_input_per_mtok, "output_per_mtok": e.cost_output_per_mtok}
+            data.append(item)
         return {"object": "list", "data": data}
 
     @app.get("/usage")

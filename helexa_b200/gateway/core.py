@@ -26,6 +26,9 @@ class CatalogueEntry:
     tensor_parallel: int = 1
     memory_mb: int = 0
     load_spec: dict = field(default_factory=dict)
+    # advertised price per million tokens (the reference's catalogue cost fields)
+    cost_input_per_mtok: float | None = None
+    cost_output_per_mtok: float | None = None
 
     @property
     def pinned(self) -> bool:

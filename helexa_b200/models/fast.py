@@ -268,8 +268,10 @@ class FastModel:
         self._tma_ok_cache: dict = {}
         self.sampler = SamplerState(max_slots, device) if device.type == "cuda" else None
         # decode MoE block as one persistent kernel (router, top-k, experts, down and the TP
-        # exchange with grid barriers, csrc/moe_fused.cu) instead of three launches
-        self.moe_fused = os.environ.get("HELEXA_MOE_FUSED", "1") == "1" and cfg.num_experts > 0
+        # exchange with grid barriers, csrc/moe_fused.cu) instead of three launches. Off by
+        # default: the 80B decode step measured 4.39 ms with it vs 3.95 ms with the three
+        # kernels (HELEXA_MOE_FUSED=1 turns it on)
+        self.moe_fused = os.environ.get("HELEXA_MOE_FUSED", "0") == "1" and cfg.num_experts > 0
         self._moe_bar = torch.zeros(4, dtype=torch.int32, device=device) if device.type == "cuda" else None
         if self.C is not None:
             self._gemm_err()  # allocated before any graph capture

@@ -26,6 +26,7 @@ from typing import Any
 
 import torch
 
+from ..utils.trace import span
 from .prefix_cache import PrefixCache, stable_snapshot_cut
 from .sampling import HostSampler, SamplingParams
 
@@ -170,6 +171,10 @@ class Engine:
                 raise
 
     def _join(self, req: Request):
+        with span("engine.join", slow_ms=5000, request=req.id, prompt_tokens=len(req.prompt)):
+            self._join_inner(req)
+
+    def _join_inner(self, req: Request):
         r = self.runner
         slot = self._free.pop()
         t0 = time.perf_counter()
@@ -238,6 +243,10 @@ class Engine:
         self.stats["requests"] += 1
 
     def _decode_round(self):
+        with span("engine.decode_round", slow_ms=1000, live=len(self._live)):
+            self._decode_round_inner()
+
+    def _decode_round_inner(self):
         r = self.runner
         greedy = [s for s in self._live if s.sampler is None]
         sampled = [s for s in self._live if s.sampler is not None]

@@ -17,6 +17,7 @@ import uuid
 from dataclasses import dataclass, field
 
 from .admission import AdmissionController, AdmissionRejection
+from ..utils.trace import request_span
 from .engine import Engine, FinishEvent, TokenEvent
 from .sampling import GenerationDefaults, SamplingParams
 from .tokenizer import IncrementalDetokenizer, StreamParser, parse_tool_call_body
@@ -200,6 +201,8 @@ class ServedModel:
                     if n_tool and reason == "stop":
                         reason = "tool_calls"
                     self.ema.update(len(ids) - ev.cached_tokens, ev.prefill_ms, ev.completion_tokens, ev.decode_ms)
+                    request_span(rid, self.model_id, principal, ev.prompt_tokens, ev.cached_tokens,
+                                 ev.completion_tokens, ev.prefill_ms, ev.decode_ms, ev.reason)
                     if ev.reason == "error":
                         self.status = "poisoned"
                     yield Finish(reason, ev.prompt_tokens, ev.completion_tokens, reasoning_tokens, ev.cached_tokens,

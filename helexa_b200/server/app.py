@@ -55,23 +55,99 @@ def build_info() -> dict:
             "cuda": torch.version.cuda, "python": platform.python_version(), "target": "sm_100a"}
 
 
-def discover_devices() -> dict:
-    """GPU inventory from nvidia-smi CSV (discovery.rs:205-240), with a torch fallback."""
+def classify_driver_mismatch(output: str) -> str | None:
+    """The userspace NVML version when nvidia-smi failed with the "Driver/library version
+    mismatch" error (driver libraries updated, kernel module not reloaded: every CUDA
+    call on the host fails until a reboot), "unknown" without a version, None for any
+    other failure (discovery.rs:103-158)."""
+    if "Driver/library version mismatch" not in output:
+        return None
+    for line in output.splitlines():
+        line = line.strip()
+        if line.startswith("NVML library version:"):
+            return line.split(":", 1)[1].strip() or "unknown"
+    return "unknown"
+
+
+def kernel_module_version(proc_text: str) -> str | None:
+    """Loaded kernel-module version from /proc/driver/nvidia/version's NVRM line."""
+    for line in proc_text.splitlines():
+        if line.startswith("NVRM version:"):
+            for tok in line.split():
+                parts = tok.split(".")
+                if len(parts) >= 2 and parts[0].isdigit() and parts[1].isdigit():
+                    return tok
+    return None
+
+
+def discover_devices(run=None, proc_version: str | None = None) -> dict:
+    """GPU inventory from nvidia-smi CSV (discovery.rs:205-240). A failing nvidia-smi is
+    classified: a driver/library mismatch becomes `cuda_unavailable_reason` with the
+    operator action. `run` and `proc_version` replace the subprocess / proc file in tests."""
     devices = []
     driver = None
+    reason = None
+    run = run or (lambda cmd: subprocess.run(cmd, capture_output=True, text=True, timeout=10))
     try:
-        out = subprocess.run(["nvidia-smi", "--query-gpu=index,name,memory.total,memory.free,driver_version,"
-                              "compute_cap", "--format=csv,noheader,nounits"], capture_output=True, text=True,
-                             timeout=10)
-        for line in out.stdout.strip().splitlines():
+        out = run(["nvidia-smi", "--query-gpu=index,name,memory.total,memory.free,driver_version,"
+                   "compute_cap,temperature.gpu,utilization.gpu,power.draw",
+                   "--format=csv,noheader,nounits"])
+        if out.returncode != 0:
+            user = classify_driver_mismatch((out.stdout or "") + (out.stderr or ""))
+            if user is not None:
+                if proc_version is None:
+                    try:
+                        with open("/proc/driver/nvidia/version") as f:
+                            proc_version = f.read()
+                    except OSError:
+                        proc_version = ""
+                km = kernel_module_version(proc_version) or "unknown"
+                reason = (f"host NVIDIA driver/library mismatch (userspace NVML {user} vs loaded kernel module "
+                          f"{km}): reboot the host to reload the kernel module; CUDA inference is unavailable "
+                          "until then")
+        for line in (out.stdout or "").strip().splitlines():
             f = [x.strip() for x in line.split(",")]
             if len(f) >= 6:
-                devices.append({"index": int(f[0]), "name": f[1], "memory_total_mb": int(float(f[2])),
-                                "memory_free_mb": int(float(f[3])), "compute_capability": f[5]})
+                dev = {"index": int(f[0]), "name": f[1], "memory_total_mb": int(float(f[2])),
+                       "memory_free_mb": int(float(f[3])), "compute_capability": f[5]}
+                for key, i in (("temperature_c", 6), ("utilization_pct", 7), ("power_w", 8)):
+                    try:
+                        dev[key] = float(f[i])
+                    except (IndexError, ValueError):
+                        pass
+                devices.append(dev)
                 driver = f[4]
-    except Exception:
+    except (OSError, subprocess.SubprocessError):
         pass
-    return {"devices": devices, "driver_version": driver, "hostname": platform.node()}
+    out = {"devices": devices, "driver_version": driver, "hostname": platform.node()}
+    if reason:
+        out["cuda_unavailable_reason"] = reason
+    return out
+
+
+class HealthCache:
+    """Latest device reading, refreshed every `interval_s` by a background task
+    (health.rs: nvidia-smi every 5 s) so /health never blocks on nvidia-smi."""
+
+    def __init__(self, interval_s: float = 5.0, probe=discover_devices):
+        self.interval_s = interval_s
+        self.probe = probe
+        self.reading: dict = {"devices": [], "polled_at": None}
+
+    def poll_once(self):
+        try:
+            r = self.probe()
+            self.reading = {"devices": r.get("devices", []), "polled_at": time.time(),
+                            **({"cuda_unavailable_reason": r["cuda_unavailable_reason"]}
+                               if "cuda_unavailable_reason" in r else {})}
+        except Exception:  # keep the last known reading
+            pass
+
+    async def run(self):
+        import asyncio
+        while True:
+            await asyncio.to_thread(self.poll_once)
+            await asyncio.sleep(self.interval_s)
 
 
 def create_app(registry: ModelRegistry | None = None, default_models: list[dict] | None = None) -> FastAPI:
@@ -80,6 +156,7 @@ def create_app(registry: ModelRegistry | None = None, default_models: list[dict]
     app.state.registry = reg
     app.state.activation = {"pending": [], "failed": {}, "ready": []}
     app.state.shutting_down = False
+    app.state.health_cache = HealthCache(float(os.environ.get("HELEXA_HEALTH_POLL_S", "5")))
 
     @app.middleware("http")
     async def _refuse_while_shutting_down(request, call_next):
@@ -93,6 +170,7 @@ def create_app(registry: ModelRegistry | None = None, default_models: list[dict]
     @app.on_event("startup")
     async def _prewarm():
         import asyncio
+        app.state.health_task = asyncio.get_running_loop().create_task(app.state.health_cache.run())
 
         async def load_defaults():
             for d in default_models or []:
@@ -115,6 +193,9 @@ def create_app(registry: ModelRegistry | None = None, default_models: list[dict]
     @app.on_event("shutdown")
     async def _shutdown():
         app.state.shutting_down = True
+        t = getattr(app.state, "health_task", None)
+        if t is not None:
+            t.cancel()
         await reg.unload_all()
 
     # ---- node surface ---------------------------------------------------------
@@ -146,8 +227,10 @@ def create_app(registry: ModelRegistry | None = None, default_models: list[dict]
                            "kv_available_mb": m.admission.kv_available_mb(),
                            "prefill_tok_s": round(m.ema.prefill_tok_s, 1),
                            "decode_tok_s": round(m.ema.decode_tok_s, 1)}
-        return {"status": "ok", "uptime_s": round(time.time() - START_TIME, 1), "models": models,
-                "activation": app.state.activation}
+        hc = app.state.health_cache.reading
+        status = "unavailable" if "cuda_unavailable_reason" in hc else "ok"
+        return {"status": status, "uptime_s": round(time.time() - START_TIME, 1), "models": models,
+                "activation": app.state.activation, "devices": hc}
 
     @app.get("/models")
     async def models():
@@ -306,7 +389,9 @@ def main():
     ap.add_argument("--config", help="TOML/JSON config with default_models")
     args = ap.parse_args()
     from ..config.settings import load_settings
+    from ..utils.trace import setup_logging
     settings = load_settings(args.config)
+    setup_logging(settings.get("log"), settings.get("log_format"))
     app = create_app(default_models=settings.get("default_models", []))
     uvicorn.run(app, host=settings.get("host", args.host), port=int(settings.get("port", args.port)))
 

@@ -231,3 +231,13 @@ def test_cli_gateway_config_and_status(tmp_path):
                "http://gw/v1/models": {"data": [{"id": "m1", "loaded_on": ["a"], "limit": {"context": 4096}}]}}
     out = status_report("http://gw/", get=replies.__getitem__)
     assert "Fleet health" in out and "m1" in out and "a(loaded)" in out and "ctx=4096" in out
+
+
+def test_models_listing_advertises_cost():
+    cat = Catalogue([CatalogueEntry("m1", "preset:x", cost_input_per_mtok=0.2, cost_output_per_mtok=0.8)])
+    fleet = MockFleet()
+    app = create_gateway(cat, [NodeState("a", "http://a.node")], transport=httpx.MockTransport(fleet.handler),
+                         poll_interval_s=3600)
+    with TestClient(app) as c:
+        d = c.get("/v1/models").json()["data"][0]
+        assert d["cost"] == {"input_per_mtok": 0.2, "output_per_mtok": 0.8}

@@ -100,7 +100,7 @@ def test_model_decodes_through_fused_moe_in_a_graph(monkeypatch):
     w = _realistic(cfg, random_weights(cfg, seed=0, std=0.05))
     outs = []
     for fused in ("1", "0"):
-        monkeypatch.setenv("HELEXA_MOE_FUSED", fused)
+        monkeypatch.setenv("HELEXA_MOE_FUSED", fused)  # the fused kernel is opt-in
         fm = FastModel.from_hf(cfg, w, "cuda", max_slots=1, max_len=256)
         assert fm.moe_fused == (fused == "1")
         prompt = torch.arange(40, dtype=torch.int32, device="cuda") * 7 % cfg.vocab_size

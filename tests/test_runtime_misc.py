@@ -101,3 +101,47 @@ def test_capabilities_endpoint(tmp_path):
     with TestClient(create_app()) as c:
         assert c.get("/capabilities", params={"source": str(tmp_path)}).json()["capabilities"] == ["image"]
         assert c.get("/capabilities", params={"source": str(tmp_path / "nope")}).status_code == 404
+
+
+def test_device_discovery_driver_mismatch_and_health_cache():
+    """A failing nvidia-smi with the driver/library mismatch message becomes an
+    operator-facing reason (userspace NVML version vs the loaded kernel module); a normal
+    run parses the inventory; the health cache keeps the last reading."""
+    import subprocess as sp
+
+    from helexa_b200.server.app import HealthCache, classify_driver_mismatch, discover_devices
+    msg = "Failed to initialize NVML: Driver/library version mismatch\nNVML library version: 580.159\n"
+    assert classify_driver_mismatch(msg) == "580.159"
+    assert classify_driver_mismatch("No devices were found") is None
+    bad = lambda cmd: sp.CompletedProcess(cmd, 18, stdout=msg, stderr="")  # noqa: E731
+    proc = "NVRM version: NVIDIA UNIX Open Kernel Module for x86_64  580.126.09  Release Build\n"
+    d = discover_devices(run=bad, proc_version=proc)
+    assert d["devices"] == [] and "580.159" in d["cuda_unavailable_reason"]
+    assert "580.126.09" in d["cuda_unavailable_reason"]
+    ok = lambda cmd: sp.CompletedProcess(cmd, 0, stdout="0, NVIDIA B200, 183359, 180000, 580.159, 10.0, 31, 0, 140.5\n",
+                                         stderr="")  # noqa: E731
+    d = discover_devices(run=ok)
+    assert d["driver_version"] == "580.159" and d["devices"][0]["memory_free_mb"] == 180000
+    assert d["devices"][0]["power_w"] == 140.5
+    calls = []
+    hc = HealthCache(probe=lambda: calls.append(1) or discover_devices(run=ok))
+    hc.poll_once()
+    assert hc.reading["devices"][0]["name"] == "NVIDIA B200" and hc.reading["polled_at"]
+    hc.probe = lambda: (_ for _ in ()).throw(RuntimeError("smi hung"))
+    hc.poll_once()  # a failed poll keeps the last known reading
+    assert hc.reading["devices"][0]["name"] == "NVIDIA B200"
+
+
+def test_structured_logging_and_spans(capsys):
+    import json as _json
+
+    from helexa_b200.utils.trace import request_span, setup_logging, span
+    log = setup_logging("DEBUG", "json")
+    with span("unit.work", items=3):
+        pass
+    request_span("req-1", "m", None, 10, 4, 5, 12.5, 40.0, "stop")
+    lines = [_json.loads(x) for x in capsys.readouterr().err.strip().splitlines()]
+    assert lines[0]["span"] == "unit.work" and lines[0]["items"] == 3 and lines[0]["ms"] >= 0
+    assert lines[1]["request_id"] == "req-1" and lines[1]["cached_tokens"] == 4 and lines[1]["principal"] == "anonymous"
+    setup_logging("WARNING", "text")
+    assert log.level == 30
