@@ -48,6 +48,7 @@ void gemv_tma_argmax(torch::Tensor W, torch::Tensor x, c10::optional<torch::Tens
                      c10::optional<std::vector<int64_t>> bases, int64_t rank, int64_t slot_elems,
                      c10::optional<torch::Tensor> ctr, double timeout_s);
 bool gemv_tma_ok(int64_t N, int64_t K, int64_t x_rows, int64_t groups_per_rb);
+torch::Tensor gguf_pad_q6k(torch::Tensor W);
 void sample_step(torch::Tensor logits, int64_t V, torch::Tensor slots, torch::Tensor temp, torch::Tensor top_k,
                  torch::Tensor top_p, torch::Tensor penalty, torch::Tensor seed, torch::Tensor ctr, torch::Tensor hist,
                  torch::Tensor hist_n, torch::Tensor hist_at, torch::Tensor hist_cap, torch::Tensor tok,
@@ -145,6 +146,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("out_tokens"), py::arg("step"), py::arg("v_off"), py::arg("err"), py::arg("bases") = py::none(),
         py::arg("rank") = 0, py::arg("slot_elems") = 0, py::arg("ctr") = py::none(), py::arg("timeout_s") = 5.0);
   m.def("gemv_tma_ok", &gemv_tma_ok);
+  m.def("gguf_pad_q6k", &gguf_pad_q6k);
   m.def("attn_prefill_tc", &attn_prefill_tc);
   m.def("sample_step", &sample_step);
   m.def("moe_fused", &moe_fused, py::arg("x"), py::arg("norm_w"), py::arg("eps"), py::arg("router"), py::arg("w_gu"),

@@ -77,6 +77,14 @@ HX_DEVICE bf16x8 ld_stream(const bf16x8* p) {
   return v;
 }
 
+HX_DEVICE uint4 ld_stream_u4(const uint4* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
 HX_DEVICE float silu(float x) { return x / (1.f + __expf(-x)); }
 
 // Programmatic dependent launch: wait until the previous kernel's memory is visible /

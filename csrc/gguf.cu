@@ -15,7 +15,9 @@
 
 namespace hx {
 
-enum GgufType : int { kQ8_0 = 8, kQ4_K = 12, kQ6_K = 14 };
+// kQ6_Kp: Q6_K superblocks padded from 210 to 224 bytes on the device (same bytes, a
+// 16-byte-aligned stride, so the wide-load GEMV can read them); internal type id.
+enum GgufType : int { kQ8_0 = 8, kQ4_K = 12, kQ6_K = 14, kQ6_Kp = 114 };
 
 template <int T>
 struct GgufBlock;
@@ -25,6 +27,8 @@ template <>
 struct GgufBlock<kQ4_K> { static constexpr int bytes = 144, vals = 256; };
 template <>
 struct GgufBlock<kQ6_K> { static constexpr int bytes = 210, vals = 256; };
+template <>
+struct GgufBlock<kQ6_Kp> { static constexpr int bytes = 224, vals = 256; };
 
 HX_DEVICE float half_at(const uint8_t* p) {
   unsigned short h = (unsigned short)p[0] | ((unsigned short)p[1] << 8);
@@ -61,7 +65,7 @@ HX_DEVICE void dequant8(const uint8_t* __restrict__ row, int v, float* out) {
 #pragma unroll
     for (int i = 0; i < 8; ++i) out[i] = ds * ((qb[i] >> shift) & 0xF) - dm;
   } else {
-    const uint8_t* b = row + (v >> 5) * 210;
+    const uint8_t* b = row + (v >> 5) * GgufBlock<T>::bytes;
     const int idx = (v & 31) * 8;
     const int h = idx >> 7, k = (idx & 127) >> 5, l0 = idx & 31;
     const float d = half_at(b + 208);
@@ -179,6 +183,275 @@ __global__ void __launch_bounds__(256) gguf_gemv_kernel(const uint8_t* __restric
   }
 }
 
+// ---------------------------------------------------------------------------
+// Wide-load k-quant GEMV (Q4_K, padded Q6_K): one warp per output row; eight lanes
+// share a 256-value superblock, each lane taking 32 of its values with 8- and 16-byte
+// loads (the superblock header -- scales, d, dmin -- is one 16-byte load that the eight
+// lanes share through L1). Per sub-block run the dot product is factored as
+// d * s * sum(q x) - dmin * m * sum(x), so the inner loop is integer unpacking and two
+// FMAs per value. Superblocks of several iterations are requested before any is used.
+// ---------------------------------------------------------------------------
+struct Q4Raw { uint4 hdr, qs; };            // header (d, dmin, 12 scale bytes), 16 qs bytes
+struct Q6Raw { uint2 ql0, ql1, qh; uint4 sc; uint4 dw; };
+
+template <int T>
+struct WideRaw;
+template <> struct WideRaw<kQ4_K> { using type = Q4Raw; };
+template <> struct WideRaw<kQ6_Kp> { using type = Q6Raw; };
+
+HX_DEVICE float h2f(unsigned short h) { return __half2float(__ushort_as_half(h)); }
+
+template <int T>
+HX_DEVICE void wide_load(const uint8_t* sb, int c, typename WideRaw<T>::type& r) {
+  if constexpr (T == kQ4_K) {
+    r.hdr = __ldg(reinterpret_cast<const uint4*>(sb));
+    r.qs = ld_stream_u4(reinterpret_cast<const uint4*>(sb + 16 + 16 * c));
+  } else {
+    const int h = c >> 2, l0 = (c & 3) * 8;
+    r.ql0 = __ldg(reinterpret_cast<const uint2*>(sb + 64 * h + l0));
+    r.ql1 = __ldg(reinterpret_cast<const uint2*>(sb + 64 * h + 32 + l0));
+    r.qh = __ldg(reinterpret_cast<const uint2*>(sb + 128 + 32 * h + l0));
+    r.sc = __ldg(reinterpret_cast<const uint4*>(sb + 192));
+    r.dw = __ldg(reinterpret_cast<const uint4*>(sb + 208));
+  }
+}
+
+// sum over this lane's 32 values of w * x; xs = the superblock's 256 x values (f32, smem)
+template <int T>
+HX_DEVICE float wide_dot(const typename WideRaw<T>::type& r, int c, const float* xs) {
+  if constexpr (T == kQ4_K) {
+    const uint8_t* hb = reinterpret_cast<const uint8_t*>(&r.hdr);
+    const float d = h2f(*reinterpret_cast<const unsigned short*>(hb)), dmin = h2f(*reinterpret_cast<const unsigned short*>(hb + 2));
+    const uint8_t* sc = hb + 4;
+    const int g = c >> 1, l0 = (c & 1) * 16;
+    float out = 0.f;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int j = 2 * g + half;  // sub-block: low nibbles -> 2g, high nibbles -> 2g+1
+      int s, m;
+      if (j < 4) {
+        s = sc[j] & 63;
+        m = sc[j + 4] & 63;
+      } else {
+        s = (sc[j + 4] & 0xF) | ((sc[j - 4] >> 6) << 4);
+        m = (sc[j + 4] >> 4) | ((sc[j] >> 6) << 4);
+      }
+      const float* xr = xs + j * 32 + l0;
+      const uint8_t* qb = reinterpret_cast<const uint8_t*>(&r.qs);
+      float sq = 0.f, sx = 0.f;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float q = (float)((qb[i] >> (4 * half)) & 0xF);
+        sq = fmaf(q, xr[i], sq);
+        sx += xr[i];
+      }
+      out += d * s * sq - dmin * m * sx;
+    }
+    return out;
+  } else {
+    const int h = c >> 2, l0 = (c & 3) * 8;
+    const int8_t* sc = reinterpret_cast<const int8_t*>(&r.sc);
+    const float d = h2f(*reinterpret_cast<const unsigned short*>(&r.dw));
+    const uint8_t* a = reinterpret_cast<const uint8_t*>(&r.ql0);
+    const uint8_t* b2 = reinterpret_cast<const uint8_t*>(&r.ql1);
+    const uint8_t* qh = reinterpret_cast<const uint8_t*>(&r.qh);
+    float out = 0.f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {  // value blocks 128h + 32k + l0 .. +8
+      const float* xr = xs + 128 * h + 32 * k + l0;
+      const float ds = d * sc[8 * h + (l0 >> 4) + 2 * k];
+      float sq = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int lo = (k & 1) ? b2[i] : a[i];
+        const int q = (((k >> 1) ? (lo >> 4) : lo) & 0xF) | (((qh[i] >> (2 * k)) & 3) << 4);
+        sq = fmaf((float)(q - 32), xr[i], sq);
+      }
+      out = fmaf(ds, sq, out);
+    }
+    return out;
+  }
+}
+
+template <int T, int B, int MODE>
+__global__ void __launch_bounds__(256) gguf_gemv_wide_kernel(const uint8_t* __restrict__ W, long long row_bytes,
+                                                             const __nv_bfloat16* __restrict__ x, void* y, int ldy,
+                                                             const __nv_bfloat16* resid, const float* norm_w,
+                                                             float eps, int N, int K) {
+  extern __shared__ __align__(16) float xs[];  // [B][K] f32
+  __shared__ float red[8];
+  constexpr int SB = GgufBlock<T>::bytes;
+  constexpr int U = 3;  // superblock groups (4 superblocks per warp step) in flight per lane
+  using Raw = typename WideRaw<T>::type;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n = blockIdx.x * 8 + warp;
+  const int nsb = K / 256;
+  const int c = lane & 7, sub = lane >> 3;  // lane's 32-value slice, superblock within the step
+  const bool active = n < N;
+  const uint8_t* row = W + (long long)min(n, N - 1) * row_bytes;
+  Raw cur[U];
+  // weights never depend on the previous kernel: request the first steps before the wait
+  if (active) {
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int s = min(4 * u + sub, nsb - 1);
+      wide_load<T>(row + (long long)s * SB, c, cur[u]);
+    }
+  }
+  pdl_wait_prior();
+  pdl_launch_dependents();
+  for (int b = 0; b < B; ++b) {
+    const __nv_bfloat16* xr = x + (long long)b * K;
+    float inv = 1.f;
+    if (norm_w) {
+      float ss = 0.f;
+      for (int k = threadIdx.x; k < K; k += 256) {
+        const float f = __bfloat162float(xr[k]);
+        ss += f * f;
+      }
+      ss = block_sum(ss, red);
+      inv = rsqrtf(ss / K + eps);
+    }
+    for (int k = threadIdx.x; k < K; k += 256) {
+      const float f = __bfloat162float(xr[k]);
+      xs[b * K + k] = norm_w ? __bfloat162float(__float2bfloat16(f * inv * norm_w[k])) : f;
+    }
+  }
+  __syncthreads();
+  if (!active) return;
+  float acc[B];
+#pragma unroll
+  for (int b = 0; b < B; ++b) acc[b] = 0.f;
+  for (int s0 = 0; s0 < nsb; s0 += 4 * U) {
+    Raw nxt[U];
+    const bool more = s0 + 4 * U < nsb;
+    if (more) {
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int s = min(s0 + 4 * U + 4 * u + sub, nsb - 1);
+        wide_load<T>(row + (long long)s * SB, c, nxt[u]);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int s = s0 + 4 * u + sub;
+      if (s < nsb) {
+#pragma unroll
+        for (int b = 0; b < B; ++b) acc[b] += wide_dot<T>(cur[u], c, xs + b * K + s * 256);
+      }
+    }
+    if (more) {
+#pragma unroll
+      for (int u = 0; u < U; ++u) cur[u] = nxt[u];
+    }
+  }
+#pragma unroll
+  for (int b = 0; b < B; ++b) acc[b] = warp_sum(acc[b]);
+  if (lane) return;
+#pragma unroll
+  for (int b = 0; b < B; ++b) {
+    const long long ob = (long long)b * ldy;
+    if (MODE == 3) {
+      reinterpret_cast<float*>(y)[ob + n] = acc[b];
+    } else if (MODE == 1) {
+      const float br = __bfloat162float(__float2bfloat16(acc[b]));
+      reinterpret_cast<__nv_bfloat16*>(y)[ob + n] = __float2bfloat16(__bfloat162float(resid[ob + n]) + br);
+    } else {
+      reinterpret_cast<__nv_bfloat16*>(y)[ob + n] = __float2bfloat16(acc[b]);
+    }
+  }
+}
+
+// SwiGLU over interleaved rows needs a row pair per warp: lanes 0-15 take the gate row,
+// lanes 16-31 the up row (four lanes per superblock).
+template <int T, int B>
+__global__ void __launch_bounds__(256) gguf_gemv_wide_swiglu_kernel(const uint8_t* __restrict__ W, long long row_bytes,
+                                                                    const __nv_bfloat16* __restrict__ x, void* y,
+                                                                    int ldy, const float* norm_w, float eps, int N,
+                                                                    int K) {
+  extern __shared__ __align__(16) float xs[];
+  __shared__ float red[8];
+  constexpr int SB = GgufBlock<T>::bytes;
+  constexpr int U = 3;
+  using Raw = typename WideRaw<T>::type;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int pair = blockIdx.x * 8 + warp;
+  const int nsb = K / 256;
+  const int half = lane >> 4;            // 0: gate row, 1: up row
+  const int c = lane & 7, sub = (lane >> 3) & 1;  // two superblocks per half-warp step
+  const bool active = 2 * pair + 1 < N;
+  const uint8_t* row = W + (long long)min(2 * pair + half, N - 1) * row_bytes;
+  Raw cur[U];
+  if (active) {
+#pragma unroll
+    for (int u = 0; u < U; ++u) wide_load<T>(row + (long long)min(2 * u + sub, nsb - 1) * SB, c, cur[u]);
+  }
+  pdl_wait_prior();
+  pdl_launch_dependents();
+  for (int b = 0; b < B; ++b) {
+    const __nv_bfloat16* xr = x + (long long)b * K;
+    float inv = 1.f;
+    if (norm_w) {
+      float ss = 0.f;
+      for (int k = threadIdx.x; k < K; k += 256) {
+        const float f = __bfloat162float(xr[k]);
+        ss += f * f;
+      }
+      ss = block_sum(ss, red);
+      inv = rsqrtf(ss / K + eps);
+    }
+    for (int k = threadIdx.x; k < K; k += 256) {
+      const float f = __bfloat162float(xr[k]);
+      xs[b * K + k] = norm_w ? __bfloat162float(__float2bfloat16(f * inv * norm_w[k])) : f;
+    }
+  }
+  __syncthreads();
+  if (!active) return;
+  float acc[B];
+#pragma unroll
+  for (int b = 0; b < B; ++b) acc[b] = 0.f;
+  for (int s0 = 0; s0 < nsb; s0 += 2 * U) {
+    Raw nxt[U];
+    const bool more = s0 + 2 * U < nsb;
+    if (more) {
+#pragma unroll
+      for (int u = 0; u < U; ++u) wide_load<T>(row + (long long)min(s0 + 2 * U + 2 * u + sub, nsb - 1) * SB, c, nxt[u]);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int s = s0 + 2 * u + sub;
+      if (s < nsb) {
+#pragma unroll
+        for (int b = 0; b < B; ++b) acc[b] += wide_dot<T>(cur[u], c, xs + b * K + s * 256);
+      }
+    }
+    if (more) {
+#pragma unroll
+      for (int u = 0; u < U; ++u) cur[u] = nxt[u];
+    }
+  }
+  // reduce within each half-warp (16 lanes), then lane 0 combines gate and up
+#pragma unroll
+  for (int b = 0; b < B; ++b) {
+    float v = acc[b];
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const float up = __shfl_sync(0xffffffffu, v, 16);
+    if (lane == 0) {
+      const float g = __bfloat162float(__float2bfloat16(v));
+      const float u = __bfloat162float(__float2bfloat16(up));
+      reinterpret_cast<__nv_bfloat16*>(y)[(long long)b * ldy + pair] = __float2bfloat16(silu(g) * u);
+    }
+  }
+}
+
+// 210-byte Q6_K superblocks -> 224-byte padded superblocks (same bytes + 14 zero bytes)
+__global__ void q6k_pad_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, long long nsb) {
+  const long long s = blockIdx.x * (long long)blockDim.y + threadIdx.y;
+  if (s >= nsb) return;
+  for (int i = threadIdx.x; i < 224; i += blockDim.x) dst[s * 224 + i] = i < 210 ? src[s * 210 + i] : 0;
+}
+
 template <int T>
 __global__ void gguf_dequant_kernel(const uint8_t* __restrict__ W, long long row_bytes, __nv_bfloat16* __restrict__ out,
                                     int N, int K) {
@@ -213,6 +486,46 @@ static void gg_launch(const uint8_t* W, long long rb, const torch::Tensor& x, vo
 #undef HX_GG_B
 }
 
+template <int T, int MODE>
+static void gg_wide_launch(const uint8_t* W, long long rb, const torch::Tensor& x, void* y, int ldy,
+                           const __nv_bfloat16* resid, const float* nw, float eps, int N, int K, int B,
+                           cudaStream_t st) {
+  const size_t smem = (size_t)B * K * sizeof(float);
+  auto xp = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
+#define HX_GW_B(BB)                                                                                                 \
+  {                                                                                                                 \
+    if constexpr (MODE == 2) {                                                                                      \
+      auto k = gguf_gemv_wide_swiglu_kernel<T, BB>;                                                                 \
+      if (smem + 4096 > 48 * 1024) HX_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)); \
+      HX_CUDA_CHECK(hx_launch_pdl(k, dim3((N / 2 + 7) / 8), dim3(256), smem, st, W, rb, xp, y, ldy, nw, eps, N, K)); \
+    } else {                                                                                                        \
+      auto k = gguf_gemv_wide_kernel<T, BB, MODE>;                                                                  \
+      if (smem + 4096 > 48 * 1024) HX_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)); \
+      HX_CUDA_CHECK(hx_launch_pdl(k, dim3((N + 7) / 8), dim3(256), smem, st, W, rb, xp, y, ldy, resid, nw, eps, N, K)); \
+    }                                                                                                               \
+  }
+  switch (B) {
+    case 1: HX_GW_B(1) break;
+    case 2: HX_GW_B(2) break;
+    case 4: HX_GW_B(4) break;
+    case 8: HX_GW_B(8) break;
+    default: TORCH_CHECK(false, "gguf_gemv batch must be 1, 2, 4 or 8");
+  }
+#undef HX_GW_B
+}
+
+template <int T>
+static void gg_wide_mode(int mode, const uint8_t* W, long long rb, const torch::Tensor& x, void* y, int ldy,
+                         const __nv_bfloat16* resid, const float* nw, float eps, int N, int K, int B, cudaStream_t st) {
+  switch (mode) {
+    case 0: gg_wide_launch<T, 0>(W, rb, x, y, ldy, resid, nw, eps, N, K, B, st); break;
+    case 1: gg_wide_launch<T, 1>(W, rb, x, y, ldy, resid, nw, eps, N, K, B, st); break;
+    case 2: gg_wide_launch<T, 2>(W, rb, x, y, ldy, resid, nw, eps, N, K, B, st); break;
+    case 3: gg_wide_launch<T, 3>(W, rb, x, y, ldy, resid, nw, eps, N, K, B, st); break;
+    default: TORCH_CHECK(false, "bad mode");
+  }
+}
+
 template <int T>
 static void gg_mode(int mode, const uint8_t* W, long long rb, const torch::Tensor& x, void* y, int ldy,
                     const __nv_bfloat16* resid, const float* nw, float eps, int N, int K, int B, cudaStream_t st) {
@@ -229,6 +542,7 @@ static void block_of(int t, int& bb, int& bv) {
   if (t == kQ8_0) { bb = 34; bv = 32; }
   else if (t == kQ4_K) { bb = 144; bv = 256; }
   else if (t == kQ6_K) { bb = 210; bv = 256; }
+  else if (t == kQ6_Kp) { bb = 224; bv = 256; }
   else TORCH_CHECK(false, "unsupported GGUF type ", t);
 }
 
@@ -367,8 +681,13 @@ void gguf_gemv(torch::Tensor W, int64_t type, int64_t K, torch::Tensor x, torch:
   auto rp = resid ? reinterpret_cast<const __nv_bfloat16*>(resid->data_ptr()) : nullptr;
   auto np = norm_w ? norm_w->data_ptr<float>() : nullptr;
   const long long rb = W.size(1);
-  if (type == kQ8_0) gg_mode<kQ8_0>((int)mode, wp, rb, x, y.data_ptr(), y.stride(0), rp, np, (float)eps, N, (int)K, B, st);
+  const bool wide = (type == kQ4_K || type == kQ6_Kp) && K % 256 == 0 && rb % 16 == 0 &&
+                    reinterpret_cast<uintptr_t>(W.data_ptr()) % 16 == 0 && !(mode == 2 && N % 2);
+  if (wide && type == kQ4_K) gg_wide_mode<kQ4_K>((int)mode, wp, rb, x, y.data_ptr(), y.stride(0), rp, np, (float)eps, N, (int)K, B, st);
+  else if (wide) gg_wide_mode<kQ6_Kp>((int)mode, wp, rb, x, y.data_ptr(), y.stride(0), rp, np, (float)eps, N, (int)K, B, st);
+  else if (type == kQ8_0) gg_mode<kQ8_0>((int)mode, wp, rb, x, y.data_ptr(), y.stride(0), rp, np, (float)eps, N, (int)K, B, st);
   else if (type == kQ4_K) gg_mode<kQ4_K>((int)mode, wp, rb, x, y.data_ptr(), y.stride(0), rp, np, (float)eps, N, (int)K, B, st);
+  else if (type == kQ6_Kp) gg_mode<kQ6_Kp>((int)mode, wp, rb, x, y.data_ptr(), y.stride(0), rp, np, (float)eps, N, (int)K, B, st);
   else gg_mode<kQ6_K>((int)mode, wp, rb, x, y.data_ptr(), y.stride(0), rp, np, (float)eps, N, (int)K, B, st);
 }
 
@@ -384,6 +703,7 @@ void gguf_dequant(torch::Tensor W, int64_t type, int64_t K, torch::Tensor out) {
   auto op = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   if (type == kQ8_0) gguf_dequant_kernel<kQ8_0><<<grid, 256, 0, st>>>(W.data_ptr<uint8_t>(), W.size(1), op, N, (int)K);
   else if (type == kQ4_K) gguf_dequant_kernel<kQ4_K><<<grid, 256, 0, st>>>(W.data_ptr<uint8_t>(), W.size(1), op, N, (int)K);
+  else if (type == kQ6_Kp) gguf_dequant_kernel<kQ6_Kp><<<grid, 256, 0, st>>>(W.data_ptr<uint8_t>(), W.size(1), op, N, (int)K);
   else gguf_dequant_kernel<kQ6_K><<<grid, 256, 0, st>>>(W.data_ptr<uint8_t>(), W.size(1), op, N, (int)K);
   HX_CUDA_CHECK(cudaGetLastError());
 }
@@ -404,6 +724,19 @@ torch::Tensor gguf_quant(torch::Tensor W, int64_t type) {
   if (type == kQ8_0) gguf_quant_kernel<kQ8_0><<<grid, 128, 0, st>>>(wp, N, K, out.data_ptr<uint8_t>(), out.size(1));
   else if (type == kQ4_K) gguf_quant_kernel<kQ4_K><<<grid, 128, 0, st>>>(wp, N, K, out.data_ptr<uint8_t>(), out.size(1));
   else gguf_quant_kernel<kQ6_K><<<grid, 128, 0, st>>>(wp, N, K, out.data_ptr<uint8_t>(), out.size(1));
+  HX_CUDA_CHECK(cudaGetLastError());
+  return out;
+}
+
+// Q6_K block rows [N, nsb * 210] -> padded rows [N, nsb * 224] (type kQ6_Kp).
+torch::Tensor gguf_pad_q6k(torch::Tensor W) {
+  TORCH_CHECK(W.is_cuda() && W.scalar_type() == at::kByte && W.dim() == 2 && W.is_contiguous() && W.size(1) % 210 == 0,
+              "W uint8 [N, nsb * 210]");
+  const long long N = W.size(0), nsb_row = W.size(1) / 210, nsb = N * nsb_row;
+  auto out = torch::empty({N, nsb_row * 224}, W.options());
+  if (nsb == 0) return out;
+  q6k_pad_kernel<<<(unsigned)((nsb + 7) / 8), dim3(32, 8), 0, at::cuda::getCurrentCUDAStream()>>>(
+      W.data_ptr<uint8_t>(), out.data_ptr<uint8_t>(), nsb);
   HX_CUDA_CHECK(cudaGetLastError());
   return out;
 }

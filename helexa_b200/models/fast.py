@@ -141,6 +141,7 @@ class SamplerState:
 
 # GGUF type ids (ggml): the block formats the kernels read
 GGUF_Q8_0, GGUF_Q4_K, GGUF_Q6_K = 8, 12, 14
+GGUF_Q6_K_PADDED = 114  # device-side Q6_K with superblocks padded to 224 bytes
 _GGUF_BLOCK = {GGUF_Q8_0: (34, 32), GGUF_Q4_K: (144, 256), GGUF_Q6_K: (210, 256)}
 # quantization schemes -> type per fused weight (Q4_K_M: ffn_down in Q6_K, the rest Q4_K;
 # the fused [q|k|v] projection keeps one type, so attn_v is Q4_K here)
@@ -169,6 +170,10 @@ class QWeight:
     tp/tp_linear.rs:76-139)."""
 
     def __init__(self, raw: torch.Tensor, gtype: int, K: int):
+        if gtype == GGUF_Q6_K and raw.is_cuda:
+            # 210-byte Q6_K superblocks -> a 224-byte stride (same bytes, 16-byte aligned)
+            # so the wide-load GEMV can read them
+            raw, gtype = ops.C.gguf_pad_q6k(raw.contiguous()), GGUF_Q6_K_PADDED
         self.raw, self.type, self.K = raw, gtype, K
 
     @property

@@ -70,15 +70,22 @@ def test_gguf_file_roundtrip(tmp_path):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("gt", [G.Q8_0, G.Q4_K, G.Q6_K])
-@pytest.mark.parametrize("B,mode", [(1, 0), (2, 1), (1, 2), (4, 3)])
+@pytest.mark.parametrize("gt", [G.Q8_0, G.Q4_K, G.Q6_K, 114])
+@pytest.mark.parametrize("B,mode", [(1, 0), (2, 1), (1, 2), (4, 3), (8, 0)])
 def test_gguf_gemv_and_dequant(gt, B, mode):
+    """Decode GEMV straight from the block bytes (the wide 16-byte-per-lane kernels for
+    Q4_K and padded Q6_K = type 114) and the prefill dequantization, against the host
+    codec's dequantized weights."""
     C = _C()
     torch.manual_seed(2)
-    N, K = 384, 2048
+    N, K = 384, 2048 + 256 * (gt == 114)
     w = torch.randn(N, K) * 0.02
-    raw = C.gguf_quant_host(w.view(-1), gt).view(N, -1).cuda()
-    wd = C.gguf_dequant_host(raw.cpu().view(-1), gt, N * K).view(N, K).cuda()
+    host_t = G.Q6_K if gt == 114 else gt
+    raw = C.gguf_quant_host(w.view(-1), host_t).view(N, -1).cuda()
+    wd = C.gguf_dequant_host(raw.cpu().view(-1), host_t, N * K).view(N, K).cuda()
+    if gt == 114:
+        raw = C.gguf_pad_q6k(raw)
+        assert raw.shape[1] == K // 256 * 224
     out = torch.empty(N, K, dtype=torch.bfloat16, device="cuda")
     C.gguf_dequant(raw, gt, K, out)
     torch.testing.assert_close(out.float(), wd, atol=1e-3, rtol=1e-2)

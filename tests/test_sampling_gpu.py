@@ -44,6 +44,7 @@ def test_greedy_with_penalty_and_topk1():
     st = _state(1, V, temp=0.0, penalty=1.5)
     st["hist"][0, :3] = torch.tensor([17, 17, 4], dtype=torch.int32)
     st["hist_n"][0] = 3
+    st["hist_at"][0] = 3
     # 17 is penalised once (10 / 1.5 < 9.5): the arg-max moves to 23
     assert int(_draw(lg, st, 1)[0]) == 23
     assert int(st["hist"][0, 3]) == 23 and int(st["hist_n"][0]) == 4
