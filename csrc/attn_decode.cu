@@ -38,6 +38,7 @@ struct AttnDecodeArgs {
   __nv_bfloat16* out;          // [B, Hq*D]
   int Hq, Hkv, maxlen, rot, nsplit, gated;
   float eps, scale;
+  const int* rope_delta;       // [S] rotary position - cache index (vision prompts), or nullptr
 };
 
 // RMSNorm + RoPE of one head vector held as D/32 values per lane (lane owns dims
@@ -154,6 +155,9 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(AttnDecodeArgs a) {
   pdl_launch_dependents();
   const int p = a.pos[slot];
   const int L = p + 1;
+  // rotary position of the new token: its cache index, shifted after an image whose
+  // tokens shared positions (multimodal rotary)
+  const int prot = p + (a.rope_delta ? a.rope_delta[slot] : 0);
 
   // ---- q heads: norm + rope (bf16-exact values; the softmax scale is applied to scores)
   for (int g = warp; g < G; g += NW) {
@@ -161,7 +165,7 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(AttnDecodeArgs a) {
     float xv[PER];
 #pragma unroll
     for (int i = 0; i < PER; ++i) xv[i] = __bfloat162float(pr[hq * qw + lane * PER + i]);
-    norm_rope_head<D>(xv, a.q_norm_w, a.inv_freq, a.rot, p, a.eps, tmp[warp]);
+    norm_rope_head<D>(xv, a.q_norm_w, a.inv_freq, a.rot, prot, a.eps, tmp[warp]);
 #pragma unroll
     for (int i = 0; i < PER; ++i) qsm[g][lane * PER + i] = xv[i];
   }
@@ -173,7 +177,7 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(AttnDecodeArgs a) {
     float xv[PER];
 #pragma unroll
     for (int i = 0; i < PER; ++i) xv[i] = __bfloat162float(pr[qtot + kvh * D + lane * PER + i]);
-    norm_rope_head<D>(xv, a.k_norm_w, a.inv_freq, a.rot, p, a.eps, tmp[NW - 1]);
+    norm_rope_head<D>(xv, a.k_norm_w, a.inv_freq, a.rot, prot, a.eps, tmp[NW - 1]);
 #pragma unroll
     for (int i = 0; i < PER; ++i) {
       a.kc[cache_base + (long long)p * D + lane * PER + i] = __float2bfloat16(xv[i]);
@@ -488,7 +492,7 @@ using namespace hx;
 void attn_decode(torch::Tensor proj, c10::optional<torch::Tensor> q_norm_w, c10::optional<torch::Tensor> k_norm_w,
                  torch::Tensor inv_freq, torch::Tensor kc, torch::Tensor vc, torch::Tensor slots, torch::Tensor pos,
                  torch::Tensor part_o, torch::Tensor part_ml, torch::Tensor counters, torch::Tensor out, int64_t Hq,
-                 int64_t Hkv, int64_t D, int64_t rot, bool gated, double eps) {
+                 int64_t Hkv, int64_t D, int64_t rot, bool gated, double eps, c10::optional<torch::Tensor> rope_delta) {
   TORCH_CHECK(kc.scalar_type() == at::kBFloat16 && kc.dim() == 4 && kc.size(3) == D, "kc [S,Hkv,maxlen,D] bf16");
   TORCH_CHECK(kc.size(1) == Hkv, "kv head count mismatch");
   AttnDecodeArgs a{};
@@ -508,6 +512,10 @@ void attn_decode(torch::Tensor proj, c10::optional<torch::Tensor> q_norm_w, c10:
   a.Hq = Hq; a.Hkv = Hkv; a.maxlen = kc.size(2); a.rot = rot; a.gated = gated;
   a.nsplit = part_o.size(2);
   a.eps = (float)eps; a.scale = 1.f / sqrtf((float)D);
+  if (rope_delta) {
+    TORCH_CHECK(rope_delta->scalar_type() == at::kInt && rope_delta->numel() >= kc.size(0), "rope_delta int32 [S]");
+    a.rope_delta = rope_delta->data_ptr<int>();
+  }
   const int B = slots.numel();
   TORCH_CHECK(part_o.size(0) >= B && part_o.size(1) == Hq && part_o.size(3) == D, "part_o shape");
   TORCH_CHECK(counters.numel() >= B * Hkv, "counters too small");

@@ -15,7 +15,7 @@ void gdn_decode(torch::Tensor proj, torch::Tensor conv_w, torch::Tensor conv_rin
 void attn_decode(torch::Tensor proj, c10::optional<torch::Tensor> q_norm_w, c10::optional<torch::Tensor> k_norm_w,
                  torch::Tensor inv_freq, torch::Tensor kc, torch::Tensor vc, torch::Tensor slots, torch::Tensor pos,
                  torch::Tensor part_o, torch::Tensor part_ml, torch::Tensor counters, torch::Tensor out, int64_t Hq,
-                 int64_t Hkv, int64_t D, int64_t rot, bool gated, double eps);
+                 int64_t Hkv, int64_t D, int64_t rot, bool gated, double eps, c10::optional<torch::Tensor> rope_delta);
 void gemv_ar(torch::Tensor W, torch::Tensor inp, torch::Tensor x, std::vector<int64_t> bases, int64_t rank,
              int64_t slot_elems, torch::Tensor epoch, torch::Tensor err, double timeout_s);
 void moe_down_ar(torch::Tensor Wd, torch::Tensor act, torch::Tensor ids, torch::Tensor wts, torch::Tensor x,
@@ -26,7 +26,8 @@ void attn_prefill(torch::Tensor q, torch::Tensor kc, torch::Tensor vc, torch::Te
 void add_rmsnorm(torch::Tensor x, c10::optional<torch::Tensor> o, torch::Tensor w, torch::Tensor h, double eps);
 void qk_rope_kv(torch::Tensor qkv, int64_t Hq, int64_t Hkv, int64_t D, int64_t qw, c10::optional<torch::Tensor> q_norm,
                 c10::optional<torch::Tensor> k_norm, torch::Tensor inv_freq, int64_t rot, torch::Tensor kc,
-                torch::Tensor vc, int64_t p0, torch::Tensor q_out, double eps);
+                torch::Tensor vc, int64_t p0, torch::Tensor q_out, double eps, c10::optional<torch::Tensor> pos3,
+                c10::optional<torch::Tensor> axes, int64_t rope_off);
 void conv_ring_update(torch::Tensor proj, torch::Tensor ring, int64_t p0);
 void rs_norm_ag(std::vector<int64_t> bases, int64_t rank, int64_t stage_off, int64_t h_off, torch::Tensor x,
                 torch::Tensor w, double eps, torch::Tensor ctr, torch::Tensor err, double timeout_s, int64_t ctas);
@@ -127,11 +128,17 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_route_prefill", &moe_route_prefill);
   m.def("gemm_grouped_dev", &gemm_grouped_dev);
   m.def("gdn_decode", &gdn_decode);
-  m.def("attn_decode", &attn_decode);
+  m.def("attn_decode", &attn_decode, py::arg("proj"), py::arg("q_norm_w"), py::arg("k_norm_w"), py::arg("inv_freq"),
+        py::arg("kc"), py::arg("vc"), py::arg("slots"), py::arg("pos"), py::arg("part_o"), py::arg("part_ml"),
+        py::arg("counters"), py::arg("out"), py::arg("Hq"), py::arg("Hkv"), py::arg("D"), py::arg("rot"),
+        py::arg("gated"), py::arg("eps"), py::arg("rope_delta") = py::none());
   m.def("attn_prefill", &attn_prefill, py::arg("q"), py::arg("kc"), py::arg("vc"), py::arg("out"), py::arg("Hq"),
         py::arg("p0"), py::arg("scale"), py::arg("gate") = py::none(), py::arg("gate_head_stride") = 0);
   m.def("add_rmsnorm", &add_rmsnorm);
-  m.def("qk_rope_kv", &qk_rope_kv);
+  m.def("qk_rope_kv", &qk_rope_kv, py::arg("qkv"), py::arg("Hq"), py::arg("Hkv"), py::arg("D"), py::arg("qw"),
+        py::arg("q_norm"), py::arg("k_norm"), py::arg("inv_freq"), py::arg("rot"), py::arg("kc"), py::arg("vc"),
+        py::arg("p0"), py::arg("q_out"), py::arg("eps"), py::arg("pos3") = py::none(), py::arg("axes") = py::none(),
+        py::arg("rope_off") = 0);
   m.def("conv_ring_update", &conv_ring_update);
   m.def("rs_norm_ag", &rs_norm_ag);
   m.def("rs_norm_ag_flag_bytes", &rs_norm_ag_flag_bytes);

@@ -81,6 +81,9 @@ struct QKRopeArgs {
   __nv_bfloat16* vc;
   int maxlen, T, p0, Hq, Hkv, rot;
   float eps;
+  const int* pos3;           // [3, T] multimodal rotary positions (t, h, w), or nullptr
+  const signed char* axes;   // [rot / 2] axis each rotary frequency reads (0 t, 1 h, 2 w)
+  int rope_off;              // rotary position - cache index for text after an image
 };
 
 // One warp per (token, head) over Hq query heads, then Hkv key heads, then Hkv value
@@ -132,8 +135,10 @@ __global__ void __launch_bounds__(256) qk_rope_kv_kernel(QKRopeArgs a) {
     for (int i = 0; i < EPL; ++i) {
       const int d = lane * EPL + i;
       if (d < a.rot) {
+        const int f = d < half ? d : d - half;
+        const int rp = a.pos3 ? a.pos3[a.axes[f] * a.T + t] : pos + a.rope_off;
         float s, c;
-        sincosf((float)pos * a.inv_freq[d < half ? d : d - half], &s, &c);
+        sincosf((float)rp * a.inv_freq[f], &s, &c);
         v[i] = v[i] * c + pv[i] * s;
       }
     }
@@ -190,7 +195,8 @@ void add_rmsnorm(torch::Tensor x, c10::optional<torch::Tensor> o, torch::Tensor 
 // [T, Hq*D] bf16.
 void qk_rope_kv(torch::Tensor qkv, int64_t Hq, int64_t Hkv, int64_t D, int64_t qw, c10::optional<torch::Tensor> q_norm,
                 c10::optional<torch::Tensor> k_norm, torch::Tensor inv_freq, int64_t rot, torch::Tensor kc,
-                torch::Tensor vc, int64_t p0, torch::Tensor q_out, double eps) {
+                torch::Tensor vc, int64_t p0, torch::Tensor q_out, double eps, c10::optional<torch::Tensor> pos3,
+                c10::optional<torch::Tensor> axes, int64_t rope_off) {
   TORCH_CHECK(qkv.scalar_type() == at::kBFloat16 && qkv.stride(1) == 1 && qkv.dim() == 2, "qkv [T, *] bf16");
   const int T = qkv.size(0);
   TORCH_CHECK(qkv.size(1) >= Hq * qw + 2 * Hkv * D, "qkv too narrow");
@@ -212,6 +218,15 @@ void qk_rope_kv(torch::Tensor qkv, int64_t Hq, int64_t Hkv, int64_t D, int64_t q
   a.kc = reinterpret_cast<__nv_bfloat16*>(kc.data_ptr());
   a.vc = reinterpret_cast<__nv_bfloat16*>(vc.data_ptr());
   a.maxlen = kc.size(1); a.T = T; a.p0 = p0; a.Hq = Hq; a.Hkv = Hkv; a.rot = rot; a.eps = (float)eps;
+  a.rope_off = (int)rope_off;
+  if (pos3) {
+    TORCH_CHECK(axes.has_value() && pos3->scalar_type() == at::kInt && pos3->is_contiguous() && pos3->dim() == 2 &&
+                    pos3->size(0) == 3 && pos3->size(1) == T && axes->scalar_type() == at::kChar &&
+                    axes->numel() >= rot / 2,
+                "pos3 int32 [3, T] and axes int8 [rot/2]");
+    a.pos3 = pos3->data_ptr<int>();
+    a.axes = reinterpret_cast<const signed char*>(axes->data_ptr<int8_t>());
+  }
   const long long warps = (long long)T * (Hq + 2 * Hkv);
   dim3 grid((unsigned)((warps + 7) / 8));
   auto st = at::cuda::getCurrentCUDAStream();

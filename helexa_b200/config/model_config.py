@@ -61,6 +61,11 @@ class ModelConfig:
     linear_value_head_dim: int = 0
     linear_conv_kernel_dim: int = 4
     rope_scaling: dict | None = None  # e.g. {"rope_type": "llama3", "factor": 8, ...}
+    # multimodal rotary (vision-language checkpoints): [temporal, height, width] split of
+    # the rotary half-dim, interleaved per frequency (Qwen3-VL) or in blocks (Qwen2-VL)
+    mrope_section: list[int] = field(default_factory=list)
+    mrope_interleaved: bool = True
+    vision: dict | None = None         # the checkpoint's vision_config, when present
     # bookkeeping
     name: str = ""
     eos_token_ids: list[int] = field(default_factory=list)
@@ -223,6 +228,11 @@ class ModelConfig:
             family = "llama"
         else:
             raise ValueError(f"unsupported model_type {mt!r} (architectures {archs})")
+        vision = raw.get("vision_config")
+        if "text_config" in raw:  # vision-language checkpoints nest the LM config
+            outer = raw
+            raw = dict(raw["text_config"])
+            raw.setdefault("vocab_size", outer.get("vocab_size"))
         rope = raw.get("rope_parameters") or raw.get("rope_scaling") or {}
         theta = float(rope.get("rope_theta", raw.get("rope_theta", 1e6)))
         prf = float(raw.get("partial_rotary_factor", rope.get("partial_rotary_factor",
@@ -264,6 +274,9 @@ class ModelConfig:
             linear_value_head_dim=int(raw.get("linear_value_head_dim", 0) or 0),
             linear_conv_kernel_dim=int(raw.get("linear_conv_kernel_dim", 4) or 4),
             eos_token_ids=eos_ids, bos_token_id=raw.get("bos_token_id"),
+            mrope_section=list(rope.get("mrope_section") or []),
+            mrope_interleaved=bool(rope.get("mrope_interleaved", True)),
+            vision=vision,
         )
 
     @classmethod

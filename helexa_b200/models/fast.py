@@ -272,6 +272,15 @@ class FastModel:
         self.attn_engine = os.environ.get("HELEXA_ATTN_PREFILL", "tc")
         self._tma_ok_cache: dict = {}
         self.sampler = SamplerState(max_slots, device) if device.type == "cuda" else None
+        # multimodal rotary (vision-language configs): per-frequency axis map, and per slot
+        # the rotary position minus the cache index (negative after an image)
+        self.mrope = bool(cfg.mrope_section)
+        self.rope_delta = torch.zeros(max_slots, dtype=torch.int32, device=device)
+        self._rope_delta_host = [0] * max_slots
+        self.mrope_axes = None
+        if self.mrope:
+            from .mrope import mrope_axis_map
+            self.mrope_axes = mrope_axis_map(cfg.rotary_dim // 2, cfg.mrope_section, cfg.mrope_interleaved).to(device)
         # decode MoE block as one persistent kernel (router, top-k, experts, down and the TP
         # exchange with grid barriers, csrc/moe_fused.cu) instead of three launches. Off by
         # default: the 80B decode step measured 4.39 ms with it vs 3.95 ms with the three
@@ -474,7 +483,7 @@ class FastModel:
             self._gemv(lw["w_qkv"], nb.x, nb.proj_attn, ops.STORE_BF16, None, lw["ln1"], eps)
             C.attn_decode(nb.proj_attn, lw.get("q_norm"), lw.get("k_norm"), self.inv_freq, self.kc[i], self.vc[i],
                           nb.slots, self.pos, nb.part_o, nb.part_ml, nb.counters, nb.attn_out, d.hq, d.hkv, d.D,
-                          cfg.rotary_dim, cfg.attn_output_gate, eps)
+                          cfg.rotary_dim, cfg.attn_output_gate, eps, self.rope_delta if self.mrope else None)
             self._row_parallel(lw["o_w"], nb.attn_out, nb)
         if cfg.layer_uses_moe(i):
             E, k = cfg.num_experts, cfg.num_experts_per_tok
@@ -851,8 +860,10 @@ class FastModel:
             # q/k-norm + partial RoPE + KV-cache append in one kernel; the sigmoid output
             # gate is applied in the attention kernel's epilogue
             q = torch.empty(T, d.hq * D, dtype=torch.bfloat16, device=h.device)
+            pos3 = self._pos3
             self.C.qk_rope_kv(qkv, d.hq, d.hkv, D, d.qw, lw.get("q_norm"), lw.get("k_norm"), self.inv_freq,
-                              cfg.rotary_dim, self.kc[i][slot], self.vc[i][slot], p0, q, cfg.rms_norm_eps)
+                              cfg.rotary_dim, self.kc[i][slot], self.vc[i][slot], p0, q, cfg.rms_norm_eps,
+                              pos3, self.mrope_axes if pos3 is not None else None, self._rope_delta_host[slot])
             o = torch.empty(T, d.hq * D, dtype=torch.bfloat16, device=h.device)
             gate = qkv[:, D:] if cfg.attn_output_gate else None
             if self.attn_engine == "tc":
@@ -956,27 +967,48 @@ class FastModel:
         return out
 
     @torch.no_grad()
-    def prefill(self, slot: int, tokens: torch.Tensor, p0: int) -> torch.Tensor:
+    _pos3 = None
+
+    @torch.no_grad()
+    def prefill(self, slot: int, tokens: torch.Tensor | None, p0: int, embeds: torch.Tensor | None = None,
+                pos3: torch.Tensor | None = None, next_pos: int | None = None) -> torch.Tensor:
         """Run `tokens` (device int tensor [T]) for `slot` starting at position p0.
 
         Updates the slot's KV / GDN state and position; returns the last token's
         f32 logits [V]. Prompts longer than `prefill_cap` run as consecutive chunks.
+        Vision-language prompts pass `embeds` [T, H] (image tokens spliced in) instead of
+        token ids, their M-RoPE positions `pos3` [3, T] and `next_pos`, the rotary
+        position of the token after the prompt (models/mrope.py).
         """
-        T = tokens.shape[0]
+        T = tokens.shape[0] if tokens is not None else embeds.shape[0]
         if p0 + T > self.max_len:
             raise ValueError(f"sequence of {p0 + T} tokens exceeds max_len {self.max_len}")
+        if pos3 is not None and not self.mrope:
+            raise ValueError("multimodal positions need a config with mrope_section")
         cap = self.prefill_cap
         logits = None
         for s in range(0, T, cap):
-            logits = self._prefill_chunk(slot, tokens[s:s + cap], p0 + s)
+            self._pos3 = pos3[:, s:s + cap].to(self.device, torch.int32).contiguous() if pos3 is not None else None
+            logits = self._prefill_chunk(slot, tokens[s:s + cap] if tokens is not None else None, p0 + s,
+                                         embeds[s:s + cap] if embeds is not None else None)
+        self._pos3 = None
+        if next_pos is not None:
+            self.set_rope_delta(slot, next_pos - (p0 + T))
         return logits
 
-    def _prefill_chunk(self, slot: int, tokens: torch.Tensor, p0: int) -> torch.Tensor:
+    def set_rope_delta(self, slot: int, delta: int):
+        self._rope_delta_host[slot] = int(delta)
+        self.rope_delta[slot] = int(delta)
+
+    def _prefill_chunk(self, slot: int, tokens: torch.Tensor | None, p0: int,
+                       embeds: torch.Tensor | None = None) -> torch.Tensor:
         cfg = self.cfg
-        T = tokens.shape[0]
+        T = tokens.shape[0] if tokens is not None else embeds.shape[0]
         H = cfg.hidden_size
         L = cfg.num_hidden_layers
-        if self.C is not None:
+        if embeds is not None:
+            x = embeds.to(device=self.device, dtype=torch.bfloat16).contiguous().clone()
+        elif self.C is not None:
             x = torch.empty(T, H, dtype=torch.bfloat16, device=self.device)
             self.C.embed(self.embed_w, tokens.to(torch.int32).contiguous(), x)
         else:

@@ -158,13 +158,14 @@ def delta_rule_chunked(q, k, v, g, beta, state, chunk: int = 64):
 class RefState:
     """Per-sequence cache: K/V per full-attention layer, conv+recurrent per GDN layer."""
     length: int = 0
+    rope_delta: int = 0        # rotary position - cache index (negative after an image)
     k: dict[int, torch.Tensor] = field(default_factory=dict)       # [L, Hkv, D]
     v: dict[int, torch.Tensor] = field(default_factory=dict)
     conv: dict[int, torch.Tensor] = field(default_factory=dict)    # [C, K-1]
     rec: dict[int, torch.Tensor] = field(default_factory=dict)     # [Hv, Dk, Dv] f32
 
     def clone(self) -> "RefState":
-        return RefState(self.length,
+        return RefState(self.length, self.rope_delta,
                         {i: t.clone() for i, t in self.k.items()},
                         {i: t.clone() for i, t in self.v.items()},
                         {i: t.clone() for i, t in self.conv.items()},
@@ -198,7 +199,7 @@ class ReferenceModel:
         return RefState()
 
     # ---- blocks ---------------------------------------------------------
-    def _attn(self, i: int, x: torch.Tensor, st: RefState, pos0: int) -> torch.Tensor:
+    def _attn(self, i: int, x: torch.Tensor, st: RefState, pos0: int, pos3=None) -> torch.Tensor:
         c, p = self.cfg, f"model.layers.{i}.self_attn."
         T = x.shape[0]
         H, Hk, D = c.num_attention_heads, c.num_key_value_heads, c.head_dim
@@ -213,8 +214,14 @@ class ReferenceModel:
         if c.qk_norm:
             q = rms_norm(q, self.w[p + "q_norm.weight"], c.rms_norm_eps, c.norm_offset).to(x.dtype)
             k = rms_norm(k, self.w[p + "k_norm.weight"], c.rms_norm_eps, c.norm_offset).to(x.dtype)
-        pos = torch.arange(pos0, pos0 + T, device=x.device)
-        cos, sin = rope_cos_sin(pos, c.rotary_dim, c.rope_theta, c.rope_inv_freq())
+        if pos3 is not None:  # multimodal rotary: per-token (t, h, w) positions
+            from .mrope import mrope_axis_map, mrope_cos_sin
+            inv = c.rope_inv_freq()
+            axes = mrope_axis_map(inv.numel(), c.mrope_section, c.mrope_interleaved)
+            cos, sin = mrope_cos_sin(pos3.to(x.device), inv.to(x.device), axes.to(x.device))
+        else:
+            pos = torch.arange(pos0, pos0 + T, device=x.device) + st.rope_delta
+            cos, sin = rope_cos_sin(pos, c.rotary_dim, c.rope_theta, c.rope_inv_freq())
         q = apply_rope(q.float(), cos, sin).to(x.dtype)
         k = apply_rope(k.float(), cos, sin).to(x.dtype)
         if i in st.k:
@@ -299,23 +306,32 @@ class ReferenceModel:
 
     # ---- forward ----------------------------------------------------------
     @torch.no_grad()
-    def forward(self, tokens: torch.Tensor, st: RefState, all_logits: bool = False) -> torch.Tensor:
+    def forward(self, tokens: torch.Tensor, st: RefState, all_logits: bool = False, embeds=None, pos3=None,
+                next_pos: int | None = None) -> torch.Tensor:
         """Run `tokens` ([T] int64) after the state's current length. Returns fp32 logits
-        of the last token ([V]) or of every token ([T, V])."""
+        of the last token ([V]) or of every token ([T, V]). Vision-language prompts pass
+        `embeds` [T, H] (image tokens spliced in), their M-RoPE positions `pos3` [3, T]
+        and `next_pos`, the rotary position of the token after the prompt."""
         c = self.cfg
-        tokens = tokens.to(self.device)
         pos0 = st.length
-        x = self.w["model.embed_tokens.weight"][tokens]
+        if embeds is not None:
+            x = embeds.to(device=self.device, dtype=self.dtype)
+        else:
+            tokens = tokens.to(self.device)
+            x = self.w["model.embed_tokens.weight"][tokens]
         for i in range(c.num_hidden_layers):
             p = f"model.layers.{i}."
             h = rms_norm(x, self.w[p + "input_layernorm.weight"], c.rms_norm_eps, c.norm_offset).to(x.dtype)
-            h = self._gdn(i, h, st) if c.is_linear(i) else self._attn(i, h, st, pos0)
+            h = self._gdn(i, h, st) if c.is_linear(i) else self._attn(i, h, st, pos0, pos3)
             x = x + h
             h = rms_norm(x, self.w[p + "post_attention_layernorm.weight"], c.rms_norm_eps,
                          c.norm_offset).to(x.dtype)
             h = self._moe(i, h) if c.layer_uses_moe(i) else self._mlp(p + "mlp.", h)
             x = x + h
-        st.length += tokens.shape[0]
+        T = x.shape[0]
+        st.length += T
+        if next_pos is not None:
+            st.rope_delta = next_pos - st.length
         if not all_logits:
             x = x[-1:]
         x = rms_norm(x, self.w["model.norm.weight"], c.rms_norm_eps, c.norm_offset).to(x.dtype)

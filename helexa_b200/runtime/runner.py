@@ -20,6 +20,7 @@ class Snapshot:
     conv: dict = field(default_factory=dict)   # layer -> ring / conv state
     rec: dict = field(default_factory=dict)    # layer -> recurrent state
     ref_state: object = None                   # CPU reference model state
+    rope_delta: int = 0                        # multimodal rotary offset at the cut
 
     @property
     def nbytes(self) -> int:
@@ -59,6 +60,7 @@ class FastRunner:
     def reset(self, slot: int):
         m = self.m
         m.pos[slot] = 0
+        m.set_rope_delta(slot, 0)
         for t in m.rec.values():
             t[slot].zero_()
         for t in m.conv.values():
@@ -149,6 +151,7 @@ class FastRunner:
         for i in m.conv:
             snap.conv[i] = m.conv[i][slot].clone()
             snap.rec[i] = m.rec[i][slot].clone()
+        snap.rope_delta = m._rope_delta_host[slot]
         return snap
 
     def restore(self, slot: int, snap: Snapshot):
@@ -161,6 +164,7 @@ class FastRunner:
             m.conv[i][slot] = snap.conv[i]
             m.rec[i][slot] = snap.rec[i]
         m.pos[slot] = L
+        m.set_rope_delta(slot, snap.rope_delta)
         self.host_pos[slot] = L
 
 
