@@ -966,7 +966,6 @@ class FastModel:
         self.C.moe_combine(y, rows, wts, out)
         return out
 
-    @torch.no_grad()
     _pos3 = None
 
     @torch.no_grad()
