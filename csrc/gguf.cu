@@ -8,6 +8,7 @@
 //   gguf_dequant  rows -> bf16, for the prefill GEMM.
 //
 // Replaces candle's QMatMul GEMV / dequant-then-cuBLAS switch (tp/tp_linear.rs:76-139).
+#include <cstdlib>
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 
@@ -445,6 +446,249 @@ __global__ void __launch_bounds__(256) gguf_gemv_wide_swiglu_kernel(const uint8_
   }
 }
 
+// ---------------------------------------------------------------------------
+// Integer-dot k-quant GEMV. The activation row is quantized once per call to int8 in
+// blocks of 32 values (scale = max|x| / 127, the same block size as a k-quant
+// sub-block) with the exact float sum of every 8 values kept beside it. The weight
+// loop then needs no int->float conversion per value: four 4-bit or 6-bit weights and
+// four int8 activations meet in one dp4a, and each 8- or 16-value run costs one
+// float multiply-add for its scale and one for its offset (Q4_K: dmin * m * sum(x),
+// Q6_K: 32 * sum(x)). The float-per-value kernels above issue about 8 instructions per
+// weight value and stall on their shared-memory x reads; at 4.5 bits per value that
+// caps them near 1 TB/s on B200, below HBM speed.
+//
+// x is read straight from global memory (L1-resident: every warp of a CTA walks the
+// same row), so there is no shared-memory staging and no limit on K or the batch.
+// ---------------------------------------------------------------------------
+
+// x [B, K] bf16 (optionally RMS-normalised by norm_w and rounded to bf16 first, as the
+// float kernels do) -> xq int8 [B, K], xd f32 [B, K/32] block scales, xs8 f32 [B, K/8]
+// sums of the (normalised) values. One CTA per batch row.
+__global__ void __launch_bounds__(512) gguf_quant_x_kernel(const __nv_bfloat16* __restrict__ x, const float* norm_w,
+                                                           float eps, int K, int8_t* __restrict__ xq,
+                                                           float* __restrict__ xd, float* __restrict__ xs8) {
+  __shared__ float red[16];
+  pdl_wait_prior();
+  pdl_launch_dependents();
+  const int b = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const __nv_bfloat16* xr = x + (long long)b * K;
+  float inv = 1.f;
+  if (norm_w) {
+    float ss = 0.f;
+    for (int k = threadIdx.x; k < K; k += blockDim.x) {
+      const float f = __bfloat162float(xr[k]);
+      ss += f * f;
+    }
+    ss = block_sum(ss, red);
+    inv = rsqrtf(ss / K + eps);
+  }
+  for (int blk = warp; blk < K / 32; blk += nw) {
+    const int k = blk * 32 + lane;
+    float v = __bfloat162float(xr[k]);
+    if (norm_w) v = __bfloat162float(__float2bfloat16(v * inv * norm_w[k]));
+    const float amax = warp_max(fabsf(v));
+    const float scale = amax > 0.f ? 127.f / amax : 0.f;
+    const int q = max(-127, min(127, __float2int_rn(v * scale)));
+    xq[(long long)b * K + k] = (int8_t)q;
+    float s8 = v;
+    s8 += __shfl_xor_sync(0xffffffffu, s8, 1);
+    s8 += __shfl_xor_sync(0xffffffffu, s8, 2);
+    s8 += __shfl_xor_sync(0xffffffffu, s8, 4);
+    if ((lane & 7) == 0) xs8[(long long)b * (K / 8) + k / 8] = s8;
+    if (lane == 0) xd[(long long)b * (K / 32) + blk] = amax / 127.f;
+  }
+}
+
+HX_DEVICE int lop_nib(unsigned w, int hi) { return (int)((hi ? (w >> 4) : w) & 0x0F0F0F0Fu); }
+
+// This lane's share of one superblock (the same value slices as wide_dot) against the
+// quantized activations of that superblock: q = 256 int8, d = 8 block scales, s8 = 32
+// sums of 8.
+template <int T>
+HX_DEVICE float q8_dot(const typename WideRaw<T>::type& r, int c, const int8_t* q, const float* d8,
+                       const float* s8) {
+  // every field is pulled out of the loaded words with shifts: a byte pointer into a
+  // register struct indexed by the lane would put the struct in local memory
+  if constexpr (T == kQ4_K) {
+    const float d = h2f((unsigned short)(r.hdr.x & 0xFFFFu)), dmin = h2f((unsigned short)(r.hdr.x >> 16));
+    const int g = c >> 1, l0 = (c & 1) * 16, sh = 8 * ((2 * g) & 3);
+    const unsigned qw[4] = {r.qs.x, r.qs.y, r.qs.z, r.qs.w};
+    float out = 0.f;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int j = 2 * g + half;  // sub-block: low nibbles -> 2g, high nibbles -> 2g+1
+      const int sj = sh + 8 * half;
+      const unsigned by = (r.hdr.y >> sj) & 0xFFu, bz = (r.hdr.z >> sj) & 0xFFu, bw = (r.hdr.w >> sj) & 0xFFu;
+      int s, m;
+      if (j < 4) {
+        s = by & 63;
+        m = bz & 63;
+      } else {
+        s = (bw & 0xF) | ((by >> 6) << 4);
+        m = (bw >> 4) | ((bz >> 6) << 4);
+      }
+      const int4 xv = __ldg(reinterpret_cast<const int4*>(q + j * 32 + l0));
+      int acc = __dp4a(lop_nib(qw[0], half), xv.x, 0);
+      acc = __dp4a(lop_nib(qw[1], half), xv.y, acc);
+      acc = __dp4a(lop_nib(qw[2], half), xv.z, acc);
+      acc = __dp4a(lop_nib(qw[3], half), xv.w, acc);
+      const int e = (j * 32 + l0) >> 3;
+      out = fmaf(d * (float)s * __ldg(&d8[j]), (float)acc, out);
+      out = fmaf(-dmin * (float)m, __ldg(&s8[e]) + __ldg(&s8[e + 1]), out);
+    }
+    return out;
+  } else {
+    const int h = c >> 2, l0 = (c & 3) * 8;
+    const float d = h2f((unsigned short)(r.dw.x & 0xFFFFu));
+    // the lane's four scales sit at byte 8h + (l0 >> 4) + 2k, k = 0..3: words 2h and 2h+1
+    const unsigned sw0 = h ? r.sc.z : r.sc.x, sw1 = h ? r.sc.w : r.sc.y;
+    const int sb = 8 * (l0 >> 4);
+    float out = 0.f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {  // value runs 128h + 32k + l0 .. +8
+      const uint2 lo = (k & 1) ? r.ql1 : r.ql0;
+      const int hi = k >> 1;
+      const int w0 = lop_nib(lo.x, hi) | (int)(((r.qh.x >> (2 * k)) & 0x03030303u) << 4);
+      const int w1 = lop_nib(lo.y, hi) | (int)(((r.qh.y >> (2 * k)) & 0x03030303u) << 4);
+      const int o = 128 * h + 32 * k + l0;
+      const int2 xv = __ldg(reinterpret_cast<const int2*>(q + o));
+      const int acc = __dp4a(w1, xv.y, __dp4a(w0, xv.x, 0));
+      const unsigned sw = k < 2 ? sw0 : sw1;
+      const int scv = (int)(signed char)((sw >> (sb + 16 * (k & 1))) & 0xFFu);
+      out = fmaf(d * (float)scv, fmaf(__ldg(&d8[o >> 5]), (float)acc, -32.f * __ldg(&s8[o >> 3])), out);
+    }
+    return out;
+  }
+}
+
+template <int T, int B, int MODE>
+__global__ void __launch_bounds__(256) gguf_gemv_q8_kernel(const uint8_t* __restrict__ W, long long row_bytes,
+                                                           const int8_t* __restrict__ xq, const float* __restrict__ xd,
+                                                           const float* __restrict__ xs8, void* y, int ldy,
+                                                           const __nv_bfloat16* resid, int N, int K) {
+  constexpr int SB = GgufBlock<T>::bytes;
+  constexpr int U = 3;
+  using Raw = typename WideRaw<T>::type;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n = blockIdx.x * 8 + warp;
+  const int nsb = K / 256;
+  const int c = lane & 7, sub = lane >> 3;
+  const bool active = n < N;
+  const uint8_t* row = W + (long long)min(n, N - 1) * row_bytes;
+  Raw cur[U];
+  if (active) {
+#pragma unroll
+    for (int u = 0; u < U; ++u) wide_load<T>(row + (long long)min(4 * u + sub, nsb - 1) * SB, c, cur[u]);
+  }
+  pdl_wait_prior();
+  pdl_launch_dependents();
+  if (!active) return;
+  float acc[B];
+#pragma unroll
+  for (int b = 0; b < B; ++b) acc[b] = 0.f;
+  for (int s0 = 0; s0 < nsb; s0 += 4 * U) {
+    Raw nxt[U];
+    const bool more = s0 + 4 * U < nsb;
+    if (more) {
+#pragma unroll
+      for (int u = 0; u < U; ++u) wide_load<T>(row + (long long)min(s0 + 4 * U + 4 * u + sub, nsb - 1) * SB, c, nxt[u]);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int s = s0 + 4 * u + sub;
+      if (s < nsb) {
+#pragma unroll
+        for (int b = 0; b < B; ++b)
+          acc[b] += q8_dot<T>(cur[u], c, xq + (long long)b * K + s * 256, xd + (long long)b * (K / 32) + s * 8,
+                              xs8 + (long long)b * (K / 8) + s * 32);
+      }
+    }
+    if (more) {
+#pragma unroll
+      for (int u = 0; u < U; ++u) cur[u] = nxt[u];
+    }
+  }
+#pragma unroll
+  for (int b = 0; b < B; ++b) acc[b] = warp_sum(acc[b]);
+  if (lane) return;
+#pragma unroll
+  for (int b = 0; b < B; ++b) {
+    const long long ob = (long long)b * ldy;
+    if (MODE == 3) {
+      reinterpret_cast<float*>(y)[ob + n] = acc[b];
+    } else if (MODE == 1) {
+      const float br = __bfloat162float(__float2bfloat16(acc[b]));
+      reinterpret_cast<__nv_bfloat16*>(y)[ob + n] = __float2bfloat16(__bfloat162float(resid[ob + n]) + br);
+    } else {
+      reinterpret_cast<__nv_bfloat16*>(y)[ob + n] = __float2bfloat16(acc[b]);
+    }
+  }
+}
+
+// SwiGLU over interleaved gate/up rows: lanes 0-15 the gate row, 16-31 the up row.
+template <int T, int B>
+__global__ void __launch_bounds__(256) gguf_gemv_q8_swiglu_kernel(const uint8_t* __restrict__ W, long long row_bytes,
+                                                                  const int8_t* __restrict__ xq,
+                                                                  const float* __restrict__ xd,
+                                                                  const float* __restrict__ xs8, void* y, int ldy,
+                                                                  int N, int K) {
+  constexpr int SB = GgufBlock<T>::bytes;
+  constexpr int U = 3;
+  using Raw = typename WideRaw<T>::type;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int pair = blockIdx.x * 8 + warp;
+  const int nsb = K / 256;
+  const int half = lane >> 4;
+  const int c = lane & 7, sub = (lane >> 3) & 1;
+  const bool active = 2 * pair + 1 < N;
+  const uint8_t* row = W + (long long)min(2 * pair + half, N - 1) * row_bytes;
+  Raw cur[U];
+  if (active) {
+#pragma unroll
+    for (int u = 0; u < U; ++u) wide_load<T>(row + (long long)min(2 * u + sub, nsb - 1) * SB, c, cur[u]);
+  }
+  pdl_wait_prior();
+  pdl_launch_dependents();
+  if (!active) return;
+  float acc[B];
+#pragma unroll
+  for (int b = 0; b < B; ++b) acc[b] = 0.f;
+  for (int s0 = 0; s0 < nsb; s0 += 2 * U) {
+    Raw nxt[U];
+    const bool more = s0 + 2 * U < nsb;
+    if (more) {
+#pragma unroll
+      for (int u = 0; u < U; ++u) wide_load<T>(row + (long long)min(s0 + 2 * U + 2 * u + sub, nsb - 1) * SB, c, nxt[u]);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int s = s0 + 2 * u + sub;
+      if (s < nsb) {
+#pragma unroll
+        for (int b = 0; b < B; ++b)
+          acc[b] += q8_dot<T>(cur[u], c, xq + (long long)b * K + s * 256, xd + (long long)b * (K / 32) + s * 8,
+                              xs8 + (long long)b * (K / 8) + s * 32);
+      }
+    }
+    if (more) {
+#pragma unroll
+      for (int u = 0; u < U; ++u) cur[u] = nxt[u];
+    }
+  }
+#pragma unroll
+  for (int b = 0; b < B; ++b) {
+    float v = acc[b];
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const float up = __shfl_sync(0xffffffffu, v, 16);
+    if (lane == 0) {
+      const float g = __bfloat162float(__float2bfloat16(v));
+      const float u = __bfloat162float(__float2bfloat16(up));
+      reinterpret_cast<__nv_bfloat16*>(y)[(long long)b * ldy + pair] = __float2bfloat16(silu(g) * u);
+    }
+  }
+}
+
 // 210-byte Q6_K superblocks -> 224-byte padded superblocks (same bytes + 14 zero bytes)
 __global__ void q6k_pad_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, long long nsb) {
   const long long s = blockIdx.x * (long long)blockDim.y + threadIdx.y;
@@ -512,6 +756,50 @@ static void gg_wide_launch(const uint8_t* W, long long rb, const torch::Tensor& 
     default: TORCH_CHECK(false, "gguf_gemv batch must be 1, 2, 4 or 8");
   }
 #undef HX_GW_B
+}
+
+template <int T, int MODE>
+static void gg_q8_launch(const uint8_t* W, long long rb, const int8_t* xq, const float* xd, const float* xs8, void* y,
+                         int ldy, const __nv_bfloat16* resid, int N, int K, int B, cudaStream_t st) {
+#define HX_GQ_B(BB)                                                                                                 \
+  {                                                                                                                 \
+    if constexpr (MODE == 2) {                                                                                      \
+      HX_CUDA_CHECK(hx_launch_pdl(gguf_gemv_q8_swiglu_kernel<T, BB>, dim3((N / 2 + 7) / 8), dim3(256), 0, st, W, rb, \
+                                  xq, xd, xs8, y, ldy, N, K));                                                      \
+    } else {                                                                                                        \
+      HX_CUDA_CHECK(hx_launch_pdl(gguf_gemv_q8_kernel<T, BB, MODE>, dim3((N + 7) / 8), dim3(256), 0, st, W, rb, xq, \
+                                  xd, xs8, y, ldy, resid, N, K));                                                   \
+    }                                                                                                               \
+  }
+  switch (B) {
+    case 1: HX_GQ_B(1) break;
+    case 2: HX_GQ_B(2) break;
+    case 4: HX_GQ_B(4) break;
+    case 8: HX_GQ_B(8) break;
+    default: TORCH_CHECK(false, "gguf_gemv batch must be 1, 2, 4 or 8");
+  }
+#undef HX_GQ_B
+}
+
+template <int T>
+static void gg_q8_mode(int mode, const uint8_t* W, long long rb, const torch::Tensor& x, void* y, int ldy,
+                       const __nv_bfloat16* resid, const float* nw, float eps, int N, int K, int B, cudaStream_t st) {
+  // quantized activations live in the caching allocator (a graph capture keeps them in
+  // its private pool): int8 [B, K] | f32 [B, K/32] | f32 [B, K/8]
+  auto ws = torch::empty({(long long)B * K + (long long)B * (K / 32) * 4 + (long long)B * (K / 8) * 4},
+                         x.options().dtype(at::kByte));
+  int8_t* xq = reinterpret_cast<int8_t*>(ws.data_ptr());
+  float* xd = reinterpret_cast<float*>(ws.data_ptr<uint8_t>() + (long long)B * K);
+  float* xs8 = xd + (long long)B * (K / 32);
+  HX_CUDA_CHECK(hx_launch_pdl(gguf_quant_x_kernel, dim3(B), dim3(512), 0, st,
+                              reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), nw, eps, K, xq, xd, xs8));
+  switch (mode) {
+    case 0: gg_q8_launch<T, 0>(W, rb, xq, xd, xs8, y, ldy, resid, N, K, B, st); break;
+    case 1: gg_q8_launch<T, 1>(W, rb, xq, xd, xs8, y, ldy, resid, N, K, B, st); break;
+    case 2: gg_q8_launch<T, 2>(W, rb, xq, xd, xs8, y, ldy, resid, N, K, B, st); break;
+    case 3: gg_q8_launch<T, 3>(W, rb, xq, xd, xs8, y, ldy, resid, N, K, B, st); break;
+    default: TORCH_CHECK(false, "bad mode");
+  }
 }
 
 template <int T>
@@ -683,7 +971,14 @@ void gguf_gemv(torch::Tensor W, int64_t type, int64_t K, torch::Tensor x, torch:
   const long long rb = W.size(1);
   const bool wide = (type == kQ4_K || type == kQ6_Kp) && K % 256 == 0 && rb % 16 == 0 &&
                     reinterpret_cast<uintptr_t>(W.data_ptr()) % 16 == 0 && !(mode == 2 && N % 2);
-  if (wide && type == kQ4_K) gg_wide_mode<kQ4_K>((int)mode, wp, rb, x, y.data_ptr(), y.stride(0), rp, np, (float)eps, N, (int)K, B, st);
+  static const bool q8 = [] {
+    const char* e = std::getenv("HELEXA_GGUF_XQ");
+    return !(e && e[0] == '0');
+  }();
+  TORCH_CHECK(x.is_contiguous(), "x must be contiguous");
+  if (wide && q8 && type == kQ4_K) gg_q8_mode<kQ4_K>((int)mode, wp, rb, x, y.data_ptr(), y.stride(0), rp, np, (float)eps, N, (int)K, B, st);
+  else if (wide && q8) gg_q8_mode<kQ6_Kp>((int)mode, wp, rb, x, y.data_ptr(), y.stride(0), rp, np, (float)eps, N, (int)K, B, st);
+  else if (wide && type == kQ4_K) gg_wide_mode<kQ4_K>((int)mode, wp, rb, x, y.data_ptr(), y.stride(0), rp, np, (float)eps, N, (int)K, B, st);
   else if (wide) gg_wide_mode<kQ6_Kp>((int)mode, wp, rb, x, y.data_ptr(), y.stride(0), rp, np, (float)eps, N, (int)K, B, st);
   else if (type == kQ8_0) gg_mode<kQ8_0>((int)mode, wp, rb, x, y.data_ptr(), y.stride(0), rp, np, (float)eps, N, (int)K, B, st);
   else if (type == kQ4_K) gg_mode<kQ4_K>((int)mode, wp, rb, x, y.data_ptr(), y.stride(0), rp, np, (float)eps, N, (int)K, B, st);

@@ -75,6 +75,17 @@ def tiny_qwen3() -> ModelConfig:
     )
 
 
+def tiny_qwen3_vl() -> ModelConfig:
+    """Tiny vision-language model: the tiny Qwen3 LM with interleaved M-RoPE and a
+    2-block vision tower (patch 4, 2 x 2 merge) whose merger emits the LM width."""
+    import dataclasses
+    return dataclasses.replace(
+        tiny_qwen3(), name="tiny-qwen3-vl", mrope_section=[11, 11, 10], mrope_interleaved=True,
+        vision={"depth": 2, "hidden_size": 64, "intermediate_size": 128, "num_heads": 4,
+                "num_position_embeddings": 64, "out_hidden_size": 256, "patch_size": 4,
+                "temporal_patch_size": 2, "spatial_merge_size": 2, "in_channels": 3})
+
+
 def tiny_qwen3_moe() -> ModelConfig:
     return ModelConfig(
         family="qwen3_moe", name="tiny-qwen3-moe", vocab_size=1024, hidden_size=256,
@@ -108,6 +119,7 @@ PRESETS = {
     "llama-3.1-8b": llama3_8b,
     "tiny-qwen3-next": tiny_qwen3_next,
     "tiny-qwen3": tiny_qwen3,
+    "tiny-qwen3-vl": tiny_qwen3_vl,
     "tiny-qwen3-moe": tiny_qwen3_moe,
     "qwen3-next-80b-a3b": qwen3_next_80b_a3b,
     "qwen3-8b": qwen3_8b,

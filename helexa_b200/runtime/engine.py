@@ -53,6 +53,7 @@ class Request:
     params: SamplingParams
     id: str = ""
     principal: str | None = None
+    mm: Any = None          # MultimodalPrompt (runtime/multimodal.py): prefilled from embeddings
     events: "queue.Queue[Any]" = field(default_factory=queue.Queue)
     cancelled: threading.Event = field(default_factory=threading.Event)
 
@@ -106,7 +107,8 @@ class Engine:
         self._thread.start()
 
     # ---- public ------------------------------------------------------------
-    def submit(self, prompt: list[int], params: SamplingParams, principal: str | None = None) -> Request:
+    def submit(self, prompt: list[int], params: SamplingParams, principal: str | None = None,
+               mm=None) -> Request:
         if self.poisoned:
             raise EngineError(f"model poisoned: {self.poisoned}")
         if not prompt:
@@ -114,12 +116,14 @@ class Engine:
         if len(prompt) + params.max_tokens + 1 > self.runner.max_len:
             raise ValueError(f"prompt ({len(prompt)}) + max_tokens ({params.max_tokens}) exceeds the context "
                              f"window ({self.runner.max_len})")
-        req = Request(prompt=list(prompt), params=params, principal=principal, id=f"req-{next(self._ids)}")
+        if mm is not None and not hasattr(self.runner, "prefill_mm"):
+            raise ValueError("this model's runner cannot prefill image inputs")
+        req = Request(prompt=list(prompt), params=params, principal=principal, mm=mm, id=f"req-{next(self._ids)}")
         self._in.put(req)
         return req
 
-    def generate(self, prompt: list[int], params: SamplingParams) -> tuple[list[int], FinishEvent]:
-        req = self.submit(prompt, params)
+    def generate(self, prompt: list[int], params: SamplingParams, mm=None) -> tuple[list[int], FinishEvent]:
+        req = self.submit(prompt, params, mm=mm)
         toks: list[int] = []
         for ev in req.iter_events():
             if isinstance(ev, TokenEvent):
@@ -180,6 +184,14 @@ class Engine:
         t0 = time.perf_counter()
         p0 = 0
         cached = 0
+        if req.mm is not None:
+            # image prompts: one embedding prefill; the prefix cache is keyed by token ids,
+            # which do not identify an image, so it is neither read nor written
+            r.reset(slot)
+            logits = r.prefill_mm(slot, req.mm)
+            self.stats["prefill_tokens"] += len(req.prompt)
+            self._start(req, slot, logits, t0, 0)
+            return
         snap = self.prefix_cache.longest_match(req.prompt) if self.prefix_cache else None
         if snap is not None:
             r.restore(slot, snap.snapshot)
@@ -197,7 +209,11 @@ class Engine:
                 p0 = cut
         logits = r.prefill(slot, prompt[p0:], p0)
         self.stats["prefill_tokens"] += len(prompt) - cached
-        seq = _Seq(req=req, slot=slot, history=list(prompt), t_start=t0, cached=cached)
+        self._start(req, slot, logits, t0, cached)
+
+    def _start(self, req: Request, slot: int, logits, t0: float, cached: int):
+        """First token from the prefill logits; the sequence joins the decode batch."""
+        seq = _Seq(req=req, slot=slot, history=list(req.prompt), t_start=t0, cached=cached)
         if not req.params.greedy:
             seq.sampler = HostSampler(req.params)
             seq.seed = int(req.params.seed) if req.params.seed is not None else \

@@ -128,6 +128,13 @@ def build_served_model(spec: ModelSpec) -> ServedModel:
             model.quantize_(spec.quant.upper())
         runner = FastRunner(model)
         kv_bpt = cfg.kv_bytes_per_token()
+        vget = None
+        if cfg.vision and src.kind == "preset":
+            from ..models.vision import VisionConfig, random_vision_weights
+            vget = random_vision_weights(VisionConfig.from_dict(cfg.vision)).__getitem__
+        elif cfg.vision and src.kind != "gguf":
+            vget = st.get
+        embed_table, vdev = model.embed_w, dev
     else:
         from ..models.reference import ReferenceModel
         if src.kind == "preset":
@@ -144,6 +151,8 @@ def build_served_model(spec: ModelSpec) -> ServedModel:
         model = ReferenceModel(cfg, w)
         runner = RefRunner(model, num_slots=spec.max_batch, max_len=max_len)
         kv_bpt = 0
+        vget = w.__getitem__ if cfg.vision and src.kind != "gguf" else None
+        embed_table, vdev = w["model.embed_tokens.weight"], "cpu"
     pc = PrefixCache(spec.prefix_cache_mb << 20, spec.prefix_cache_entries) if spec.prefix_cache_mb else None
     im_start = tok.token_id("<|im_start|>")
     engine = Engine(runner, prefix_cache=pc, im_start_id=im_start, max_batch=spec.max_batch)
@@ -155,6 +164,12 @@ def build_served_model(spec: ModelSpec) -> ServedModel:
     sm = ServedModel(model_id=spec.model_id, engine=engine, tokenizer=tok, config=cfg, admission=adm,
                      defaults=defaults, devices=spec.devices or ([0] if use_cuda else []),
                      tensor_parallel=spec.tensor_parallel, spec=asdict(spec), kv_bytes_per_token=kv_bpt)
+    if vget is not None:
+        # vision tower beside the LM (a GGUF LM carries its tower in a separate mmproj
+        # file, which this node does not load: such models serve text only)
+        from .multimodal import VisionFrontend
+        sm.vision = VisionFrontend.from_weights(cfg, vget, embed_table, tok, device=vdev)
+        sm.capabilities = sorted(set(sm.capabilities) | {"vision"})
     if use_cuda:
         # KV pools are preallocated for every slot at max_len, so the admission budget is
         # that pool (a request reserves its prompt + output tokens against it)

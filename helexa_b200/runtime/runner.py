@@ -77,6 +77,17 @@ class FastRunner:
         self.m.check_errors()  # a timed-out wait makes the outputs invalid: poison, don't serve
         return logits
 
+    def prefill_mm(self, slot: int, mm) -> torch.Tensor:
+        """Prefill a multimodal prompt (runtime/multimodal.py MultimodalPrompt) at
+        position 0 from its input embeddings and M-RoPE positions; later decode steps
+        rotate at the prompt's next rotary position."""
+        m = self.m
+        emb = mm.embeds.to(m.device, torch.bfloat16)
+        logits = m.prefill(slot, None, 0, embeds=emb, pos3=mm.pos3, next_pos=mm.next_pos)
+        self.host_pos[slot] = len(mm.tokens)
+        m.check_errors()
+        return logits
+
     def decode(self, slots: list[int], tokens: list[int], steps: int) -> list[list[int]]:
         """Run `steps` greedy steps for the given slots starting from `tokens`; returns
         the produced tokens per slot. Pads to a captured batch size with the pad slot."""
@@ -189,6 +200,12 @@ class RefRunner:
         assert self.states[slot].length == p0
         lg = self.m.forward(torch.tensor(tokens), self.states[slot])
         self.host_pos[slot] = p0 + len(tokens)
+        return lg
+
+    def prefill_mm(self, slot: int, mm) -> torch.Tensor:
+        assert self.states[slot].length == 0
+        lg = self.m.forward(None, self.states[slot], embeds=mm.embeds, pos3=mm.pos3, next_pos=mm.next_pos)
+        self.host_pos[slot] = len(mm.tokens)
         return lg
 
     def decode_logits(self, slots: list[int], tokens: list[int]) -> torch.Tensor:

@@ -20,6 +20,7 @@ from .admission import AdmissionController, AdmissionRejection
 from ..utils.trace import request_span
 from .engine import Engine, FinishEvent, TokenEvent
 from .sampling import GenerationDefaults, SamplingParams
+from .multimodal import request_images
 from .tokenizer import IncrementalDetokenizer, StreamParser, parse_tool_call_body
 
 
@@ -115,6 +116,7 @@ class ServedModel:
     # NEURON_MIN_FREE_VRAM_MB guard
     min_free_vram_mb: int = int(os.environ.get("HELEXA_MIN_FREE_VRAM_MB", "1500"))
     free_vram_mb: object = None  # callable -> MiB free on the tightest device, or None (no check)
+    vision: object = None        # VisionFrontend (runtime/multimodal.py) for image inputs, or None
 
     # prompts must prefill within this many seconds at the measured prefill rate
     max_prefill_s: float = float(os.environ.get("HELEXA_MAX_PREFILL_S", "120"))
@@ -161,8 +163,22 @@ class ServedModel:
                      prompt_ids: list[int] | None = None, start_in_reasoning: bool | None = None):
         if self.status != "loaded":
             raise RequestError(f"model {self.model_id} is {self.status}", 503, "model_unavailable")
+        mm = None
         if prompt_ids is None:
             ids, think = self.render_chat(request, include_thinking)
+            try:
+                uris = request_images(request.get("messages"))
+            except ValueError as e:
+                raise RequestError(str(e)) from e
+            if uris:
+                if self.vision is None:
+                    raise RequestError(f"model {self.model_id} does not accept image inputs", 400,
+                                       "unsupported_content")
+                try:
+                    mm = await asyncio.to_thread(self.vision.build, ids, uris)
+                except ValueError as e:
+                    raise RequestError(f"image input: {e}") from e
+                ids = mm.tokens
         else:
             ids, think = prompt_ids, False
         if start_in_reasoning is not None:
@@ -173,7 +189,10 @@ class ServedModel:
         permit = await self.admission.enter(principal, kv_mb)
         req = None
         try:
-            req = self.engine.submit(ids, params, principal)
+            try:
+                req = self.engine.submit(ids, params, principal, mm=mm)
+            except ValueError as e:
+                raise RequestError(str(e)) from e
             rid = "chatcmpl-" + uuid.uuid4().hex[:24]
             yield Start(rid, self.model_id, int(time.time()))
             detok = IncrementalDetokenizer(self.tokenizer)

@@ -17,7 +17,9 @@ import json
 import os
 from dataclasses import dataclass
 
-SPECIALS = ["<|endoftext|>", "<|im_start|>", "<|im_end|>", "<think>", "</think>", "<tool_call>", "</tool_call>"]
+SPECIALS = ["<|endoftext|>", "<|im_start|>", "<|im_end|>", "<think>", "</think>", "<tool_call>", "</tool_call>",
+            "<|vision_start|>", "<|image_pad|>", "<|vision_end|>"]
+IMAGE_PART_TYPES = ("image_url", "input_image", "image")
 
 
 def _content_text(content) -> str:
@@ -29,6 +31,9 @@ def _content_text(content) -> str:
     for p in content:
         if isinstance(p, dict) and p.get("type") in ("text", "input_text", "output_text"):
             parts.append(p.get("text", ""))
+        elif isinstance(p, dict) and p.get("type") in IMAGE_PART_TYPES:
+            # one pad per image; the vision front end expands it to the image's tokens
+            parts.append("<|vision_start|><|image_pad|><|vision_end|>")
     return "".join(parts)
 
 

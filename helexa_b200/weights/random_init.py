@@ -60,6 +60,9 @@ def weight_shapes(cfg: ModelConfig) -> dict[str, tuple[int, ...]]:
             s[m + "gate_proj.weight"] = (cfg.intermediate_size, h)
             s[m + "up_proj.weight"] = (cfg.intermediate_size, h)
             s[m + "down_proj.weight"] = (h, cfg.intermediate_size)
+    if cfg.vision:
+        from ..models.vision import VisionConfig, vision_weight_shapes
+        s.update(vision_weight_shapes(VisionConfig.from_dict(cfg.vision)))
     return s
 
 

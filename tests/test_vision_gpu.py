@@ -59,3 +59,21 @@ def test_multimodal_prefill_and_decode_match_reference():
         wl = ref.forward(torch.tensor([tok]), st)
         assert _cos(nb.logits[0], wl) > 0.995
         tok = int(wl.argmax())
+
+
+def test_cuda_served_chat_with_image():
+    """The node serves an image chat on CUDA: registry builds the tower beside the
+    FastModel, the engine prefills the spliced embeddings through FastRunner.prefill_mm
+    and decodes in captured graphs at the shifted rotary position."""
+    from fastapi.testclient import TestClient
+    from helexa_b200.server.app import create_app
+    from test_multimodal_cpu import _messages, _png
+    with TestClient(create_app()) as c:
+        r = c.post("/models/load", json={"model_id": "vl", "source": "preset:tiny-qwen3-vl", "device": "cuda",
+                                         "max_batch": 2, "max_len": 512})
+        assert r.status_code == 200, r.text
+        body = {"model": "vl", "messages": _messages(_png()), "max_tokens": 6, "temperature": 0}
+        r = c.post("/v1/chat/completions", json=body)
+        assert r.status_code == 200, r.text
+        u = r.json()["usage"]
+        assert u["prompt_tokens"] > 64 and 1 <= u["completion_tokens"] <= 6
