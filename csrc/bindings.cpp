@@ -113,6 +113,10 @@ void gguf_gemv(torch::Tensor W, int64_t type, int64_t K, torch::Tensor x, torch:
                c10::optional<torch::Tensor> resid, c10::optional<torch::Tensor> norm_w, double eps);
 void gguf_dequant(torch::Tensor W, int64_t type, int64_t K, torch::Tensor out);
 torch::Tensor gguf_quant(torch::Tensor W, int64_t type);
+void gguf_experts(torch::Tensor W, int64_t type, int64_t K, torch::Tensor x, torch::Tensor ids, torch::Tensor act,
+                  int64_t J, c10::optional<torch::Tensor> norm_w, double eps, int64_t e_base, int64_t e_count);
+void gguf_moe_down(torch::Tensor W, int64_t type, int64_t I, torch::Tensor act, torch::Tensor ids, torch::Tensor wts,
+                   torch::Tensor x, int64_t J, int64_t e_base, int64_t e_count);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("set_pdl", [](bool on) { hx_pdl_enabled() = on; });
@@ -173,6 +177,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gguf_gemv", &gguf_gemv);
   m.def("gguf_dequant", &gguf_dequant);
   m.def("gguf_quant", &gguf_quant);
+  m.def("gguf_experts", &gguf_experts, py::arg("W"), py::arg("type"), py::arg("K"), py::arg("x"), py::arg("ids"),
+        py::arg("act"), py::arg("J"), py::arg("norm_w") = py::none(), py::arg("eps") = 0.0, py::arg("e_base") = 0,
+        py::arg("e_count") = 0);
+  m.def("gguf_moe_down", &gguf_moe_down, py::arg("W"), py::arg("type"), py::arg("I"), py::arg("act"), py::arg("ids"),
+        py::arg("wts"), py::arg("x"), py::arg("J"), py::arg("e_base") = 0, py::arg("e_count") = 0);
   m.def("gdn_prefill", &gdn_prefill);
   m.def("gemv_router", &gemv_router);
   m.def("gemv_argmax", &gemv_argmax);

@@ -185,15 +185,12 @@ __global__ void __launch_bounds__(256) gguf_gemv_kernel(const uint8_t* __restric
 }
 
 // ---------------------------------------------------------------------------
-// Wide-load k-quant GEMV (Q4_K, padded Q6_K): one warp per output row; eight lanes
-// share a 256-value superblock, each lane taking 32 of its values with 8- and 16-byte
-// loads (the superblock header -- scales, d, dmin -- is one 16-byte load that the eight
-// lanes share through L1). Per sub-block run the dot product is factored as
-// d * s * sum(q x) - dmin * m * sum(x), so the inner loop is integer unpacking and two
-// FMAs per value. Superblocks of several iterations are requested before any is used.
+// Wide-load lane slices of a 256-value superblock (Q4_K, padded Q6_K): eight lanes
+// share a superblock, each taking 32 of its values with 8- and 16-byte loads; the Q4_K
+// header (d, dmin, 12 scale bytes) is one 16-byte load the eight lanes share through L1.
 // ---------------------------------------------------------------------------
 struct Q4Raw { uint4 hdr, qs; };            // header (d, dmin, 12 scale bytes), 16 qs bytes
-struct Q6Raw { uint2 ql0, ql1, qh; uint4 sc; uint4 dw; };
+struct Q6Raw { uint2 ql0, ql1, qh, sc; unsigned d; };  // sc: the 8 scale bytes of the lane's half
 
 template <int T>
 struct WideRaw;
@@ -212,237 +209,8 @@ HX_DEVICE void wide_load(const uint8_t* sb, int c, typename WideRaw<T>::type& r)
     r.ql0 = __ldg(reinterpret_cast<const uint2*>(sb + 64 * h + l0));
     r.ql1 = __ldg(reinterpret_cast<const uint2*>(sb + 64 * h + 32 + l0));
     r.qh = __ldg(reinterpret_cast<const uint2*>(sb + 128 + 32 * h + l0));
-    r.sc = __ldg(reinterpret_cast<const uint4*>(sb + 192));
-    r.dw = __ldg(reinterpret_cast<const uint4*>(sb + 208));
-  }
-}
-
-// sum over this lane's 32 values of w * x; xs = the superblock's 256 x values (f32, smem)
-template <int T>
-HX_DEVICE float wide_dot(const typename WideRaw<T>::type& r, int c, const float* xs) {
-  if constexpr (T == kQ4_K) {
-    const uint8_t* hb = reinterpret_cast<const uint8_t*>(&r.hdr);
-    const float d = h2f(*reinterpret_cast<const unsigned short*>(hb)), dmin = h2f(*reinterpret_cast<const unsigned short*>(hb + 2));
-    const uint8_t* sc = hb + 4;
-    const int g = c >> 1, l0 = (c & 1) * 16;
-    float out = 0.f;
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      const int j = 2 * g + half;  // sub-block: low nibbles -> 2g, high nibbles -> 2g+1
-      int s, m;
-      if (j < 4) {
-        s = sc[j] & 63;
-        m = sc[j + 4] & 63;
-      } else {
-        s = (sc[j + 4] & 0xF) | ((sc[j - 4] >> 6) << 4);
-        m = (sc[j + 4] >> 4) | ((sc[j] >> 6) << 4);
-      }
-      const float* xr = xs + j * 32 + l0;
-      const uint8_t* qb = reinterpret_cast<const uint8_t*>(&r.qs);
-      float sq = 0.f, sx = 0.f;
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const float q = (float)((qb[i] >> (4 * half)) & 0xF);
-        sq = fmaf(q, xr[i], sq);
-        sx += xr[i];
-      }
-      out += d * s * sq - dmin * m * sx;
-    }
-    return out;
-  } else {
-    const int h = c >> 2, l0 = (c & 3) * 8;
-    const int8_t* sc = reinterpret_cast<const int8_t*>(&r.sc);
-    const float d = h2f(*reinterpret_cast<const unsigned short*>(&r.dw));
-    const uint8_t* a = reinterpret_cast<const uint8_t*>(&r.ql0);
-    const uint8_t* b2 = reinterpret_cast<const uint8_t*>(&r.ql1);
-    const uint8_t* qh = reinterpret_cast<const uint8_t*>(&r.qh);
-    float out = 0.f;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {  // value blocks 128h + 32k + l0 .. +8
-      const float* xr = xs + 128 * h + 32 * k + l0;
-      const float ds = d * sc[8 * h + (l0 >> 4) + 2 * k];
-      float sq = 0.f;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int lo = (k & 1) ? b2[i] : a[i];
-        const int q = (((k >> 1) ? (lo >> 4) : lo) & 0xF) | (((qh[i] >> (2 * k)) & 3) << 4);
-        sq = fmaf((float)(q - 32), xr[i], sq);
-      }
-      out = fmaf(ds, sq, out);
-    }
-    return out;
-  }
-}
-
-template <int T, int B, int MODE>
-__global__ void __launch_bounds__(256) gguf_gemv_wide_kernel(const uint8_t* __restrict__ W, long long row_bytes,
-                                                             const __nv_bfloat16* __restrict__ x, void* y, int ldy,
-                                                             const __nv_bfloat16* resid, const float* norm_w,
-                                                             float eps, int N, int K) {
-  extern __shared__ __align__(16) float xs[];  // [B][K] f32
-  __shared__ float red[8];
-  constexpr int SB = GgufBlock<T>::bytes;
-  constexpr int U = 3;  // superblock groups (4 superblocks per warp step) in flight per lane
-  using Raw = typename WideRaw<T>::type;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n = blockIdx.x * 8 + warp;
-  const int nsb = K / 256;
-  const int c = lane & 7, sub = lane >> 3;  // lane's 32-value slice, superblock within the step
-  const bool active = n < N;
-  const uint8_t* row = W + (long long)min(n, N - 1) * row_bytes;
-  Raw cur[U];
-  // weights never depend on the previous kernel: request the first steps before the wait
-  if (active) {
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int s = min(4 * u + sub, nsb - 1);
-      wide_load<T>(row + (long long)s * SB, c, cur[u]);
-    }
-  }
-  pdl_wait_prior();
-  pdl_launch_dependents();
-  for (int b = 0; b < B; ++b) {
-    const __nv_bfloat16* xr = x + (long long)b * K;
-    float inv = 1.f;
-    if (norm_w) {
-      float ss = 0.f;
-      for (int k = threadIdx.x; k < K; k += 256) {
-        const float f = __bfloat162float(xr[k]);
-        ss += f * f;
-      }
-      ss = block_sum(ss, red);
-      inv = rsqrtf(ss / K + eps);
-    }
-    for (int k = threadIdx.x; k < K; k += 256) {
-      const float f = __bfloat162float(xr[k]);
-      xs[b * K + k] = norm_w ? __bfloat162float(__float2bfloat16(f * inv * norm_w[k])) : f;
-    }
-  }
-  __syncthreads();
-  if (!active) return;
-  float acc[B];
-#pragma unroll
-  for (int b = 0; b < B; ++b) acc[b] = 0.f;
-  for (int s0 = 0; s0 < nsb; s0 += 4 * U) {
-    Raw nxt[U];
-    const bool more = s0 + 4 * U < nsb;
-    if (more) {
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int s = min(s0 + 4 * U + 4 * u + sub, nsb - 1);
-        wide_load<T>(row + (long long)s * SB, c, nxt[u]);
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int s = s0 + 4 * u + sub;
-      if (s < nsb) {
-#pragma unroll
-        for (int b = 0; b < B; ++b) acc[b] += wide_dot<T>(cur[u], c, xs + b * K + s * 256);
-      }
-    }
-    if (more) {
-#pragma unroll
-      for (int u = 0; u < U; ++u) cur[u] = nxt[u];
-    }
-  }
-#pragma unroll
-  for (int b = 0; b < B; ++b) acc[b] = warp_sum(acc[b]);
-  if (lane) return;
-#pragma unroll
-  for (int b = 0; b < B; ++b) {
-    const long long ob = (long long)b * ldy;
-    if (MODE == 3) {
-      reinterpret_cast<float*>(y)[ob + n] = acc[b];
-    } else if (MODE == 1) {
-      const float br = __bfloat162float(__float2bfloat16(acc[b]));
-      reinterpret_cast<__nv_bfloat16*>(y)[ob + n] = __float2bfloat16(__bfloat162float(resid[ob + n]) + br);
-    } else {
-      reinterpret_cast<__nv_bfloat16*>(y)[ob + n] = __float2bfloat16(acc[b]);
-    }
-  }
-}
-
-// SwiGLU over interleaved rows needs a row pair per warp: lanes 0-15 take the gate row,
-// lanes 16-31 the up row (four lanes per superblock).
-template <int T, int B>
-__global__ void __launch_bounds__(256) gguf_gemv_wide_swiglu_kernel(const uint8_t* __restrict__ W, long long row_bytes,
-                                                                    const __nv_bfloat16* __restrict__ x, void* y,
-                                                                    int ldy, const float* norm_w, float eps, int N,
-                                                                    int K) {
-  extern __shared__ __align__(16) float xs[];
-  __shared__ float red[8];
-  constexpr int SB = GgufBlock<T>::bytes;
-  constexpr int U = 3;
-  using Raw = typename WideRaw<T>::type;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int pair = blockIdx.x * 8 + warp;
-  const int nsb = K / 256;
-  const int half = lane >> 4;            // 0: gate row, 1: up row
-  const int c = lane & 7, sub = (lane >> 3) & 1;  // two superblocks per half-warp step
-  const bool active = 2 * pair + 1 < N;
-  const uint8_t* row = W + (long long)min(2 * pair + half, N - 1) * row_bytes;
-  Raw cur[U];
-  if (active) {
-#pragma unroll
-    for (int u = 0; u < U; ++u) wide_load<T>(row + (long long)min(2 * u + sub, nsb - 1) * SB, c, cur[u]);
-  }
-  pdl_wait_prior();
-  pdl_launch_dependents();
-  for (int b = 0; b < B; ++b) {
-    const __nv_bfloat16* xr = x + (long long)b * K;
-    float inv = 1.f;
-    if (norm_w) {
-      float ss = 0.f;
-      for (int k = threadIdx.x; k < K; k += 256) {
-        const float f = __bfloat162float(xr[k]);
-        ss += f * f;
-      }
-      ss = block_sum(ss, red);
-      inv = rsqrtf(ss / K + eps);
-    }
-    for (int k = threadIdx.x; k < K; k += 256) {
-      const float f = __bfloat162float(xr[k]);
-      xs[b * K + k] = norm_w ? __bfloat162float(__float2bfloat16(f * inv * norm_w[k])) : f;
-    }
-  }
-  __syncthreads();
-  if (!active) return;
-  float acc[B];
-#pragma unroll
-  for (int b = 0; b < B; ++b) acc[b] = 0.f;
-  for (int s0 = 0; s0 < nsb; s0 += 2 * U) {
-    Raw nxt[U];
-    const bool more = s0 + 2 * U < nsb;
-    if (more) {
-#pragma unroll
-      for (int u = 0; u < U; ++u) wide_load<T>(row + (long long)min(s0 + 2 * U + 2 * u + sub, nsb - 1) * SB, c, nxt[u]);
-    }
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int s = s0 + 2 * u + sub;
-      if (s < nsb) {
-#pragma unroll
-        for (int b = 0; b < B; ++b) acc[b] += wide_dot<T>(cur[u], c, xs + b * K + s * 256);
-      }
-    }
-    if (more) {
-#pragma unroll
-      for (int u = 0; u < U; ++u) cur[u] = nxt[u];
-    }
-  }
-  // reduce within each half-warp (16 lanes), then lane 0 combines gate and up
-#pragma unroll
-  for (int b = 0; b < B; ++b) {
-    float v = acc[b];
-#pragma unroll
-    for (int o = 8; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    const float up = __shfl_sync(0xffffffffu, v, 16);
-    if (lane == 0) {
-      const float g = __bfloat162float(__float2bfloat16(v));
-      const float u = __bfloat162float(__float2bfloat16(up));
-      reinterpret_cast<__nv_bfloat16*>(y)[(long long)b * ldy + pair] = __float2bfloat16(silu(g) * u);
-    }
+    r.sc = __ldg(reinterpret_cast<const uint2*>(sb + 192 + 8 * h));
+    r.d = __ldg(reinterpret_cast<const unsigned*>(sb + 208));
   }
 }
 
@@ -461,47 +229,53 @@ __global__ void __launch_bounds__(256) gguf_gemv_wide_swiglu_kernel(const uint8_
 // same row), so there is no shared-memory staging and no limit on K or the batch.
 // ---------------------------------------------------------------------------
 
-// x [B, K] bf16 (optionally RMS-normalised by norm_w and rounded to bf16 first, as the
-// float kernels do) -> xq int8 [B, K], xd f32 [B, K/32] block scales, xs8 f32 [B, K/8]
-// sums of the (normalised) values. One CTA per batch row.
+// x [B, K] bf16 (optionally RMS-normalised by norm_w and rounded to bf16 first, as a
+// bf16 model's normalised activations are) -> xq int8 [B, K], xd f32 [B, K/32] block
+// scales, xs8 f32 [B, K/8] sums of the (normalised) values. grid (ceil(K/32/16), B):
+// each CTA's 16 warps quantize 16 blocks; with a norm every CTA first reduces the
+// whole row's sum of squares (a few KB read from L2), so no CTA waits on another.
 __global__ void __launch_bounds__(512) gguf_quant_x_kernel(const __nv_bfloat16* __restrict__ x, const float* norm_w,
                                                            float eps, int K, int8_t* __restrict__ xq,
                                                            float* __restrict__ xd, float* __restrict__ xs8) {
   __shared__ float red[16];
   pdl_wait_prior();
   pdl_launch_dependents();
-  const int b = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const int b = blockIdx.y, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const __nv_bfloat16* xr = x + (long long)b * K;
   float inv = 1.f;
   if (norm_w) {
     float ss = 0.f;
-    for (int k = threadIdx.x; k < K; k += blockDim.x) {
-      const float f = __bfloat162float(xr[k]);
-      ss += f * f;
+    for (int k = threadIdx.x * 8; k < K; k += blockDim.x * 8) {
+      float f[8];
+      unpack8(*reinterpret_cast<const bf16x8*>(xr + k), f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss += f[i] * f[i];
     }
     ss = block_sum(ss, red);
     inv = rsqrtf(ss / K + eps);
   }
-  for (int blk = warp; blk < K / 32; blk += nw) {
-    const int k = blk * 32 + lane;
-    float v = __bfloat162float(xr[k]);
-    if (norm_w) v = __bfloat162float(__float2bfloat16(v * inv * norm_w[k]));
-    const float amax = warp_max(fabsf(v));
-    const float scale = amax > 0.f ? 127.f / amax : 0.f;
-    const int q = max(-127, min(127, __float2int_rn(v * scale)));
-    xq[(long long)b * K + k] = (int8_t)q;
-    float s8 = v;
-    s8 += __shfl_xor_sync(0xffffffffu, s8, 1);
-    s8 += __shfl_xor_sync(0xffffffffu, s8, 2);
-    s8 += __shfl_xor_sync(0xffffffffu, s8, 4);
-    if ((lane & 7) == 0) xs8[(long long)b * (K / 8) + k / 8] = s8;
-    if (lane == 0) xd[(long long)b * (K / 32) + blk] = amax / 127.f;
-  }
+  const int blk = blockIdx.x * 16 + warp;
+  if (blk >= K / 32) return;
+  const int k = blk * 32 + lane;
+  float v = __bfloat162float(xr[k]);
+  if (norm_w) v = __bfloat162float(__float2bfloat16(v * inv * norm_w[k]));
+  const float amax = warp_max(fabsf(v));
+  const float scale = amax > 0.f ? 127.f / amax : 0.f;
+  const int q = max(-127, min(127, __float2int_rn(v * scale)));
+  xq[(long long)b * K + k] = (int8_t)q;
+  float s8 = v;
+  s8 += __shfl_xor_sync(0xffffffffu, s8, 1);
+  s8 += __shfl_xor_sync(0xffffffffu, s8, 2);
+  s8 += __shfl_xor_sync(0xffffffffu, s8, 4);
+  if ((lane & 7) == 0) xs8[(long long)b * (K / 8) + k / 8] = s8;
+  if (lane == 0) xd[(long long)b * (K / 32) + blk] = amax / 127.f;
 }
+
+static inline dim3 quant_x_grid(int K, int rows) { return dim3((K / 32 + 15) / 16, rows); }
 
 HX_DEVICE int lop_nib(unsigned w, int hi) { return (int)((hi ? (w >> 4) : w) & 0x0F0F0F0Fu); }
 
-// This lane's share of one superblock (the same value slices as wide_dot) against the
+// This lane's share of one superblock (the slices wide_load fetched) against the
 // quantized activations of that superblock: q = 256 int8, d = 8 block scales, s8 = 32
 // sums of 8.
 template <int T>
@@ -539,9 +313,9 @@ HX_DEVICE float q8_dot(const typename WideRaw<T>::type& r, int c, const int8_t* 
     return out;
   } else {
     const int h = c >> 2, l0 = (c & 3) * 8;
-    const float d = h2f((unsigned short)(r.dw.x & 0xFFFFu));
-    // the lane's four scales sit at byte 8h + (l0 >> 4) + 2k, k = 0..3: words 2h and 2h+1
-    const unsigned sw0 = h ? r.sc.z : r.sc.x, sw1 = h ? r.sc.w : r.sc.y;
+    const float d = h2f((unsigned short)(r.d & 0xFFFFu));
+    // the lane's four scales sit at byte (l0 >> 4) + 2k, k = 0..3, of its half's 8 bytes
+    const unsigned sw0 = r.sc.x, sw1 = r.sc.y;
     const int sb = 8 * (l0 >> 4);
     float out = 0.f;
 #pragma unroll
@@ -561,56 +335,79 @@ HX_DEVICE float q8_dot(const typename WideRaw<T>::type& r, int c, const int8_t* 
   }
 }
 
-template <int T, int B, int MODE>
-__global__ void __launch_bounds__(256) gguf_gemv_q8_kernel(const uint8_t* __restrict__ W, long long row_bytes,
-                                                           const int8_t* __restrict__ xq, const float* __restrict__ xd,
-                                                           const float* __restrict__ xs8, void* y, int ldy,
-                                                           const __nv_bfloat16* resid, int N, int K) {
+// S warps share one output row (each takes every S-th group of four superblocks) and
+// meet in shared memory: short N with long K (o_proj, down_proj) then still fills the
+// GPU with several resident waves instead of one and a half.
+template <int T, int B, int MODE, int S>
+__global__ void __launch_bounds__(256, (B <= 2 ? 3 : 2)) gguf_gemv_q8_kernel(
+    const uint8_t* __restrict__ W, long long row_bytes, const int8_t* __restrict__ xq, const float* __restrict__ xd,
+    const float* __restrict__ xs8, void* y, int ldy, const __nv_bfloat16* resid, int N, int K) {
   constexpr int SB = GgufBlock<T>::bytes;
-  constexpr int U = 3;
+  constexpr int U = 2;                 // warp steps of loads in flight beyond the current one
+  constexpr int STEP = 4 * S;          // superblocks one step of the row's S warps covers
   using Raw = typename WideRaw<T>::type;
+  __shared__ float red[8][B];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n = blockIdx.x * 8 + warp;
+  const int n = blockIdx.x * (8 / S) + warp / S, part = warp % S;
   const int nsb = K / 256;
   const int c = lane & 7, sub = lane >> 3;
+  const int first = part * 4 + sub;    // this lane group's first superblock
   const bool active = n < N;
   const uint8_t* row = W + (long long)min(n, N - 1) * row_bytes;
   Raw cur[U];
   if (active) {
 #pragma unroll
-    for (int u = 0; u < U; ++u) wide_load<T>(row + (long long)min(4 * u + sub, nsb - 1) * SB, c, cur[u]);
+    for (int u = 0; u < U; ++u) wide_load<T>(row + (long long)min(first + u * STEP, nsb - 1) * SB, c, cur[u]);
   }
   pdl_wait_prior();
   pdl_launch_dependents();
-  if (!active) return;
   float acc[B];
 #pragma unroll
   for (int b = 0; b < B; ++b) acc[b] = 0.f;
-  for (int s0 = 0; s0 < nsb; s0 += 4 * U) {
-    Raw nxt[U];
-    const bool more = s0 + 4 * U < nsb;
-    if (more) {
+  if (active) {
+    for (int s0 = 0; s0 < nsb; s0 += U * STEP) {
+      Raw nxt[U];
+      const bool more = s0 + U * STEP < nsb;
+      if (more) {
 #pragma unroll
-      for (int u = 0; u < U; ++u) wide_load<T>(row + (long long)min(s0 + 4 * U + 4 * u + sub, nsb - 1) * SB, c, nxt[u]);
-    }
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int s = s0 + 4 * u + sub;
-      if (s < nsb) {
-#pragma unroll
-        for (int b = 0; b < B; ++b)
-          acc[b] += q8_dot<T>(cur[u], c, xq + (long long)b * K + s * 256, xd + (long long)b * (K / 32) + s * 8,
-                              xs8 + (long long)b * (K / 8) + s * 32);
+        for (int u = 0; u < U; ++u)
+          wide_load<T>(row + (long long)min(s0 + U * STEP + first + u * STEP, nsb - 1) * SB, c, nxt[u]);
       }
-    }
-    if (more) {
 #pragma unroll
-      for (int u = 0; u < U; ++u) cur[u] = nxt[u];
+      for (int u = 0; u < U; ++u) {
+        const int s = s0 + first + u * STEP;
+        if (s < nsb) {
+#pragma unroll
+          for (int b = 0; b < B; ++b)
+            acc[b] += q8_dot<T>(cur[u], c, xq + (long long)b * K + s * 256, xd + (long long)b * (K / 32) + s * 8,
+                                xs8 + (long long)b * (K / 8) + s * 32);
+        }
+      }
+      if (more) {
+#pragma unroll
+        for (int u = 0; u < U; ++u) cur[u] = nxt[u];
+      }
     }
   }
 #pragma unroll
   for (int b = 0; b < B; ++b) acc[b] = warp_sum(acc[b]);
-  if (lane) return;
+  if constexpr (S > 1) {
+    if (lane == 0) {
+#pragma unroll
+      for (int b = 0; b < B; ++b) red[warp][b] = acc[b];
+    }
+    __syncthreads();
+    if (part != 0 || lane != 0 || !active) return;
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+      float t = 0.f;
+#pragma unroll
+      for (int q = 0; q < S; ++q) t += red[warp + q][b];  // fixed order: deterministic
+      acc[b] = t;
+    }
+  } else {
+    if (lane || !active) return;
+  }
 #pragma unroll
   for (int b = 0; b < B; ++b) {
     const long long ob = (long long)b * ldy;
@@ -689,6 +486,91 @@ __global__ void __launch_bounds__(256) gguf_gemv_q8_swiglu_kernel(const uint8_t*
   }
 }
 
+// ---------------------------------------------------------------------------
+// Quantized MoE experts at decode (the reference's moe_gemm_gguf, tp/tp_qwen3_5.rs:
+// 1153-1231). Experts are stacked [G, R, K] as block rows (G = routed experts plus
+// the shared expert at index E, as the router's ids name them).
+//
+// gate/up: grid (ceil(I/8), routes); the warp of pair p of route r runs gate row 2p and
+// up row 2p+1 of expert ids[r] against batch row r / J of the quantized input and
+// writes act[r, p] = silu(gate) * up. Routes to experts outside [e_base, e_base +
+// e_count) (another rank's, under expert parallelism) are skipped.
+// ---------------------------------------------------------------------------
+template <int T>
+__global__ void __launch_bounds__(256) gguf_experts_q8_kernel(const uint8_t* __restrict__ W, long long row_bytes,
+                                                              const int8_t* __restrict__ xq,
+                                                              const float* __restrict__ xd,
+                                                              const float* __restrict__ xs8, const int* __restrict__ ids,
+                                                              __nv_bfloat16* __restrict__ act, int I, int K, int J,
+                                                              int e_base, int e_count) {
+  constexpr int SB = GgufBlock<T>::bytes;
+  using Raw = typename WideRaw<T>::type;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = blockIdx.y, pair = blockIdx.x * 8 + warp;
+  const int nsb = K / 256;
+  const int half = lane >> 4, c = lane & 7, sub = (lane >> 3) & 1;
+  pdl_wait_prior();  // ids come from the router
+  pdl_launch_dependents();
+  const int e = ids[r] - e_base;
+  if (pair >= I || e < 0 || (e_count > 0 && e >= e_count)) return;
+  const uint8_t* row = W + ((long long)e * 2 * I + 2 * pair + half) * row_bytes;
+  const int b = r / J;
+  const int8_t* q = xq + (long long)b * K;
+  const float* d8 = xd + (long long)b * (K / 32);
+  const float* s8 = xs8 + (long long)b * (K / 8);
+  float acc = 0.f;
+  for (int s = sub; s < nsb; s += 2) {
+    Raw raw;
+    wide_load<T>(row + (long long)s * SB, c, raw);
+    acc += q8_dot<T>(raw, c, q + s * 256, d8 + s * 8, s8 + s * 32);
+  }
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  const float up = __shfl_sync(0xffffffffu, acc, 16);
+  if (lane == 0) {
+    const float g = __bfloat162float(__float2bfloat16(acc));
+    const float u = __bfloat162float(__float2bfloat16(up));
+    act[(long long)r * I + pair] = __float2bfloat16(silu(g) * u);
+  }
+}
+
+// down + weighted combine + residual: grid (ceil(H/8), B); the warp of output row h of
+// batch row b walks (route, superblock) units of its J routes -- four units per warp
+// step -- and adds bf16(sum_j wts[j] * W_d[ids[j]][h] . act[j]) to x[b, h].
+template <int T>
+__global__ void __launch_bounds__(256) gguf_moe_down_q8_kernel(const uint8_t* __restrict__ W, long long row_bytes,
+                                                               const int8_t* __restrict__ aq,
+                                                               const float* __restrict__ ad,
+                                                               const float* __restrict__ as8,
+                                                               const int* __restrict__ ids,
+                                                               const float* __restrict__ wts, __nv_bfloat16* x, int H,
+                                                               int I, int J, int e_base, int e_count) {
+  constexpr int SB = GgufBlock<T>::bytes;
+  using Raw = typename WideRaw<T>::type;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = blockIdx.y, h = blockIdx.x * 8 + warp;
+  const int nsb = I / 256;
+  const int c = lane & 7, sub = lane >> 3;
+  pdl_wait_prior();
+  pdl_launch_dependents();
+  if (h >= H) return;
+  float acc = 0.f;
+  for (int u = sub; u < J * nsb; u += 4) {
+    const int j = u / nsb, s = u - j * nsb, r = b * J + j;
+    const int e = ids[r] - e_base;
+    if (e < 0 || (e_count > 0 && e >= e_count)) continue;
+    Raw raw;
+    wide_load<T>(W + ((long long)e * H + h) * row_bytes + (long long)s * SB, c, raw);
+    acc = fmaf(wts[r], q8_dot<T>(raw, c, aq + (long long)r * I + s * 256, ad + (long long)r * (I / 32) + s * 8,
+                                 as8 + (long long)r * (I / 8) + s * 32), acc);
+  }
+  acc = warp_sum(acc);
+  if (lane == 0) {
+    const float br = __bfloat162float(__float2bfloat16(acc));
+    x[(long long)b * H + h] = __float2bfloat16(__bfloat162float(x[(long long)b * H + h]) + br);
+  }
+}
+
 // 210-byte Q6_K superblocks -> 224-byte padded superblocks (same bytes + 14 zero bytes)
 __global__ void q6k_pad_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, long long nsb) {
   const long long s = blockIdx.x * (long long)blockDim.y + threadIdx.y;
@@ -731,44 +613,26 @@ static void gg_launch(const uint8_t* W, long long rb, const torch::Tensor& x, vo
 }
 
 template <int T, int MODE>
-static void gg_wide_launch(const uint8_t* W, long long rb, const torch::Tensor& x, void* y, int ldy,
-                           const __nv_bfloat16* resid, const float* nw, float eps, int N, int K, int B,
-                           cudaStream_t st) {
-  const size_t smem = (size_t)B * K * sizeof(float);
-  auto xp = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
-#define HX_GW_B(BB)                                                                                                 \
-  {                                                                                                                 \
-    if constexpr (MODE == 2) {                                                                                      \
-      auto k = gguf_gemv_wide_swiglu_kernel<T, BB>;                                                                 \
-      if (smem + 4096 > 48 * 1024) HX_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)); \
-      HX_CUDA_CHECK(hx_launch_pdl(k, dim3((N / 2 + 7) / 8), dim3(256), smem, st, W, rb, xp, y, ldy, nw, eps, N, K)); \
-    } else {                                                                                                        \
-      auto k = gguf_gemv_wide_kernel<T, BB, MODE>;                                                                  \
-      if (smem + 4096 > 48 * 1024) HX_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)); \
-      HX_CUDA_CHECK(hx_launch_pdl(k, dim3((N + 7) / 8), dim3(256), smem, st, W, rb, xp, y, ldy, resid, nw, eps, N, K)); \
-    }                                                                                                               \
-  }
-  switch (B) {
-    case 1: HX_GW_B(1) break;
-    case 2: HX_GW_B(2) break;
-    case 4: HX_GW_B(4) break;
-    case 8: HX_GW_B(8) break;
-    default: TORCH_CHECK(false, "gguf_gemv batch must be 1, 2, 4 or 8");
-  }
-#undef HX_GW_B
-}
-
-template <int T, int MODE>
 static void gg_q8_launch(const uint8_t* W, long long rb, const int8_t* xq, const float* xd, const float* xs8, void* y,
                          int ldy, const __nv_bfloat16* resid, int N, int K, int B, cudaStream_t st) {
+  // warps per row: keep >= ~4 resident waves of row work on 148 SMs; rows need at least
+  // 4 superblocks per warp for a split to pay
+  const int nsb = K / 256;
+  const int S = (N >= 16384 || nsb < 8) ? 1 : (N >= 4096 || nsb < 16) ? 2 : 4;
 #define HX_GQ_B(BB)                                                                                                 \
   {                                                                                                                 \
     if constexpr (MODE == 2) {                                                                                      \
       HX_CUDA_CHECK(hx_launch_pdl(gguf_gemv_q8_swiglu_kernel<T, BB>, dim3((N / 2 + 7) / 8), dim3(256), 0, st, W, rb, \
                                   xq, xd, xs8, y, ldy, N, K));                                                      \
+    } else if (S == 1) {                                                                                            \
+      HX_CUDA_CHECK(hx_launch_pdl(gguf_gemv_q8_kernel<T, BB, MODE, 1>, dim3((N + 7) / 8), dim3(256), 0, st, W, rb,  \
+                                  xq, xd, xs8, y, ldy, resid, N, K));                                               \
+    } else if (S == 2) {                                                                                            \
+      HX_CUDA_CHECK(hx_launch_pdl(gguf_gemv_q8_kernel<T, BB, MODE, 2>, dim3((N + 3) / 4), dim3(256), 0, st, W, rb,  \
+                                  xq, xd, xs8, y, ldy, resid, N, K));                                               \
     } else {                                                                                                        \
-      HX_CUDA_CHECK(hx_launch_pdl(gguf_gemv_q8_kernel<T, BB, MODE>, dim3((N + 7) / 8), dim3(256), 0, st, W, rb, xq, \
-                                  xd, xs8, y, ldy, resid, N, K));                                                   \
+      HX_CUDA_CHECK(hx_launch_pdl(gguf_gemv_q8_kernel<T, BB, MODE, 4>, dim3((N + 1) / 2), dim3(256), 0, st, W, rb,  \
+                                  xq, xd, xs8, y, ldy, resid, N, K));                                               \
     }                                                                                                               \
   }
   switch (B) {
@@ -791,25 +655,13 @@ static void gg_q8_mode(int mode, const uint8_t* W, long long rb, const torch::Te
   int8_t* xq = reinterpret_cast<int8_t*>(ws.data_ptr());
   float* xd = reinterpret_cast<float*>(ws.data_ptr<uint8_t>() + (long long)B * K);
   float* xs8 = xd + (long long)B * (K / 32);
-  HX_CUDA_CHECK(hx_launch_pdl(gguf_quant_x_kernel, dim3(B), dim3(512), 0, st,
+  HX_CUDA_CHECK(hx_launch_pdl(gguf_quant_x_kernel, quant_x_grid(K, B), dim3(512), 0, st,
                               reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), nw, eps, K, xq, xd, xs8));
   switch (mode) {
     case 0: gg_q8_launch<T, 0>(W, rb, xq, xd, xs8, y, ldy, resid, N, K, B, st); break;
     case 1: gg_q8_launch<T, 1>(W, rb, xq, xd, xs8, y, ldy, resid, N, K, B, st); break;
     case 2: gg_q8_launch<T, 2>(W, rb, xq, xd, xs8, y, ldy, resid, N, K, B, st); break;
     case 3: gg_q8_launch<T, 3>(W, rb, xq, xd, xs8, y, ldy, resid, N, K, B, st); break;
-    default: TORCH_CHECK(false, "bad mode");
-  }
-}
-
-template <int T>
-static void gg_wide_mode(int mode, const uint8_t* W, long long rb, const torch::Tensor& x, void* y, int ldy,
-                         const __nv_bfloat16* resid, const float* nw, float eps, int N, int K, int B, cudaStream_t st) {
-  switch (mode) {
-    case 0: gg_wide_launch<T, 0>(W, rb, x, y, ldy, resid, nw, eps, N, K, B, st); break;
-    case 1: gg_wide_launch<T, 1>(W, rb, x, y, ldy, resid, nw, eps, N, K, B, st); break;
-    case 2: gg_wide_launch<T, 2>(W, rb, x, y, ldy, resid, nw, eps, N, K, B, st); break;
-    case 3: gg_wide_launch<T, 3>(W, rb, x, y, ldy, resid, nw, eps, N, K, B, st); break;
     default: TORCH_CHECK(false, "bad mode");
   }
 }
@@ -975,11 +827,10 @@ void gguf_gemv(torch::Tensor W, int64_t type, int64_t K, torch::Tensor x, torch:
     const char* e = std::getenv("HELEXA_GGUF_XQ");
     return !(e && e[0] == '0');
   }();
-  TORCH_CHECK(x.is_contiguous(), "x must be contiguous");
+  TORCH_CHECK(x.is_contiguous() && reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0,
+              "x must be contiguous and 16-byte aligned");
   if (wide && q8 && type == kQ4_K) gg_q8_mode<kQ4_K>((int)mode, wp, rb, x, y.data_ptr(), y.stride(0), rp, np, (float)eps, N, (int)K, B, st);
   else if (wide && q8) gg_q8_mode<kQ6_Kp>((int)mode, wp, rb, x, y.data_ptr(), y.stride(0), rp, np, (float)eps, N, (int)K, B, st);
-  else if (wide && type == kQ4_K) gg_wide_mode<kQ4_K>((int)mode, wp, rb, x, y.data_ptr(), y.stride(0), rp, np, (float)eps, N, (int)K, B, st);
-  else if (wide) gg_wide_mode<kQ6_Kp>((int)mode, wp, rb, x, y.data_ptr(), y.stride(0), rp, np, (float)eps, N, (int)K, B, st);
   else if (type == kQ8_0) gg_mode<kQ8_0>((int)mode, wp, rb, x, y.data_ptr(), y.stride(0), rp, np, (float)eps, N, (int)K, B, st);
   else if (type == kQ4_K) gg_mode<kQ4_K>((int)mode, wp, rb, x, y.data_ptr(), y.stride(0), rp, np, (float)eps, N, (int)K, B, st);
   else if (type == kQ6_Kp) gg_mode<kQ6_Kp>((int)mode, wp, rb, x, y.data_ptr(), y.stride(0), rp, np, (float)eps, N, (int)K, B, st);
@@ -1034,4 +885,76 @@ torch::Tensor gguf_pad_q6k(torch::Tensor W) {
       W.data_ptr<uint8_t>(), out.data_ptr<uint8_t>(), nsb);
   HX_CUDA_CHECK(cudaGetLastError());
   return out;
+}
+
+// ---- quantized MoE experts (decode) ----
+static torch::Tensor q8_workspace(const torch::Tensor& like, int rows, int K, int8_t** xq, float** xd, float** xs8) {
+  auto ws = torch::empty({(long long)rows * K + (long long)rows * (K / 32) * 4 + (long long)rows * (K / 8) * 4},
+                         like.options().dtype(at::kByte));
+  *xq = reinterpret_cast<int8_t*>(ws.data_ptr());
+  *xd = reinterpret_cast<float*>(ws.data_ptr<uint8_t>() + (long long)rows * K);
+  *xs8 = *xd + (long long)rows * (K / 32);
+  return ws;
+}
+
+static bool q8_type_ok(const torch::Tensor& W, int64_t type) {
+  return (type == kQ4_K || type == kQ6_Kp) && reinterpret_cast<uintptr_t>(W.data_ptr()) % 16 == 0 &&
+         W.size(1) % 16 == 0;
+}
+
+// W: uint8 [G * 2I, K/256 * bytes] (gate/up rows interleaved per expert); x bf16 [B, K];
+// ids int32 [B*J]; act bf16 [B*J, I]
+void gguf_experts(torch::Tensor W, int64_t type, int64_t K, torch::Tensor x, torch::Tensor ids, torch::Tensor act,
+                  int64_t J, c10::optional<torch::Tensor> norm_w, double eps, int64_t e_base, int64_t e_count) {
+  TORCH_CHECK(W.is_cuda() && W.scalar_type() == at::kByte && W.dim() == 2 && W.is_contiguous(), "W uint8 [G*2I, bytes]");
+  TORCH_CHECK(q8_type_ok(W, type) && K % 256 == 0, "quantized experts need Q4_K or padded Q6_K rows of whole superblocks");
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.is_contiguous() && x.size(1) == K &&
+              reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0, "x [B, K] bf16, 16-byte aligned");
+  TORCH_CHECK(ids.scalar_type() == at::kInt && act.scalar_type() == at::kBFloat16 && act.is_contiguous(), "ids / act");
+  const int B = x.size(0), R = ids.numel(), I = act.size(1);
+  TORCH_CHECK(R == B * J && act.size(0) == R, "ids [B*J], act [B*J, I]");
+  auto st = at::cuda::getCurrentCUDAStream();
+  int8_t* xq; float *xd, *xs8;
+  auto ws = q8_workspace(x, B, K, &xq, &xd, &xs8);
+  const float* np = norm_w ? norm_w->data_ptr<float>() : nullptr;
+  HX_CUDA_CHECK(hx_launch_pdl(gguf_quant_x_kernel, quant_x_grid((int)K, B), dim3(512), 0, st,
+                              reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), np, (float)eps, (int)K, xq, xd, xs8));
+  auto ap = reinterpret_cast<__nv_bfloat16*>(act.data_ptr());
+  const dim3 grid((I + 7) / 8, R);
+  if (type == kQ4_K)
+    HX_CUDA_CHECK(hx_launch_pdl(gguf_experts_q8_kernel<kQ4_K>, grid, dim3(256), 0, st, W.data_ptr<uint8_t>(),
+                                (long long)W.size(1), xq, xd, xs8, ids.data_ptr<int>(), ap, I, (int)K, (int)J,
+                                (int)e_base, (int)e_count));
+  else
+    HX_CUDA_CHECK(hx_launch_pdl(gguf_experts_q8_kernel<kQ6_Kp>, grid, dim3(256), 0, st, W.data_ptr<uint8_t>(),
+                                (long long)W.size(1), xq, xd, xs8, ids.data_ptr<int>(), ap, I, (int)K, (int)J,
+                                (int)e_base, (int)e_count));
+}
+
+// W: uint8 [G * H, I/256 * bytes]; act bf16 [B*J, I]; wts f32 [B*J]; x bf16 [B, H] updated in place
+void gguf_moe_down(torch::Tensor W, int64_t type, int64_t I, torch::Tensor act, torch::Tensor ids, torch::Tensor wts,
+                   torch::Tensor x, int64_t J, int64_t e_base, int64_t e_count) {
+  TORCH_CHECK(W.is_cuda() && W.scalar_type() == at::kByte && W.dim() == 2 && W.is_contiguous(), "W uint8 [G*H, bytes]");
+  TORCH_CHECK(q8_type_ok(W, type) && I % 256 == 0, "quantized experts need Q4_K or padded Q6_K rows of whole superblocks");
+  TORCH_CHECK(act.scalar_type() == at::kBFloat16 && act.is_contiguous() && act.size(1) == I, "act [B*J, I] bf16");
+  TORCH_CHECK(wts.scalar_type() == at::kFloat && ids.scalar_type() == at::kInt, "ids int32, wts f32");
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.is_contiguous(), "x [B, H] bf16");
+  const int R = act.size(0), B = x.size(0), H = x.size(1);
+  TORCH_CHECK(R == B * J && ids.numel() == R && wts.numel() == R, "routes");
+  auto st = at::cuda::getCurrentCUDAStream();
+  int8_t* aq; float *ad, *as8;
+  auto ws = q8_workspace(act, R, I, &aq, &ad, &as8);
+  HX_CUDA_CHECK(hx_launch_pdl(gguf_quant_x_kernel, quant_x_grid((int)I, R), dim3(512), 0, st,
+                              reinterpret_cast<const __nv_bfloat16*>(act.data_ptr()), (const float*)nullptr, 0.f, (int)I,
+                              aq, ad, as8));
+  auto xp = reinterpret_cast<__nv_bfloat16*>(x.data_ptr());
+  const dim3 grid((H + 7) / 8, B);
+  if (type == kQ4_K)
+    HX_CUDA_CHECK(hx_launch_pdl(gguf_moe_down_q8_kernel<kQ4_K>, grid, dim3(256), 0, st, W.data_ptr<uint8_t>(),
+                                (long long)W.size(1), aq, ad, as8, ids.data_ptr<int>(), wts.data_ptr<float>(), xp, H,
+                                (int)I, (int)J, (int)e_base, (int)e_count));
+  else
+    HX_CUDA_CHECK(hx_launch_pdl(gguf_moe_down_q8_kernel<kQ6_Kp>, grid, dim3(256), 0, st, W.data_ptr<uint8_t>(),
+                                (long long)W.size(1), aq, ad, as8, ids.data_ptr<int>(), wts.data_ptr<float>(), xp, H,
+                                (int)I, (int)J, (int)e_base, (int)e_count));
 }

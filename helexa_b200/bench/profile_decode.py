@@ -54,7 +54,8 @@ class SkippingModel(FastModel):
                           cfg.norm_topk_prob, nb.ids, nb.wts, nb.counter)
             if "experts" not in skip:
                 C.gemv_experts(lw["w_gu"], nb.x, nb.ids.view(-1), nb.act_moe, ops.SILU_PAIR, J, lw["ln2"], eps)
-                C.moe_down(lw["w_d"], nb.act_moe, nb.ids, nb.wts, nb.x, None)
+                if "down" not in skip:
+                    C.moe_down(lw["w_d"], nb.act_moe, nb.ids, nb.wts, nb.x, None)
 
 
 def main():
@@ -68,7 +69,7 @@ def main():
     ap.add_argument("--eager", action="store_true")
     ap.add_argument("--quant", default=None, help="in-situ quantization (Q8_0, Q6_K, Q4_K, Q4_K_M)")
     ap.add_argument("--no-pdl", action="store_true", help="launch without programmatic dependent launch")
-    ap.add_argument("--skip", default="", help="profiling only: comma list of gdn,attn,gdn_core,attn_core,ffn,experts")
+    ap.add_argument("--skip", default="", help="profiling only: comma list of gdn,attn,gdn_core,attn_core,ffn,experts,down")
     args = ap.parse_args()
     if args.no_pdl:
         from .. import ops

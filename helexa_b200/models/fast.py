@@ -208,8 +208,54 @@ class QWeightCat:
         return torch.cat([p.dequant(C) if isinstance(p, QWeight) else p for p in self.parts], 0)
 
 
+class QExperts:
+    """Stacked MoE expert weights [G, R, K] held as GGUF block rows (uint8 [G * R,
+    row_bytes]; G = routed experts plus the shared expert at index E). Decode reads
+    them through the quantized expert kernels (gguf_experts / gguf_moe_down); prefill
+    dequantizes the whole stack into a bf16 scratch shared by every layer and runs the
+    grouped tcgen05 GEMM on it (the reference's moe_gemm_gguf serves these blocks,
+    tp/tp_qwen3_5.rs:1153-1231)."""
+
+    def __init__(self, raw: torch.Tensor, gtype: int, G: int, R: int, K: int):
+        if gtype == GGUF_Q6_K and raw.is_cuda:
+            raw, gtype = ops.C.gguf_pad_q6k(raw.contiguous()), GGUF_Q6_K_PADDED
+        self.raw, self.type, self.G, self.R, self.K = raw, gtype, G, R, K
+
+    @property
+    def shape(self):
+        return (self.G, self.R, self.K)
+
+    def nbytes(self) -> int:
+        return self.raw.numel()
+
+    def expert_bytes(self) -> int:
+        return self.raw.numel() // self.G
+
+    def dequant(self, C, out: torch.Tensor | None = None) -> torch.Tensor:
+        """bf16 [G, R, K] (into `out`'s storage when given)."""
+        n = self.G * self.R * self.K
+        if out is None or out.numel() < n:
+            out = torch.empty(n, dtype=torch.bfloat16, device=self.raw.device)
+        v = out.view(-1)[:n].view(self.G * self.R, self.K)
+        C.gguf_dequant(self.raw, self.type, self.K, v)
+        return v.view(self.G, self.R, self.K)
+
+
+def _extra_launches(w) -> int:
+    """Launches a quantized weight adds over one GEMV: the activation quantization in
+    front of each integer-dot GEMV, one GEMV per row segment, and for expert stacks
+    the quantization in front of the down projection as well."""
+    if isinstance(w, QExperts):
+        return 2
+    if isinstance(w, QWeightCat):
+        return len(w.parts) - 1 + sum(_extra_launches(p) for p in w.parts)
+    if isinstance(w, QWeight):
+        return 1 if w.type in (GGUF_Q4_K, GGUF_Q6_K_PADDED) and w.K % 256 == 0 else 0
+    return 0
+
+
 def _tbytes(t) -> int:
-    if isinstance(t, (QWeight, QWeightCat)):
+    if isinstance(t, (QWeight, QWeightCat, QExperts)):
         return t.nbytes()
     return t.numel() * t.element_size()
 
@@ -226,6 +272,7 @@ class FastModel:
         self.cfg, self.dims, self.device = cfg, dims, device
         self.layers, self.embed_w, self.lm_head, self.final_norm = layers, embed, lm_head, final_norm
         self.max_slots, self.max_len = max_slots, max_len
+        self._xscratch = None  # bf16 scratch for dequantized expert stacks (prefill)
         self.comm = comm  # parallel.TPComm or None (single rank)
         self.C = ops.C if device.type == "cuda" else None
         # vocab-parallel lm_head under the fused TP path: each rank streams V / ws rows per
@@ -388,7 +435,7 @@ class FastModel:
         for i, lw in enumerate(self.layers):
             for k, t in lw.items():
                 if k in ("w_gu", "w_d") and cfg.layer_uses_moe(i):
-                    per = t[0].numel() * t.element_size()
+                    per = t.expert_bytes() if isinstance(t, QExperts) else t[0].numel() * t.element_size()
                     n += per * (cfg.num_experts_per_tok + (1 if self.has_shared else 0))
                 else:
                     n += _tbytes(t)
@@ -491,6 +538,10 @@ class FastModel:
             C.gemv_router(lw["router"], nb.x, nb.rlogits, lw["ln2"], eps, E, k, self.has_shared,
                           cfg.norm_topk_prob, nb.ids, nb.wts, nb.counter)
             Wgu, Wd = lw["w_gu"], lw["w_d"]
+            if isinstance(Wgu, QExperts):
+                C.gguf_experts(Wgu.raw, Wgu.type, Wgu.K, nb.x, nb.ids.view(-1), nb.act_moe, J, lw["ln2"], eps)
+                C.gguf_moe_down(Wd.raw, Wd.type, Wd.K, nb.act_moe, nb.ids.view(-1), nb.wts.view(-1), nb.x, J)
+                return
             if self.moe_fused and nb.B <= 8 and not (d.ep and not self.comm.fused):
                 try:
                     self._moe_fused_call(lw, nb, E, k, J)
@@ -591,14 +642,16 @@ class FastModel:
             n += 3 + ((1 if self.moe_fused else 3) if cfg.layer_uses_moe(i) else 2)
             if self.comm is not None and self.dims.ws > 1:
                 n += self.comm.launches_per_reduce * 2
+            n += sum(_extra_launches(w) for w in self.layers[i].values())
         return n
 
-    def quantize_(self, scheme: str) -> None:
-        """In-situ quantization (the reference's ISQ, tp/isq.rs:252-326) of the dense
-        linear projections into GGUF k-quant blocks on the device: GDN in/out, attention
-        qkv/o and dense-MLP gate-up/down. Router, stacked experts, embedding and lm_head
-        stay bf16. Weights whose input width is not a multiple of the block size stay
-        bf16 too (a tensor-parallel shard must hold whole superblocks)."""
+    def quantize_(self, scheme: str, experts: bool = True) -> None:
+        """In-situ quantization (the reference's ISQ, tp/isq.rs:252-326) of the linear
+        projections into GGUF k-quant blocks on the device: GDN in/out, attention
+        qkv/o, dense-MLP gate-up/down and (`experts`, single rank, k-quant schemes) the
+        stacked MoE experts. Router, embedding and lm_head stay bf16. Weights whose
+        input width is not a multiple of the block size stay bf16 too (a
+        tensor-parallel shard must hold whole superblocks)."""
         if scheme not in QUANT_SCHEMES:
             raise ValueError(f"unknown quantization {scheme!r}; one of {sorted(QUANT_SCHEMES)}")
         if self.C is None:
@@ -608,6 +661,19 @@ class FastModel:
             keys = ["w_in", "out_w", "w_qkv", "o_w"]
             if not self.cfg.layer_uses_moe(i):
                 keys += ["w_gu", "w_d"]
+            elif experts and self.dims.ws == 1:
+                # stacked experts: every expert's rows quantized in one pass (whole rows on
+                # one rank; sharded-intermediate experts would split down_proj superblocks)
+                gts = {k: rule.get(k, rule["*"]) for k in ("w_gu", "w_d")}
+                ok = not any(isinstance(lw[k], QExperts) or lw[k].shape[2] % 256 or
+                             gts[k] not in (GGUF_Q4_K, GGUF_Q6_K) for k in gts)
+                for k, gt in (gts.items() if ok else ()):  # both stacks quantized or neither
+                    w = lw[k]
+                    G, R, K = w.shape
+                    lw[k] = QExperts(self.C.gguf_quant(w.reshape(G * R, K).contiguous(), gt), gt, G, R, K)
+                    del w
+                if ok:
+                    self.moe_fused = False
             for k in keys:
                 w = lw.get(k)
                 if w is None or isinstance(w, (QWeight, QWeightCat)) or w.dim() != 2:
@@ -954,11 +1020,18 @@ class FastModel:
         A = torch.empty(T * J, H, dtype=torch.bfloat16, device=dev)
         self.C.moe_route_prefill(logits, E, k, shared, cfg.norm_topk_prob, hn.contiguous(), ids, wts, rows, counts,
                                  offsets, cursor, tiles, ntiles, A, d.e0 if d.ep else 0, d.e_local if d.ep else 0)
-        I2 = lw["w_gu"].shape[1]
+        Wgu, Wd = lw["w_gu"], lw["w_d"]
+        if isinstance(Wgu, QExperts):
+            # quantized experts: dequantize the stacks into the shared bf16 scratch
+            need = max(Wgu.G * Wgu.R * Wgu.K, Wd.G * Wd.R * Wd.K)
+            if self._xscratch is None or self._xscratch[0].numel() < need:
+                self._xscratch = [torch.empty(need, dtype=torch.bfloat16, device=dev) for _ in range(2)]
+            Wgu, Wd = Wgu.dequant(self.C, self._xscratch[0]), Wd.dequant(self.C, self._xscratch[1])
+        I2 = Wgu.shape[1]
         act = torch.empty(T * J, I2 // 2, dtype=torch.bfloat16, device=dev)
-        self.C.gemm_grouped_dev(A, lw["w_gu"].view(-1, H), act, tiles, ntiles, I2, 1, self._gemm_err())
+        self.C.gemm_grouped_dev(A, Wgu.reshape(-1, H), act, tiles, ntiles, I2, 1, self._gemm_err())
         y = torch.empty(T * J, H, dtype=torch.bfloat16, device=dev)
-        self.C.gemm_grouped_dev(act, lw["w_d"].view(-1, lw["w_d"].shape[-1]), y, tiles, ntiles, H, 0,
+        self.C.gemm_grouped_dev(act, Wd.reshape(-1, Wd.shape[-1]), y, tiles, ntiles, H, 0,
                                 self._gemm_err())
         if out is None:
             out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)

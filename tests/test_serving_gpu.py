@@ -25,7 +25,9 @@ def _oracle_greedy(cfg, w, prompt, n):
     holds token-exact against HF transformers (tests/test_reference_parity.py; HF's own
     Qwen3-Next path would dispatch to library Triton kernels on a GPU box)."""
     from helexa_b200.models.reference import ReferenceModel
-    m = ReferenceModel(cfg, w)
+    # the CUDA model serves bf16 weights: the oracle holds the same rounded values in
+    # fp32, so only activation precision separates the two
+    m = ReferenceModel(cfg, {k: v.bfloat16().float() for k, v in w.items()})
     st = m.new_state()
     lg = m.forward(torch.tensor(prompt), st).double()
     toks, margins = [], []
@@ -50,15 +52,27 @@ def test_cuda_greedy_matches_oracle(name):
     want, margins = _oracle_greedy(cfg, w, prompt, 16)
     fm = FastModel.from_hf(cfg, w, "cuda", max_slots=2, max_len=256)
     r = FastRunner(fm, graph_steps=4)
+    # free-running greedy through captured 4-step graphs: agree until a near-tie
     r.reset(0)
     lg = r.prefill(0, prompt, 0)
     got = [int(lg.argmax())]
     while len(got) < 16:
         got += r.decode([0], [got[-1]], 4)[0]
     got = got[:16]
-    # bf16 weights and activations vs the fp32 oracle: logit differences of ~1e-2
-    n = _margin_rule(want, margins, got, 2e-2)
-    assert n >= 4, f"diverged at step {n}"
+    # bf16 activations vs fp32: teacher-forced logits differ by up to ~0.2 on these
+    # tiny random models, so a token may differ only where the oracle's top-2 margin
+    # is below that
+    tol = 0.25
+    _margin_rule(want, margins, got, tol)
+    # teacher-forced through the runner (one-step graphs fed the oracle's tokens):
+    # every step agrees unless the oracle itself is near a tie there
+    r.reset(0)
+    tf = [int(r.prefill(0, prompt, 0).argmax())]
+    for i in range(1, 16):
+        tf.append(r.decode([0], [want[i - 1]], 1)[0][0])
+    bad = [i for i in range(16) if tf[i] != want[i] and margins[i] >= tol]
+    assert not bad, [(i, want[i], tf[i], margins[i]) for i in bad]
+    assert sum(a == b for a, b in zip(tf, want)) >= 12
 
 
 def test_fast_runner_snapshot_restore_equals_continuation():
