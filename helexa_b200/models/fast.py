@@ -365,17 +365,19 @@ class FastModel:
         block rows (no host dequantization, no re-quantization) and run through the
         fused-dequant GEMVs at decode and dequant-then-tcgen05-GEMM at prefill; tensor
         parallel shards are cut on block boundaries (weights/gguf.py QuantLayer)."""
-        from ..weights.gguf import QuantLayer, QuantRows, quant_block_of
-        if cfg.family not in ("qwen3", "llama") or cfg.num_experts:
-            # MoE / hybrid GGUF files: dequantize on load (quantized experts are not served
-            # natively yet)
+        from ..weights.gguf import QuantExperts, QuantLayer, QuantRows, quant_block_of
+        if cfg.family not in ("qwen3", "llama", "qwen3_moe"):
+            # hybrid (GDN) GGUF files: dequantize on load
             return cls.from_hf(cfg, g.hf_get, device, rank=rank, ws=ws, **kw)
         device = torch.device(device)
-        blk = max(quant_block_of(g, f"blk.{i}.ffn_down.weight") for i in range(cfg.num_hidden_layers))
-        dims = layout.local_dims(cfg, rank, ws, inter_block=blk)
+        dense = [i for i in range(cfg.num_hidden_layers) if not cfg.layer_uses_moe(i)]
+        blk = max([quant_block_of(g, f"blk.{i}.ffn_down.weight") for i in dense] or [1])
+        dims = layout.local_dims(cfg, rank, ws, ep=kw.pop("ep", False), inter_block=blk)
         ql = QuantLayer(g)
 
         def dev(t):
+            if isinstance(t, QuantExperts):
+                return QExperts(t.raw.contiguous().to(device), t.gtype, t.G, t.R, t.K)
             if isinstance(t, QuantRows):
                 return QWeight(t.raw.contiguous().to(device), t.gtype, t.K)
             if isinstance(t, list):

@@ -143,7 +143,7 @@ def build_served_model(spec: ModelSpec) -> ServedModel:
         elif src.kind == "gguf":
             from ..weights.gguf import GGUFFile
             g = GGUFFile(src.path)
-            w = {n: g.tensor(t) for t, n in ((t, _hf(t)) for t in g.tensors) if n}
+            w = g.hf_state_dict()
         else:
             from ..weights.loader import SafetensorsDir
             st = SafetensorsDir(src.path)
@@ -200,11 +200,6 @@ def _build_tp_cpu(spec, src, cfg):
     runner = spawn_pool(spec.tensor_parallel, "helexa_b200.runtime.tp_pool:cpu_ref_runner", args, backend="gloo",
                         init_timeout_s=300)
     return serve_runner(spec, src, cfg, runner, [], runner.max_len)
-
-
-def _hf(gname: str):
-    from ..weights.gguf import _hf_name
-    return _hf_name(gname)
 
 
 class ModelRegistry:

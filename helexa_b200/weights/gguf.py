@@ -48,6 +48,8 @@ def _hf_name(gname: str) -> str | None:
     if not gname.startswith("blk."):
         return None
     _, i, rest = gname.split(".", 2)
+    if rest in _EXPS:  # [E, rows, cols] stack: no single HF tensor (hf_get slices it)
+        return None
     m = {
         "attn_norm.weight": "input_layernorm.weight", "ffn_norm.weight": "post_attention_layernorm.weight",
         "attn_q.weight": "self_attn.q_proj.weight", "attn_k.weight": "self_attn.k_proj.weight",
@@ -57,6 +59,19 @@ def _hf_name(gname: str) -> str | None:
         "ffn_down.weight": "mlp.down_proj.weight", "ffn_gate_inp.weight": "mlp.gate.weight",
     }.get(rest)
     return None if m is None else f"model.layers.{i}.{m}"
+
+
+# qwen3moe expert stacks: GGUF keeps every expert of a projection in one 3D tensor
+_EXPS = {"ffn_gate_exps.weight": "gate_proj", "ffn_up_exps.weight": "up_proj", "ffn_down_exps.weight": "down_proj"}
+_EXP_OF = {v: k for k, v in _EXPS.items()}
+
+
+def expert_name(hf: str) -> tuple[str, int] | None:
+    """`model.layers.{i}.mlp.experts.{e}.{proj}.weight` -> (GGUF stack name, e)."""
+    parts = hf.split(".")
+    if len(parts) == 8 and parts[3] == "mlp" and parts[4] == "experts" and parts[6] in _EXP_OF:
+        return f"blk.{parts[2]}.{_EXP_OF[parts[6]]}", int(parts[5])
+    return None
 
 
 def hf_to_gguf_name(hf: str) -> str:
@@ -160,7 +175,30 @@ class GGUFFile:
             return raw.view(torch.bfloat16).reshape(t.shape).float()
         return ops.C.gguf_dequant_host(raw.clone(), t.gtype, int(np.prod(t.shape))).reshape(t.shape)
 
+    def hf_state_dict(self) -> dict[str, torch.Tensor]:
+        """Every tensor decoded under its HF name; expert stacks split per expert."""
+        out = {}
+        for name in self.tensors:
+            hf = _hf_name(name)
+            if hf is not None:
+                out[hf] = self.tensor(name)
+                continue
+            rest = name.split(".", 2)[2] if name.startswith("blk.") else ""
+            if rest in _EXPS:
+                i = name.split(".")[1]
+                st = self.tensor(name)
+                for e in range(st.shape[0]):
+                    out[f"model.layers.{i}.mlp.experts.{e}.{_EXPS[rest]}.weight"] = st[e]
+        return out
+
     def hf_get(self, hf_name: str) -> torch.Tensor:
+        ex = expert_name(hf_name)
+        if ex is not None:
+            # one expert of a stack: the stack is decoded once and kept until another is asked for
+            name, e = ex
+            if getattr(self, "_stack", (None,))[0] != name:
+                self._stack = (name, self.tensor(name))
+            return self._stack[1][e]
         return self.tensor(hf_to_gguf_name(hf_name))
 
     def model_config(self) -> ModelConfig:
@@ -357,6 +395,9 @@ class QuantLayer:
         if cfg.qk_norm:
             out["q_norm"] = norm_f32(cfg, g.tensor(p + "attn_q_norm.weight"))
             out["k_norm"] = norm_f32(cfg, g.tensor(p + "attn_k_norm.weight"))
+        if cfg.layer_uses_moe(i):
+            out.update(self.moe(cfg, dims, i))
+            return out
         i0, i1 = dims.inter0, dims.inter0 + dims.inter
         gate = self.rows(p + "ffn_gate.weight", i0, i1)
         up = self.rows(p + "ffn_up.weight", i0, i1)
@@ -367,6 +408,54 @@ class QuantLayer:
         out["w_gu"] = gu
         out["w_d"] = self.cols(p + "ffn_down.weight", i0, i1)
         return out
+
+
+    def moe(self, cfg: ModelConfig, dims, i: int) -> dict:
+        """Router (bf16) and the expert stacks of a qwen3moe layer. Whole experts on
+        this rank (a single rank) keep their block rows: gate and up
+        rows interleave per expert into [E * 2I] rows, down stays [E * H] rows. An
+        expert sharded along its intermediate dim (tensor parallel) would split the
+        down projection's superblocks, so such shards are dequantized."""
+        from ..models.layout import interleave_rows
+        p = f"blk.{i}."
+        g = self.g
+        E, I, H = cfg.num_experts, cfg.moe_intermediate_size, cfg.hidden_size
+        out = {"router": g.tensor(p + "ffn_gate_inp.weight")}
+        e0, ne = (dims.e0, dims.e_local) if dims.ep else (0, E)
+        # (expert parallel ranks would need the quantized down kernel's cross-rank sum:
+        # their local experts are dequantized for now)
+        whole = dims.ws == 1
+        names = [p + n for n in ("ffn_gate_exps.weight", "ffn_up_exps.weight", "ffn_down_exps.weight")]
+        types = [g.tensors[n].gtype for n in names]
+        if whole and types[0] == types[1] and all(t in (Q4_K, Q6_K) for t in types):
+            bb, _ = _blocks(types[0])
+            gate = g.raw(names[0]).view(E, I, -1)[e0:e0 + ne]
+            up = g.raw(names[1]).view(E, I, -1)[e0:e0 + ne]
+            gu = torch.stack([gate, up], 2).reshape(ne * 2 * I, gate.shape[-1])
+            dn = g.raw(names[2]).view(E, H, -1)[e0:e0 + ne].reshape(ne * H, -1)
+            out["w_gu"] = QuantExperts(gu, types[0], ne, 2 * I, H)
+            out["w_d"] = QuantExperts(dn, types[2], ne, H, I)
+            return out
+        gate, up, down = (g.tensor(n) for n in names)
+        if dims.ep:
+            gate, up, down = gate[e0:e0 + ne], up[e0:e0 + ne], down[e0:e0 + ne]
+            i0, i1 = 0, I
+        else:
+            per = I // dims.ws
+            i0, i1 = dims.rank * per, (dims.rank + 1) * per
+        out["w_gu"] = torch.stack([interleave_rows(gate[e, i0:i1], up[e, i0:i1]) for e in range(gate.shape[0])])
+        out["w_d"] = down[:, :, i0:i1].contiguous()
+        return out
+
+
+@dataclass
+class QuantExperts:
+    """Expert stacks as GGUF block rows: uint8 [G * R, K / block * bytes]."""
+    raw: torch.Tensor
+    gtype: int
+    G: int
+    R: int
+    K: int
 
 
 def _dequant_rows(q: QuantRows) -> torch.Tensor:
