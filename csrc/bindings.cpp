@@ -30,7 +30,8 @@ void qk_rope_kv(torch::Tensor qkv, int64_t Hq, int64_t Hkv, int64_t D, int64_t q
                 c10::optional<torch::Tensor> axes, int64_t rope_off);
 void conv_ring_update(torch::Tensor proj, torch::Tensor ring, int64_t p0);
 void rs_norm_ag(std::vector<int64_t> bases, int64_t rank, int64_t stage_off, int64_t h_off, torch::Tensor x,
-                torch::Tensor w, double eps, torch::Tensor ctr, torch::Tensor err, double timeout_s, int64_t ctas);
+                torch::Tensor w, double eps, torch::Tensor ctr, torch::Tensor err, double timeout_s, int64_t ctas,
+                int64_t mc);
 int64_t rs_norm_ag_flag_bytes();
 void gemv_tma(torch::Tensor W, torch::Tensor x, torch::Tensor y, int64_t mode, c10::optional<torch::Tensor> resid,
               c10::optional<torch::Tensor> norm_w, double eps, torch::Tensor err);
@@ -144,7 +145,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("p0"), py::arg("q_out"), py::arg("eps"), py::arg("pos3") = py::none(), py::arg("axes") = py::none(),
         py::arg("rope_off") = 0);
   m.def("conv_ring_update", &conv_ring_update);
-  m.def("rs_norm_ag", &rs_norm_ag);
+  m.def("rs_norm_ag", &rs_norm_ag, py::arg("bases"), py::arg("rank"), py::arg("stage_off"), py::arg("h_off"),
+        py::arg("x"), py::arg("w"), py::arg("eps"), py::arg("ctr"), py::arg("err"), py::arg("timeout_s"),
+        py::arg("ctas"), py::arg("mc") = 0);
   m.def("rs_norm_ag_flag_bytes", &rs_norm_ag_flag_bytes);
   m.def("gemv_tma", &gemv_tma);
   m.def("gemv_tma_ar", &gemv_tma_ar);

@@ -46,7 +46,25 @@ struct TPPrefill {
   unsigned* ctr;             // local [2]: last completed epoch, CTA completion count
   int* err;
   unsigned long long timeout_ns;
+  char* mc;                  // NVLink multicast (NVLS) address of the region, or nullptr
 };
+
+// NVLS: one load returns the sum over every rank's copy of these 16 bytes, reduced in
+// the NVSwitch (f32 accumulation); one store writes 16 bytes into every rank's copy.
+HX_DEVICE bf16x8 mm_ld_reduce_bf16x8(const void* mc) {
+  uint4 r;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(mc)
+               : "memory");
+  return *reinterpret_cast<bf16x8*>(&r);
+}
+HX_DEVICE void mm_st_bf16x8(void* mc, const bf16x8& v) {
+  const uint4 u = *reinterpret_cast<const uint4*>(&v);
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc), "r"(u.x), "r"(u.y),
+               "r"(u.z), "r"(u.w)
+               : "memory");
+}
 
 HX_DEVICE unsigned* pf_flag(const TPPrefill& p, int dst, int which, int cta, int src) {
   return reinterpret_cast<unsigned*>(p.base[dst]) + ((size_t)which * kPFMaxCtas + cta) * kPFMaxRanks + src;
@@ -110,7 +128,27 @@ __global__ void __launch_bounds__(256) rs_norm_ag_kernel(TPPrefill p, __nv_bfloa
         for (int i = 0; i < CH; ++i)
 #pragma unroll
           for (int j = 0; j < 8; ++j) s[i][j] = 0.f;
-        for (int src = 0; src < p.ws; ++src) {  // rank order: identical sums on every rank
+        if (p.mc) {
+          // the switch sums every rank's partial; only the owner reduces a row and it
+          // broadcasts the result, so every rank still sees identical values
+          const bf16x8* part = reinterpret_cast<const bf16x8*>(p.mc + p.stage_off) + (long long)t * nv;
+          bf16x8 q[CH];
+#pragma unroll
+          for (int i = 0; i < CH; ++i) {
+            const int v = c0 + lane + 32 * i;
+            if (v < nv) q[i] = mm_ld_reduce_bf16x8(part + v);
+          }
+#pragma unroll
+          for (int i = 0; i < CH; ++i) {
+            if (c0 + lane + 32 * i < nv) {
+              float f[8];
+              unpack8(q[i], f);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) s[i][j] = f[j];
+            }
+          }
+        }
+        for (int src = 0; src < (p.mc ? 0 : p.ws); ++src) {  // rank order: identical sums on every rank
           const bf16x8* part = reinterpret_cast<const bf16x8*>(p.base[src] + p.stage_off) + (long long)t * nv;
           bf16x8 q[CH];
 #pragma unroll
@@ -153,8 +191,12 @@ __global__ void __launch_bounds__(256) rs_norm_ag_kernel(TPPrefill p, __nv_bfloa
 #pragma unroll
         for (int j = 0; j < 8; ++j) g[j] = g[j] * inv * w[v * 8 + j];
         const bf16x8 hv = pack8(g);
-        for (int dst = 0; dst < p.ws; ++dst)
-          reinterpret_cast<bf16x8*>(p.base[dst] + p.h_off)[(long long)t * nv + v] = hv;
+        if (p.mc) {
+          mm_st_bf16x8(reinterpret_cast<bf16x8*>(p.mc + p.h_off) + (long long)t * nv + v, hv);
+        } else {
+          for (int dst = 0; dst < p.ws; ++dst)
+            reinterpret_cast<bf16x8*>(p.base[dst] + p.h_off)[(long long)t * nv + v] = hv;
+        }
       }
       __syncwarp();
     }
@@ -177,7 +219,8 @@ using namespace hx;
 // the staging buffer holds this rank's row-parallel partial [T, H] bf16; x [T, H] bf16
 // (owned rows updated); w f32 [H]; h rows land in every rank's h buffer.
 void rs_norm_ag(std::vector<int64_t> bases, int64_t rank, int64_t stage_off, int64_t h_off, torch::Tensor x,
-                torch::Tensor w, double eps, torch::Tensor ctr, torch::Tensor err, double timeout_s, int64_t ctas) {
+                torch::Tensor w, double eps, torch::Tensor ctr, torch::Tensor err, double timeout_s, int64_t ctas,
+                int64_t mc) {
   const int ws = bases.size();
   TORCH_CHECK(ws >= 1 && ws <= kPFMaxRanks && rank >= 0 && rank < ws, "1..8 ranks");
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.is_contiguous() && x.dim() == 2, "x [T,H] bf16");
@@ -193,6 +236,8 @@ void rs_norm_ag(std::vector<int64_t> bases, int64_t rank, int64_t stage_off, int
   p.ctr = reinterpret_cast<unsigned*>(ctr.data_ptr());
   p.err = err.data_ptr<int>();
   p.timeout_ns = (unsigned long long)(timeout_s * 1e9);
+  p.mc = reinterpret_cast<char*>(mc);
+  TORCH_CHECK(mc % 16 == 0, "multicast address must be 16-byte aligned");
   auto st = at::cuda::getCurrentCUDAStream();
   auto xp = reinterpret_cast<__nv_bfloat16*>(x.data_ptr());
   const size_t smem = (size_t)8 * H * sizeof(__nv_bfloat16);  // one row per warp

@@ -52,6 +52,21 @@ stage, hbuf = comm.prefill_region(T, H)
 stage.copy_(torch.randn(T * H, device=dev).bfloat16())
 xs = torch.randn(T, H, device=dev).bfloat16(); w = torch.rand(H, device=dev) + 0.5
 res[f"prefill_rs_norm_ag_{T}x{H}"] = t_eager(lambda: comm.rs_norm_ag(xs, w, 1e-6))
+# the same step through NVLink multicast (switch-side reduction, multicast stores)
+g = torch.Generator(device=dev).manual_seed(7)
+part0 = torch.randn(T * H, device=dev, generator=g).bfloat16()
+x0 = torch.randn(T, H, device=dev, generator=torch.Generator(device=dev).manual_seed(8)).bfloat16()
+stage.copy_(part0); xa = x0.clone(); comm.rs_norm_ag(xa, w, 1e-6); torch.cuda.synchronize(); dist.barrier()
+h_p2p = hbuf.view(T, H).clone()
+comm.nvls, comm._pf_elems = True, 0
+stage2, hbuf2 = comm.prefill_region(T, H)
+res["nvls_available"] = float(comm.pf_mc != 0)
+if comm.pf_mc:
+    stage2.copy_(part0); xb = x0.clone(); comm.rs_norm_ag(xb, w, 1e-6); torch.cuda.synchronize(); dist.barrier()
+    res["nvls_vs_p2p_max_abs_diff"] = (hbuf2.view(T, H).float() - h_p2p.float()).abs().max().item()
+    res[f"prefill_rs_norm_ag_nvls_{T}x{H}"] = t_eager(lambda: comm.rs_norm_ag(xs, w, 1e-6))
+elif rank == 0:
+    print("nvls unavailable:", comm.nvls_error)
 o = torch.randn(T, H, device=dev).bfloat16(); hh = torch.empty_like(o)
 def nccl_path():
     dist.all_reduce(o)

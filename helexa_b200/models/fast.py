@@ -884,14 +884,17 @@ class FastModel:
         d, lw, cfg = self.dims, self.layers[i], self.cfg
         T = h.shape[0]
         kd, vd, K = d.gdn_kd, d.gdn_vd, cfg.linear_conv_kernel_dim
+        self._mark("gdn.in_proj")
         proj = self._linear(h, lw["w_in"])
         if self.C is not None:
             ring = self.conv[i][slot]
             o = torch.empty(T, vd, dtype=torch.bfloat16, device=h.device)
+            self._mark("gdn.core")
             self.C.gdn_prefill(proj, lw["conv_w"], ring, lw["A_log"], lw["dt_bias"], lw["gnorm"], self.rec[i][slot],
                                o, d.hk, d.hv, d.dk, p0, cfg.rms_norm_eps)
             # the ring keeps the last K conv inputs (slot = position % K) for decode
             self.C.conv_ring_update(proj, ring, p0)
+            self._mark("gdn.out_proj")
             return self._linear(o, lw["out_w"], out=out)
         mixed = proj[:, :2 * kd + vd]
         z = proj[:, 2 * kd + vd:2 * kd + 2 * vd]
@@ -923,8 +926,10 @@ class FastModel:
     def _attn_prefill(self, i: int, h: torch.Tensor, slot: int, p0: int, out=None) -> torch.Tensor:
         d, lw, cfg = self.dims, self.layers[i], self.cfg
         T, D = h.shape[0], d.D
+        self._mark("attn.qkv")
         qkv = self._linear(h, lw["w_qkv"])
         if self.C is not None:
+            self._mark("attn.rope_kv")
             # q/k-norm + partial RoPE + KV-cache append in one kernel; the sigmoid output
             # gate is applied in the attention kernel's epilogue
             q = torch.empty(T, d.hq * D, dtype=torch.bfloat16, device=h.device)
@@ -934,11 +939,13 @@ class FastModel:
                               pos3, self.mrope_axes if pos3 is not None else None, self._rope_delta_host[slot])
             o = torch.empty(T, d.hq * D, dtype=torch.bfloat16, device=h.device)
             gate = qkv[:, D:] if cfg.attn_output_gate else None
+            self._mark("attn.core")
             if self.attn_engine == "tc":
                 self.C.attn_prefill_tc(q, self.kc[i][slot], self.vc[i][slot], o, d.hq, p0, D ** -0.5, gate, d.qw,
                                        self._gemm_err())
             else:
                 self.C.attn_prefill(q, self.kc[i][slot], self.vc[i][slot], o, d.hq, p0, D ** -0.5, gate, d.qw)
+            self._mark("attn.o_proj")
             return self._linear(o, lw["o_w"], out=out)
         from .reference import apply_rope, rope_cos_sin
         qp = qkv[:, :d.hq * d.qw].view(T, d.hq, d.qw)
@@ -973,6 +980,7 @@ class FastModel:
             return self._linear(self._linear(hn, lw["w_gu"], 1), lw["w_d"], out=out)
         E, k = cfg.num_experts, cfg.num_experts_per_tok
         T = hn.shape[0]
+        self._mark("moe.router")
         logits = self._linear(hn, lw["router"], 2)
         if self.C is not None:
             return self._moe_prefill_device(lw, hn, logits, E, k, out)
@@ -1020,6 +1028,7 @@ class FastModel:
         tiles = torch.empty((T * J + 127) // 128 + G, 4, dtype=i32, device=dev)
         ntiles = torch.empty(1, dtype=i32, device=dev)
         A = torch.empty(T * J, H, dtype=torch.bfloat16, device=dev)
+        self._mark("moe.route")
         self.C.moe_route_prefill(logits, E, k, shared, cfg.norm_topk_prob, hn.contiguous(), ids, wts, rows, counts,
                                  offsets, cursor, tiles, ntiles, A, d.e0 if d.ep else 0, d.e_local if d.ep else 0)
         Wgu, Wd = lw["w_gu"], lw["w_d"]
@@ -1031,12 +1040,15 @@ class FastModel:
             Wgu, Wd = Wgu.dequant(self.C, self._xscratch[0]), Wd.dequant(self.C, self._xscratch[1])
         I2 = Wgu.shape[1]
         act = torch.empty(T * J, I2 // 2, dtype=torch.bfloat16, device=dev)
+        self._mark("moe.gemm_gate_up")
         self.C.gemm_grouped_dev(A, Wgu.reshape(-1, H), act, tiles, ntiles, I2, 1, self._gemm_err())
         y = torch.empty(T * J, H, dtype=torch.bfloat16, device=dev)
+        self._mark("moe.gemm_down")
         self.C.gemm_grouped_dev(act, Wd.reshape(-1, Wd.shape[-1]), y, tiles, ntiles, H, 0,
                                 self._gemm_err())
         if out is None:
             out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+        self._mark("moe.combine")
         out.zero_()  # the combine accumulates into its output
         self.C.moe_combine(y, rows, wts, out)
         return out
@@ -1097,17 +1109,24 @@ class FastModel:
                 tm.mark("gdn" if cfg.is_linear(i) else "attn")
             o = self._gdn_prefill(i, h, slot, p0, out) if cfg.is_linear(i) else \
                 self._attn_prefill(i, h, slot, p0, out)
+            self._mark("norm")
             self._reduce_add_norm(x, o, lw["ln2"], h)
             if tm is not None:
                 tm.mark("moe" if cfg.layer_uses_moe(i) else "mlp")
             o = self._ffn_prefill(i, h, out)
             nxt = self.layers[i + 1]["ln1"] if i + 1 < L else self.final_norm
+            self._mark("norm")
             self._reduce_add_norm(x, o, nxt, h)
         if tm is not None:
             tm.mark("head")
         self.pos[slot] = p0 + T
         # h holds the final-normed rows (all-gathered under TP): the lm_head reads the last
         return self.full_logits(self._linear(h[-1:], self.lm_head, 2))[0]
+
+    def _mark(self, name: str):
+        """Start a named prefill sub-phase on the optional PhaseTimer (profiling)."""
+        if self.prefill_timer is not None:
+            self.prefill_timer.mark(name)
 
     def full_logits(self, local: torch.Tensor) -> torch.Tensor:
         """[n, V_local] logits of this rank's vocabulary slice -> [n, V] on every rank."""

@@ -52,6 +52,11 @@ class TPComm:
         if self.mode not in ("p2p", "p2p1", "nccl", "host"):
             raise ValueError(f"unknown TP mode {self.mode!r}")
         self.fused = self.mode == "p2p"
+        # prefill reduce-scatter / all-gather through NVLink multicast (NVLS) when the
+        # devices support it (HELEXA_TP_NVLS=1); otherwise plain peer loads and stores
+        self.nvls = self.device.type == "cuda" and os.environ.get("HELEXA_TP_NVLS", "0") == "1"
+        self.nvls_error = None
+        self.pf_mc = 0
         self.launches_per_reduce = 0 if self.fused else 1
         if self.mode in ("p2p", "p2p1"):
             self._init_p2p(max_elems)
@@ -113,6 +118,19 @@ class TPComm:
         nbytes = need * 2
         self._pf_stage_off = flag
         self._pf_h_off = flag + nbytes
+        self.pf_mc = 0
+        if self.nvls:
+            region = self._nvls_region(flag + 2 * nbytes)
+            if region is not None:
+                self._pf_region = region
+                self._pf_elems, self._pf_hidden = need, hidden
+                self.pf_ctr = torch.zeros(2, dtype=torch.int32, device=self.device)
+                region[:flag].zero_()
+                bf = region[flag:flag + 2 * nbytes].view(torch.bfloat16)
+                self._pf_stage, self._pf_h = bf[:need], bf[need:]
+                torch.cuda.synchronize(self.device)
+                dist.barrier(group=self.group)
+                return self._pf_stage, self._pf_h
         region, handle = C.ipc_alloc(flag + 2 * nbytes, self.device.index)
         handles: list = [None] * self.ws
         dist.all_gather_object(handles, bytes(handle.numpy().tobytes()), group=self.group)
@@ -138,6 +156,31 @@ class TPComm:
         dist.barrier(group=self.group)
         return self._pf_stage, self._pf_h
 
+    def _nvls_region(self, nbytes: int):
+        """The prefill region in symmetric memory bound to an NVLink multicast object
+        (torch's symmetric-memory rendezvous maps every rank's copy and the multicast
+        address): the fused kernel then reduces with multimem.ld_reduce in the switch
+        and broadcasts with multimem.st. None (peer-memory path) when the devices have
+        no multicast support."""
+        try:
+            import torch.distributed._symmetric_memory as symm_mem
+            g = self.group if self.group is not None else dist.group.WORLD
+            try:
+                symm_mem.enable_symm_mem_for_group(g.group_name)
+            except Exception:
+                pass
+            t = symm_mem.empty(nbytes, dtype=torch.uint8, device=self.device)
+            hdl = symm_mem.rendezvous(t, g.group_name)
+            if not hdl.has_multicast_support():
+                return None
+            self.pf_bases = [int(p) for p in hdl.buffer_ptrs]
+            self.pf_mc = int(hdl.multicast_ptr)
+            self._pf_symm = hdl
+            return t
+        except Exception as e:  # no symmetric memory here: peer-memory path
+            self.nvls_error = repr(e)
+            return None
+
     def rs_norm_ag(self, x: torch.Tensor, w: torch.Tensor, eps: float):
         """x[own rows] += sum over ranks of the staged partials; every rank's h buffer
         receives RMSNorm(x) * w for all rows (csrc/tp_prefill.cu)."""
@@ -148,7 +191,7 @@ class TPComm:
         rows = (T + self.ws - 1) // self.ws
         ctas = max(1, min(2 * self.sms_hint, (rows + 7) // 8))
         ops.C.rs_norm_ag(self.pf_bases, self.rank, self._pf_stage_off, self._pf_h_off, x, w, eps, self.pf_ctr,
-                         self.err, self.timeout_s, ctas)
+                         self.err, self.timeout_s, ctas, self.pf_mc)
 
     @property
     def sms_hint(self) -> int:

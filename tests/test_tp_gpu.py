@@ -44,6 +44,9 @@ def _run(rank, ws, port, mode, q, name="tiny-qwen3-next", ep=False):
 def _run_inner(rank, ws, port, mode, q, name, ep):
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    if mode and mode.endswith("+nvls"):  # the prefill reduction through NVLink multicast
+        os.environ["HELEXA_TP_NVLS"] = "1"
+        mode = mode[:-5]
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
     dist.init_process_group("nccl", rank=rank, world_size=ws, device_id=dev)
@@ -91,7 +94,8 @@ def _run_inner(rank, ws, port, mode, q, name, ep):
         torch.cuda.synchronize()
         if comm is not None:
             comm.check()
-        q.put((rank, lg.float().cpu().numpy(), torch.stack(tf).numpy(), nb.out_tokens[0, :16].cpu().numpy()))
+        info = {"nvls": bool(comm is not None and comm.pf_mc), "nvls_error": getattr(comm, "nvls_error", None)}
+        q.put((rank, lg.float().cpu().numpy(), torch.stack(tf).numpy(), nb.out_tokens[0, :16].cpu().numpy(), info))
         if comm is not None:
             comm.close()
     finally:
@@ -110,8 +114,8 @@ def _launch(ws, mode, name="tiny-qwen3-next", ep=False):
     res, t0 = {}, time.time()
     while len(res) < ws:
         try:
-            r, a, t, b = q.get(timeout=5)
-            res[r] = (torch.from_numpy(a), torch.from_numpy(t), torch.from_numpy(b))
+            r, a, t, b, info = q.get(timeout=5)
+            res[r] = (torch.from_numpy(a), torch.from_numpy(t), torch.from_numpy(b), info)
         except queue.Empty:
             dead = [p.exitcode for p in ps if p.exitcode not in (None, 0)]
             if dead or time.time() - t0 > 240:
@@ -177,3 +181,18 @@ def test_ep2_matches_single_gpu():
         step_cos = [_cos(res[r][1][i], single[1][i]) for i in range(single[1].shape[0])]
         assert sorted(step_cos)[len(step_cos) // 2] > 0.99 and min(step_cos) > 0.85, step_cos
         assert torch.equal(res[r][2], res[0][2])
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_tp2_nvls_prefill_matches_p2p():
+    """The prefill reduce-scatter + norm + all-gather through NVLink multicast
+    (multimem.ld_reduce in the switch, multimem.st broadcast) reproduces the peer-memory
+    kernel's prefill and the single GPU."""
+    res = _results(2, "p2p+nvls")
+    if not res[0][3]["nvls"]:
+        pytest.skip(f"no NVLink multicast on this box: {res[0][3]['nvls_error']}")
+    p2p, single = _results(2, "p2p"), _results(1, None)[0]
+    for r in range(2):
+        assert _cos(res[r][0], p2p[r][0]) > 0.999
+        assert _cos(res[r][0], single[0]) > 0.995
+        assert torch.equal(res[r][0], res[0][0])  # ranks agree bit for bit
