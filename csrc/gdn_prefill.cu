@@ -30,53 +30,85 @@ namespace hx {
 
 constexpr int kGC = 64;  // chunk length
 
-// grid (T, 2*Hk + Hv), block D (= Dk = Dv).
+// grid (ceil(T / kPrepTok), 2*Hk + Hv), block D (= Dk = Dv): thread d of a CTA owns one
+// channel of one group (a q head, a k head or a v head) for kPrepTok consecutive tokens
+// and slides the causal conv window along them in registers, so each input value is
+// read once (one CTA per token and group was launch-bound: half a million 128-thread
+// CTAs per layer at 8K tokens).
+constexpr int kPrepTok = 32;
+constexpr int kMaxConv = 4;
+
 template <int D>
-__global__ void gdn_prep_kernel(const __nv_bfloat16* __restrict__ proj, int ldp, const float* __restrict__ conv_w,
-                                const __nv_bfloat16* __restrict__ ring, int KC, int p0, const float* __restrict__ A_log,
-                                const float* __restrict__ dt_bias, int Hk, int Hv, int Tp, __nv_bfloat16* __restrict__ qo,
-                                __nv_bfloat16* __restrict__ ko, __nv_bfloat16* __restrict__ vo, float* __restrict__ go,
-                                float* __restrict__ bo) {
-  __shared__ float red[D / 32];
-  const int t = blockIdx.x, grp = blockIdx.y, d = threadIdx.x;
+__global__ void __launch_bounds__(D) gdn_prep_kernel(const __nv_bfloat16* __restrict__ proj, int ldp,
+                                                     const float* __restrict__ conv_w,
+                                                     const __nv_bfloat16* __restrict__ ring, int KC, int p0,
+                                                     const float* __restrict__ A_log, const float* __restrict__ dt_bias,
+                                                     int Hk, int Hv, int T, int Tp, __nv_bfloat16* __restrict__ qo,
+                                                     __nv_bfloat16* __restrict__ ko, __nv_bfloat16* __restrict__ vo,
+                                                     float* __restrict__ go, float* __restrict__ bo) {
+  __shared__ float red[2][D / 32];
+  const int t0 = blockIdx.x * kPrepTok, grp = blockIdx.y, d = threadIdx.x;
   const int kd = Hk * D;
   int c;
   if (grp < Hk) c = grp * D + d;
   else if (grp < 2 * Hk) c = kd + (grp - Hk) * D + d;
   else c = 2 * kd + (grp - 2 * Hk) * D + d;
-  float acc = 0.f;
-  for (int j = 0; j < KC; ++j) {
-    const int tt = t - (KC - 1) + j;  // token index relative to this prefill
+  // right-aligned taps: win[j] holds the input at token t - (kMaxConv-1) + j and w[j] its
+  // tap (zero for j < kMaxConv - KC), so every index below is a compile-time constant
+  float w[kMaxConv], win[kMaxConv];
+#pragma unroll
+  for (int j = 0; j < kMaxConv; ++j) {
+    const int tap = j - (kMaxConv - KC);
+    w[j] = tap >= 0 ? conv_w[c * KC + tap] : 0.f;
+    win[j] = 0.f;
+  }
+#pragma unroll
+  for (int j = 0; j < kMaxConv - 1; ++j) {
+    const int tt = t0 - (kMaxConv - 1) + j;  // token index relative to this prefill
+    if (j < kMaxConv - KC) continue;          // outside the kernel's reach
     float xv;
     if (tt >= 0) xv = __bfloat162float(proj[(long long)tt * ldp + c]);
     else {
       const int pp = p0 + tt;  // absolute position of an earlier token
       xv = pp >= 0 ? __bfloat162float(ring[c * KC + (pp % KC)]) : 0.f;
     }
-    acc += conv_w[c * KC + j] * xv;
+    win[j] = xv;
   }
-  float y = __bfloat162float(__float2bfloat16(silu(acc)));
-  if (grp < 2 * Hk) {
-    float ss = warp_sum(y * y);
-    if ((d & 31) == 0) red[d >> 5] = ss;
-    __syncthreads();
-    float tot = 0.f;
-    for (int w = 0; w < D / 32; ++w) tot += red[w];
-    float sc = rsqrtf(tot + 1e-6f) * (grp < Hk ? rsqrtf((float)D) : 1.f);
-    const int h = grp < Hk ? grp : grp - Hk;
-    __nv_bfloat16* dst = grp < Hk ? qo : ko;
-    dst[((long long)h * Tp + t) * D + d] = __float2bfloat16(y * sc);
-  } else {
-    const int h = grp - 2 * Hk;
-    vo[((long long)h * Tp + t) * D + d] = __float2bfloat16(y);
-    if (d == 0) {
-      const __nv_bfloat16* pr = proj + (long long)t * ldp + 2 * kd + 2 * Hv * D;
-      float bb = __bfloat162float(pr[h]);
-      float aa = __bfloat162float(pr[Hv + h]);
-      float sp = aa + dt_bias[h];
-      sp = sp > 20.f ? sp : log1pf(expf(sp));
-      go[(long long)h * Tp + t] = -expf(A_log[h]) * sp;
-      bo[(long long)h * Tp + t] = 1.f / (1.f + expf(-bb));
+  const int t1 = min(T, t0 + kPrepTok);
+  for (int t = t0; t < t1; ++t) {
+    win[kMaxConv - 1] = __bfloat162float(proj[(long long)t * ldp + c]);
+    float acc = 0.f;
+#pragma unroll
+    for (int j = kMaxConv - 4; j < kMaxConv; ++j)
+      if (j >= kMaxConv - KC) acc += w[j] * win[j];
+#pragma unroll
+    for (int j = 0; j < kMaxConv - 1; ++j) win[j] = win[j + 1];
+    const float y = __bfloat162float(__float2bfloat16(silu(acc)));
+    if (grp < 2 * Hk) {
+      // L2 norm over the head; red is double-buffered, so one barrier per token suffices
+      const float ss = warp_sum(y * y);
+      float* r = red[t & 1];
+      if ((d & 31) == 0) r[d >> 5] = ss;
+      __syncthreads();
+      float tot = 0.f;
+#pragma unroll
+      for (int q = 0; q < D / 32; ++q) tot += r[q];
+      const float sc = rsqrtf(tot + 1e-6f) * (grp < Hk ? rsqrtf((float)D) : 1.f);
+      const int h = grp < Hk ? grp : grp - Hk;
+      __nv_bfloat16* dst = grp < Hk ? qo : ko;
+      dst[((long long)h * Tp + t) * D + d] = __float2bfloat16(y * sc);
+    } else {
+      const int h = grp - 2 * Hk;
+      vo[((long long)h * Tp + t) * D + d] = __float2bfloat16(y);
+      if (d == 0) {
+        const __nv_bfloat16* pr = proj + (long long)t * ldp + 2 * kd + 2 * Hv * D;
+        const float bb = __bfloat162float(pr[h]);
+        const float aa = __bfloat162float(pr[Hv + h]);
+        float sp = aa + dt_bias[h];
+        sp = sp > 20.f ? sp : log1pf(expf(sp));
+        go[(long long)h * Tp + t] = -expf(A_log[h]) * sp;
+        bo[(long long)h * Tp + t] = 1.f / (1.f + expf(-bb));
+      }
     }
   }
 }
@@ -426,22 +458,35 @@ __global__ void __launch_bounds__(256, 1) gdn_scan_kernel(const __nv_bfloat16* _
   }
 }
 
-// out[t, h*D + d] = rmsnorm(o[t, h, :])[d] * w[d] * silu(z[t, h, d]);  grid (T, Hv), block D
+// out[t, h*D + d] = rmsnorm(o[t, h, :])[d] * w[d] * silu(z[t, h, d]); one warp per
+// (token, head) row, eight rows per CTA (no block barriers).
 template <int D>
-__global__ void gdn_onorm_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ proj, int ldp,
-                                 int zoff, const float* __restrict__ nw, float eps, int Hv,
-                                 __nv_bfloat16* __restrict__ out) {
-  __shared__ float red[D / 32];
-  const int t = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
-  float x = __bfloat162float(o[((long long)t * Hv + h) * D + d]);
-  float ss = warp_sum(x * x);
-  if ((d & 31) == 0) red[d >> 5] = ss;
-  __syncthreads();
-  float tot = 0.f;
-  for (int w = 0; w < D / 32; ++w) tot += red[w];
-  float nrm = __bfloat162float(__float2bfloat16(x * rsqrtf(tot / D + eps))) * nw[d];
-  float z = __bfloat162float(proj[(long long)t * ldp + zoff + h * D + d]);
-  out[(long long)t * Hv * D + h * D + d] = __float2bfloat16(nrm * silu(z));
+__global__ void __launch_bounds__(256) gdn_onorm_kernel(const __nv_bfloat16* __restrict__ o,
+                                                        const __nv_bfloat16* __restrict__ proj, int ldp, int zoff,
+                                                        const float* __restrict__ nw, float eps, int Hv, int rows,
+                                                        __nv_bfloat16* __restrict__ out) {
+  constexpr int PL = D / 32;  // values per lane
+  const int lane = threadIdx.x & 31, row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int t = row / Hv, h = row - t * Hv;
+  const __nv_bfloat16* orow = o + (long long)row * D + lane * PL;
+  const __nv_bfloat16* zrow = proj + (long long)t * ldp + zoff + h * D + lane * PL;
+  float x[PL], z[PL];
+#pragma unroll
+  for (int i = 0; i < PL; ++i) {
+    x[i] = __bfloat162float(orow[i]);
+    z[i] = __bfloat162float(zrow[i]);
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < PL; ++i) ss += x[i] * x[i];
+  const float inv = rsqrtf(warp_sum(ss) / D + eps);
+  __nv_bfloat16* dst = out + (long long)t * Hv * D + h * D + lane * PL;
+#pragma unroll
+  for (int i = 0; i < PL; ++i) {
+    const float nrm = __bfloat162float(__float2bfloat16(x[i] * inv)) * nw[lane * PL + i];
+    dst[i] = __float2bfloat16(nrm * silu(z[i]));
+  }
 }
 
 }  // namespace hx
@@ -456,6 +501,7 @@ void gdn_prefill(torch::Tensor proj, torch::Tensor conv_w, torch::Tensor ring, t
                  torch::Tensor dt_bias, torch::Tensor norm_w, torch::Tensor state, torch::Tensor out, int64_t Hk,
                  int64_t Hv, int64_t D, int64_t p0, double eps) {
   TORCH_CHECK(D == 128 || D == 64 || D == 32, "GDN head dim must be 32, 64 or 128");
+  TORCH_CHECK(conv_w.size(1) >= 1 && conv_w.size(1) <= kMaxConv, "conv kernel of 1..4 taps");
   TORCH_CHECK(proj.is_contiguous() && state.is_contiguous() && out.is_contiguous(), "contiguous inputs");
   const int T = proj.size(0), ldp = proj.size(1);
   const int nch = (T + kGC - 1) / kGC, Tp = nch * kGC;
@@ -472,10 +518,10 @@ void gdn_prefill(torch::Tensor proj, torch::Tensor conv_w, torch::Tensor ring, t
   auto bp = [](const torch::Tensor& t) { return reinterpret_cast<__nv_bfloat16*>(t.data_ptr()); };
 #define HX_GDN_LAUNCH(DD)                                                                                           \
   {                                                                                                                 \
-    gdn_prep_kernel<DD><<<dim3(T, 2 * Hk + Hv), DD, 0, st>>>(bp(proj), ldp, conv_w.data_ptr<float>(), bp(ring), KC, \
-                                                             (int)p0, A_log.data_ptr<float>(),                      \
-                                                             dt_bias.data_ptr<float>(), Hk, Hv, Tp, bp(qn), bp(kn), \
-                                                             bp(vn), g.data_ptr<float>(), beta.data_ptr<float>());  \
+    gdn_prep_kernel<DD><<<dim3((T + kPrepTok - 1) / kPrepTok, 2 * Hk + Hv), DD, 0, st>>>(                      \
+        bp(proj), ldp, conv_w.data_ptr<float>(), bp(ring), KC, (int)p0, A_log.data_ptr<float>(),                     \
+        dt_bias.data_ptr<float>(), Hk, Hv, T, Tp, bp(qn), bp(kn), bp(vn), g.data_ptr<float>(),                       \
+        beta.data_ptr<float>());                                                                                     \
     const size_t sm1 = (size_t)(4 * kGC * (DD + 8) + kGC * (kGC + 8)) * 2 + (size_t)(kGC * (kGC + 1) + 2 * kGC) * 4; \
     HX_CUDA_CHECK(cudaFuncSetAttribute(gdn_chunk_kernel<DD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm1)); \
     gdn_chunk_kernel<DD><<<dim3(nch, Hv), 256, sm1, st>>>(bp(qn), bp(kn), bp(vn), g.data_ptr<float>(),             \
@@ -487,8 +533,9 @@ void gdn_prefill(torch::Tensor proj, torch::Tensor conv_w, torch::Tensor ring, t
     gdn_scan_kernel<DD><<<dim3(DD / 32, Hv), 256, sm2, st>>>(bp(U), bp(Wm), bp(P), bp(Qg), bp(Kd),                \
                                                              GC.data_ptr<float>(), state.data_ptr<float>(), Hv, T, \
                                                              nch, bp(o));                                          \
-    gdn_onorm_kernel<DD><<<dim3(T, Hv), DD, 0, st>>>(bp(o), bp(proj), ldp, 2 * Hk * DD + Hv * DD,                  \
-                                                     norm_w.data_ptr<float>(), (float)eps, Hv, bp(out));            \
+    gdn_onorm_kernel<DD><<<dim3((T * Hv + 7) / 8), 256, 0, st>>>(bp(o), bp(proj), ldp, 2 * Hk * DD + Hv * DD,      \
+                                                                  norm_w.data_ptr<float>(), (float)eps, Hv, T * Hv, \
+                                                                  bp(out));                                         \
   }
   if (D == 128) HX_GDN_LAUNCH(128)
   else if (D == 64) HX_GDN_LAUNCH(64)

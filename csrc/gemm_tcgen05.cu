@@ -23,6 +23,8 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 #include <unordered_map>
 
@@ -51,6 +53,7 @@ struct GemmParams {
   int num_entries;
   const int* num_entries_dev;  // grouped mode: device-side entry count (overrides num_entries)
   int b_rows_per_group;    // grouped mode: tile b_row0 holds a group index scaled by this
+  int tma_store;           // 1: the epilogue stages 32 x 32 chunks in shared memory and TMA-stores them
   int* err;
 };
 
@@ -62,11 +65,15 @@ struct GemmSmem {
   uint64_t tfull[2], tempty[2];
   uint32_t tmem_base;
   int abort;
+  // epilogue staging: per epilogue warp two 4 KB buffers (32 rows x up to 128 bytes),
+  // 1 KB aligned so the TMA swizzle pattern matches the absolute address bits
+  alignas(1024) unsigned char stg[4][2][4096];
 };
 
 template <int BN, int STAGES>
 __global__ void __launch_bounds__(192, 1) gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap mapA,
                                                               const __grid_constant__ CUtensorMap mapB,
+                                                              const __grid_constant__ CUtensorMap mapC,
                                                               GemmParams p) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // re-align to 1 KB (the 128B-swizzle atoms must start on 1024-byte boundaries)
@@ -86,6 +93,7 @@ __global__ void __launch_bounds__(192, 1) gemm_tcgen05_kernel(const __grid_const
     tc::fence_barrier_init();
     tc::prefetch_tmap(&mapA);
     tc::prefetch_tmap(&mapB);
+    if (p.tma_store) tc::prefetch_tmap(&mapC);
   }
   if (warp == 1) {
     tc::tmem_alloc(&s->tmem_base, kTmemCols);
@@ -160,9 +168,17 @@ __global__ void __launch_bounds__(192, 1) gemm_tcgen05_kernel(const __grid_const
     }
   } else {
     // ------------------------------ epilogue (warps 2-5) ----------------------
+    // Each warp owns a 32-row slab (its TMEM lane quarter). With TMA stores, every
+    // 32-column chunk is written row-per-lane into a swizzled shared-memory buffer
+    // (bank-conflict free) and one lane issues a bulk tensor store of the 32-row box;
+    // two buffers alternate so the next chunk is staged while the previous one drains.
+    // Per-thread row stores -- one 16-byte piece per row per instruction, 32 rows per
+    // warp instruction -- capped the store rate near 0.4 TB/s, which bounded every GEMM
+    // whose output is large next to its K. Grouped tiles whose slab holds rows of the
+    // next tile (fewer than 32 valid rows left) keep the per-thread path.
     const int q = warp & 3;              // TMEM lane quarter this warp may access
     const int row_in_tile = q * 32 + lane;
-    int it = 0;
+    int it = 0, staged = 0;
     for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++it) {
       const int acc = it & 1;
       const uint32_t tph = (it >> 1) & 1;
@@ -173,14 +189,54 @@ __global__ void __launch_bounds__(192, 1) gemm_tcgen05_kernel(const __grid_const
       const bool valid = row_in_tile < rows;
       const long long orow = (long long)(out_row + row_in_tile);
       const int n0 = n_blk * BN;
+      const bool use_tma = p.tma_store && (p.tiles == nullptr || rows - q * 32 >= 32);
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         float v[32];
         tc::tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + acc * BN + c * 32, v);
         const int col = n0 + c * 32;
-        if (!valid || col >= p.N) continue;
+        if (col >= p.N) continue;
+        if (use_tma) {
+          unsigned char* buf = s->stg[q][staged & 1];
+          if (staged >= 2) {  // the store issued from this buffer two chunks ago has read it
+            if (lane == 0) tc::bulk_wait_read<1>();
+            __syncwarp();
+          }
+          if (p.epi == kEpiF32) {  // 128-byte rows, 128B swizzle: chunk j at j ^ (row % 8)
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              *reinterpret_cast<float4*>(buf + lane * 128 + 16 * (j ^ (lane & 7))) =
+                  make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+          } else if (p.epi == kEpiSwiGLU) {  // 32-byte rows, 32B swizzle: chunk j at j ^ ((row / 4) % 2)
+            float o[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              float g = __bfloat162float(__float2bfloat16(v[2 * i]));
+              float u = __bfloat162float(__float2bfloat16(v[2 * i + 1]));
+              o[i] = silu(g) * u;
+            }
+#pragma unroll
+            for (int j = 0; j < 2; ++j)
+              *reinterpret_cast<bf16x8*>(buf + lane * 32 + 16 * (j ^ ((lane >> 2) & 1))) = pack8(o + 8 * j);
+          } else {  // 64-byte rows, 64B swizzle: chunk j at j ^ ((row / 2) % 4)
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              *reinterpret_cast<bf16x8*>(buf + lane * 64 + 16 * (j ^ ((lane >> 1) & 3))) = pack8(v + 8 * j);
+          }
+          tc::fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tc::tma_store_2d(&mapC, buf, p.epi == kEpiSwiGLU ? col / 2 : col, out_row + q * 32);
+            tc::bulk_commit();
+          }
+          ++staged;
+          continue;
+        }
+        if (!valid) continue;
         if (col + 32 > p.N) {  // ragged right edge: scalar stores of the valid columns
-          for (int i = 0; i < p.N - col; ++i) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {  // constant indices keep v in registers
+            if (i >= p.N - col) break;
             if (p.epi == kEpiF32) reinterpret_cast<float*>(p.C)[orow * p.ldc + col + i] = v[i];
             else reinterpret_cast<__nv_bfloat16*>(p.C)[orow * p.ldc + col + i] = __float2bfloat16(v[i]);
           }
@@ -211,6 +267,9 @@ __global__ void __launch_bounds__(192, 1) gemm_tcgen05_kernel(const __grid_const
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&s->tempty[acc]);
     }
+    // every bulk store has completed (global writes done, staging buffers read) before exit
+    if (lane == 0) tc::bulk_wait_all();
+    __syncwarp();
   }
   tc::tc_fence_before();
   __syncthreads();
@@ -257,9 +316,28 @@ static CUtensorMap make_map(const void* ptr, int64_t rows, int64_t cols, int64_t
   return m;
 }
 
+// Output map for the TMA-store epilogue: box = 32 rows x box_cols elements of one
+// 32-column chunk (bf16: 64-byte rows, f32: 128-byte rows, SwiGLU output: 32-byte rows),
+// swizzled to the row length so the staging writes are bank-conflict free.
+static bool make_store_map(CUtensorMap* m, void* ptr, int64_t rows, int64_t cols, int64_t ld, int elem_bytes,
+                           int box_cols) {
+  if (reinterpret_cast<uintptr_t>(ptr) % 16 || (ld * elem_bytes) % 16 || rows <= 0 || cols <= 0) return false;
+  const int row_bytes = box_cols * elem_bytes;
+  const CUtensorMapSwizzle sw = row_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                : row_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                                  : CU_TENSOR_MAP_SWIZZLE_32B;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * elem_bytes)};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, 32};
+  cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapDataType dt = elem_bytes == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  return encode_fn()(m, dt, 2, ptr, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                     CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <int BN, int STAGES>
-static void launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const GemmParams& p, int total_tiles,
-                        cudaStream_t st) {
+static void launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const GemmParams& p,
+                        int total_tiles, cudaStream_t st) {
   auto k = gemm_tcgen05_kernel<BN, STAGES>;
   const size_t smem = sizeof(GemmSmem<BN, STAGES>) + 1024;
   static bool attr_set = false;
@@ -271,7 +349,7 @@ static void launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const Gemm
   HX_CUDA_CHECK(cudaGetDevice(&dev));
   HX_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
   const int grid = std::max(1, std::min(total_tiles, sms));
-  k<<<grid, 192, smem, st>>>(ma, mb, p);
+  k<<<grid, 192, smem, st>>>(ma, mb, mc, p);
   HX_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -302,7 +380,18 @@ static void gemm_common(torch::Tensor A, torch::Tensor B, torch::Tensor C, int64
   CUtensorMap mb = make_map(B.data_ptr(), B.size(0), K, B.stride(0), BN);
   const int total = (tiles ? num_entries : p.num_m_blocks) * p.num_n_blocks;
   if (total == 0) return;
-  launch_gemm<BN, 4>(ma, mb, p, total, at::cuda::getCurrentCUDAStream());
+  CUtensorMap mc;
+  static const bool tma_store_on = [] {
+    const char* e = std::getenv("HELEXA_GEMM_TMA_STORE");
+    return !(e && e[0] == '0');
+  }();
+  const int out_cols = epi == kEpiSwiGLU ? N / 2 : N;
+  const int out_rows = tiles ? (int)C.size(0) : M;
+  p.tma_store = tma_store_on && C.dim() == 2 && C.stride(1) == 1 &&
+                make_store_map(&mc, C.data_ptr(), out_rows, out_cols, p.ldc, (int)C.element_size(),
+                               epi == kEpiSwiGLU ? 16 : 32);
+  if (!p.tma_store) memset(&mc, 0, sizeof(mc));
+  launch_gemm<BN, 4>(ma, mb, mc, p, total, at::cuda::getCurrentCUDAStream());
 }
 
 // C = A @ B^T (bf16 in, f32 accumulate); epi: 0 bf16, 1 SwiGLU on interleaved columns, 2 f32.
