@@ -13,6 +13,8 @@ _C = None
 def _load():
     global _C
     if _C is None:
+        import torch  # noqa: F401 - loads libc10/libtorch that the extension links against
+
         try:
             _C = importlib.import_module("helexa_b200._C")
         except ImportError as e:  # pragma: no cover - only without a build
