@@ -324,7 +324,9 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
 
 template <int B, int MODE>
 static void launch_b(const GemvArgs& a, int jobs, cudaStream_t s) {
-  constexpr int RPW = 2;
+  // the router's few hundred rows take one row per warp (twice the CTAs: its time is
+  // the per-CTA streaming latency, not bandwidth)
+  constexpr int RPW = MODE == kRouter ? 1 : 2;
   dim3 grid((a.N + 8 * RPW - 1) / (8 * RPW), jobs);
   size_t smem = (size_t)B * a.K * sizeof(__nv_bfloat16);
   // U = 16-byte loads per lane and row per batch (two batches in flight). Long rows of
