@@ -69,6 +69,7 @@ struct AttnSmem {
 
 struct AttnTcArgs {
   int T, p0, L, G, Hq, maxlen;
+  int causal;                      // 0: every query sees all L keys (bidirectional)
   float sl2;                       // scale * log2(e)
   __nv_bfloat16* o;
   int ldo;
@@ -91,7 +92,7 @@ __global__ void __launch_bounds__(192, 1) attn_prefill_tc_kernel(const __grid_co
   const int qt = gridDim.x - 1 - blockIdx.x;  // latest (longest) query tiles first
   const int h = blockIdx.y, kvh = h / a.G;
   const int t0 = qt * 128;
-  const int kend = min(a.L, a.p0 + t0 + 128);
+  const int kend = a.causal ? min(a.L, a.p0 + t0 + 128) : a.L;
   const int nb = (kend + BN - 1) / BN;
 
   if (threadIdx.x == 0) {
@@ -199,12 +200,12 @@ __global__ void __launch_bounds__(192, 1) attn_prefill_tc_kernel(const __grid_co
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&s->s_empty[st]);
       const int k0 = j * BN;
-      const bool diag = k0 + BN - 1 > a.p0 + t0 || k0 + BN > a.L;  // block needs masking
+      const bool diag = (a.causal && k0 + BN - 1 > a.p0 + t0) || k0 + BN > a.L;  // block needs masking
       float mx = -INFINITY;
 #pragma unroll
       for (int c = 0; c < BN; ++c) {
         float v = sv[c] * a.sl2;
-        if (diag && (k0 + c > pos || k0 + c >= a.L)) v = -INFINITY;
+        if (diag && ((a.causal && k0 + c > pos) || k0 + c >= a.L)) v = -INFINITY;
         sv[c] = v;
         mx = fmaxf(mx, v);
       }
@@ -356,9 +357,11 @@ static void launch_attn_tc(const CUtensorMap& mq, const CUtensorMap& mk, const C
 using namespace hx;
 
 // q [T, >= Hq*D] bf16 (normed, rotated); kc / vc the slot's caches [Hkv, maxlen, D] with
-// keys 0 .. p0+T-1 written; out [T, >= Hq*D]; gate as for attn_prefill.
+// keys 0 .. p0+T-1 written; out [T, >= Hq*D]; gate as for attn_prefill. causal=false:
+// every query attends to all p0+T keys (the diffusion transformer's joint sequence).
 void attn_prefill_tc(torch::Tensor q, torch::Tensor kc, torch::Tensor vc, torch::Tensor out, int64_t Hq, int64_t p0,
-                     double scale, c10::optional<torch::Tensor> gate, int64_t gate_head_stride, torch::Tensor err) {
+                     double scale, c10::optional<torch::Tensor> gate, int64_t gate_head_stride, torch::Tensor err,
+                     bool causal) {
   TORCH_CHECK(q.is_cuda() && q.scalar_type() == at::kBFloat16 && q.dim() == 2 && q.stride(1) == 1, "q [T, Hq*D]");
   TORCH_CHECK(kc.is_contiguous() && vc.is_contiguous() && kc.dim() == 3 && vc.sizes() == kc.sizes(), "kc / vc");
   const int T = q.size(0), Hkv = kc.size(0), maxlen = kc.size(1), D = kc.size(2);
@@ -375,7 +378,7 @@ void attn_prefill_tc(torch::Tensor q, torch::Tensor kc, torch::Tensor vc, torch:
       Lpad, (long long)maxlen * D);
   HX_CUDA_CHECK(cudaGetLastError());
   AttnTcArgs a{};
-  a.T = T; a.p0 = (int)p0; a.L = L; a.G = (int)(Hq / Hkv); a.Hq = (int)Hq; a.maxlen = maxlen;
+  a.T = T; a.p0 = (int)p0; a.L = L; a.causal = causal ? 1 : 0; a.G = (int)(Hq / Hkv); a.Hq = (int)Hq; a.maxlen = maxlen;
   a.sl2 = (float)scale * 1.4426950408889634f;
   a.o = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   a.ldo = out.stride(0);

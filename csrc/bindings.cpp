@@ -61,7 +61,7 @@ void moe_fused(torch::Tensor x, torch::Tensor norm_w, double eps, torch::Tensor 
                c10::optional<std::vector<int64_t>> bases, int64_t rank, int64_t slot_elems,
                c10::optional<torch::Tensor> ctr, double timeout_s);
 void attn_prefill_tc(torch::Tensor q, torch::Tensor kc, torch::Tensor vc, torch::Tensor out, int64_t Hq, int64_t p0,
-                     double scale, c10::optional<torch::Tensor> gate, int64_t gate_head_stride, torch::Tensor err);
+                     double scale, c10::optional<torch::Tensor> gate, int64_t gate_head_stride, torch::Tensor err, bool causal);
 void gemv_experts_ep(torch::Tensor W, torch::Tensor x, torch::Tensor ids, torch::Tensor y, int64_t mode,
                      int64_t x_row_div, c10::optional<torch::Tensor> norm_w, double eps, int64_t e_base);
 void moe_down_ar_ep(torch::Tensor Wd, torch::Tensor act, torch::Tensor ids, torch::Tensor wts, torch::Tensor x,
@@ -119,6 +119,12 @@ void gguf_experts(torch::Tensor W, int64_t type, int64_t K, torch::Tensor x, tor
 void gguf_moe_down(torch::Tensor W, int64_t type, int64_t I, torch::Tensor act, torch::Tensor ids, torch::Tensor wts,
                    torch::Tensor x, int64_t J, int64_t e_base, int64_t e_count);
 
+void dit_norm_mod(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> scale, torch::Tensor y, double eps);
+void dit_gate_res(torch::Tensor x, torch::Tensor y, torch::Tensor w, c10::optional<torch::Tensor> gate, double eps);
+void dit_qk_rope(torch::Tensor qkv, c10::optional<torch::Tensor> qw, c10::optional<torch::Tensor> kw,
+                 torch::Tensor ang, int64_t H, int64_t Dh, double eps, torch::Tensor q, torch::Tensor k,
+                 torch::Tensor v);
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("set_pdl", [](bool on) { hx_pdl_enabled() = on; });
   m.def("gemv", &gemv);
@@ -161,7 +167,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("rank") = 0, py::arg("slot_elems") = 0, py::arg("ctr") = py::none(), py::arg("timeout_s") = 5.0);
   m.def("gemv_tma_ok", &gemv_tma_ok);
   m.def("gguf_pad_q6k", &gguf_pad_q6k);
-  m.def("attn_prefill_tc", &attn_prefill_tc);
+  m.def("attn_prefill_tc", &attn_prefill_tc, py::arg("q"), py::arg("kc"), py::arg("vc"), py::arg("out"), py::arg("Hq"),
+        py::arg("p0"), py::arg("scale"), py::arg("gate"), py::arg("gate_head_stride"), py::arg("err"),
+        py::arg("causal") = true);
   m.def("sample_step", &sample_step);
   m.def("moe_fused", &moe_fused, py::arg("x"), py::arg("norm_w"), py::arg("eps"), py::arg("router"), py::arg("w_gu"),
         py::arg("w_d"), py::arg("E"), py::arg("topk"), py::arg("has_shared"), py::arg("norm_topk"),
@@ -169,6 +177,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("e_count") = 0, py::arg("bases") = py::none(), py::arg("rank") = 0, py::arg("slot_elems") = 0,
         py::arg("ctr") = py::none(), py::arg("timeout_s") = 5.0);
   m.def("embed", &embed);
+  m.def("dit_norm_mod", &dit_norm_mod);
+  m.def("dit_gate_res", &dit_gate_res);
+  m.def("dit_qk_rope", &dit_qk_rope);
   m.def("argmax_step", &argmax_step);
   m.def("ipc_alloc", &ipc_alloc);
   m.def("ipc_open", &ipc_open);

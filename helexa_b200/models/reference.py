@@ -338,6 +338,24 @@ class ReferenceModel:
         logits = (x @ self.w["lm_head.weight"].t()).float()
         return logits if all_logits else logits[0]
 
+    @torch.no_grad()
+    def hidden(self, tokens: torch.Tensor, n_layers: int) -> torch.Tensor:
+        """Hidden states [T, H] after the first `n_layers` decoder layers (no final norm)
+        of a fresh sequence -- the caption features a diffusion text encoder takes."""
+        c = self.cfg
+        st = self.new_state()
+        x = self.w["model.embed_tokens.weight"][tokens.to(self.device)]
+        for i in range(n_layers):
+            p = f"model.layers.{i}."
+            h = rms_norm(x, self.w[p + "input_layernorm.weight"], c.rms_norm_eps, c.norm_offset).to(x.dtype)
+            h = self._gdn(i, h, st) if c.is_linear(i) else self._attn(i, h, st, 0)
+            x = x + h
+            h = rms_norm(x, self.w[p + "post_attention_layernorm.weight"], c.rms_norm_eps,
+                         c.norm_offset).to(x.dtype)
+            h = self._moe(i, h) if c.layer_uses_moe(i) else self._mlp(p + "mlp.", h)
+            x = x + h
+        return x
+
     # ---- snapshots --------------------------------------------------------
     def snapshot(self, st: RefState) -> RefState:
         return st.clone()

@@ -205,6 +205,7 @@ def _build_tp_cpu(spec, src, cfg):
 class ModelRegistry:
     def __init__(self):
         self.models: dict[str, ServedModel] = {}
+        self.image_models: dict = {}  # model id -> image_serving.ServedImageModel
         self.specs: dict[str, ModelSpec] = {}
         self.loading: dict[str, asyncio.Future] = {}
         self.recovering: set[str] = set()
@@ -227,14 +228,25 @@ class ModelRegistry:
                         "capabilities": m.capabilities,
                         "limit": {"context": lim.context, "input": lim.input, "output": lim.output},
                         "tool_call": True, "reasoning": True, "servable": m.status == "loaded"})
+        out += [m.describe() for m in self.image_models.values()]
         for mid in self.loading:
-            if mid not in self.models:
+            if mid not in self.models and mid not in self.image_models:
                 out.append({"id": mid, "status": "loading"})
         return out
 
     async def load(self, spec: ModelSpec) -> ServedModel:
         if spec.model_id in self.models:
             return self.models[spec.model_id]
+        from .image_serving import build_image_model, is_image_source
+        if is_image_source(spec.source):
+            if spec.model_id in self.image_models:
+                return self.image_models[spec.model_id]
+            if spec.tensor_parallel > 1:
+                raise LoadError("image models load on one device", "unsupported_parallelism")
+            m = await asyncio.to_thread(build_image_model, spec)
+            self.image_models[spec.model_id] = m
+            self.specs[spec.model_id] = spec
+            return m
         fut = self.loading.get(spec.model_id)
         if fut is not None:
             return await asyncio.shield(fut)
@@ -258,6 +270,13 @@ class ModelRegistry:
             self.loading.pop(spec.model_id, None)
 
     async def unload(self, model_id: str, force: bool = False) -> bool:
+        im = self.image_models.pop(model_id, None)
+        if im is not None:
+            im.status = "unloading"
+            del im
+            if torch.cuda.is_available():
+                torch.cuda.empty_cache()
+            return True
         m = self.models.get(model_id)
         if m is None:
             return False
@@ -290,5 +309,5 @@ class ModelRegistry:
             self.recovering.discard(model_id)
 
     async def unload_all(self):
-        for mid in list(self.models):
+        for mid in list(self.models) + list(self.image_models):
             await self.unload(mid, force=True)

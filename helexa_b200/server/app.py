@@ -5,7 +5,7 @@ OpenAI / Anthropic endpoints, on FastAPI.
   POST /models/load /models/unload
   GET  /models/{id}/endpoint /models/{id}/capabilities
   POST /v1/chat/completions /v1/completions /v1/responses /v1/messages
-  POST /v1/images/generations   (no image model: a clean `wrong_modality` 400)
+  POST /v1/images/generations   (Z-Image models; a text model answers `wrong_modality` 400)
 
 Chat handling (api.rs:313-389): `max_completion_tokens` aliases `max_tokens`; the
 `x-include-thinking` header opts into reasoning output and is the default for
@@ -253,7 +253,9 @@ def create_app(registry: ModelRegistry | None = None, default_models: list[dict]
                         "model_load_failed" if e.code == "load_failed" else e.code)
         except (ValueError, FileNotFoundError, KeyError) as e:
             return _err(422, str(e), "model_load_failed")
-        return {"status": "loaded", "model_id": m.model_id, "limit": m.limits.__dict__}
+        lim = getattr(m, "limits", None)
+        return {"status": "loaded", "model_id": m.model_id, "limit": lim.__dict__ if lim is not None else None,
+                "capabilities": m.capabilities}
 
     @app.post("/models/unload")
     async def unload(req: Request):
@@ -373,8 +375,19 @@ def create_app(registry: ModelRegistry | None = None, default_models: list[dict]
 
     @app.post("/v1/images/generations")
     async def images(request: Request):
+        from ..runtime.image_serving import ImageRequestError
         body = await request.json()
-        return _err(400, f"model {body.get('model')!r} does not generate images", "wrong_modality")
+        mid = body.get("model")
+        im = reg.image_models.get(mid) if mid else (
+            next(iter(reg.image_models.values())) if len(reg.image_models) == 1 else None)
+        if im is None:
+            if mid in reg.models:
+                return _err(400, f"model {mid!r} does not generate images", "wrong_modality")
+            return _err(404, f"image model {mid!r} is not loaded", "model_not_found")
+        try:
+            return await im.generate(body)
+        except ImageRequestError as e:
+            return _err(e.status, str(e), e.code)
 
     return app
 
