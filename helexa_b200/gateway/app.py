@@ -227,8 +227,13 @@ def create_gateway(catalogue: Catalogue, nodes: list[NodeState], api_keys: dict[
         for mid, e in catalogue.entries.items():
             loaded = [n.name for n in router.nodes.values() if n.models.get(mid, {}).get("status") == "loaded"]
             lim = next((n.models[mid].get("limit") for n in router.nodes.values() if mid in n.models), None)
+            caps = sorted({c for n in router.nodes.values() if n.models.get(mid, {}).get("status") == "loaded"
+                           for c in n.models[mid].get("capabilities", [])})
             item = {"id": mid, "object": "model", "owned_by": "helexa", "aliases": e.aliases,
-                    "loaded_on": loaded, "limit": lim}
+                    "loaded_on": loaded, "limit": lim, "loaded": bool(loaded),
+                    # a catalogue entry can be cold-loaded on any healthy node
+                    "feasible_on": [n.name for n in router.nodes.values() if n.healthy],
+                    "capabilities": caps}
             if e.cost_input_per_mtok is not None or e.cost_output_per_mtok is not None:
                 item["cost"] = {"input_per_mtok": e.cost_input_per_mtok, "output_per_mtok": e.cost_output_per_mtok}
             data.append(item)
@@ -244,8 +249,10 @@ def create_gateway(catalogue: Catalogue, nodes: list[NodeState], api_keys: dict[
 
     @app.get("/health")
     async def health():
-        return {"status": "ok", "nodes": {n.name: {"healthy": n.healthy, "models": list(n.models)}
-                                          for n in router.nodes.values()}}
+        ns = list(router.nodes.values())
+        return {"status": "ok", "nodes": {"healthy": sum(1 for n in ns if n.healthy), "total": len(ns),
+                                          "by_name": {n.name: {"healthy": n.healthy, "models": list(n.models)}
+                                                      for n in ns}}}
 
     @app.get("/")
     async def root():

@@ -1,0 +1,168 @@
+"""Federation router and tools service (the reference's helexa-router and helexa-tools
+tests: selection order, failover, alias rewrite, catalogue merge, SSRF rules,
+redirect re-checks, content-type gates, extraction and truncation)."""
+import json
+import socket
+
+import httpx
+import pytest
+from fastapi.testclient import TestClient
+
+from helexa_b200.mesh import router as rt
+from helexa_b200.mesh import tools
+
+
+def _entry(mid, loaded, feasible=(), ctx=4096, cost=None, caps=("text",)):
+    e = {"id": mid, "object": "model", "loaded": loaded, "feasible_on": list(feasible), "limit": {"context": ctx},
+         "capabilities": list(caps)}
+    if cost:
+        e["cost"] = cost
+    return e
+
+
+def _cortex_transport(state):
+    """Mock cortexes a (loaded m1) and b (feasible m1, loaded m2); state['down'] lists
+    cortexes whose connections fail."""
+    def handler(req: httpx.Request):
+        host = req.url.host
+        if host in state["down"]:
+            raise httpx.ConnectError("down", request=req)
+        if req.url.path == "/v1/models":
+            data = {"a": [_entry("m1", True, ctx=8192, cost={"input_per_mtok": 2, "output_per_mtok": 2})],
+                    "b": [_entry("m1", False, ["n1"], ctx=4096, cost={"input_per_mtok": 1, "output_per_mtok": 1},
+                                 caps=("text", "vision")),
+                          _entry("m2", True)]}[host]
+            return httpx.Response(200, json={"data": data})
+        if req.url.path == "/health":
+            return httpx.Response(200, json={"nodes": {"healthy": {"a": 1, "b": 3}[host], "total": 3}})
+        body = json.loads(req.content)
+        state["hits"].append((host, req.url.path, body["model"]))
+        return httpx.Response(200, json={"served_by": host, "model": body["model"]})
+    return httpx.MockTransport(handler)
+
+
+def _router(state, region=None):
+    cfg = rt.RouterConfig(cortexes=[rt.CortexEndpoint("a", "http://a", "eu"), rt.CortexEndpoint("b", "http://b", "us")],
+                          aliases={"fast": "m2"}, region=region)
+    return rt.create_router(cfg, transport=_cortex_transport(state), poll=False)
+
+
+def test_router_selection_failover_alias_and_catalogue():
+    state = {"down": set(), "hits": []}
+    app = _router(state)
+    with TestClient(app) as c:
+        c.portal.call(app.state.poll_once)
+        # loaded beats feasible even with fewer healthy nodes
+        r = c.post("/v1/chat/completions", json={"model": "m1", "messages": []})
+        assert r.status_code == 200 and r.json()["served_by"] == "a"
+        # alias rewrite
+        r = c.post("/v1/chat/completions", json={"model": "fast", "messages": []})
+        assert r.json() == {"served_by": "b", "model": "m2"}
+        # failover when the preferred cortex refuses connections
+        state["down"].add("a")
+        r = c.post("/v1/messages", json={"model": "m1", "messages": []})
+        assert r.json()["served_by"] == "b"
+        state["down"].clear()
+        assert c.post("/v1/chat/completions", json={"model": "nope"}).status_code == 404
+        assert c.post("/v1/chat/completions", content=b"{}").json()["error"]["code"] == "missing_model_field"
+        models = {m["id"]: m for m in c.get("/v1/models").json()["data"]}
+        m1 = models["m1"]
+        assert m1["loaded"] and m1["feasible_on"] == ["a", "b"] and m1["limit"]["context"] == 4096
+        assert m1["cost"]["input_per_mtok"] == 1 and set(m1["capabilities"]) == {"text", "vision"}
+        assert m1["locations"] == [{"node": "a", "status": "loaded"}]
+        assert c.get("/health").json()["cortexes"] == {"configured": 2, "reachable": 2}
+
+
+def test_router_unreachable_after_three_failed_polls():
+    st = rt.RouterState(rt.RouterConfig(cortexes=[rt.CortexEndpoint("a", "http://a")]))
+    st.observe("a", [_entry("m1", True)], 1)
+    assert st.select("m1")[0] == "candidates"
+    for i in range(3):
+        st.observe("a", None)
+        assert st.topology["a"].reachable == (i < 2)
+    assert st.select("m1") == ("unreachable", None)
+    assert st.select("zzz") == ("unknown", None)
+
+
+def test_router_region_and_health_ranking():
+    cfg = rt.RouterConfig(cortexes=[rt.CortexEndpoint("x", "http://x", "us"), rt.CortexEndpoint("y", "http://y", "eu"),
+                                    rt.CortexEndpoint("z", "http://z", "eu")], region="eu")
+    st = rt.RouterState(cfg)
+    for n, h in (("x", 9), ("y", 1), ("z", 2)):
+        st.observe(n, [_entry("m", True)], h)
+    assert [e.name for e in st.select("m")[1]] == ["z", "y", "x"]
+
+
+def test_ssrf_rules():
+    ok = ["https://example.com/page", "http://sub.example.co.uk/x?y=1", "https://93.184.216.34/"]
+    for u in ok:
+        tools.check_url(u)
+    bad = ["ftp://example.com/", "file:///etc/passwd", "http://localhost/", "http://intranet/",
+           "http://build.corp.internal:8090/", "http://printer.local/", "http://nas.lan/", "http://x.home.arpa/",
+           "http://127.0.0.1/", "http://10.1.2.3/", "http://172.16.0.1/", "http://192.168.1.1/", "http://169.254.169.254/",
+           "http://100.64.0.1/", "http://0.0.0.0/", "http://198.18.0.1/", "http://224.0.0.1/", "http://[::1]/",
+           "http://[fd00::1]/", "http://[fe80::1]/", "http://[::ffff:127.0.0.1]/", "http://[2001:db8::1]/"]
+    for u in bad:
+        with pytest.raises(tools.Denied):
+            tools.check_url(u)
+    assert tools.ip_allowed("2606:4700::1111")
+
+    def resolver(host, port, type=0):
+        return {"good.example": [(0, 0, 0, "", ("93.184.216.34", port))],
+                "rebind.example": [(0, 0, 0, "", ("93.184.216.34", port)), (0, 0, 0, "", ("10.0.0.5", port))]}[host]
+    assert tools.resolve_validated("good.example", 80, resolver) == "93.184.216.34"
+    with pytest.raises(tools.Denied):
+        tools.resolve_validated("rebind.example", 80, resolver)
+
+
+def _fake_resolver(host, port, type=0):
+    table = {"site.example": "93.184.216.34", "evil.example": "10.0.0.9"}
+    if host not in table:
+        raise socket.gaierror("nx")
+    return [(0, 0, 0, "", (table[host], port))]
+
+
+def _site_transport():
+    page = ("<html><head><title> The Title </title><script>var x=1</script></head><body><nav>menu</nav>"
+            "<article><h1>Heading</h1><p>First   para.</p><p>Second &amp; last.</p></article><footer>f</footer>"
+            "</body></html>")
+
+    def handler(req: httpx.Request):
+        assert req.url.host == "93.184.216.34" and req.headers["host"].startswith("site.example")
+        p = req.url.path
+        if p == "/page":
+            return httpx.Response(200, text=page, headers={"content-type": "text/html; charset=utf-8"})
+        if p == "/plain":
+            return httpx.Response(200, text="x" * 50, headers={"content-type": "text/plain"})
+        if p == "/pdf":
+            return httpx.Response(200, content=b"%PDF", headers={"content-type": "application/pdf"})
+        if p == "/hop":
+            return httpx.Response(302, headers={"location": "/page"})
+        if p == "/to-internal":
+            return httpx.Response(302, headers={"location": "http://evil.example/"})
+        if p == "/loop":
+            return httpx.Response(302, headers={"location": "/loop"})
+        return httpx.Response(404)
+    return httpx.MockTransport(handler)
+
+
+def test_tools_fetch_service():
+    app = tools.create_tools_app(tools.ToolsConfig(max_text_chars=20), transport=_site_transport(),
+                                 resolver=_fake_resolver)
+    with TestClient(app) as c:
+        assert c.get("/health").json()["status"] == "ok"
+        j = c.get("/fetch", params={"url": "http://site.example/page"}).json()
+        assert j["title"] == "The Title" and j["text"].startswith("Heading\nFirst para.") and j["truncated"]
+        assert "menu" not in j["text"] and "var x" not in j["text"]
+        j = c.get("/fetch", params={"url": "http://site.example/hop"}).json()
+        assert j["url"] == "http://site.example/page"
+        j = c.get("/fetch", params={"url": "http://site.example/plain"}).json()
+        assert j["text"] == "x" * 20 and j["truncated"] and j["title"] == ""
+        assert c.get("/fetch", params={"url": "http://site.example/pdf"}).status_code == 415
+        assert c.get("/fetch", params={"url": "http://site.example/to-internal"}).status_code == 400
+        assert c.get("/fetch", params={"url": "http://site.example/loop"}).status_code == 502
+        assert c.get("/fetch", params={"url": "http://site.example/missing"}).status_code == 502
+        assert c.get("/fetch", params={"url": "http://127.0.0.1/"}).status_code == 400
+        assert c.get("/fetch", params={"url": "http://nx.example/"}).status_code == 400
+    full = tools.extract_readable("<p>a</p><p>b</p>")
+    assert full == ("", "a\nb")
