@@ -166,3 +166,95 @@ def test_tools_fetch_service():
         assert c.get("/fetch", params={"url": "http://nx.example/"}).status_code == 400
     full = tools.extract_readable("<p>a</p><p>b</p>")
     assert full == ("", "a\nb")
+
+
+# ---- upstream ledger ------------------------------------------------------------
+from helexa_b200.mesh import upstream as up  # noqa: E402
+
+
+def test_ledger_reserve_settle_release_no_overshoot():
+    L = up.Ledger()
+    aid = L.create_account("a@x.io", allocation=1000)
+    k1, raw1 = L.create_key(aid, "all")
+    k2, _ = L.create_key(aid, "capped", "hardcap", 300)
+    k3, _ = L.create_key(aid, "half", "percent", 50)
+    assert L.resolve_key(raw1)["hard_cap"] == 1000 and L.resolve_key("nope") is None
+    r = L.reserve(aid, k2, 300)
+    with pytest.raises(up.InsufficientQuota) as e:
+        L.reserve(aid, k2, 1)
+    assert e.value.available == 0
+    L.settle(r, 120)                    # charge 120, return 180
+    assert L.snapshot(aid, k2) == {"hard_cap": 300, "spent": 120, "reserved": 0}
+    L.settle(r, 999)                    # idempotent
+    assert L.account(aid)["allocation_spent"] == 120
+    r = L.reserve(aid, k3, 500)
+    L.settle(r, 10_000)                 # capped at the reservation
+    assert L.snapshot(aid, k3)["spent"] == 500
+    # account-level availability now 1000 - 620 = 380 even for the 100% key
+    with pytest.raises(up.InsufficientQuota) as e:
+        L.reserve(aid, k1, 381)
+    assert e.value.available == 380
+    r = L.reserve(aid, k1, 380)
+    L.release(r)
+    assert L.account(aid)["allocation_reserved"] == 0 and L.account(aid)["allocation_spent"] == 620
+    r = L.reserve(aid, k1, 10)
+    L.db.execute("UPDATE reservations SET created_at = created_at - 10000 WHERE id = ?", (r,))
+    assert L.sweep_stale(60) == 1 and L.account(aid)["allocation_reserved"] == 0
+    assert L.archive_key(aid, k1) and L.resolve_key(raw1) is None
+    code = L.mint_code(5000)
+    assert L.redeem(aid, code) == 5000
+    with pytest.raises(up.LedgerError):
+        L.redeem(aid, code)
+
+
+def test_ledger_concurrent_reservations_never_overshoot():
+    import threading
+    L = up.Ledger()
+    aid = L.create_account(allocation=1000)
+    kid, _ = L.create_key(aid)
+    ok = []
+
+    def worker():
+        for _ in range(20):
+            try:
+                ok.append(L.reserve(aid, kid, 7))
+            except up.InsufficientQuota:
+                pass
+
+    ts = [threading.Thread(target=worker) for _ in range(8)]
+    for t in ts:
+        t.start()
+    for t in ts:
+        t.join()
+    assert len(ok) == 1000 // 7 and L.account(aid)["allocation_reserved"] == 7 * len(ok)
+
+
+def test_upstream_http_surface():
+    app = up.create_upstream(up.UpstreamConfig(operator_tokens={"op-secret": "op1"}, signup_allocation=100))
+    with TestClient(app) as c:
+        r = c.post("/web/v1/register", json={"email": "u@x.io", "password": "correct horse"})
+        sess = {"Authorization": "Bearer " + r.json()["session"]}
+        assert c.post("/web/v1/register", json={"email": "u@x.io", "password": "correct horse"}).status_code == 409
+        assert c.post("/web/v1/login", json={"email": "u@x.io", "password": "wrong pass"}).status_code == 401
+        assert c.post("/web/v1/login", json={"email": "u@x.io", "password": "correct horse"}).status_code == 200
+        key = c.post("/web/v1/keys", json={"label": "cli", "limit_kind": "hardcap", "limit_value": 60},
+                     headers=sess).json()
+        assert c.get("/web/v1/allocation", headers=sess).json()["available"] == 100
+        op = {"Authorization": "Bearer op-secret"}
+        assert c.post("/authz/v1/resolve", json={"api_key": key["key"]}).status_code == 401
+        res = c.post("/authz/v1/resolve", json={"api_key": key["key"]}, headers=op).json()
+        p = res["principal"]
+        assert res["snapshot"]["hard_cap"] == 60
+        rid = c.post("/authz/v1/reserve", json={**p, "max_tokens": 50}, headers=op).json()["reservation_id"]
+        rej = c.post("/authz/v1/reserve", json={**p, "max_tokens": 20}, headers=op).json()
+        assert rej == {"rejected": {"kind": "insufficient_quota", "requested": 20, "available": 10}}
+        c.post("/authz/v1/settle", json={"reservation_id": rid, "actual_tokens": 30}, headers=op)
+        assert c.post("/authz/v1/snapshot", json=p, headers=op).json() == {"hard_cap": 60, "spent": 30, "reserved": 0}
+        assert c.post("/authz/v1/served-usage", json={"model": "m", "prompt_tokens": 3, "completion_tokens": 4},
+                      headers=op).json() == {"ok": True}
+        code = app.state.ledger.mint_code(40)
+        assert c.post("/web/v1/redeem", json={"code": code}, headers=sess).json() == {"added": 40}
+        assert c.get("/web/v1/account", headers=sess).json()["allocation_total"] == 140
+        ks = c.get("/web/v1/keys", headers=sess).json()["keys"]
+        assert c.post(f"/web/v1/keys/{ks[0]['id']}/archive", headers=sess).json() == {"ok": True}
+        assert c.get("/web/v1/account").status_code == 401
