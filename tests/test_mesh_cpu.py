@@ -258,3 +258,65 @@ def test_upstream_http_surface():
         ks = c.get("/web/v1/keys", headers=sess).json()["keys"]
         assert c.post(f"/web/v1/keys/{ks[0]['id']}/archive", headers=sess).json() == {"ok": True}
         assert c.get("/web/v1/account").status_code == 401
+
+
+# ---- bench daemon ---------------------------------------------------------------
+from helexa_b200.mesh import benchd  # noqa: E402
+
+
+def _node_transport(reject_every=3):
+    n = {"chat": 0}
+
+    def sse(events):
+        return "".join(f"data: {json.dumps(e)}\n\n" for e in events) + "data: [DONE]\n\n"
+
+    def handler(req: httpx.Request):
+        p = req.url.path
+        if p == "/version":
+            return httpx.Response(200, json={"git_sha": "abc123"})
+        if p == "/v1/models":
+            return httpx.Response(200, json={"data": [{"id": "llm", "capabilities": ["text"]},
+                                                      {"id": "img", "capabilities": ["image"]}]})
+        if p == "/v1/images/generations":
+            return httpx.Response(200, json={"data": [{"b64_json": ""}], "usage": {"helexa_image_units": 2.36}})
+        body = json.loads(req.content)
+        if body.get("tools"):
+            return httpx.Response(200, json={"choices": [{"message": {"tool_calls": [{"id": "c1"}]}}]})
+        n["chat"] += 1
+        if n["chat"] % reject_every == 0:
+            return httpx.Response(429, json={"error": {"code": "rate_limit_exceeded"}})
+        evs = [{"choices": [{"delta": {"content": "tok"}}]} for _ in range(5)]
+        evs.append({"choices": [], "usage": {"prompt_tokens": 100, "completion_tokens": 5}})
+        return httpx.Response(200, text=sse(evs), headers={"content-type": "text/event-stream"})
+    return httpx.MockTransport(handler)
+
+
+def test_bench_daemon_cycle_store_and_api():
+    assert 100 * 4 <= len(benchd.build_prompt(100)) <= 100 * 4 + len(benchd.QUESTION)
+    store = benchd.Store()
+    d = benchd.BenchDaemon([benchd.Target("node", "http://node")], store, transport=_node_transport(reject_every=100))
+    asyncio_run = __import__("asyncio").run
+    asyncio_run(d.cycle())
+    rows = store.runs()
+    by = {(r["model"], r["scenario"]): r for r in rows}
+    assert set(by) == {("llm", "chat-128"), ("llm", "chat-4096"), ("llm", "concurrency-4"), ("llm", "tool-call"),
+                       ("img", "image-512")}
+    assert all(r["version"] == "abc123" and r["error"] is None for r in rows)
+    assert by[("llm", "chat-128")]["completion_tokens"] == 5 and by[("llm", "chat-128")]["prompt_tokens"] == 100
+    assert by[("llm", "concurrency-4")]["concurrency"] == 4 and by[("llm", "concurrency-4")]["completion_tokens"] == 20
+    assert by[("llm", "tool-call")]["capability"] == "tool_call"
+    assert by[("img", "image-512")]["image_units"] == 2.36
+    # admission shedding is counted, not an error
+    store2 = benchd.Store()
+    d2 = benchd.BenchDaemon([benchd.Target("node", "http://node")], store2, transport=_node_transport(reject_every=2),
+                            scenarios=[benchd.Scenario("concurrency-4", "concurrency", 64, 4)])
+    asyncio_run(d2.cycle())
+    r = store2.runs()[0]
+    assert r["rejected"] == 2 and r["error"] is None
+    api = benchd.create_bench_api(store)
+    with TestClient(api) as c:
+        assert c.get("/api/health").json()["runs"] == 5
+        s = c.get("/api/summary").json()["summary"]
+        assert {x["scenario"] for x in s} >= {"chat-128", "image-512"} and all(x["version"] == "abc123" for x in s)
+        assert len(c.get("/api/series", params={"model": "llm", "scenario": "chat-128"}).json()["points"]) == 1
+        assert len(c.get("/api/runs", params={"limit": 2}).json()["runs"]) == 2
