@@ -320,3 +320,138 @@ def test_bench_daemon_cycle_store_and_api():
         assert {x["scenario"] for x in s} >= {"chat-128", "image-512"} and all(x["version"] == "abc123" for x in s)
         assert len(c.get("/api/series", params={"model": "llm", "scenario": "chat-128"}).json()["points"]) == 1
         assert len(c.get("/api/runs", params={"limit": 2}).json()["runs"]) == 2
+
+
+# ---- ACP bridge -----------------------------------------------------------------
+from helexa_b200.mesh import acp  # noqa: E402
+
+
+class _ScriptProvider:
+    def __init__(self, rounds):
+        self.rounds, self.seen = list(rounds), []
+
+    async def stream(self, messages, tools):
+        self.seen.append([dict(m) for m in messages])
+        text, calls = self.rounds.pop(0)
+        for piece in text:
+            yield "text", piece
+        yield "tool_calls", calls
+
+
+def _drive(provider, script, allow=True):
+    """Run the agent against an in-memory editor; `script` is the list of requests the
+    editor sends. Returns every message the agent wrote and the editor's files."""
+    import asyncio
+    files = {"/w/a.py": "x = 1\n"}
+    out = []
+
+    async def main():
+        reader = asyncio.StreamReader()
+        agent = None
+
+        def write(b):
+            msg = json.loads(b)
+            out.append(msg)
+            if "method" in msg and "id" in msg:  # a request to the editor
+                m, p = msg["method"], msg["params"]
+                if m == "fs/read_text_file":
+                    res = {"content": files[p["path"]]}
+                elif m == "fs/write_text_file":
+                    files[p["path"]] = p["content"]
+                    res = None
+                elif m == "session/request_permission":
+                    res = {"outcome": {"outcome": "selected", "optionId": "allow" if allow else "reject"}}
+                else:
+                    res = {}
+                reader.feed_data((json.dumps({"jsonrpc": "2.0", "id": msg["id"], "result": res}) + "\n").encode())
+
+        agent = acp.AcpAgent(provider, reader, write)
+        task = asyncio.create_task(agent.serve())
+        for req in script:
+            if callable(req):
+                req = req(out)
+            reader.feed_data((json.dumps(req) + "\n").encode())
+            for _ in range(50):
+                await asyncio.sleep(0.005)
+        reader.feed_eof()
+        await task
+
+    asyncio.run(main())
+    return out, files
+
+
+def _sid(out):
+    return next(m["result"]["sessionId"] for m in out if m.get("id") == 2 and "result" in m)
+
+
+def test_acp_prompt_tool_loop_and_permissions():
+    rounds = [("Looking", [{"id": "c1", "name": "read_file", "arguments": json.dumps({"path": "/w/a.py"})}]),
+              ("", [{"id": "c2", "name": "edit_file",
+                     "arguments": json.dumps({"path": "/w/a.py", "old_text": "x = 1", "new_text": "x = 2"})}]),
+              ("Done.", [])]
+    prov = _ScriptProvider(rounds)
+    out, files = _drive(prov, [
+        {"jsonrpc": "2.0", "id": 1, "method": "initialize", "params": {"protocolVersion": 1}},
+        {"jsonrpc": "2.0", "id": 2, "method": "session/new", "params": {"cwd": "/w"}},
+        lambda o: {"jsonrpc": "2.0", "id": 3, "method": "session/prompt",
+                   "params": {"sessionId": _sid(o), "prompt": [{"type": "text", "text": "bump x"}]}},
+        {"jsonrpc": "2.0", "id": 4, "method": "nope/nope", "params": {}},
+    ])
+    res = {m["id"]: m for m in out if "id" in m and ("result" in m or "error" in m)}
+    assert res[1]["result"]["protocolVersion"] == 1
+    assert res[3]["result"] == {"stopReason": "end_turn"}
+    assert res[4]["error"]["code"] == -32601
+    assert files["/w/a.py"] == "x = 2\n"
+    ups = [m["params"]["update"] for m in out if m.get("method") == "session/update"]
+    assert [u["sessionUpdate"] for u in ups if u["sessionUpdate"] != "agent_message_chunk"] == \
+        ["tool_call", "tool_call_update", "tool_call", "tool_call_update"]
+    assert all(u["status"] == "completed" for u in ups if u["sessionUpdate"] == "tool_call_update")
+    text = "".join(u["content"]["text"] for u in ups if u["sessionUpdate"] == "agent_message_chunk")
+    assert text == "LookingDone."
+    assert any(m.get("method") == "session/request_permission" for m in out)  # edit is gated in default mode
+    # the tool result went back to the model
+    assert prov.seen[1][-1] == {"role": "tool", "tool_call_id": "c1", "content": "x = 1\n"}
+
+
+def test_acp_rejected_permission_and_bypass_mode():
+    rounds = [("", [{"id": "c1", "name": "write_file", "arguments": json.dumps({"path": "/w/a.py", "content": "y"})}]),
+              ("ok", [])]
+    out, files = _drive(_ScriptProvider(rounds), [
+        {"jsonrpc": "2.0", "id": 1, "method": "initialize", "params": {}},
+        {"jsonrpc": "2.0", "id": 2, "method": "session/new", "params": {"cwd": "/w"}},
+        lambda o: {"jsonrpc": "2.0", "id": 3, "method": "session/prompt",
+                   "params": {"sessionId": _sid(o), "prompt": [{"type": "text", "text": "w"}]}},
+    ], allow=False)
+    assert files["/w/a.py"] == "x = 1\n"
+    ups = [m["params"]["update"] for m in out if m.get("method") == "session/update"]
+    assert [u["status"] for u in ups if u["sessionUpdate"] == "tool_call_update"] == ["failed"]
+    rounds = [("", [{"id": "c1", "name": "write_file", "arguments": json.dumps({"path": "/w/a.py", "content": "y"})}]),
+              ("ok", [])]
+    out, files = _drive(_ScriptProvider(rounds), [
+        {"jsonrpc": "2.0", "id": 1, "method": "initialize", "params": {}},
+        {"jsonrpc": "2.0", "id": 2, "method": "session/new", "params": {"cwd": "/w"}},
+        lambda o: {"jsonrpc": "2.0", "id": 5, "method": "session/set_mode",
+                   "params": {"sessionId": _sid(o), "modeId": "bypassPermissions"}},
+        lambda o: {"jsonrpc": "2.0", "id": 3, "method": "session/prompt",
+                   "params": {"sessionId": _sid(o), "prompt": [{"type": "text", "text": "w"}]}},
+    ])
+    assert files["/w/a.py"] == "y"
+    assert not any(m.get("method") == "session/request_permission" for m in out)
+
+
+def test_acp_openai_provider_parses_streamed_tool_calls():
+    import asyncio
+    evs = [{"choices": [{"delta": {"content": "Hi"}}]},
+           {"choices": [{"delta": {"tool_calls": [{"index": 0, "id": "t1", "function": {"name": "read_",
+                                                                                         "arguments": "{\"pa"}}]}}]},
+           {"choices": [{"delta": {"tool_calls": [{"index": 0, "function": {"name": "file",
+                                                                             "arguments": "th\": \"/x\"}"}}]}}]}]
+    body = "".join(f"data: {json.dumps(e)}\n\n" for e in evs) + "data: [DONE]\n\n"
+    tr = httpx.MockTransport(lambda r: httpx.Response(200, text=body, headers={"content-type": "text/event-stream"}))
+    p = acp.OpenAIProvider("http://gw/v1", "m", transport=tr)
+
+    async def run():
+        return [x async for x in p.stream([], acp.TOOLS)]
+
+    got = asyncio.run(run())
+    assert got == [("text", "Hi"), ("tool_calls", [{"id": "t1", "name": "read_file", "arguments": "{\"path\": \"/x\"}"}])]
