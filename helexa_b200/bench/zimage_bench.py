@@ -38,6 +38,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=1)
     ap.add_argument("--reps", type=int, default=2)
     ap.add_argument("--layers", type=int, default=0, help="truncate the DiT (profiling only)")
+    ap.add_argument("--quant", default=None, help="q8_0: in-situ quantized DiT projections")
     args = ap.parse_args()
     dev = torch.device("cuda", 0)
     cfg = zi.DiTConfig()
@@ -46,6 +47,8 @@ def main():
     w = zi.random_weights(zi.dit_weight_shapes(cfg), seed=0, device=dev, dtype=torch.bfloat16)
     dit = zi.ZImageDiT(cfg, w, dev)
     del w
+    if args.quant:
+        dit.quantize_(args.quant)
     vcfg = zi.VaeConfig()
     vae = zi.VaeDecoder(vcfg, zi.random_weights(zi.vae_decoder_shapes(vcfg), seed=1, device=dev), dev, torch.bfloat16)
     lh, lw = zi.validate_dims(args.size, args.size)
@@ -82,7 +85,7 @@ def main():
     calls = res[0][2]
     fl = dit_flops(cfg, n_img, args.cap) * calls
     assert dit.err.item() == 0, "device error word set"
-    print(json.dumps({"model": "Z-Image-Turbo (6B DiT, random-init bf16)", "size": args.size, "steps": args.steps,
+    print(json.dumps({"model": "Z-Image-Turbo (6B DiT, random-init bf16)", "quant": args.quant, "size": args.size, "steps": args.steps,
                       "dit_forwards": calls, "caption_tokens": args.cap, "image_tokens": n_img,
                       "denoise_ms": round(den, 1), "ms_per_dit_forward": round(den / max(calls, 1), 2),
                       "vae_decode_ms": round(dec, 1), "total_ms": round(den + dec, 1),

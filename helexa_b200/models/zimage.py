@@ -166,6 +166,14 @@ def parse_size(size: str | None) -> tuple[int, int]:
     return width, height
 
 
+def parse_image_quant(quant: str) -> str:
+    """The image path serves q8_0 (bf16 when no quant is given); anything else is an
+    error rather than an untested precision."""
+    if quant.lower() in ("q8_0", "q8"):
+        return "Q8_0"
+    raise ValueError(f"unsupported image quant '{quant}'; the image path serves q8_0 (bf16 when quant is omitted)")
+
+
 def is_diffusers_layout(filenames) -> bool:
     return "model_index.json" in set(filenames)
 
@@ -487,7 +495,26 @@ class ZImageDiT:
         f = _rms(f, w[pre + "ffn_norm2.weight"], eps)
         return x + ((f.float() * gf).to(x.dtype) if c is not None else f)
 
-    def _gemm(self, x: torch.Tensor, W: torch.Tensor, epi: int = 0) -> torch.Tensor:
+    def quantize_(self, scheme: str = "q8_0") -> None:
+        """In-situ q8_0 quantization of the transformer blocks' projections (the
+        reference's image-path ISQ, harness/image.rs:528-539 accepts q8_0 only): the
+        weights live as Q8_0 block rows (about half the bytes of bf16) and each GEMM
+        dequantizes its weight to bf16 scratch first."""
+        if parse_image_quant(scheme) != "Q8_0":
+            raise ValueError(scheme)
+        if not self.cuda:
+            raise RuntimeError("quantized DiT serving needs the CUDA extension")
+        from .fast import GGUF_Q8_0, QWeight
+        for k in list(self.w):
+            if k.endswith(("qkv", "gu", "attention.to_out.0.weight", "feed_forward.w2.weight")):
+                w = self.w[k]
+                self.w[k] = QWeight(self.C.gguf_quant(w, GGUF_Q8_0), GGUF_Q8_0, w.shape[1])
+                del w
+        self.quant = "q8_0"
+
+    def _gemm(self, x: torch.Tensor, W, epi: int = 0) -> torch.Tensor:
+        if not isinstance(W, torch.Tensor):
+            W = W.dequant(self.C)
         N = W.shape[0] // 2 if epi == 1 else W.shape[0]
         y = torch.empty(x.shape[0], N, dtype=torch.bfloat16, device=self.device)
         self.C.gemm(x, W, y, epi, self.err)

@@ -172,5 +172,8 @@ def build_image_model(spec) -> ServedImageModel:
         pipe = _preset_pipeline(src.split(":", 1)[1], dev)
     else:
         pipe = load_pipeline_dir(src.split(":", 1)[1] if src.startswith("dir:") else src, dev)
+    if spec.quant:
+        zi.parse_image_quant(spec.quant)  # reject anything but q8_0 before any work
+        pipe.dit.quantize_(spec.quant)
     return ServedImageModel(model_id=spec.model_id, pipeline=pipe, devices=[dev.index] if use_cuda else [],
                             spec={"source": spec.source})

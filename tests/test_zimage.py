@@ -42,6 +42,13 @@ def test_prompt_size_units_layout():
     assert not zi.is_supported_pipeline_class("not json")
 
 
+def test_image_quant_parse():
+    assert zi.parse_image_quant("q8_0") == "Q8_0" and zi.parse_image_quant("Q8") == "Q8_0"
+    for bad in ("q4_k", "fp8", ""):
+        with pytest.raises(ValueError):
+            zi.parse_image_quant(bad)
+
+
 def test_png_roundtrip():
     g = torch.Generator().manual_seed(0)
     rgb = torch.randint(0, 256, (5, 7, 3), generator=g, dtype=torch.uint8)
@@ -213,6 +220,20 @@ def test_dit_gpu_matches_fp32_oracle():
         cos = torch.nn.functional.cosine_similarity(a.flatten(), b.flatten(), dim=0).item()
         assert cos > 0.995, cos
     assert gpu.err.item() == 0
+
+
+@pytest.mark.gpu
+def test_quantized_dit_tracks_bf16():
+    dev = torch.device("cuda", 0)
+    dcfg = zi.tiny_dit_config(cap_feat_dim=256)
+    dw = zi.random_weights(zi.dit_weight_shapes(dcfg), seed=2, std=0.05)
+    a = zi.ZImageDiT(dcfg, dw, dev)
+    b = zi.ZImageDiT(dcfg, dw, dev)
+    b.quantize_("q8_0")
+    g = torch.Generator().manual_seed(4)
+    lat, cap = torch.randn(16, 16, 16, generator=g), torch.randn(9, 256, generator=g)
+    ya, yb = a.forward(lat, 0.5, cap).float(), b.forward(lat, 0.5, cap).float()
+    assert torch.nn.functional.cosine_similarity(ya.flatten(), yb.flatten(), dim=0).item() > 0.995
 
 
 @pytest.mark.gpu
