@@ -202,7 +202,7 @@ def main() -> None:
             "e2e": {"value": round(float(e2e[0]), 2), "unit": "tok/s",
                     "ttft_p50_ms": round(float(e2e[1]) * 1e3, 2),
                     "h2d_bytes_per_step": args.prompt * 4, "d2h_bytes_per_step": args.decode * 4 + 4},
-            "gpu_launches": launches, "gpu_launches_scope": "this package's kernels per request (prefill + every decode step) x steps; PyTorch ops in prefill (RoPE, gate, embedding gather) not counted",
+            "gpu_launches": launches, "gpu_launches_scope": "this package's kernels per request (prefill + every decode step) x steps; PyTorch allocator fills and the MoE routing counter reset not counted",
             "clocks": clocks,
             "device_errors": device_errors,
         }

@@ -67,7 +67,7 @@ void gemv_experts_ep(torch::Tensor W, torch::Tensor x, torch::Tensor ids, torch:
 void moe_down_ar_ep(torch::Tensor Wd, torch::Tensor act, torch::Tensor ids, torch::Tensor wts, torch::Tensor x,
                     std::vector<int64_t> bases, int64_t rank, int64_t slot_elems, torch::Tensor epoch,
                     torch::Tensor err, double timeout_s, int64_t e_base);
-void moe_combine(torch::Tensor y, torch::Tensor rows, torch::Tensor wts, torch::Tensor x);
+void moe_combine(torch::Tensor y, torch::Tensor rows, torch::Tensor wts, torch::Tensor x, bool accumulate);
 void moe_route_prefill(torch::Tensor logits, int64_t E, int64_t k, bool has_shared, bool norm_topk, torch::Tensor hn,
                        torch::Tensor ids, torch::Tensor wts, torch::Tensor rows, torch::Tensor counts,
                        torch::Tensor offsets, torch::Tensor cursor, torch::Tensor tiles, torch::Tensor ntiles,
@@ -131,7 +131,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemv_experts", &gemv_experts);
   m.def("moe_topk", &moe_topk);
   m.def("moe_down", &moe_down);
-  m.def("moe_combine", &moe_combine);
+  m.def("moe_combine", &moe_combine, py::arg("y"), py::arg("rows"), py::arg("wts"), py::arg("x"),
+        py::arg("accumulate") = true);
   m.def("gemv_ar", &gemv_ar);
   m.def("moe_down_ar", &moe_down_ar);
   m.def("gemv_experts_ep", &gemv_experts_ep);

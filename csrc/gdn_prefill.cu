@@ -75,8 +75,29 @@ __global__ void __launch_bounds__(D) gdn_prep_kernel(const __nv_bfloat16* __rest
     win[j] = xv;
   }
   const int t1 = min(T, t0 + kPrepTok);
-  for (int t = t0; t < t1; ++t) {
-    win[kMaxConv - 1] = __bfloat162float(proj[(long long)t * ldp + c]);
+  // every input of this thread's tokens is requested before any is used (32 loads in
+  // flight per thread instead of one dependent load per token)
+  float xin[kPrepTok];
+#pragma unroll
+  for (int i = 0; i < kPrepTok; ++i)
+    xin[i] = t0 + i < t1 ? __bfloat162float(proj[(long long)(t0 + i) * ldp + c]) : 0.f;
+  if (grp >= 2 * Hk && d < kPrepTok && t0 + d < t1) {
+    // gating of this value head, one token per lane: beta = sigmoid(b),
+    // g = -exp(A_log) * softplus(a + dt_bias)
+    const int h = grp - 2 * Hk, t = t0 + d;
+    const __nv_bfloat16* pr = proj + (long long)t * ldp + 2 * kd + 2 * Hv * D;
+    const float bb = __bfloat162float(pr[h]);
+    const float aa = __bfloat162float(pr[Hv + h]);
+    float sp = aa + dt_bias[h];
+    sp = sp > 20.f ? sp : log1pf(expf(sp));
+    go[(long long)h * Tp + t] = -expf(A_log[h]) * sp;
+    bo[(long long)h * Tp + t] = 1.f / (1.f + expf(-bb));
+  }
+#pragma unroll
+  for (int i = 0; i < kPrepTok; ++i) {
+    const int t = t0 + i;
+    if (t >= t1) break;  // uniform across the CTA
+    win[kMaxConv - 1] = xin[i];
     float acc = 0.f;
 #pragma unroll
     for (int j = kMaxConv - 4; j < kMaxConv; ++j)
@@ -100,15 +121,6 @@ __global__ void __launch_bounds__(D) gdn_prep_kernel(const __nv_bfloat16* __rest
     } else {
       const int h = grp - 2 * Hk;
       vo[((long long)h * Tp + t) * D + d] = __float2bfloat16(y);
-      if (d == 0) {
-        const __nv_bfloat16* pr = proj + (long long)t * ldp + 2 * kd + 2 * Hv * D;
-        const float bb = __bfloat162float(pr[h]);
-        const float aa = __bfloat162float(pr[Hv + h]);
-        float sp = aa + dt_bias[h];
-        sp = sp > 20.f ? sp : log1pf(expf(sp));
-        go[(long long)h * Tp + t] = -expf(A_log[h]) * sp;
-        bo[(long long)h * Tp + t] = 1.f / (1.f + expf(-bb));
-      }
     }
   }
 }
@@ -507,8 +519,13 @@ void gdn_prefill(torch::Tensor proj, torch::Tensor conv_w, torch::Tensor ring, t
   const int nch = (T + kGC - 1) / kGC, Tp = nch * kGC;
   auto bfo = proj.options();
   auto f32 = proj.options().dtype(at::kFloat);
-  auto qn = torch::zeros({Hk, Tp, D}, bfo), kn = torch::zeros({Hk, Tp, D}, bfo), vn = torch::zeros({Hv, Tp, D}, bfo);
-  auto g = torch::zeros({Hv, Tp}, f32), beta = torch::zeros({Hv, Tp}, f32);
+  // the prep kernel writes tokens 0..T-1; only the padding of the last chunk needs zeros
+  auto qn = torch::empty({Hk, Tp, D}, bfo), kn = torch::empty({Hk, Tp, D}, bfo), vn = torch::empty({Hv, Tp, D}, bfo);
+  auto g = torch::empty({Hv, Tp}, f32), beta = torch::empty({Hv, Tp}, f32);
+  if (Tp > T) {
+    for (auto* t : {&qn, &kn, &vn}) t->narrow(1, T, Tp - T).zero_();
+    for (auto* t : {&g, &beta}) t->narrow(1, T, Tp - T).zero_();
+  }
   auto U = torch::empty({Hv, nch, kGC, D}, bfo), Wm = torch::empty({Hv, nch, kGC, D}, bfo);
   auto Qg = torch::empty({Hv, nch, kGC, D}, bfo), Kd = torch::empty({Hv, nch, kGC, D}, bfo);
   auto P = torch::empty({Hv, nch, kGC, kGC}, bfo), GC = torch::empty({Hv, nch, kGC}, f32);

@@ -73,7 +73,8 @@ __global__ void moe_topk_kernel(const float* __restrict__ logits, int ld, int E,
 // of token t live at rows[t, :] of the grouped-GEMM output). Replaces a scatter-add of
 // f32 copies; one CTA per token, 8 values per thread.
 __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ y, const int* __restrict__ rows,
-                                   const float* __restrict__ wts, __nv_bfloat16* __restrict__ x, int H, int J) {
+                                   const float* __restrict__ wts, __nv_bfloat16* __restrict__ x, int H, int J,
+                                   int accumulate) {
   const int t = blockIdx.x;
   for (int v = threadIdx.x; v < H / 8; v += blockDim.x) {
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
@@ -86,9 +87,9 @@ __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ y, const in
 #pragma unroll
       for (int i = 0; i < 8; ++i) acc[i] = fmaf(w, f[i], acc[i]);
     }
-    float xv[8];
+    float xv[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     bf16x8* xp = reinterpret_cast<bf16x8*>(x + (long long)t * H) + v;
-    unpack8(*xp, xv);
+    if (accumulate) unpack8(*xp, xv);
 #pragma unroll
     for (int i = 0; i < 8; ++i) xv[i] += __bfloat162float(__float2bfloat16(acc[i]));
     *xp = pack8(xv);
@@ -232,7 +233,8 @@ __global__ void moe_route_place_kernel(const int* __restrict__ ids, int T, int J
 
 using namespace hx;
 
-void moe_combine(torch::Tensor y, torch::Tensor rows, torch::Tensor wts, torch::Tensor x) {
+// accumulate: x += the weighted sum (else x = the sum, no read of x)
+void moe_combine(torch::Tensor y, torch::Tensor rows, torch::Tensor wts, torch::Tensor x, bool accumulate) {
   TORCH_CHECK(y.scalar_type() == at::kBFloat16 && x.scalar_type() == at::kBFloat16 && y.is_contiguous() &&
                   x.is_contiguous(), "bf16 contiguous y / x");
   TORCH_CHECK(rows.scalar_type() == at::kInt && wts.scalar_type() == at::kFloat && rows.sizes() == wts.sizes(),
@@ -242,7 +244,7 @@ void moe_combine(torch::Tensor y, torch::Tensor rows, torch::Tensor wts, torch::
   if (T == 0) return;
   moe_combine_kernel<<<T, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(y.data_ptr()), rows.data_ptr<int>(), wts.data_ptr<float>(),
-      reinterpret_cast<__nv_bfloat16*>(x.data_ptr()), H, rows.size(1));
+      reinterpret_cast<__nv_bfloat16*>(x.data_ptr()), H, rows.size(1), accumulate ? 1 : 0);
   HX_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -1049,8 +1049,7 @@ class FastModel:
         if out is None:
             out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
         self._mark("moe.combine")
-        out.zero_()  # the combine accumulates into its output
-        self.C.moe_combine(y, rows, wts, out)
+        self.C.moe_combine(y, rows, wts, out, accumulate=False)  # writes every row of out
         return out
 
     _pos3 = None
