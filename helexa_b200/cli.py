@@ -3,6 +3,11 @@
   python -m helexa_b200.cli node   [--host H] [--port P] [--config node.toml]
   python -m helexa_b200.cli serve  [--config cortex.toml]
   python -m helexa_b200.cli status [--endpoint http://localhost:31313]
+  python -m helexa_b200.cli router   --config router.toml [--port 8088]
+  python -m helexa_b200.cli tools    [--port 8889]
+  python -m helexa_b200.cli upstream [--db ledger.sqlite] [--operator-token T=op] [--port 8090]
+  python -m helexa_b200.cli bench    --target name=http://host:port [--db bench.sqlite]
+  python -m helexa_b200.cli acp      [--base-url http://127.0.0.1:31313/v1] [--model M]
 
 `serve` and `status` are the reference's `cortex serve|status` (cortex-cli/src/main.rs:
 15-111). The gateway config is TOML:
@@ -98,7 +103,55 @@ def main(argv: list[str] | None = None) -> int:
     s.add_argument("-c", "--config", default="cortex.toml")
     st = sub.add_parser("status", help="print fleet health and model placements")
     st.add_argument("-e", "--endpoint", default="http://localhost:31313")
+    r = sub.add_parser("router", help="run the federation router in front of several gateways")
+    r.add_argument("--config", required=True)
+    r.add_argument("--host", default="0.0.0.0")
+    r.add_argument("--port", type=int, default=8088)
+    t = sub.add_parser("tools", help="run the SSRF-guarded fetch tool service")
+    t.add_argument("--host", default="127.0.0.1")
+    t.add_argument("--port", type=int, default=8889)
+    u = sub.add_parser("upstream", help="run the account ledger service")
+    u.add_argument("--db", default="helexa-ledger.sqlite")
+    u.add_argument("--operator-token", action="append", default=[], help="TOKEN=operator (repeatable)")
+    u.add_argument("--signup-allocation", type=int, default=0)
+    u.add_argument("--host", default="127.0.0.1")
+    u.add_argument("--port", type=int, default=8090)
+    b = sub.add_parser("bench", help="run the continuous benchmark daemon")
+    b.add_argument("--target", action="append", required=True, help="name=http://host:port (repeatable)")
+    b.add_argument("--db", default="helexa-bench.sqlite")
+    b.add_argument("--interval", type=float, default=3600.0)
+    b.add_argument("--port", type=int, default=8099)
+    a = sub.add_parser("acp", help="run the ACP editor agent on stdin / stdout")
+    a.add_argument("--base-url", default="http://127.0.0.1:31313/v1")
+    a.add_argument("--model", default="default")
+    a.add_argument("--api-key")
     args = ap.parse_args(argv)
+    if args.cmd in ("router", "tools", "upstream"):
+        import uvicorn
+        if args.cmd == "router":
+            from .mesh.router import RouterConfig, create_router
+            app = create_router(RouterConfig.load(args.config))
+        elif args.cmd == "tools":
+            from .mesh.tools import create_tools_app
+            app = create_tools_app()
+        else:
+            from .mesh.upstream import UpstreamConfig, create_upstream
+            toks = dict(x.split("=", 1) for x in args.operator_token)
+            app = create_upstream(UpstreamConfig(db_path=args.db, operator_tokens=toks,
+                                                 signup_allocation=args.signup_allocation))
+        uvicorn.run(app, host=args.host, port=args.port)
+        return 0
+    if args.cmd == "bench":
+        from .mesh.benchd import main as bench_main
+        argv2 = sum((["--target", x] for x in args.target), []) + ["--db", args.db, "--interval",
+                                                                   str(args.interval), "--port", str(args.port)]
+        bench_main(argv2)
+        return 0
+    if args.cmd == "acp":
+        from .mesh.acp import main as acp_main
+        acp_main(["--base-url", args.base_url, "--model", args.model] +
+                 (["--api-key", args.api_key] if args.api_key else []))
+        return 0
     if args.cmd == "node":
         from .server.app import main as node_main
         sys.argv = [sys.argv[0], "--host", args.host, "--port", str(args.port)] + \
