@@ -30,6 +30,7 @@
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 
+#include <cstdlib>
 #include <mutex>
 
 #include "tc_common.cuh"
@@ -56,13 +57,13 @@ HX_DEVICE void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::
 // generic-proxy shared-memory writes (P) -> visible to the tensor core's async proxy
 HX_DEVICE void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-template <int D, int BN>
+template <int D, int BN, int NT = 1>
 struct AttnSmem {
-  alignas(1024) __nv_bfloat16 Q[128 * D];       // D/64 chunks of [128 x 64], 128B-swizzled
+  alignas(1024) __nv_bfloat16 Q[NT][128 * D];   // per query tile: D/64 chunks of [128 x 64], 128B-swizzled
   alignas(1024) __nv_bfloat16 K[2][BN * D];     // per stage: D/64 chunks of [BN x 64]
   alignas(1024) __nv_bfloat16 Vt[2][D * BN];    // per stage: BN/64 chunks of [D x 64]
-  alignas(1024) __nv_bfloat16 P[128 * BN];      // BN/64 chunks of [128 x 64]
-  uint64_t q_full, kv_full[2], kv_empty[2], s_full[2], s_empty[2], p_full, o_done;
+  alignas(1024) __nv_bfloat16 P[NT][128 * BN];  // per query tile: BN/64 chunks of [128 x 64]
+  uint64_t q_full, kv_full[2], kv_empty[2], s_full[NT][2], s_empty[NT][2], p_full[NT], o_done[NT];
   uint32_t tmem_base;
   int abort;
 };
@@ -78,21 +79,26 @@ struct AttnTcArgs {
   int* err;
 };
 
-template <int D, int BN>
-__global__ void __launch_bounds__(192, 1) attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap mapQ,
+// NT query tiles per CTA share each K / V tile; with NT = 2 each tile has its own
+// softmax warpgroup, so one tile's softmax runs while the tensor core works on the
+// other's scores (the single-tile CTA leaves the tensor core idle during its softmax).
+template <int D, int BN, int NT = 1>
+__global__ void __launch_bounds__(64 + 128 * NT, 1) attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap mapQ,
                                                                  const __grid_constant__ CUtensorMap mapK,
                                                                  const __grid_constant__ CUtensorMap mapVt,
                                                                  AttnTcArgs a) {
   static_assert(D % 64 == 0 && BN % 64 == 0 && D <= 256 && BN <= 128, "tile shape");
+  static_assert(NT * (D + 2 * BN) <= 512, "TMEM: NT x (O + two S buffers) columns");
   constexpr uint32_t kTmemCols = 512;
-  constexpr uint32_t O_COL = 0, S_COL = D;  // O [0, D); S buffers [D, D + 2 BN)
+  // tile t: O at [t D, (t+1) D); its two S buffers after all O blocks
+  constexpr uint32_t S_COL = NT * D;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
-  auto* s = reinterpret_cast<AttnSmem<D, BN>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  auto* s = reinterpret_cast<AttnSmem<D, BN, NT>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qt = gridDim.x - 1 - blockIdx.x;  // latest (longest) query tiles first
   const int h = blockIdx.y, kvh = h / a.G;
-  const int t0 = qt * 128;
-  const int kend = a.causal ? min(a.L, a.p0 + t0 + 128) : a.L;
+  const int t0 = qt * 128 * NT;  // first row of the CTA's first query tile
+  const int kend = a.causal ? min(a.L, a.p0 + t0 + 128 * NT) : a.L;
   const int nb = (kend + BN - 1) / BN;
 
   if (threadIdx.x == 0) {
@@ -100,11 +106,15 @@ __global__ void __launch_bounds__(192, 1) attn_prefill_tc_kernel(const __grid_co
     for (int i = 0; i < 2; ++i) {
       tc::mbar_init(&s->kv_full[i], 1);
       tc::mbar_init(&s->kv_empty[i], 1);
-      tc::mbar_init(&s->s_full[i], 1);
-      tc::mbar_init(&s->s_empty[i], 4);
+      for (int u = 0; u < NT; ++u) {
+        tc::mbar_init(&s->s_full[u][i], 1);
+        tc::mbar_init(&s->s_empty[u][i], 4);
+      }
     }
-    tc::mbar_init(&s->p_full, 4);
-    tc::mbar_init(&s->o_done, 1);
+    for (int u = 0; u < NT; ++u) {
+      tc::mbar_init(&s->p_full[u], 4);
+      tc::mbar_init(&s->o_done[u], 1);
+    }
     s->abort = 0;
     tc::fence_barrier_init();
     tc::prefetch_tmap(&mapQ);
@@ -123,9 +133,12 @@ __global__ void __launch_bounds__(192, 1) attn_prefill_tc_kernel(const __grid_co
   if (warp == 0) {
     // --------------------------------- TMA producer -----------------------------------
     if (lane == 0) {
-      tc::mbar_expect_tx(&s->q_full, 128 * D * 2);
+      tc::mbar_expect_tx(&s->q_full, NT * 128 * D * 2);
 #pragma unroll
-      for (int c = 0; c < D / 64; ++c) tc::tma_load_2d(s->Q + c * 128 * 64, &mapQ, &s->q_full, h * D + c * 64, t0);
+      for (int u = 0; u < NT; ++u)
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c)
+          tc::tma_load_2d(s->Q[u] + c * 128 * 64, &mapQ, &s->q_full, h * D + c * 64, t0 + u * 128);
       for (int j = 0; j < nb && !s->abort; ++j) {
         const int st = j & 1;
         if (j >= 2 && !tc::mbar_wait(&s->kv_empty[st], ((j >> 1) - 1) & 1, a.err, 5001)) { s->abort = 1; break; }
@@ -143,35 +156,44 @@ __global__ void __launch_bounds__(192, 1) attn_prefill_tc_kernel(const __grid_co
     if (lane == 0) {
       constexpr uint32_t idesc_s = tc::idesc_bf16_f32(128, BN);
       constexpr uint32_t idesc_o = tc::idesc_bf16_f32(128, D);
-      const uint32_t q0 = tc::smem_u32(s->Q), p0s = tc::smem_u32(s->P);
       bool ok = tc::mbar_wait(&s->q_full, 0, a.err, 5002);
-      auto pv = [&](int j) -> bool {  // O += P_j V_j
-        if (!tc::mbar_wait(&s->p_full, j & 1, a.err, 5003)) return false;
-        tc::tc_fence_after();
+      auto pv = [&](int j) -> bool {  // O_u += P_u,j V_j for every tile, then free stage j
         const uint32_t v0 = tc::smem_u32(s->Vt[j & 1]);
 #pragma unroll
-        for (int k = 0; k < BN / 16; ++k) {
-          const uint32_t ad = p0s + (k >> 2) * 128 * 128 + (k & 3) * 32;
-          const uint32_t bd = v0 + (k >> 2) * D * 128 + (k & 3) * 32;
-          tc::umma_bf16(tmem + O_COL, tc::sdesc_k128(ad), tc::sdesc_k128(bd), idesc_o, (j > 0 || k > 0) ? 1u : 0u);
+        for (int u = 0; u < NT; ++u) {
+          if (!tc::mbar_wait(&s->p_full[u], j & 1, a.err, 5003)) return false;
+          tc::tc_fence_after();
+          const uint32_t p0s = tc::smem_u32(s->P[u]);
+#pragma unroll
+          for (int k = 0; k < BN / 16; ++k) {
+            const uint32_t ad = p0s + (k >> 2) * 128 * 128 + (k & 3) * 32;
+            const uint32_t bd = v0 + (k >> 2) * D * 128 + (k & 3) * 32;
+            tc::umma_bf16(tmem + u * D, tc::sdesc_k128(ad), tc::sdesc_k128(bd), idesc_o, (j > 0 || k > 0) ? 1u : 0u);
+          }
+          tc::umma_commit(&s->o_done[u]);
         }
-        tc::umma_commit(&s->o_done);
         tc::umma_commit(&s->kv_empty[j & 1]);
         return true;
       };
       for (int j = 0; j < nb && ok && !s->abort; ++j) {
         const int st = j & 1;
         if (!tc::mbar_wait(&s->kv_full[st], (j >> 1) & 1, a.err, 5004)) { ok = false; break; }
-        if (j >= 2 && !tc::mbar_wait(&s->s_empty[st], ((j >> 1) - 1) & 1, a.err, 5005)) { ok = false; break; }
-        tc::tc_fence_after();
         const uint32_t k0 = tc::smem_u32(s->K[st]);
 #pragma unroll
-        for (int k = 0; k < D / 16; ++k) {
-          const uint32_t ad = q0 + (k >> 2) * 128 * 128 + (k & 3) * 32;
-          const uint32_t bd = k0 + (k >> 2) * BN * 128 + (k & 3) * 32;
-          tc::umma_bf16(tmem + S_COL + st * BN, tc::sdesc_k128(ad), tc::sdesc_k128(bd), idesc_s, k > 0 ? 1u : 0u);
+        for (int u = 0; u < NT; ++u) {
+          if (j >= 2 && !tc::mbar_wait(&s->s_empty[u][st], ((j >> 1) - 1) & 1, a.err, 5005)) { ok = false; break; }
+          tc::tc_fence_after();
+          const uint32_t q0 = tc::smem_u32(s->Q[u]);
+#pragma unroll
+          for (int k = 0; k < D / 16; ++k) {
+            const uint32_t ad = q0 + (k >> 2) * 128 * 128 + (k & 3) * 32;
+            const uint32_t bd = k0 + (k >> 2) * BN * 128 + (k & 3) * 32;
+            tc::umma_bf16(tmem + S_COL + (u * 2 + st) * BN, tc::sdesc_k128(ad), tc::sdesc_k128(bd), idesc_s,
+                          k > 0 ? 1u : 0u);
+          }
+          tc::umma_commit(&s->s_full[u][st]);
         }
-        tc::umma_commit(&s->s_full[st]);
+        if (!ok) break;
         if (j >= 1 && !pv(j - 1)) { ok = false; break; }
       }
       if (ok && !s->abort && nb > 0) ok = pv(nb - 1);
@@ -180,8 +202,10 @@ __global__ void __launch_bounds__(192, 1) attn_prefill_tc_kernel(const __grid_co
   } else {
     // --------------------------- softmax / correction / epilogue ----------------------
     const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int u = (warp - 2) >> 2;  // this warpgroup's query tile
     const int row = q * 32 + lane;
-    const int t = t0 + row;
+    const int t = t0 + u * 128 + row;
+    const uint32_t O_COL = u * D;
     const int pos = a.p0 + t;
     const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
     float m_used = -INFINITY, l = 0.f;
@@ -191,16 +215,17 @@ __global__ void __launch_bounds__(192, 1) attn_prefill_tc_kernel(const __grid_co
     // __all_sync, the lazy rescale with __any_sync)
     for (int j = 0; j < nb; ++j) {
       const int st = j & 1;
-      if (!__all_sync(0xffffffffu, tc::mbar_wait(&s->s_full[st], (j >> 1) & 1, a.err, 5006))) { ok = false; break; }
+      if (!__all_sync(0xffffffffu, tc::mbar_wait(&s->s_full[u][st], (j >> 1) & 1, a.err, 5006))) { ok = false; break; }
       tc::tc_fence_after();
       float sv[BN];
 #pragma unroll
-      for (int c = 0; c < BN / 32; ++c) tc::tmem_ld32(tmem + lane_addr + S_COL + st * BN + c * 32, sv + c * 32);
+      for (int c = 0; c < BN / 32; ++c)
+        tc::tmem_ld32(tmem + lane_addr + S_COL + (u * 2 + st) * BN + c * 32, sv + c * 32);
       tc::tc_fence_before();
       __syncwarp();
-      if (lane == 0) tc::mbar_arrive(&s->s_empty[st]);
+      if (lane == 0) tc::mbar_arrive(&s->s_empty[u][st]);
       const int k0 = j * BN;
-      const bool diag = (a.causal && k0 + BN - 1 > a.p0 + t0) || k0 + BN > a.L;  // block needs masking
+      const bool diag = (a.causal && k0 + BN - 1 > a.p0 + t0 + u * 128) || k0 + BN > a.L;  // needs masking
       float mx = -INFINITY;
 #pragma unroll
       for (int c = 0; c < BN; ++c) {
@@ -210,7 +235,7 @@ __global__ void __launch_bounds__(192, 1) attn_prefill_tc_kernel(const __grid_co
         mx = fmaxf(mx, v);
       }
       // PV_{j-1} must be complete before P is overwritten or O is rescaled
-      if (j >= 1 && !__all_sync(0xffffffffu, tc::mbar_wait(&s->o_done, (j - 1) & 1, a.err, 5007))) {
+      if (j >= 1 && !__all_sync(0xffffffffu, tc::mbar_wait(&s->o_done[u], (j - 1) & 1, a.err, 5007))) {
         ok = false;
         break;
       }
@@ -236,7 +261,7 @@ __global__ void __launch_bounds__(192, 1) attn_prefill_tc_kernel(const __grid_co
         }
       }
       // P_j = exp2(s - m_used) as bf16, 128B-swizzled K-major rows of 64 keys
-      unsigned char* prow = reinterpret_cast<unsigned char*>(s->P) + row * 128;
+      unsigned char* prow = reinterpret_cast<unsigned char*>(s->P[u]) + row * 128;
 #pragma unroll
       for (int c = 0; c < BN / 64; ++c) {
 #pragma unroll
@@ -255,10 +280,10 @@ __global__ void __launch_bounds__(192, 1) attn_prefill_tc_kernel(const __grid_co
       fence_proxy_async_smem();
       tc::tc_fence_before();
       __syncwarp();
-      if (lane == 0) tc::mbar_arrive(&s->p_full);
+      if (lane == 0) tc::mbar_arrive(&s->p_full[u]);
     }
     // epilogue: O / l (+ gate) -> bf16
-    if (ok && nb > 0 && __all_sync(0xffffffffu, tc::mbar_wait(&s->o_done, (nb - 1) & 1, a.err, 5008))) {
+    if (ok && nb > 0 && __all_sync(0xffffffffu, tc::mbar_wait(&s->o_done[u], (nb - 1) & 1, a.err, 5008))) {
       tc::tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
 #pragma unroll 1
@@ -342,13 +367,13 @@ static CUtensorMap attn_map(const void* ptr, int64_t rows, int64_t cols, int64_t
   return m;
 }
 
-template <int D, int BN>
+template <int D, int BN, int NT = 1>
 static void launch_attn_tc(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const AttnTcArgs& a,
                            int qtiles, int Hq, cudaStream_t st) {
-  auto k = attn_prefill_tc_kernel<D, BN>;
-  const size_t smem = sizeof(AttnSmem<D, BN>) + 1024;
+  auto k = attn_prefill_tc_kernel<D, BN, NT>;
+  const size_t smem = sizeof(AttnSmem<D, BN, NT>) + 1024;
   HX_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  k<<<dim3(qtiles, Hq), 192, smem, st>>>(mq, mk, mv, a);
+  k<<<dim3((qtiles + NT - 1) / NT, Hq), 64 + 128 * NT, smem, st>>>(mq, mk, mv, a);
   HX_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -397,9 +422,20 @@ void attn_prefill_tc(torch::Tensor q, torch::Tensor kc, torch::Tensor vc, torch:
     const CUtensorMap mv = attn_map(vt.data_ptr(), (int64_t)Hkv * D, Lpad, Lpad, D);
     launch_attn_tc<256, 64>(mq, mk, mv, a, qtiles, (int)Hq, st);
   } else if (D == 128) {
-    const CUtensorMap mk = attn_map(kc.data_ptr(), (int64_t)Hkv * maxlen, D, D, 128);
+    // two query tiles per CTA with 64-key blocks (HELEXA_ATTN_PINGPONG=0: one tile,
+    // 128-key blocks)
+    static const bool single = [] {
+      const char* e = std::getenv("HELEXA_ATTN_PINGPONG");
+      return e && e[0] == '0';
+    }();
     const CUtensorMap mv = attn_map(vt.data_ptr(), (int64_t)Hkv * D, Lpad, Lpad, D);
-    launch_attn_tc<128, 128>(mq, mk, mv, a, qtiles, (int)Hq, st);
+    if (single) {
+      const CUtensorMap mk = attn_map(kc.data_ptr(), (int64_t)Hkv * maxlen, D, D, 128);
+      launch_attn_tc<128, 128>(mq, mk, mv, a, qtiles, (int)Hq, st);
+    } else {
+      const CUtensorMap mk = attn_map(kc.data_ptr(), (int64_t)Hkv * maxlen, D, D, 64);
+      launch_attn_tc<128, 64, 2>(mq, mk, mv, a, qtiles, (int)Hq, st);
+    }
   } else {
     const CUtensorMap mk = attn_map(kc.data_ptr(), (int64_t)Hkv * maxlen, D, D, 128);
     const CUtensorMap mv = attn_map(vt.data_ptr(), (int64_t)Hkv * D, Lpad, Lpad, D);
