@@ -125,6 +125,9 @@ void dit_qk_rope(torch::Tensor qkv, c10::optional<torch::Tensor> qw, c10::option
                  torch::Tensor ang, int64_t H, int64_t Dh, double eps, torch::Tensor q, torch::Tensor k,
                  torch::Tensor v);
 
+void gemm_q(torch::Tensor A, torch::Tensor Wq, int64_t type, int64_t K, torch::Tensor C, int64_t epi,
+            torch::Tensor err);
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("set_pdl", [](bool on) { hx_pdl_enabled() = on; });
   m.def("gemv", &gemv);
@@ -187,6 +190,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ipc_close", &ipc_close);
   m.def("ar_oneshot", &ar_oneshot);
   m.def("gemm", &gemm);
+  m.def("gemm_q", &gemm_q);
   m.def("gguf_dequant_host", &gguf_dequant_host);
   m.def("gguf_quant_host", &gguf_quant_host);
   m.def("gguf_gemv", &gguf_gemv);

@@ -28,6 +28,7 @@
 #include <mutex>
 #include <unordered_map>
 
+#include "gguf_blocks.cuh"
 #include "tc_common.cuh"
 
 namespace hx {
@@ -55,6 +56,8 @@ struct GemmParams {
   int b_rows_per_group;    // grouped mode: tile b_row0 holds a group index scaled by this
   int tma_store;           // 1: the epilogue stages 32 x 32 chunks in shared memory and TMA-stores them
   int* err;
+  const uint8_t* qb;       // quantized B (QT != 0): N rows of q_row_bytes GGUF block bytes
+  long long q_row_bytes;
 };
 
 template <int BN, int STAGES>
@@ -70,8 +73,13 @@ struct GemmSmem {
   alignas(1024) unsigned char stg[4][2][4096];
 };
 
-template <int BN, int STAGES>
-__global__ void __launch_bounds__(192, 1) gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap mapA,
+// QT = 0: B arrives by TMA. QT = a GGUF block type (Q8_0 / Q4_K / padded Q6_K): B stays
+// quantized in global memory and four more warps (6-9) dequantize each B stage into
+// the 128B-swizzled K-major layout the MMA reads, so no bf16 copy of the weight is
+// ever written to global memory; each converter warp arrives on the stage's barrier
+// beside the A tile's TMA transaction count.
+template <int BN, int STAGES, int QT = 0>
+__global__ void __launch_bounds__(QT ? 320 : 192, 1) gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap mapA,
                                                               const __grid_constant__ CUtensorMap mapB,
                                                               const __grid_constant__ CUtensorMap mapC,
                                                               GemmParams p) {
@@ -83,16 +91,16 @@ __global__ void __launch_bounds__(192, 1) gemm_tcgen05_kernel(const __grid_const
                                   : p.num_m_blocks;
   const int total_tiles = num_entries * p.num_n_blocks;
   const int kblocks = (p.K + kBK - 1) / kBK;
-  constexpr uint32_t kStageBytes = (kBM + BN) * kBK * 2;
+  constexpr uint32_t kStageBytes = (QT ? kBM : kBM + BN) * kBK * 2;  // bytes the TMA brings per stage
   constexpr uint32_t kTmemCols = 2 * BN;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < STAGES; ++i) { tc::mbar_init(&s->full[i], 1); tc::mbar_init(&s->empty[i], 1); }
+    for (int i = 0; i < STAGES; ++i) { tc::mbar_init(&s->full[i], QT ? 5 : 1); tc::mbar_init(&s->empty[i], 1); }
     for (int i = 0; i < 2; ++i) { tc::mbar_init(&s->tfull[i], 1); tc::mbar_init(&s->tempty[i], 4); }
     s->abort = 0;
     tc::fence_barrier_init();
     tc::prefetch_tmap(&mapA);
-    tc::prefetch_tmap(&mapB);
+    if (!QT) tc::prefetch_tmap(&mapB);
     if (p.tma_store) tc::prefetch_tmap(&mapC);
   }
   if (warp == 1) {
@@ -133,7 +141,7 @@ __global__ void __launch_bounds__(192, 1) gemm_tcgen05_kernel(const __grid_const
           if (!tc::mbar_wait(&s->empty[stage], phase ^ 1, p.err, 11)) { s->abort = 1; break; }
           tc::mbar_expect_tx(&s->full[stage], kStageBytes);
           tc::tma_load_2d(s->A[stage], &mapA, &s->full[stage], kb * kBK, a_row);
-          tc::tma_load_2d(s->B[stage], &mapB, &s->full[stage], kb * kBK, b_row);
+          if (!QT) tc::tma_load_2d(s->B[stage], &mapB, &s->full[stage], kb * kBK, b_row);
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
       }
@@ -166,6 +174,41 @@ __global__ void __launch_bounds__(192, 1) gemm_tcgen05_kernel(const __grid_const
         tc::umma_commit(&s->tfull[acc]);
       }
     }
+  } else if (QT && warp >= 6) {
+    // ------------------------- dequantizing B producer (warps 6-9) -------------------
+    // Thread ct writes 16-byte pieces (8 values) of the BN x 64 stage: piece i is row
+    // i / 8, column chunk i % 8, stored at row * 128 + ((chunk ^ (row % 8)) * 16) -- the
+    // 128-byte swizzle a TMA load of the same box would produce.
+    const int ct = threadIdx.x - 192;
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < total_tiles && ok && !s->abort; t += gridDim.x) {
+      int a_row, b_row, rows, out_row, n_blk;
+      tile_coords(t, a_row, b_row, rows, out_row, n_blk);
+      for (int kb = 0; kb < kblocks; ++kb) {
+        if (!__all_sync(0xffffffffu, tc::mbar_wait(&s->empty[stage], phase ^ 1, p.err, 15))) { ok = false; break; }
+        unsigned char* dst = reinterpret_cast<unsigned char*>(s->B[stage]);
+#pragma unroll 4
+        for (int i = ct; i < BN * 8; i += 128) {
+          const int r = i >> 3, u = i & 7;
+          const int n = b_row + r, v = kb * 8 + u;  // weight row, 8-value group along K
+          float f[8];
+          if (n < p.N && v * 8 < p.K) {
+            if constexpr (QT != 0) dequant8<QT>(p.qb + (long long)n * p.q_row_bytes, v, f);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) f[e] = 0.f;
+          }
+          *reinterpret_cast<bf16x8*>(dst + r * 128 + ((u ^ (r & 7)) << 4)) = pack8(f);
+        }
+        tc::fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&s->full[stage]);
+        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+      }
+    }
+    if (!ok) s->abort = 1;
   } else {
     // ------------------------------ epilogue (warps 2-5) ----------------------
     // Each warp owns a 32-row slab (its TMEM lane quarter). With TMA stores, every
@@ -335,10 +378,10 @@ static bool make_store_map(CUtensorMap* m, void* ptr, int64_t rows, int64_t cols
                      CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int QT = 0>
 static void launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const GemmParams& p,
                         int total_tiles, cudaStream_t st) {
-  auto k = gemm_tcgen05_kernel<BN, STAGES>;
+  auto k = gemm_tcgen05_kernel<BN, STAGES, QT>;
   const size_t smem = sizeof(GemmSmem<BN, STAGES>) + 1024;
   static bool attr_set = false;
   if (!attr_set) {
@@ -349,7 +392,7 @@ static void launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUte
   HX_CUDA_CHECK(cudaGetDevice(&dev));
   HX_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
   const int grid = std::max(1, std::min(total_tiles, sms));
-  k<<<grid, 192, smem, st>>>(ma, mb, mc, p);
+  k<<<grid, QT ? 320 : 192, smem, st>>>(ma, mb, mc, p);
   HX_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -397,6 +440,47 @@ static void gemm_common(torch::Tensor A, torch::Tensor B, torch::Tensor C, int64
 // C = A @ B^T (bf16 in, f32 accumulate); epi: 0 bf16, 1 SwiGLU on interleaved columns, 2 f32.
 void gemm(torch::Tensor A, torch::Tensor B, torch::Tensor C, int64_t epi, torch::Tensor err) {
   gemm_common(A, B, C, epi, nullptr, 0, B.size(0), err);
+}
+
+// C = A @ W^T with W held as GGUF block rows (uint8 [N, row_bytes]; type Q8_0, Q4_K or
+// padded Q6_K): the dequantization runs inside the GEMM's producer, one shared-memory
+// stage at a time (the reference dequantizes the whole weight to f16 and calls cuBLAS
+// above M = 64, tp/tp_linear.rs:76-139).
+void gemm_q(torch::Tensor A, torch::Tensor Wq, int64_t type, int64_t K, torch::Tensor C, int64_t epi,
+            torch::Tensor err) {
+  TORCH_CHECK(A.is_cuda() && A.scalar_type() == at::kBFloat16 && A.dim() == 2 && A.stride(1) == 1, "A [M,K] bf16");
+  TORCH_CHECK(A.size(1) == K && K % 256 == 0, "K must match A and be a multiple of 256");
+  TORCH_CHECK(Wq.is_cuda() && Wq.scalar_type() == at::kByte && Wq.dim() == 2 && Wq.is_contiguous(), "Wq uint8 [N, row_bytes]");
+  int bytes = 0, vals = 0;
+  if (type == kQ8_0) { bytes = 34; vals = 32; }
+  else if (type == kQ4_K) { bytes = 144; vals = 256; }
+  else if (type == kQ6_Kp) { bytes = 224; vals = 256; }
+  else TORCH_CHECK(false, "gemm_q: block type must be Q8_0, Q4_K or padded Q6_K");
+  TORCH_CHECK(Wq.size(1) == K / vals * bytes, "row bytes do not match K for this block type");
+  const int M = A.size(0), N = Wq.size(0);
+  constexpr int BN = 256;
+  GemmParams p{};
+  p.M = M; p.N = N; p.K = (int)K; p.C = C.data_ptr(); p.ldc = C.stride(0); p.epi = (int)epi;
+  p.num_m_blocks = (M + kBM - 1) / kBM;
+  p.num_n_blocks = (N + BN - 1) / BN;
+  p.err = err.data_ptr<int>();
+  p.qb = Wq.data_ptr<uint8_t>();
+  p.q_row_bytes = Wq.size(1);
+  if (epi == kEpiSwiGLU) TORCH_CHECK(N % 32 == 0 && C.size(1) * 2 >= N, "SwiGLU output width");
+  TORCH_CHECK(C.scalar_type() == (epi == kEpiF32 ? at::kFloat : at::kBFloat16), "output dtype");
+  TORCH_CHECK((p.ldc * C.element_size()) % 16 == 0, "output row stride must be 16-byte aligned");
+  const int total = p.num_m_blocks * p.num_n_blocks;
+  if (total == 0) return;
+  CUtensorMap ma = make_map(A.data_ptr(), M, K, A.stride(0), kBM);
+  CUtensorMap mc;
+  const int out_cols = epi == kEpiSwiGLU ? N / 2 : N;
+  p.tma_store = C.dim() == 2 && C.stride(1) == 1 &&
+                make_store_map(&mc, C.data_ptr(), M, out_cols, p.ldc, (int)C.element_size(), epi == kEpiSwiGLU ? 16 : 32);
+  if (!p.tma_store) memset(&mc, 0, sizeof(mc));
+  auto st = at::cuda::getCurrentCUDAStream();
+  if (type == kQ8_0) launch_gemm<BN, 4, kQ8_0>(ma, ma, mc, p, total, st);
+  else if (type == kQ4_K) launch_gemm<BN, 4, kQ4_K>(ma, ma, mc, p, total, st);
+  else launch_gemm<BN, 4, kQ6_Kp>(ma, ma, mc, p, total, st);
 }
 
 // Grouped: tiles int32 [num_entries, 4] = (a_row0, b_row0, rows, out_row0); B is the

@@ -52,3 +52,31 @@ def main():
 
 if __name__ == "__main__":
     main()
+
+
+def quant_main(argv=None):
+    """Quantized weights at prefill: dequantize-in-the-GEMM (`gemm_q`) against
+    dequantize-to-bf16-then-GEMM, over M, for one Qwen3-32B-shaped projection.
+
+      python -c "from helexa_b200.bench.gemm_bench import quant_main; quant_main()"
+    """
+    from .. import ops
+    from ..models.fast import GGUF_Q4_K, GGUF_Q6_K, GGUF_Q8_0, QWeight
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--n", type=int, default=10240)
+    ap.add_argument("--k", type=int, default=5120)
+    ap.add_argument("--ms", default="16,64,128,256,512,1024")
+    args = ap.parse_args(argv)
+    C = ops.C
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    W = torch.randn(args.n, args.k, device="cuda", dtype=torch.bfloat16) * 0.05
+    for name, t in (("Q4_K", GGUF_Q4_K), ("Q6_K", GGUF_Q6_K), ("Q8_0", GGUF_Q8_0)):
+        qw = QWeight(C.gguf_quant(W, t), t, args.k)
+        for M in (int(m) for m in args.ms.split(",")):
+            A = torch.randn(M, args.k, device="cuda", dtype=torch.bfloat16)
+            out = torch.empty(M, args.n, device="cuda", dtype=torch.bfloat16)
+            t_fused = bench(lambda: C.gemm_q(A, qw.raw, qw.type, args.k, out, 0, err))
+            t_scratch = bench(lambda: C.gemm(A, qw.dequant(C), out, 0, err))
+            print(json.dumps({"type": name, "M": M, "N": args.n, "K": args.k, "fused_ms": round(t_fused, 4),
+                              "scratch_ms": round(t_scratch, 4)}))
+    assert err.item() == 0

@@ -317,6 +317,7 @@ class FastModel:
         # attention prefill: "tc" (tcgen05/TMEM, csrc/attn_prefill_tc.cu) or "mma"
         # (mma.sync tiles, csrc/attn_prefill.cu)
         self.attn_engine = os.environ.get("HELEXA_ATTN_PREFILL", "tc")
+        self.gemm_dequant = os.environ.get("HELEXA_GEMM_DEQUANT", "scratch")
         self._tma_ok_cache: dict = {}
         self.sampler = SamplerState(max_slots, device) if device.type == "cuda" else None
         # multimodal rotary (vision-language configs): per-frequency axis map, and per slot
@@ -795,6 +796,18 @@ class FastModel:
                 out.copy_(y)
                 return out
             return y
+        if isinstance(W, QWeight) and self._fused_dequant(W):
+            # dequantization inside the GEMM's producer: no bf16 copy of the weight
+            N = W.shape[0] // 2 if epi == 1 else W.shape[0]
+            dst = out if (out is not None and N % 8 == 0) else \
+                torch.empty(x.shape[0], (N + 7) // 8 * 8, dtype=torch.float32 if epi == 2 else torch.bfloat16,
+                            device=x.device)
+            self.C.gemm_q(x, W.raw, W.type, W.K, dst, epi, self._gemm_err())
+            y = dst if dst.shape[1] == N else dst[:, :N]
+            if out is not None and y is not out:
+                out.copy_(y)
+                return out
+            return y
         if isinstance(W, (QWeight, QWeightCat)):
             W = W.dequant(self.C)
         N = W.shape[0] // 2 if epi == 1 else W.shape[0]
@@ -809,6 +822,16 @@ class FastModel:
             out.copy_(y)
             return out
         return y
+
+    def _fused_dequant(self, W: "QWeight") -> bool:
+        """HELEXA_GEMM_DEQUANT=fused: quantized prefill GEMMs dequantize in the GEMM's
+        producer warps (Q8_0, Q4_K, padded Q6_K; K a multiple of 256). The default
+        dequantizes the whole weight to bf16 scratch first: measured faster at every M
+        (`gemm_bench.quant_main`: 10240 x 5120 Q4_K at M = 16, 0.41 ms fused vs 0.087 ms
+        for dequantize + GEMM; the fused producer runs on N / 256 CTAs only and
+        re-decodes each weight tile once per 128-row block).""" 
+        return (self.gemm_dequant == "fused" and W.raw.is_cuda and W.K % 256 == 0
+                and W.type in (GGUF_Q8_0, GGUF_Q4_K, GGUF_Q6_K_PADDED))
 
     def _gemm_err(self) -> torch.Tensor:
         if not hasattr(self, "_gerr"):

@@ -120,3 +120,32 @@ def test_moe_route_prefill_and_grouped_dev(shared):
             a = torch.nn.functional.silu(hgu[0::2]) * hgu[1::2]
             ref[t] += w * (a.bfloat16().float() @ w_d[g].float().t())
     _check(out, ref, 3e-2)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("gtype", ["Q8_0", "Q4_K", "Q6_K"])
+@pytest.mark.parametrize("epi", [0, 1, 2])
+def test_gemm_fused_dequant_matches_dequantized_gemm(gtype, epi):
+    """The GEMM that dequantizes GGUF blocks in its producer warps gives the same result
+    as dequantizing the whole weight to bf16 and running the bf16 GEMM (same bf16 B
+    values, same accumulation order), on ragged M and N."""
+    from helexa_b200 import ops
+    from helexa_b200.models.fast import GGUF_Q4_K, GGUF_Q6_K, GGUF_Q8_0, QWeight
+    C = ops.C
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(5)
+    M, N, K = 300, 544, 768
+    w = (torch.randn(N, K, device=dev, generator=g) * 0.05).bfloat16()
+    t = {"Q8_0": GGUF_Q8_0, "Q4_K": GGUF_Q4_K, "Q6_K": GGUF_Q6_K}[gtype]
+    qw = QWeight(C.gguf_quant(w, t), t, K)
+    x = torch.randn(M, K, device=dev, generator=g).bfloat16()
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    n_out = N // 2 if epi == 1 else N
+    dt = torch.float32 if epi == 2 else torch.bfloat16
+    ref = torch.empty(M, n_out, dtype=dt, device=dev)
+    C.gemm(x, qw.dequant(C), ref, epi, err)
+    got = torch.empty(M, n_out, dtype=dt, device=dev)
+    C.gemm_q(x, qw.raw, qw.type, K, got, epi, err)
+    torch.cuda.synchronize()
+    assert err.item() == 0
+    assert (got.float() - ref.float()).abs().max().item() <= 1e-2 * ref.float().abs().max().item()
