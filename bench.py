@@ -8,7 +8,7 @@ the launching stream, max over ranks. Weights (~160 GB at TP1) are far larger th
 the 126 MB L2, so every step streams them from HBM (no flush needed).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl helexa|reference]
-  python bench.py --model qwen3-8b --prompt 2048 --decode 256     # BASELINE's Qwen3-8B config
+  python bench.py --model qwen3-8b --prompt 2048 --decode 256     # the Qwen3-8B headline config (2048 + 256)
   python bench.py --model qwen3-32b --prompt 4096 --decode 256 --quant Q4_K_M
 """
 from __future__ import annotations

@@ -2,7 +2,7 @@
 per GPU under torchrun for tensor parallelism. Device-timed with CUDA events; every
 figure is the max over ranks.
 
-Two workloads from the BASELINE configurations that a single-request bench does not cover:
+Two serving workloads that a single-request bench does not cover:
 
 * ``--mode prefix``: a cold request of ``--prompt`` tokens, a snapshot of the first
   ``--share`` tokens (attention K/V plus a deep copy of the GDN conv ring and recurrent

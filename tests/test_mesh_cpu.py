@@ -455,3 +455,12 @@ def test_acp_openai_provider_parses_streamed_tool_calls():
 
     got = asyncio.run(run())
     assert got == [("text", "Hi"), ("tool_calls", [{"id": "t1", "name": "read_file", "arguments": "{\"path\": \"/x\"}"}])]
+
+
+def test_cli_lists_mesh_services():
+    import subprocess
+    import sys
+    out = subprocess.run([sys.executable, "-m", "helexa_b200.cli", "--help"], capture_output=True, text=True,
+                         timeout=120).stdout
+    for cmd in ("node", "serve", "status", "router", "tools", "upstream", "bench", "acp"):
+        assert cmd in out
