@@ -95,6 +95,18 @@ def tiny_qwen3_moe() -> ModelConfig:
     )
 
 
+def tiny_qwen3_moe_wide() -> ModelConfig:
+    """Tiny MoE with the 235B-A22B head layout scaled down (16 query / 4 KV heads, top-8
+    of 16 experts), so 8-way tensor / expert parallelism replicates KV heads as the
+    large model does."""
+    return ModelConfig(
+        family="qwen3_moe", name="tiny-qwen3-moe-wide", vocab_size=1024, hidden_size=256,
+        num_hidden_layers=2, num_attention_heads=16, num_key_value_heads=4, head_dim=64,
+        intermediate_size=512, rope_theta=1e6, num_experts=16, num_experts_per_tok=8,
+        moe_intermediate_size=128, norm_topk_prob=True,
+    )
+
+
 def tiny_llama() -> ModelConfig:
     return ModelConfig(
         family="llama", name="tiny-llama", vocab_size=1024, hidden_size=256, num_hidden_layers=2,
@@ -121,6 +133,7 @@ PRESETS = {
     "tiny-qwen3": tiny_qwen3,
     "tiny-qwen3-vl": tiny_qwen3_vl,
     "tiny-qwen3-moe": tiny_qwen3_moe,
+    "tiny-qwen3-moe-wide": tiny_qwen3_moe_wide,
     "qwen3-next-80b-a3b": qwen3_next_80b_a3b,
     "qwen3-8b": qwen3_8b,
     "qwen3-32b": qwen3_32b,

@@ -49,7 +49,8 @@ def _worker(rank, ws, port, name, q, ep=False):
 
 @pytest.mark.parametrize("name,ws,ep", [("tiny-qwen3-next", 2, False), ("tiny-qwen3-next", 4, False),
                                         ("tiny-qwen3-moe", 2, False), ("tiny-qwen3-moe", 2, True),
-                                        ("tiny-qwen3-moe", 4, True)])
+                                        ("tiny-qwen3-moe", 4, True), ("tiny-qwen3-moe-wide", 8, True),
+                                        ("tiny-qwen3-moe-wide", 8, False)])
 def test_tp_matches_single_rank(name, ws, ep):
     """Tensor-parallel (and, with ep, expert-parallel MoE) prefill on gloo ranks against
     the single-rank model."""
