@@ -258,6 +258,14 @@ def create_gateway(catalogue: Catalogue, nodes: list[NodeState], api_keys: dict[
     async def root():
         return {"service": "helexa-b200 gateway"}
 
+    @app.get("/ui")
+    async def ui():
+        """Browser chat client (static page; it calls this gateway's own API)."""
+        import os
+        from fastapi.responses import HTMLResponse
+        with open(os.path.join(os.path.dirname(__file__), "static", "chat.html"), encoding="utf-8") as f:
+            return HTMLResponse(f.read())
+
     @app.get("/metrics")
     async def prom():
         return Response(generate_latest(metrics.reg), media_type="text/plain; version=0.0.4")

@@ -241,3 +241,12 @@ def test_models_listing_advertises_cost():
     with TestClient(app) as c:
         d = c.get("/v1/models").json()["data"][0]
         assert d["cost"] == {"input_per_mtok": 0.2, "output_per_mtok": 0.8}
+
+
+def test_browser_chat_page():
+    fleet = MockFleet()
+    with TestClient(_app(fleet)) as c:
+        r = c.get("/ui")
+        assert r.status_code == 200 and r.headers["content-type"].startswith("text/html")
+        for needle in ("/v1/models", "/v1/chat/completions", "/v1/images/generations", "x-include-thinking"):
+            assert needle in r.text
