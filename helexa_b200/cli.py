@@ -7,6 +7,7 @@
   python -m helexa_b200.cli tools    [--port 8889]
   python -m helexa_b200.cli upstream [--db ledger.sqlite] [--operator-token T=op] [--port 8090]
   python -m helexa_b200.cli bench    --target name=http://host:port [--db bench.sqlite]
+  python -m helexa_b200.cli portal   [--db portal.sqlite] [--ledger-db ledger.sqlite] [--port 8091]
   python -m helexa_b200.cli acp      [--base-url http://127.0.0.1:31313/v1] [--model M]
 
 `serve` and `status` are the reference's `cortex serve|status` (cortex-cli/src/main.rs:
@@ -121,6 +122,11 @@ def main(argv: list[str] | None = None) -> int:
     b.add_argument("--db", default="helexa-bench.sqlite")
     b.add_argument("--interval", type=float, default=3600.0)
     b.add_argument("--port", type=int, default=8099)
+    po = sub.add_parser("portal", help="run the confidential document portal")
+    po.add_argument("--db", default="helexa-portal.sqlite")
+    po.add_argument("--ledger-db", default="helexa-ledger.sqlite")
+    po.add_argument("--host", default="127.0.0.1")
+    po.add_argument("--port", type=int, default=8091)
     a = sub.add_parser("acp", help="run the ACP editor agent on stdin / stdout")
     a.add_argument("--base-url", default="http://127.0.0.1:31313/v1")
     a.add_argument("--model", default="default")
@@ -140,6 +146,13 @@ def main(argv: list[str] | None = None) -> int:
             app = create_upstream(UpstreamConfig(db_path=args.db, operator_tokens=toks,
                                                  signup_allocation=args.signup_allocation))
         uvicorn.run(app, host=args.host, port=args.port)
+        return 0
+    if args.cmd == "portal":
+        import uvicorn
+
+        from .mesh.portal import Portal, create_portal
+        from .mesh.upstream import Ledger
+        uvicorn.run(create_portal(Portal(Ledger(args.ledger_db), args.db)), host=args.host, port=args.port)
         return 0
     if args.cmd == "bench":
         from .mesh.benchd import main as bench_main

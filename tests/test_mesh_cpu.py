@@ -462,5 +462,52 @@ def test_cli_lists_mesh_services():
     import sys
     out = subprocess.run([sys.executable, "-m", "helexa_b200.cli", "--help"], capture_output=True, text=True,
                          timeout=120).stdout
-    for cmd in ("node", "serve", "status", "router", "tools", "upstream", "bench", "acp"):
+    for cmd in ("node", "serve", "status", "router", "tools", "upstream", "bench", "acp", "portal"):
         assert cmd in out
+
+
+# ---- document portal ---------------------------------------------------------------
+from helexa_b200.mesh import portal as pt  # noqa: E402
+
+
+def test_portal_invites_grants_audit_watermark():
+    L = up.Ledger()
+    P = pt.Portal(L)
+    P.create_round("seed", "Seed round")
+    v1 = P.put_document("seed", "deck", "Deck", "Para one.\n\n<script>x</script>")
+    auto = P.mint_invite("seed", "partners", auto_grant=True)
+    manual = P.mint_invite("seed", "public")
+    dead = P.mint_invite("seed", "old")
+    P.revoke_invite(dead)
+    app = pt.create_portal(P)
+    with TestClient(app) as c:
+        assert "Sign in" in c.get("/").text
+        assert "Sign in" in c.get("/r/seed/deck").text  # no session: only the sign-in form
+        # an invite before sign-in is remembered and applied at registration
+        r = c.get(f"/i/{auto}", follow_redirects=False)
+        assert r.status_code == 303 and r.headers["location"] == "/register"
+        r = c.post("/register", data={"email": "ann@fund.io", "password": "long enough pw"})
+        assert "Seed round" in r.text
+        page = c.get("/r/seed/deck").text
+        assert "ann@fund.io" in page and "&lt;script&gt;" in page and "<script>x" not in page
+        assert f"version {v1}" in page
+        c.get("/signout")
+        assert "Sign in" in c.get("/").text
+    with TestClient(app) as c2:  # a forwarded, non-auto code yields a pending, named grant
+        c2.post("/register", data={"email": "bob@x.io", "password": "another password"})
+        c2.get(f"/i/{manual}")
+        assert "awaiting approval" in c2.get("/").text
+        assert "not available" in c2.get("/r/seed/deck").text
+        bob = L.check_password("bob@x.io", "another password")
+        P.set_grant(bob, "seed", "active")
+        assert "Para one." in c2.get("/r/seed/deck").text
+        c2.get(f"/i/{dead}")  # a revoked code changes nothing
+        P.set_grant(bob, "seed", "revoked")
+        assert "not available" in c2.get("/r/seed/deck").text
+    assert c2.post("/signin", data={"email": "bob@x.io", "password": "wrong"}).status_code == 200
+    log = P.audit_log()
+    views = [(e["email"], e["document"], e["version"]) for e in log if e["kind"] == "view"]
+    assert views == [("ann@fund.io", "deck", v1), ("bob@x.io", "deck", v1)]
+    assert any(e["kind"] == "denied" and e["email"] == "bob@x.io" for e in log)
+    # a portal session is not a ledger session and vice versa
+    assert L.session_account("nope") is None and P.session_account(L.new_session(bob)) is None
