@@ -84,7 +84,18 @@ class DiTConfig:
                    norm_eps=d.get("norm_eps", 1e-5), qk_norm=d.get("qk_norm", True),
                    cap_feat_dim=d.get("cap_feat_dim", 2560), patch=ps[0], f_patch=fps[0],
                    rope_theta=float(d.get("rope_theta", 256.0)), t_scale=float(d.get("t_scale", 1000.0)),
-                   axes_dims=tuple(d.get("axes_dims", (32, 48, 48))), axes_lens=tuple(d.get("axes_lens", (1024, 512, 512))))
+                   axes_dims=tuple(d.get("axes_dims", (32, 48, 48))), axes_lens=tuple(d.get("axes_lens", (1024, 512, 512))),
+                   adaln_dim=min(d.get("dim", 3840), 256), t_mid=d.get("t_embed_mid", 1024))
+
+    def to_json(self) -> dict:
+        """diffusers transformer/config.json keys of this configuration (plus
+        `t_embed_mid`, this repository's key for a non-default timestep-MLP width)."""
+        return {"in_channels": self.in_channels, "dim": self.dim, "n_layers": self.n_layers,
+                "n_refiner_layers": self.n_refiner_layers, "n_heads": self.n_heads, "n_kv_heads": self.n_heads,
+                "norm_eps": self.norm_eps, "qk_norm": self.qk_norm, "cap_feat_dim": self.cap_feat_dim,
+                "all_patch_size": [self.patch], "all_f_patch_size": [self.f_patch], "rope_theta": self.rope_theta,
+                "t_scale": self.t_scale, "axes_dims": list(self.axes_dims), "axes_lens": list(self.axes_lens),
+                "t_embed_mid": self.t_mid}
 
 
 @dataclass
@@ -105,6 +116,12 @@ class VaeConfig:
                    layers_per_block=d.get("layers_per_block", 2), norm_groups=d.get("norm_num_groups", 32),
                    scaling_factor=d.get("scaling_factor", 0.3611), shift_factor=d.get("shift_factor", 0.1159) or 0.0,
                    mid_attention=d.get("mid_block_add_attention", True))
+
+    def to_json(self) -> dict:
+        return {"latent_channels": self.latent_channels, "out_channels": self.out_channels,
+                "block_out_channels": list(self.block_out_channels), "layers_per_block": self.layers_per_block,
+                "norm_num_groups": self.norm_groups, "scaling_factor": self.scaling_factor,
+                "shift_factor": self.shift_factor, "mid_block_add_attention": self.mid_attention}
 
 
 def tiny_dit_config(cap_feat_dim: int = 256) -> DiTConfig:

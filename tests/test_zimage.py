@@ -275,3 +275,32 @@ def test_images_api_on_cpu():
         assert r.status_code == 404
         assert c.post("/models/unload", json={"model_id": "zimg"}).status_code == 200
         assert "zimg" not in {m["id"] for m in c.get("/models").json()["models"]}
+
+
+def test_load_pipeline_from_diffusers_directory(tmp_path):
+    """A diffusers-layout directory (model_index.json, transformer/, vae/, text_encoder/)
+    loads through the same tensor names the random-init path uses and generates."""
+    import json
+
+    from safetensors.torch import save_file
+
+    from helexa_b200.runtime.image_serving import is_image_source, load_pipeline_dir
+    from helexa_b200.weights.random_init import save_safetensors
+    lm_cfg = get_preset("tiny-qwen3")
+    dcfg = zi.tiny_dit_config(cap_feat_dim=lm_cfg.hidden_size)
+    vcfg = zi.tiny_vae_config()
+    (tmp_path / "model_index.json").write_text(json.dumps({"_class_name": "ZImagePipeline"}))
+    for sub, cfg, shapes, seed in (("transformer", dcfg, zi.dit_weight_shapes(dcfg), 2),
+                                   ("vae", vcfg, zi.vae_decoder_shapes(vcfg), 3)):
+        (tmp_path / sub).mkdir()
+        (tmp_path / sub / "config.json").write_text(json.dumps(cfg.to_json()))
+        save_file(zi.random_weights(shapes, seed=seed, std=0.05), str(tmp_path / sub / "model.safetensors"))
+    save_safetensors(lm_random_weights(lm_cfg, seed=1), lm_cfg, str(tmp_path / "text_encoder"))
+    assert is_image_source(str(tmp_path)) and not is_image_source(str(tmp_path / "vae"))
+    pipe = load_pipeline_dir(str(tmp_path), "cpu")
+    assert pipe.dit.cfg == dcfg and pipe.vae.cfg == vcfg
+    ref, _ = _tiny_pipeline()
+    lat, cap = torch.randn(16, 8, 8), torch.randn(5, dcfg.cap_feat_dim)
+    assert torch.allclose(pipe.dit.forward(lat, 0.4, cap), ref.dit.forward(lat, 0.4, cap), atol=1e-5)
+    r = pipe.generate([3, 4, 5], width=32, height=32, steps=2, seed=0)
+    assert r.rgb.shape == (32, 32, 3)
