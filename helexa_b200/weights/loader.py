@@ -139,7 +139,7 @@ def discover_capabilities(path: str) -> list[str]:
     """Capabilities of a model directory from its files alone, without loading it (the
     reference derives image / vision capability from the local HF cache the same way):
     a diffusers pipeline -> ["image"]; a config with a vision tower or vision token ids ->
-    chat + vision (this node serves the text path only); otherwise chat + completion."""
+    chat + completion + vision; otherwise chat + completion."""
     import json
     kind = classify_dir(path)
     if kind == "diffusers":
